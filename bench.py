@@ -1,0 +1,382 @@
+"""Benchmark of the B200 ternary decode path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--kind 5|0]
+
+Workload: the group-128 ternary matvec at the Qwen3-1.7B MLP gate/up shape,
+K=2048, N=6144, trit5 codes (kind 5; --kind 0 for the 2-bit image), weights drawn i.i.d. with
+P(w=0)=0.4, P(+-1)=0.3, fp16 scales |N(0,1)|*0.02, x ~ N(0,1).  Copy 0 is the exact seed-0 draw of
+the reference's generator; the other copies are independent device draws of the same
+distribution.  One step = one launch over `--copies` distinct weight copies (96 copies = 264 MB,
+more than the 126 MB L2, so every step streams from HBM) and as many distinct activations:
+each copy is quantised (the firmware's pow-2 int8), multiplied in the engine's exact integer
+arithmetic and scaled to fp32 (firmware/infer_float.c:398 infer_matvec_f).
+
+`value`: whole-job GB/s of algorithmic bytes (scales + codes, no row padding, plus x and y) with
+inputs resident in HBM; `e2e`: the same through the public API with x copied host->device and y
+device->host every step; `roofline`: the matvec kernel's achieved bandwidth against the
+measured HBM copy peak; `cpu_baseline`: the C oracle on this host's cores.
+
+Multi-GPU (torchrun): every rank runs its own copies (weak scaling, no collective on the data
+path); the time is the max over ranks.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_COLS, N_ROWS = 2048, 6144
+NOMINAL_HBM_GBS = 8000.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kind):
+    """dram bytes per launch of the timed kernel, from the committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", f"matvec_k{kind}_config0_ncu.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(kind, seconds=10.0, threads=None):
+    """The C oracle (oracle/trx_oracle.c) on this host: repeated config-0 float projections."""
+    from oracle import build as cor
+    from trixium_b200 import image, layout as L
+    lib = cor.lib()
+    if threads:
+        lib.trxo_set_threads(int(threads))
+    t, x = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=kind)
+    alg = L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * (K_COLS + N_ROWS)
+    cor.matvec_f(t.packed, N_ROWS, K_COLS, kind, t.bias, t.rshift, x)   # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cor.matvec_f(t.packed, N_ROWS, K_COLS, kind, t.bias, t.rshift, x)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return {"value": alg * n / dt / 1e9, "unit": "GB/s", "cores": int(lib.trxo_threads()), "kind": "port",
+            "sample": f"{n} config-0 float projections (K=2048, N=6144, kind {kind}) in {dt:.1f} s, "
+                      f"C oracle oracle/trx_oracle.c, OpenMP over rows"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference algorithm on the host cores (the C port of the oracle;
+    the reference itself is Python that does not travel to the GPU box)."""
+    if rank != 0:
+        return
+    from oracle import build as cor
+    from trixium_b200 import image, layout as L
+    lib = cor.lib()
+    t, x = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=args.kind)
+    alg = L.algorithmic_bytes(N_ROWS, K_COLS, args.kind) + 4 * (K_COLS + N_ROWS)
+    for _ in range(args.warmup):
+        cor.matvec_f(t.packed, N_ROWS, K_COLS, args.kind, t.bias, t.rshift, x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cor.matvec_f(t.packed, N_ROWS, K_COLS, args.kind, t.bias, t.rshift, x)
+    dt = time.perf_counter() - t0
+    value = alg * args.steps / dt / 1e9
+    cores = int(lib.trxo_threads())
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(args.kind), "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": "one config-0 float projection per step (C oracle, OpenMP)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def metric_name(kind):
+    return f"ternary matvec HBM GB/s (config 0: K=2048 N=6144, {'trit5' if kind == 5 else '2-bit'})"
+
+
+def workload_config(args):
+    return {"workload": f"config0 ternary matvec K={K_COLS} N={N_ROWS} kind={args.kind}, "
+                        f"{args.copies} distinct weight copies + activations per step",
+            "l2": f"inputs larger than L2 ({args.copies} copies per step)",
+            "global_batch": 1, "seq_len": 1, "parallelism": f"replicas{args.gpus}"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kind", type=int, default=5, choices=[0, 5])
+    ap.add_argument("--copies", type=int, default=96)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the per-launch graph and e2e legs")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from trixium_b200 import image, layout as L, ops
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    ctx = ops.Context(local)
+
+    kind, C = args.kind, args.copies
+    # Copy 0: the reference generator's seed-0 draw; copies 1..C-1 drawn on the device.
+    t0, x0 = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=kind)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    scales_all = [torch.from_numpy(t0.scales).to(dev)]
+    codes_all = [torch.from_numpy(t0.codes).to(dev)]
+    for _ in range(1, C):
+        c, s = image.synthetic_codes_scales_torch(gen, N_ROWS, K_COLS, dev)
+        codes_all.append(c)
+        scales_all.append(s)
+    # One (B, R) for every copy so a single entry describes them (max over the copies).
+    smax = max(float(s.float().abs().max()) for s in scales_all)
+    B = image.scale_bias(np.array([smax], dtype=np.float16))
+    R = max(image.result_shift(s.cpu().numpy(), B) for s in scales_all)
+    rb = L.row_bytes(K_COLS, kind)
+    wstride = N_ROWS * rb
+    W = torch.empty(C * wstride, dtype=torch.uint8, device=dev)
+    for j in range(C):
+        W[j * wstride:(j + 1) * wstride] = image.pack_rows_torch(scales_all[j], codes_all[j], kind)
+    del codes_all, scales_all
+    X = torch.randn(C, K_COLS, generator=gen, device=dev)
+    X[0] = torch.from_numpy(x0).to(dev)
+    Y = torch.empty(C, N_ROWS, dtype=torch.float32, device=dev)
+    wt = ops.DeviceTensor.from_packed(W, N_ROWS, K_COLS, kind, B, R)
+
+    # Parity of copy 0 with the C oracle before timing (bit-exact float results).
+    from oracle import build as cor
+    ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
+    ctx.raise_on_error()
+    y_or, bad = cor.matvec_f(t0.packed if (t0.bias, t0.rshift) == (B, R) else
+                             image.pack_rows(t0.scales, t0.codes, kind), N_ROWS, K_COLS, kind, B, R, x0)
+    parity = bool(bad == 0 and np.array_equal(Y[0].cpu().numpy().view(np.uint32), y_or.view(np.uint32)))
+
+    alg_per_copy = L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * (K_COLS + N_ROWS)
+    alg_per_step = alg_per_copy * C
+
+    def step():
+        ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ctx.raise_on_error()
+
+    # Per-launch variant: one launch per copy (a single 2.75 MB matvec per kernel), in a CUDA graph.
+    single_ms = None
+    try:
+        if args.no_extra:
+            raise RuntimeError("skipped (--no-extra)")
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                for j in range(C):
+                    ops.matvec_f(ctx, per_copy(ops, wt, W, j, wstride, kind, B, R), X[j], Y[j])
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                for j in range(C):
+                    ops.matvec_f(ctx, per_copy(ops, wt, W, j, wstride, kind, B, R), X[j], Y[j])
+        torch.cuda.synchronize()
+        for _ in range(3):
+            g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        single_ms = a.elapsed_time(b) / 10
+        del g
+    except Exception as exc:  # reported, not fatal
+        single_ms = None
+        print(f"per-launch graph variant failed: {exc}", file=sys.stderr)
+
+    # e2e: public API with host buffers (pinned), H2D of x and D2H of y inside the timed region.
+    Xh = X.cpu().pin_memory()
+    Yh = torch.empty(C, N_ROWS, dtype=torch.float32).pin_memory()
+    Xd = torch.empty_like(X)
+
+    def e2e_step():
+        Xd.copy_(Xh, non_blocking=True)
+        ops.matvec_f_batch(ctx, wt, wstride, Xd, K_COLS, Y, N_ROWS, C)
+        Yh.copy_(Y, non_blocking=True)
+
+    e2e_steps = 0 if args.no_extra else args.steps
+    for _ in range(0 if args.no_extra else args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max(a.elapsed_time(b), 1e-9) if e2e_steps else float("nan")
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, launch_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, launch_ms = t.tolist()
+        pt = torch.tensor([1 if parity else 0], device=dev)
+        dist.all_reduce(pt, op=dist.ReduceOp.MIN)
+        parity = bool(pt.item())
+
+    peak, peak_src = measured_peaks()
+    achieved = alg_per_step / (launch_ms * 1e-3) / 1e9
+    value = alg_per_step * args.steps * world / (ms * 1e-3) / 1e9
+    out = {
+        "metric": metric_name(kind), "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8",
+        "data": "synthetic", "config": workload_config(args),
+        "parity_copy0_bitexact": parity,
+        "frac_of_8tbs_nominal": round(value / world / NOMINAL_HBM_GBS, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                     "traffic": profile_traffic(kind),
+                     "algorithmic_bytes_per_launch": alg_per_step,
+                     "kernel": "trx::tmv_kernel (trx_matvec_f_batch)"},
+        "per_launch_single_matvec": None if single_ms is None else {
+            "ms_per_matvec": single_ms / C, "gbs": round(alg_per_copy * C / (single_ms * 1e-3) / 1e9, 1)},
+        "e2e": {"value": round(alg_per_step * args.steps * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": C * K_COLS * 4, "d2h_bytes_per_step": C * N_ROWS * 4},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(kind, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+_pc_cache = {}
+
+
+def per_copy(ops, wt, W, j, wstride, kind, B, R):
+    key = j
+    if key not in _pc_cache:
+        _pc_cache[key] = ops.DeviceTensor.from_packed(W[j * wstride:(j + 1) * wstride], N_ROWS, K_COLS, kind, B, R)
+    return _pc_cache[key]
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+/*
+ * trixium_b200.h -- C ABI of the B200 ternary decode path (libtrixium_b200.so).
+ *
+ * The library replaces the TriXium engine's matvec and the vector-unit operations that wrap it
+ * on the decode path.  Every entry point:
+ *   - takes device pointers (caller-owned) and a cudaStream_t, and only enqueues work;
+ *   - returns a trx_status (0 = ok, < 0 = error); arguments are checked on the host before
+ *     anything is enqueued, and nothing aborts the process;
+ *   - reports conditions found on the device (int48/int32 overflow, invalid trit5 bytes,
+ *     a bounded wait that ran out) in the context's error word, read with trx_get_error().
+ *
+ * Packed tensors are the converter's row packets byte for byte: per output row
+ * [ceil(G/16) x 32 bytes of fp16 group scales][codes: 2-bit (kind 0) or 5 trits per byte,
+ * 26 bytes per 128-group (kind 5), padded to 32 bytes], rows back to back
+ * (reference: model/layout.py:17-30, :184-217; model/bons.py:115-175).  The device pointer of a
+ * packed tensor must be 16-byte aligned.
+ */
+#ifndef TRIXIUM_B200_H
+#define TRIXIUM_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int trx_status;
+
+#define TRX_OK               0
+#define TRX_ERR_ARG         -1   /* bad pointer, size, alignment or parameter */
+#define TRX_ERR_LAYOUT      -2   /* kind/cols not a ternary row-packet layout; invalid trit5 byte */
+#define TRX_ERR_OVERFLOW    -3   /* |acc| >= 2^47 or |result| >= 2^31 (model/bitexact.py:116,118) */
+#define TRX_ERR_CUDA        -4   /* a CUDA runtime call failed */
+#define TRX_ERR_TIMEOUT     -5   /* a bounded device-side wait ran out */
+#define TRX_ERR_UNSUPPORTED -6
+
+/* Error-word bits (trx_get_error). */
+#define TRX_DEV_OVERFLOW   0x1u
+#define TRX_DEV_BADBYTE    0x2u
+#define TRX_DEV_TIMEOUT    0x4u
+
+#define TRX_KIND_TERNARY   0    /* KIND_TERNARY,  model/layout.py:46 */
+#define TRX_KIND_TERNARY5  5    /* KIND_TERNARY5, model/layout.py:50 */
+
+/* The fields of a BONS tensor-table entry a matvec needs (model/layout.py:311-333). */
+typedef struct trx_entry {
+    uint32_t rows;      /* output rows (this device's shard)       */
+    uint32_t cols;      /* K, a multiple of 128                     */
+    int32_t  kind;      /* TRX_KIND_TERNARY or TRX_KIND_TERNARY5   */
+    int32_t  bias;      /* B: the tensor's scale bias  (entry byte 36) */
+    int32_t  rshift;    /* R: the tensor's result shift (entry byte 37) */
+} trx_entry;
+
+/* Per-device context: the device error word and the library's scratch. */
+typedef struct trx_ctx trx_ctx;
+
+/* Create a context on `device` (allocates its scratch; call outside stream capture). */
+trx_status trx_create(trx_ctx **ctx, int device);
+trx_status trx_destroy(trx_ctx *ctx);
+
+/* Synchronise `stream`, return the accumulated device error bits in *bits and clear them. */
+trx_status trx_get_error(trx_ctx *ctx, cudaStream_t stream, uint32_t *bits);
+
+/* Bytes of one row packet and of a whole tensor (model/layout.py:215-217). */
+uint64_t trx_row_bytes(uint32_t cols, int32_t kind);
+
+/*
+ * Integer engine matvec: out[n] = (sum_g (gs[n,g]*m11[n,g]) <<or>> (e16[n,g]+B)) >> R as int32,
+ * gs the exact sum over the group of (code-1)*x8.  Bit-exact with model/bitexact.py:101-119
+ * (matvec_ternary).  x8: K int8.
+ */
+trx_status trx_matvec_i8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                         const int8_t *d_x8, int32_t *d_out, cudaStream_t stream);
+
+/*
+ * Multi-row engine matvec: nb independent rows of x8 ([nb, K] int8) against one weight pass,
+ * out [nb, rows] int32 (model/bitexact.py:121-125, matvec_ternary_rows).  nb <= 8.
+ */
+trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                              const int8_t *d_x8, int nb, int32_t *d_out, cudaStream_t stream);
+
+/*
+ * Power-of-two int8 activation quantisation: e8 = frexp(max|x|) - 7,
+ * x8 = clamp(lround(x * 2^-e8), -127, 127) with the mirror's rounding (floor(x+0.5) in fp32).
+ * model/mirror.py:45-51; firmware/infer_internal.h:60-124 (f32_quant_e8, f32_pack_q8x4).
+ * d_e8: one int32 on the device.
+ */
+trx_status trx_quantize_pow2(trx_ctx *ctx, const float *d_x, uint32_t n, int8_t *d_x8,
+                             int32_t *d_e8, cudaStream_t stream);
+
+/*
+ * Float projection in the engine's arithmetic (the firmware's infer_matvec_f,
+ * firmware/infer_float.c:398; model/mirror.py:648-678): quantise x (the whole vector, one
+ * exponent), the integer matvec, y = float(int32) * 2^(e8 + R - B).  Fused in one launch.
+ * If d_norm_w is not NULL, x is first RMS-normalised with the canonical 64-partial sum of
+ * squares: x <- (x * 1/sqrt(ss/K + eps)) * w  (model/mirror.py:697-700, :576-591).
+ * If d_resid is not NULL, y = resid + projection (the residual add, model/mirror.py:1013,1024).
+ */
+trx_status trx_matvec_f(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                        const float *d_x, const float *d_norm_w, float eps,
+                        const float *d_resid, float *d_y, cudaStream_t stream);
+
+/*
+ * fp-mode projection: y[n] = sum_g scale[n,g] * sum_{j in g} (code-1) * x_j in fp32
+ * (model/fastref.py:103-125, HybridRef.matmul for one row of X).
+ */
+trx_status trx_matvec_fp(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                         const float *d_x, float *d_y, cudaStream_t stream);
+
+/*
+ * Gate/up projection with the SwiGLU epilogue (model/mirror.py:1016-1020;
+ * model/fastref.py:253-255): act[i] = silu(gate(x)[i]) * up(x)[i], both projections in the
+ * engine's arithmetic on the same quantised (optionally RMS-normalised) x.
+ */
+trx_status trx_matvec_swiglu(trx_ctx *ctx, const trx_entry *gate, const void *d_gate,
+                             const trx_entry *up, const void *d_up,
+                             const float *d_x, const float *d_norm_w, float eps,
+                             float *d_act, cudaStream_t stream);
+
+/* Check a packed trit5 tensor for bytes above 242 (gateware/core/trit5.py:37-39).  Sets
+ * TRX_DEV_BADBYTE in the error word when one is found. */
+trx_status trx_validate_packed(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                               cudaStream_t stream);
+
+/*
+ * Batched benchmark/driver form: njobs independent float projections (one launch), job j
+ * reading x + j*x_stride and packed + j*w_stride, writing y + j*y_stride.  Same arithmetic as
+ * trx_matvec_f without norm or residual.
+ */
+trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                              uint64_t w_stride, const float *d_x, uint64_t x_stride,
+                              float *d_y, uint64_t y_stride, int njobs, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TRIXIUM_B200_H */

@@ -1,0 +1,196 @@
+"""numpy restatement of the reference's ternary decode-path numerics.  TEST INFRASTRUCTURE ONLY.
+
+Each function cites the reference lines it restates (paths relative to the TriXium tree).
+Nothing on the product path may import this module.
+"""
+
+import numpy as np
+
+f32 = np.float32
+POW3 = np.array([1, 3, 9, 27, 81], dtype=np.int64)
+
+
+# Row packets ------------------------------------------------------------------------------------
+
+def row_bytes(cols, kind):
+    """model/layout.py:189-217: ceil(G/16) scale beats + code beats (trit5: 26 B/group, padded)."""
+    g = cols // 128
+    sb = -(-g // 16) * 32
+    cb = 26 * g if kind == 5 else 32 * g
+    return sb + -(-cb // 32) * 32
+
+
+def decode_packed(packed, rows, cols, kind):
+    """model/bons.py:177-200 (decode_rows) with trit5_unpack_rows (:125-130):
+    packed bytes -> (scales fp16 (rows,G), codes uint8 (rows,cols))."""
+    g = cols // 128
+    rb = row_bytes(cols, kind)
+    d = np.frombuffer(np.asarray(packed, dtype=np.uint8).tobytes(), dtype=np.uint8).reshape(rows, rb)
+    scales = d[:, :2 * g].copy().view(np.float16)
+    body = d[:, -(-g // 16) * 32:].astype(np.int64)
+    if kind == 5:
+        b = body[:, :26 * g].reshape(rows, g, 26, 1)
+        digits = (b // POW3) % 3
+        codes = digits.reshape(rows, g, 130)[:, :, :128].reshape(rows, cols)
+    else:
+        q = body[:, :cols // 4]
+        codes = np.stack([(q >> s) & 3 for s in (0, 2, 4, 6)], axis=-1).reshape(rows, cols)
+    return scales, codes.astype(np.uint8)
+
+
+def trit5_invalid(packed, rows, cols):
+    """Bytes above 242 in the code groups (gateware/core/trit5.py:37-39 flags them)."""
+    g = cols // 128
+    rb = row_bytes(cols, 5)
+    d = np.asarray(packed, dtype=np.uint8).reshape(rows, rb)
+    body = d[:, -(-g // 16) * 32:][:, :26 * g]
+    return int((body > 242).sum())
+
+
+# Integer engine ---------------------------------------------------------------------------------
+
+def fp16_parts(s):
+    """model/bitexact.py:56-68: fp16 = m11 * 2**e16 exactly."""
+    u = np.asarray(s, dtype=np.float16).view(np.uint16).astype(np.int64)
+    e = (u >> 10) & 31
+    assert not np.any(e == 31), "fp16 inf/nan in scales"
+    m = np.where(e > 0, (u & 1023) | 1024, u & 1023)
+    return np.where(u >> 15, -m, m), np.where(e > 0, e - 25, -24)
+
+
+class OverflowError48(ArithmeticError):
+    pass
+
+
+def matvec_int(scales, codes, x8, B, R):
+    """model/bitexact.py:101-119 (matvec_ternary): exact group sums of (code-1)*x8, each times
+    m11 and shifted by e16+B (floor shift when negative), summed in int64, then >> R.
+    Raises OverflowError48 where the reference asserts (:116, :118)."""
+    rows, cols = codes.shape
+    g = cols // 128
+    w = codes.astype(np.int64).reshape(rows, g, 128) - 1
+    gs = np.einsum("rgk,gk->rg", w, np.asarray(x8, dtype=np.int64).reshape(g, 128))
+    m11, e16 = fp16_parts(scales)
+    sh = e16 + B
+    prod = gs * m11
+    contrib = np.where(sh >= 0, prod << np.clip(sh, 0, 63), prod >> np.clip(-sh, 0, 63))
+    acc = contrib.sum(axis=1)
+    if np.any(np.abs(acc) >= 2 ** 47):
+        raise OverflowError48("int48 accumulator overflow")
+    res = acc >> R
+    if np.any(np.abs(res) >= 2 ** 31):
+        raise OverflowError48("int32 result overflow")
+    return res.astype(np.int32)
+
+
+def group_sums(codes, x8):
+    """The exact per-(row, group) sums gs (model/bitexact.py:108)."""
+    rows, cols = codes.shape
+    g = cols // 128
+    w = codes.astype(np.int64).reshape(rows, g, 128) - 1
+    return np.einsum("rgk,gk->rg", w, np.asarray(x8, dtype=np.int64).reshape(g, 128))
+
+
+# Activation quantisation ------------------------------------------------------------------------
+
+def lround_mirror(x):
+    """model/mirror.py:34-35 (_lroundf) on fp32 input: floor(x + 0.5) for x >= 0 and
+    ceil(x - 0.5) below, the +-0.5 added IN FP32 (numpy keeps the fp32 dtype), so x = 0.5-2**-25
+    rounds to 1."""
+    x = np.asarray(x, dtype=f32)
+    up = np.floor((x + f32(0.5)).astype(f32))
+    dn = np.ceil((x - f32(0.5)).astype(f32))
+    return np.where(x >= 0, up, dn).astype(np.int64)
+
+
+def quantize_pow2(x):
+    """model/mirror.py:45-51 (_quantize_f_pow2) = firmware f32_quant_e8/f32_pack_q8x4
+    (firmware/infer_internal.h:60-124): e8 = frexp(amax)[1] - 7, q = clip(lround(x*2**-e8))."""
+    x = np.asarray(x, dtype=f32)
+    amax = np.abs(x).max() if x.size else f32(0)
+    if amax == 0:
+        return np.zeros(x.shape, dtype=np.int8), 0
+    e8 = int(np.frexp(f32(amax))[1]) - 7
+    q = lround_mirror((x * f32(np.exp2(-e8))).astype(f32))
+    return np.clip(q, -127, 127).astype(np.int8), e8
+
+
+def matvec_f(scales, codes, x, B, R):
+    """model/mirror.py:648-678 (matvec_f, quantised mode, one K-segment): quantise x, the
+    engine's int32 result, scaled by fp32 2**(e8+R-B)."""
+    x8, e8 = quantize_pow2(x)
+    res = matvec_int(scales, codes, x8, B, R)
+    sc = f32(np.exp2(f32(e8 + R - B)))
+    return (res.astype(f32) * sc).astype(f32)
+
+
+def matvec_f64(scales, codes, x):
+    """fp64 reference of the fp projection: sum over groups of scale * sum((code-1)*x)
+    (the float reference of test/model/test_bitexact.py:49-56, and model/fastref.py:119-125
+    without its fp32 rounding)."""
+    rows, cols = codes.shape
+    g = cols // 128
+    w = codes.astype(np.float64).reshape(rows, g, 128) - 1.0
+    gs = np.einsum("rgk,gk->rg", w, np.asarray(x, dtype=np.float64).reshape(g, 128))
+    return (gs * np.asarray(scales, dtype=np.float64)).sum(axis=1)
+
+
+def matvec_fastref(scales, codes, X):
+    """model/fastref.py:103-125: fp16 weight cache (code-1)*scale, X @ W.T in fp32."""
+    rows, cols = codes.shape
+    W = ((codes.astype(f32).reshape(rows, -1, 128) - f32(1.0))
+         * np.asarray(scales, dtype=np.float16).astype(f32)[:, :, None]).reshape(rows, cols)
+    W = W.astype(np.float16).astype(f32)
+    return np.atleast_2d(np.asarray(X, dtype=f32)) @ W.T
+
+
+# Canonical reductions (model/mirror.py:576-591, doc/units.md canonical sum64) -------------------
+
+def sumsq64(v):
+    """model/mirror.py:576-591: 64 strided fp32 partials, then the halving tree."""
+    v = np.asarray(v, dtype=f32)
+    sq = (v * v).astype(f32)
+    n = len(sq)
+    P = np.zeros(64, dtype=f32)
+    full = n // 64 * 64
+    for r in range(0, full, 64):
+        P = (P + sq[r:r + 64]).astype(f32)
+    if n - full:
+        P[:n - full] = (P[:n - full] + sq[full:]).astype(f32)
+    w = 32
+    while w:
+        P[:w] = (P[:w] + P[w:2 * w]).astype(f32)
+        w //= 2
+    return P[0]
+
+
+def rmsnorm(x, w, eps):
+    """model/mirror.py:697-700: r = 1/sqrt(ss/n + eps) (fp32 ops), (x*r)*w."""
+    x = np.asarray(x, dtype=f32)
+    ss = sumsq64(x)
+    r = f32(1.0) / f32(np.sqrt(f32(f32(ss / f32(len(x))) + f32(eps))))
+    return ((x * r).astype(f32) * np.asarray(w, dtype=f32)).astype(f32)
+
+
+def l2norm(x, eps):
+    """model/mirror.py:702-705: x * (1/max(sqrt(ss), eps))."""
+    x = np.asarray(x, dtype=f32)
+    nrm = f32(np.sqrt(sumsq64(x)))
+    nrm = max(nrm, f32(eps))
+    return (x * f32(f32(1) / nrm)).astype(f32)
+
+
+def silu(x):
+    """model/mirror.py:713 (mathematical profile): x / (1 + exp(-x)) in fp32."""
+    x = np.asarray(x, dtype=f32)
+    return (x / (f32(1.0) + np.exp(-x, dtype=f32))).astype(f32)
+
+
+def sigmoid(x):
+    x = np.asarray(x, dtype=f32)
+    return (f32(1.0) / (f32(1.0) + np.exp(-x, dtype=f32))).astype(f32)
+
+
+def argmax_first(v):
+    """Greedy argmax, ties to the smallest index (doc/units.md:149)."""
+    return int(np.argmax(np.asarray(v)))

@@ -1,0 +1,165 @@
+"""Generate the golden fixtures for the ternary decode path from the reference's own Python.
+
+Run in a container that has the TriXium reference tree (read-only) at TRIXIUM_REF
+(default /root/reference):
+
+    python tests/golden/make_golden.py
+
+It imports the reference's `model.bons` (TensorSpec + encode_rows: the converter's row-packet
+bytes, with its per-tensor B/R), `model.bitexact` (matvec_ternary, the engine's integer spec),
+`model.mirror` (_quantize_f_pow2 and _sumsq64), and writes small .npz files next to this
+script.  The GPU box never reads the reference: the tests read only these fixtures.
+
+Cases follow the reference's own tests where they exist:
+* test/model/test_bitexact.py:36-56 (seed 42, 64x512, uniform scales, uniform x8),
+* test/model/test_bitexact.py:58-70 (seed 7, 16x12288 all +1 codes, x8 = 127: the no-overflow
+  bound),
+plus the benchmark distribution at small sizes, ragged G (K = 128, 640, 2944), negative /
+subnormal / zero scales, an all-zero activation, fp32 rounding edges for the quantiser, and
+every trit5 byte value.
+"""
+
+import os
+import sys
+
+import numpy as np
+
+REF = os.environ.get("TRIXIUM_REF", "/root/reference")
+sys.path.insert(0, REF)
+
+from model import bitexact as bx          # noqa: E402
+from model import bons, layout, mirror    # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+f32 = np.float32
+
+
+def ref_pack(name, scales, codes, kind):
+    """The converter's bytes and B/R for one tensor (model/bons.py TensorSpec + encode_rows)."""
+    rows, cols = codes.shape
+    spec = bons.TensorSpec(name, layout.ROLE_FFN_GATE, 0, layout.KIND_TERNARY, rows, cols,
+                           scales=scales, values=codes)
+    spec.kind = kind          # write_image(trit5=True) switches the kind the same way.
+    packed = bons.encode_rows(spec, 0, rows)
+    return packed, spec.bias, spec.rshift
+
+
+def bench_dist(rng, rows, cols):
+    u = rng.random((rows, cols))
+    codes = np.where(u < 0.3, 0, np.where(u < 0.7, 1, 2)).astype(np.uint8)
+    scales = (np.abs(rng.standard_normal((rows, cols // 128))) * 0.02).astype(np.float16)
+    return codes, scales
+
+
+def matvec_case(name, codes, scales, x=None, x8=None):
+    rows, cols = codes.shape
+    out = {}
+    for kind in (layout.KIND_TERNARY, layout.KIND_TERNARY5):
+        packed, B, R = ref_pack(name, scales, codes, kind)
+        out[f"packed_k{kind}"] = packed
+        out["B"], out["R"] = B, R
+        # Round trip through the reference reader.
+        entry = {"kind": kind, "cols": cols}
+        s2, c2 = bons.decode_rows(entry, packed.tobytes())
+        assert np.array_equal(c2, codes) and np.array_equal(s2.view(np.uint16), scales.view(np.uint16))
+    if x8 is None:
+        x8, e8 = mirror._quantize_f_pow2(np.asarray(x, dtype=f32))
+        out["x"] = np.asarray(x, dtype=f32)
+    else:
+        e8 = 0
+    res = bx.matvec_ternary(scales, codes, x8, out["B"], out["R"])
+    out.update(rows=rows, cols=cols, scales=scales, codes=codes, x8=x8, e8=e8, y_int=res)
+    # The mirror's float result of the quantised projection (model/mirror.py:676-678).
+    sc = f32(np.exp2(f32(e8 + out["R"] - out["B"])))
+    out["y_f"] = (res.astype(np.int32).astype(f32) * sc).astype(f32)
+    # fp64 reference of the fp projection on the same fp32 x (test_bitexact.py:49-56).
+    if x is not None:
+        w = codes.astype(np.float64).reshape(rows, -1, 128) - 1.0
+        gs = np.einsum("rgk,gk->rg", w, np.asarray(x, np.float64).reshape(-1, 128))
+        out["y_f64"] = (gs * scales.astype(np.float64)).sum(axis=1)
+    np.savez_compressed(os.path.join(HERE, f"matvec_{name}.npz"), **out)
+    return out
+
+
+def main():
+    # 1. The reference's own matvec accuracy case (test_bitexact.py:36-47).
+    rng = np.random.default_rng(42)
+    M, K = 64, 512
+    scales = rng.uniform(0.01, 0.08, (M, K // 128)).astype(np.float16)
+    codes = rng.integers(0, 3, (M, K), dtype=np.uint8)
+    x8 = rng.integers(-127, 128, K, dtype=np.int8)
+    matvec_case("refacc_64x512", codes, scales, x8=x8)
+
+    # 2. The reference's no-overflow bound (test_bitexact.py:58-70).
+    rng = np.random.default_rng(7)
+    M, K = 16, 12288
+    scales = (np.exp2(rng.uniform(-10, 0, (M, K // 128))) * 0.5).astype(np.float16)
+    codes = np.full((M, K), 2, dtype=np.uint8)
+    x8 = np.full(K, 127, dtype=np.int8)
+    matvec_case("refbound_16x12288", codes, scales, x8=x8)
+
+    # 3. The benchmark distribution at small/ragged sizes (seeded draws: codes, scales, x).
+    for (rows, cols, seed) in [(48, 2048, 0), (33, 640, 1), (7, 128, 2), (64, 4096, 3),
+                               (20, 2944, 4), (16, 6144, 5), (3, 17408, 6)]:
+        rng = np.random.default_rng(seed)
+        codes, scales = bench_dist(rng, rows, cols)
+        x = rng.standard_normal(cols).astype(f32)
+        matvec_case(f"bench_{rows}x{cols}", codes, scales, x=x)
+
+    # 4. Signed, subnormal and zero scales; one all-zero-codes row (w = -1 everywhere).
+    rng = np.random.default_rng(11)
+    rows, cols = 24, 1024
+    codes = rng.integers(0, 3, (rows, cols), dtype=np.uint8)
+    codes[5] = 0
+    s = rng.standard_normal((rows, cols // 128)) * 0.05
+    s[1, :] = 6e-8                          # fp16 subnormals
+    s[2, 3] = 0.0
+    s[3, :] = -np.abs(s[3, :])
+    scales = s.astype(np.float16)
+    x = (rng.standard_normal(cols) * 3).astype(f32)
+    matvec_case("signed_24x1024", codes, scales, x=x)
+
+    # 5. An all-zero activation: x8 = 0, e8 = 0 (model/mirror.py:47-49).
+    rng = np.random.default_rng(12)
+    codes, scales = bench_dist(rng, 8, 256)
+    matvec_case("zerox_8x256", codes, scales, x=np.zeros(256, f32))
+
+    # 6. Quantiser edges: values at the fp32 rounding boundaries of floor(x + 0.5).
+    rng = np.random.default_rng(13)
+    xs = []
+    for e in (0, -3, 5):
+        base = rng.standard_normal(256).astype(f32) * f32(2.0 ** e)
+        base[0] = f32(127.99) * f32(2.0 ** (e - 7 + 7)) if e == 0 else base[0]
+        # Values whose scaled magnitude is k + 0.5 - 2**-25 and k + 0.5 exactly.
+        amax = np.abs(base).max()
+        e8 = int(np.frexp(f32(amax))[1]) - 7
+        for i, k in enumerate(range(0, 40)):
+            v = f32(k) + f32(0.5)
+            base[10 + 2 * i] = f32(np.nextafter(v, f32(0))) * f32(np.exp2(e8)) * (1 if k % 2 else -1)
+            base[11 + 2 * i] = v * f32(np.exp2(e8)) * (-1 if k % 2 else 1)
+        xs.append(base)
+    xq = np.stack(xs)
+    q = [mirror._quantize_f_pow2(v) for v in xq]
+    np.savez_compressed(os.path.join(HERE, "quantize.npz"), x=xq,
+                        x8=np.stack([a for a, _ in q]), e8=np.array([b for _, b in q]))
+
+    # 7. The canonical sum of squares (model/mirror.py:576-591) at the norm widths.
+    rng = np.random.default_rng(14)
+    sums = {}
+    for n in (64, 100, 128, 256, 2048, 4096, 5120):
+        v = (rng.standard_normal(n) * 2).astype(f32)
+        sums[f"v{n}"] = v
+        sums[f"ss{n}"] = np.array(mirror._sumsq64(v), dtype=f32)
+    np.savez_compressed(os.path.join(HERE, "sumsq64.npz"), **sums)
+
+    # 8. Every trit5 byte through the reference reader (model/bons.py:125-130).
+    g = 10
+    body = np.zeros((1, 26 * g), dtype=np.uint8)
+    body[0, :256] = np.arange(256, dtype=np.uint8)
+    digits = bons.trit5_unpack_rows(body, 128 * g)
+    np.savez_compressed(os.path.join(HERE, "trit5_bytes.npz"), body=body, codes=digits)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,39 @@
+"""The C-ABI library loads and exports every entry point include/trixium_b200.h declares.
+
+No compute runs here (no GPU in the build container): only symbol lookup and the host-only
+geometry helper.
+"""
+import os
+import re
+
+import pytest
+
+from trixium_b200 import _lib, layout as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "trixium_b200.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:trx_status|uint64_t)\s+(trx_\w+)\s*\(", src, re.M)))
+
+
+def test_header_and_binding_agree():
+    assert declared_symbols() == sorted(_lib.SYMBOLS)
+
+
+def test_library_exports_every_symbol():
+    lib = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+@pytest.mark.parametrize("cols", [128, 256, 640, 2048, 2944, 4096, 5120, 6144, 12288, 17408])
+@pytest.mark.parametrize("kind", [L.KIND_TERNARY, L.KIND_TERNARY5])
+def test_row_bytes(cols, kind):
+    assert _lib.lib().trx_row_bytes(cols, kind) == L.row_bytes(cols, kind)
+
+
+def test_row_bytes_rejects_bad_layouts():
+    assert _lib.lib().trx_row_bytes(100, 5) == 0
+    assert _lib.lib().trx_row_bytes(128, 3) == 0

@@ -1,0 +1,84 @@
+"""ctypes binding of libtrixium_b200.so (the C ABI declared in include/trixium_b200.h).
+
+The library is loaded from this package directory only; there is no fallback: if it is missing
+or fails to load, importing the ops raises.
+"""
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtrixium_b200.so")
+
+TRX_OK = 0
+ERRORS = {
+    -1: "TRX_ERR_ARG", -2: "TRX_ERR_LAYOUT", -3: "TRX_ERR_OVERFLOW", -4: "TRX_ERR_CUDA",
+    -5: "TRX_ERR_TIMEOUT", -6: "TRX_ERR_UNSUPPORTED",
+}
+DEV_OVERFLOW, DEV_BADBYTE, DEV_TIMEOUT = 0x1, 0x2, 0x4
+
+# Every symbol the header declares (tests check the library exports all of them).
+SYMBOLS = (
+    "trx_create", "trx_destroy", "trx_get_error", "trx_row_bytes", "trx_matvec_i8",
+    "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
+    "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch",
+)
+
+
+class TrxError(RuntimeError):
+    def __init__(self, status, where=""):
+        self.status = status
+        super().__init__(f"{where}: {ERRORS.get(status, status)}")
+
+
+class TrxDeviceError(RuntimeError):
+    def __init__(self, bits):
+        self.bits = bits
+        names = [n for b, n in ((DEV_OVERFLOW, "overflow"), (DEV_BADBYTE, "invalid trit5 byte"),
+                                (DEV_TIMEOUT, "bounded wait timed out")) if bits & b]
+        super().__init__("device error: " + ", ".join(names or [hex(bits)]))
+
+
+class Entry(ctypes.Structure):
+    """trx_entry: the BONS entry fields a matvec needs."""
+    _fields_ = [("rows", ctypes.c_uint32), ("cols", ctypes.c_uint32), ("kind", ctypes.c_int32),
+                ("bias", ctypes.c_int32), ("rshift", ctypes.c_int32)]
+
+
+_vp = ctypes.c_void_p
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built (python -m trixium_b200.build)")
+        L = ctypes.CDLL(LIB_PATH)
+        E = ctypes.POINTER(Entry)
+        sig = {
+            "trx_create": ([ctypes.POINTER(_vp), ctypes.c_int], ctypes.c_int),
+            "trx_destroy": ([_vp], ctypes.c_int),
+            "trx_get_error": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+            "trx_row_bytes": ([ctypes.c_uint32, ctypes.c_int32], ctypes.c_uint64),
+            "trx_matvec_i8": ([_vp, E, _vp, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_i8_rows": ([_vp, E, _vp, _vp, ctypes.c_int, _vp, _vp], ctypes.c_int),
+            "trx_quantize_pow2": ([_vp, _vp, ctypes.c_uint32, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_fp": ([_vp, E, _vp, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_swiglu": ([_vp, E, _vp, E, _vp, _vp, _vp, ctypes.c_float, _vp, _vp], ctypes.c_int),
+            "trx_validate_packed": ([_vp, E, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f_batch": ([_vp, E, _vp, ctypes.c_uint64, _vp, ctypes.c_uint64, _vp,
+                                    ctypes.c_uint64, ctypes.c_int, _vp], ctypes.c_int),
+        }
+        for name, (args, res) in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def check(status, where=""):
+    if status != TRX_OK:
+        raise TrxError(status, where)

@@ -1,0 +1,216 @@
+// C ABI of libtrixium_b200.so (declarations and contracts in include/trixium_b200.h).
+#include <cstdint>
+#include <cstdlib>
+#include <new>
+#include <cuda_runtime.h>
+
+#include "../../include/trixium_b200.h"
+#include "trx_internal.h"
+
+struct trx_ctx {
+    int device;
+    uint32_t *err;    // device error word
+    uint32_t *lut;    // replicated trit5 byte LUT (64 KiB), copied into each CTA's shared memory
+};
+
+namespace {
+
+bool ternary_kind(int k) { return k == TRX_KIND_TERNARY || k == TRX_KIND_TERNARY5; }
+
+trx_status check_entry(const trx_entry *e) {
+    if (!e) return TRX_ERR_ARG;
+    if (!ternary_kind(e->kind)) return TRX_ERR_LAYOUT;
+    if (e->rows == 0 || e->cols == 0 || (e->cols % 128) != 0) return TRX_ERR_LAYOUT;
+    if (e->cols > 32768u || e->rows > (1u << 30)) return TRX_ERR_UNSUPPORTED;
+    if (e->rshift < 0 || e->rshift > 47 || e->bias < -64 || e->bias > 64) return TRX_ERR_ARG;
+    return TRX_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+trx::MvJobs base_jobs(const trx_entry *e, const void *packed) {
+    trx::MvJobs J{};
+    J.w = static_cast<const uint8_t *>(packed);
+    J.rows = (int)e->rows;
+    J.cols = (int)e->cols;
+    J.kind = e->kind;
+    J.B = e->bias;
+    J.R = e->rshift;
+    J.njobs = 1;
+    return J;
+}
+
+}  // namespace
+
+extern "C" {
+
+trx_status trx_create(trx_ctx **ctx, int device) {
+    if (!ctx) return TRX_ERR_ARG;
+    *ctx = nullptr;
+    if (cudaSetDevice(device) != cudaSuccess) return TRX_ERR_CUDA;
+    trx_ctx *c = new (std::nothrow) trx_ctx{};
+    if (!c) return TRX_ERR_ARG;
+    c->device = device;
+    if (cudaMalloc(&c->err, 256) != cudaSuccess) {
+        delete c;
+        return TRX_ERR_CUDA;
+    }
+    if (cudaMalloc(&c->lut, trx::lut_bytes()) != cudaSuccess) {
+        cudaFree(c->err);
+        delete c;
+        return TRX_ERR_CUDA;
+    }
+    if (cudaMemset(c->err, 0, 256) != cudaSuccess || trx::launch_build_lut(c->lut, 0) != TRX_OK ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(c->err);
+        cudaFree(c->lut);
+        delete c;
+        return TRX_ERR_CUDA;
+    }
+    *ctx = c;
+    return TRX_OK;
+}
+
+trx_status trx_destroy(trx_ctx *ctx) {
+    if (!ctx) return TRX_ERR_ARG;
+    cudaFree(ctx->err);
+    cudaFree(ctx->lut);
+    delete ctx;
+    return TRX_OK;
+}
+
+trx_status trx_get_error(trx_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
+    if (!ctx || !bits) return TRX_ERR_ARG;
+    uint32_t v = 0;
+    if (cudaMemcpyAsync(&v, ctx->err, 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess) return TRX_ERR_CUDA;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return TRX_ERR_CUDA;
+    *bits = v;
+    if (v && cudaMemsetAsync(ctx->err, 0, 4, stream) != cudaSuccess) return TRX_ERR_CUDA;
+    return TRX_OK;
+}
+
+uint64_t trx_row_bytes(uint32_t cols, int32_t kind) {
+    if (!ternary_kind(kind) || cols == 0 || cols % 128) return 0;
+    const uint64_t G = cols / 128;
+    const uint64_t sb = (G + 15) / 16 * 32;
+    const uint64_t cb = kind == TRX_KIND_TERNARY5 ? 26 * G : 32 * G;
+    return sb + (cb + 31) / 32 * 32;
+}
+
+trx_status trx_matvec_i8(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8,
+                         int32_t *d_out, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x8 || !d_out || !aligned16(d_packed)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(e, d_packed);
+    J.x8 = d_x8;
+    J.y = d_out;
+    J.out = trx::OUT_I32;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int nb,
+                              int32_t *d_out, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x8 || !d_out || nb < 1 || nb > 8 || !aligned16(d_packed)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(e, d_packed);
+    J.x8 = d_x8;
+    J.x_stride = e->cols;
+    J.y = d_out;
+    J.y_stride = e->rows;
+    J.w_stride = 0;  // every row of x8 streams the same tensor
+    J.njobs = nb;
+    J.out = trx::OUT_I32;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_quantize_pow2(trx_ctx *ctx, const float *d_x, uint32_t n, int8_t *d_x8, int32_t *d_e8,
+                             cudaStream_t stream) {
+    if (!ctx || !d_x || !d_x8 || !d_e8 || n == 0 || n > (1u << 28)) return TRX_ERR_ARG;
+    return trx::launch_quantize(d_x, (int)n, d_x8, d_e8, stream);
+}
+
+trx_status trx_matvec_f(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                        const float *d_norm_w, float eps, const float *d_resid, float *d_y, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_y || !aligned16(d_packed)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(e, d_packed);
+    J.x = d_x;
+    J.norm_w = d_norm_w;
+    J.eps = eps;
+    J.resid = d_resid;
+    J.y = d_y;
+    J.out = trx::OUT_F32;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_matvec_fp(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, float *d_y,
+                         cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_y) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(e, d_packed);
+    J.x = d_x;
+    J.y = d_y;
+    J.out = trx::OUT_F32;
+    return trx::launch_matvec_fp(J, ctx->err, stream);
+}
+
+trx_status trx_matvec_swiglu(trx_ctx *ctx, const trx_entry *gate, const void *d_gate, const trx_entry *up,
+                             const void *d_up, const float *d_x, const float *d_norm_w, float eps, float *d_act,
+                             cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(gate);
+    if (s) return s;
+    s = check_entry(up);
+    if (s) return s;
+    if (gate->rows != up->rows || gate->cols != up->cols || gate->kind != up->kind) return TRX_ERR_ARG;
+    if (!d_gate || !d_up || !d_x || !d_act || !aligned16(d_gate) || !aligned16(d_up)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(gate, d_gate);
+    J.w2 = static_cast<const uint8_t *>(d_up);
+    J.B2 = up->bias;
+    J.R2 = up->rshift;
+    J.x = d_x;
+    J.norm_w = d_norm_w;
+    J.eps = eps;
+    J.y = d_act;
+    J.out = trx::OUT_SWIGLU;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_validate_packed(trx_ctx *ctx, const trx_entry *e, const void *d_packed, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed) return TRX_ERR_ARG;
+    if (e->kind != TRX_KIND_TERNARY5) return TRX_OK;  // every 2-bit byte decodes
+    return trx::launch_validate_t5(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, ctx->err,
+                                   stream);
+}
+
+trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_packed, uint64_t w_stride,
+                              const float *d_x, uint64_t x_stride, float *d_y, uint64_t y_stride, int njobs,
+                              cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_y || njobs < 1 || !aligned16(d_packed) || (w_stride % 16) != 0)
+        return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(e, d_packed);
+    J.x = d_x;
+    J.y = d_y;
+    J.w_stride = w_stride;
+    J.x_stride = x_stride;
+    J.y_stride = y_stride;
+    J.njobs = njobs;
+    J.out = trx::OUT_F32;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+}  // extern "C"

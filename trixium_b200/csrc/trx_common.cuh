@@ -1,0 +1,143 @@
+// Device helpers shared by the B200 ternary decode kernels (sm_100a).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include "../../include/trixium_b200.h"
+
+namespace trx {
+
+// Launch shape -----------------------------------------------------------------------------------
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// Bounded waits: an mbarrier wait gives up after kWaitNs nanoseconds of %globaltimer, records
+// TRX_DEV_TIMEOUT in the error word and returns (the caller then leaves the kernel).
+constexpr unsigned long long kWaitNs = 200ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Shared-memory addresses and the TMA bulk-copy / mbarrier wrappers -------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D TMA bulk copy global -> shared, completing `bytes` of transaction on `bar`.
+// dst/src 16-byte aligned, bytes a multiple of 16 (checked by the callers' geometry).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar`, bounded: returns false (and sets the timeout bit) if the
+// phase did not complete within kWaitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - t0 > kWaitNs) {
+            if (err) atomicOr(err, TRX_DEV_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Integer dot products ---------------------------------------------------------------------------
+// acc + sum_k a.byte[k] * b.byte[k], a's bytes unsigned, b's signed (PTX dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int acc) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(acc));
+    return d;
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int acc) {
+    return __dp4a(static_cast<int>(a), static_cast<int>(b), acc);
+}
+
+// acc + a.h0*b.b0 + a.h1*b.b1 (lo) / b.b2, b.b3 (hi): 16-bit signed pairs times signed bytes.
+__device__ __forceinline__ int dp2a_lo(uint32_t a16, uint32_t b8, int acc) {
+    return __dp2a_lo(static_cast<int>(a16), static_cast<int>(b8), acc);
+}
+__device__ __forceinline__ int dp2a_hi(uint32_t a16, uint32_t b8, int acc) {
+    return __dp2a_hi(static_cast<int>(a16), static_cast<int>(b8), acc);
+}
+
+// fp16 scale -> (m11, e16), value = m11 * 2^e16 exactly (model/bitexact.py:56-68).
+__device__ __forceinline__ void fp16_split(uint32_t bits, int &m11, int &e16) {
+    const int E = (bits >> 10) & 31;
+    const int mag = E ? (int)((bits & 1023u) | 1024u) : (int)(bits & 1023u);
+    m11 = (bits & 0x8000u) ? -mag : mag;
+    e16 = E ? E - 25 : -24;
+}
+
+// One group's contribution (gs*m11) shifted by e16+B: left if >= 0, arithmetic (floor) right
+// otherwise (model/bitexact.py:111-115).  Shifts are clamped to [0, 63]; any left shift that
+// large overflows the int48 accumulator check anyway.
+__device__ __forceinline__ long long group_contrib(int gs, uint32_t scale_bits, int B) {
+    int m11, e16;
+    fp16_split(scale_bits, m11, e16);
+    const long long prod = (long long)gs * (long long)m11;
+    const int sh = e16 + B;
+    if (sh >= 0) return prod << (sh > 63 ? 63 : sh);
+    const int rs = -sh;
+    return prod >> (rs > 63 ? 63 : rs);
+}
+
+// The trit5 byte LUT entry: digits d_k = (b / 3^k) % 3 (the reference reader's decode,
+// model/bons.py:125-130), packed as bytes (d0, d1, d2, d3 + 3*d4).  The last byte is the
+// byte's value / 27 for every valid byte; d4 = that / 3 is recovered in registers.
+__host__ __device__ __forceinline__ uint32_t trit5_lut_entry(uint32_t b) {
+    const uint32_t d0 = b % 3, d1 = (b / 3) % 3, d2 = (b / 9) % 3, d3 = (b / 27) % 3, d4 = (b / 81) % 3;
+    return d0 | (d1 << 8) | (d2 << 16) | ((d3 + 3 * d4) << 24);
+}
+
+// Round-half-away in the mirror's form: floor(x + 0.5f) for x >= 0, ceil(x - 0.5f) otherwise,
+// the +-0.5 added in fp32 round-to-nearest (model/mirror.py:34-35).
+__device__ __forceinline__ int lround_mirror(float x) {
+    return x >= 0.f ? (int)floorf(__fadd_rn(x, 0.5f)) : (int)ceilf(__fsub_rn(x, 0.5f));
+}
+
+// frexp exponent of a positive finite float (the e in x = m * 2^e, m in [0.5, 1)).
+__device__ __forceinline__ int frexp_exp(float a) {
+    int e;
+    frexpf(a, &e);
+    return e;
+}
+
+}  // namespace trx

@@ -1,0 +1,184 @@
+"""Device-side ops on torch CUDA tensors, through the C ABI.
+
+torch provides device memory and the current stream; every computation is a kernel of
+libtrixium_b200.so.  Tensors are passed as raw pointers, so inputs must be contiguous CUDA
+tensors of the stated dtype on the context's device.
+"""
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import layout as L
+from .image import TernaryTensor
+
+_entry_cache = {}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t, dtype, name):
+    if not (t.is_cuda and t.dtype == dtype and t.is_contiguous()):
+        raise ValueError(f"{name}: expected a contiguous CUDA {dtype} tensor, got {t.dtype} "
+                         f"on {t.device} (contiguous={t.is_contiguous()})")
+
+
+class Context:
+    """One per device: the library context (device error word, the trit5 LUT)."""
+
+    def __init__(self, device=0):
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        torch.cuda.set_device(self.device)
+        h = ctypes.c_void_p()
+        _lib.check(_lib.lib().trx_create(ctypes.byref(h), self.device.index or 0), "trx_create")
+        self.h = h
+
+    def errors(self):
+        """Synchronise the current stream and return (and clear) the device error bits."""
+        bits = ctypes.c_uint32(0)
+        _lib.check(_lib.lib().trx_get_error(self.h, _stream(), ctypes.byref(bits)), "trx_get_error")
+        return bits.value
+
+    def raise_on_error(self):
+        bits = self.errors()
+        if bits:
+            raise _lib.TrxDeviceError(bits)
+
+    def close(self):
+        if self.h:
+            _lib.lib().trx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default = {}
+
+
+def default_context(device=None):
+    dev = torch.cuda.current_device() if device is None else device
+    if dev not in _default:
+        _default[dev] = Context(dev)
+    return _default[dev]
+
+
+class DeviceTensor:
+    """A packed ternary tensor resident on the device, with its BONS entry fields."""
+
+    def __init__(self, t: TernaryTensor, device=None):
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.rows, self.cols, self.kind = t.rows, t.cols, t.kind
+        self.bias, self.rshift = t.bias, t.rshift
+        self.data = torch.from_numpy(np.ascontiguousarray(t.packed)).to(dev)
+        self.entry = _lib.Entry(self.rows, self.cols, self.kind, self.bias, self.rshift)
+
+    @classmethod
+    def from_packed(cls, packed, rows, cols, kind, bias, rshift, device=None):
+        self = cls.__new__(cls)
+        self.rows, self.cols, self.kind, self.bias, self.rshift = rows, cols, kind, bias, rshift
+        if isinstance(packed, torch.Tensor):
+            self.data = packed
+        else:
+            dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+            self.data = torch.from_numpy(np.ascontiguousarray(packed)).to(dev)
+        self.entry = _lib.Entry(rows, cols, kind, bias, rshift)
+        return self
+
+    @property
+    def nbytes(self):
+        return self.data.numel()
+
+
+def matvec_i8(ctx, w: DeviceTensor, x8, out=None):
+    _need(x8, torch.int8, "x8")
+    if out is None:
+        out = torch.empty(w.rows, dtype=torch.int32, device=x8.device)
+    _lib.check(_lib.lib().trx_matvec_i8(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x8), _ptr(out),
+                                        _stream()), "trx_matvec_i8")
+    return out
+
+
+def matvec_i8_rows(ctx, w: DeviceTensor, x8rows, out=None):
+    _need(x8rows, torch.int8, "x8rows")
+    nb = x8rows.shape[0]
+    if out is None:
+        out = torch.empty(nb, w.rows, dtype=torch.int32, device=x8rows.device)
+    _lib.check(_lib.lib().trx_matvec_i8_rows(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x8rows), nb,
+                                             _ptr(out), _stream()), "trx_matvec_i8_rows")
+    return out
+
+
+def quantize_pow2(ctx, x, x8=None, e8=None):
+    _need(x, torch.float32, "x")
+    if x8 is None:
+        x8 = torch.empty(x.numel(), dtype=torch.int8, device=x.device)
+    if e8 is None:
+        e8 = torch.empty(1, dtype=torch.int32, device=x.device)
+    _lib.check(_lib.lib().trx_quantize_pow2(ctx.h, _ptr(x), x.numel(), _ptr(x8), _ptr(e8), _stream()),
+               "trx_quantize_pow2")
+    return x8, e8
+
+
+def matvec_f(ctx, w: DeviceTensor, x, y=None, norm_w=None, eps=1e-6, resid=None):
+    _need(x, torch.float32, "x")
+    if norm_w is not None:
+        _need(norm_w, torch.float32, "norm_w")
+    if resid is not None:
+        _need(resid, torch.float32, "resid")
+    if y is None:
+        y = torch.empty(w.rows, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().trx_matvec_f(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(norm_w),
+                                       ctypes.c_float(eps), _ptr(resid), _ptr(y), _stream()), "trx_matvec_f")
+    return y
+
+
+def matvec_fp(ctx, w: DeviceTensor, x, y=None):
+    _need(x, torch.float32, "x")
+    if y is None:
+        y = torch.empty(w.rows, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().trx_matvec_fp(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(y),
+                                        _stream()), "trx_matvec_fp")
+    return y
+
+
+def matvec_swiglu(ctx, gate: DeviceTensor, up: DeviceTensor, x, act=None, norm_w=None, eps=1e-6):
+    _need(x, torch.float32, "x")
+    if act is None:
+        act = torch.empty(gate.rows, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().trx_matvec_swiglu(ctx.h, ctypes.byref(gate.entry), _ptr(gate.data),
+                                            ctypes.byref(up.entry), _ptr(up.data), _ptr(x), _ptr(norm_w),
+                                            ctypes.c_float(eps), _ptr(act), _stream()), "trx_matvec_swiglu")
+    return act
+
+
+def validate_packed(ctx, w: DeviceTensor):
+    _lib.check(_lib.lib().trx_validate_packed(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _stream()),
+               "trx_validate_packed")
+
+
+def matvec_f_batch(ctx, w: DeviceTensor, w_stride, x, x_stride, y, y_stride, njobs):
+    """njobs projections in one launch: tensor j at w.data + j*w_stride bytes, input x[j], output y[j]."""
+    _lib.check(_lib.lib().trx_matvec_f_batch(ctx.h, ctypes.byref(w.entry), _ptr(w.data), w_stride, _ptr(x),
+                                             x_stride, _ptr(y), y_stride, njobs, _stream()),
+               "trx_matvec_f_batch")
+    return y
+
+
+def row_bytes(cols, kind):
+    return int(_lib.lib().trx_row_bytes(cols, kind))
+
+
+__all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
+           "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "row_bytes", "L"]
