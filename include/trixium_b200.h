@@ -62,6 +62,9 @@ trx_status trx_destroy(trx_ctx *ctx);
 /* Synchronise `stream`, return the accumulated device error bits in *bits and clear them. */
 trx_status trx_get_error(trx_ctx *ctx, cudaStream_t stream, uint32_t *bits);
 
+/* The message of the CUDA error behind the last TRX_ERR_CUDA returned on this thread. */
+const char *trx_last_cuda_error(void);
+
 /* Bytes of one row packet and of a whole tensor (model/layout.py:215-217). */
 uint64_t trx_row_bytes(uint32_t cols, int32_t kind);
 

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_symbols():
     src = open(os.path.join(ROOT, "include", "trixium_b200.h")).read()
-    return sorted(set(re.findall(r"^\s*(?:trx_status|uint64_t)\s+(trx_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:trx_status|uint64_t|const char \*)\s*(trx_\w+)\s*\(", src, re.M)))
 
 
 def test_header_and_binding_agree():

@@ -11,7 +11,13 @@ struct trx_ctx {
     int device;
     uint32_t *err;    // device error word
     uint32_t *lut;    // replicated trit5 byte LUT (64 KiB), copied into each CTA's shared memory
+    // Split-row accumulator of matvecs with K > 4096 (zero between launches).
+    unsigned long long *acc;
+    unsigned *cnt;
+    uint64_t acc_rows;
 };
+
+static const uint64_t kAccRows = 1ull << 20;  // rows (x jobs) a split-row launch may cover
 
 namespace {
 
@@ -28,14 +34,19 @@ trx_status check_entry(const trx_entry *e) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-trx::MvJobs base_jobs(const trx_entry *e, const void *packed) {
+trx::MvJobs base_jobs(const trx_ctx *ctx, const trx_entry *e, const void *packed) {
     trx::MvJobs J{};
+    J.acc = ctx->acc;
+    J.cnt = ctx->cnt;
+    J.acc_rows = ctx->acc_rows;
     J.w = static_cast<const uint8_t *>(packed);
     J.rows = (int)e->rows;
     J.cols = (int)e->cols;
     J.kind = e->kind;
-    J.B = e->bias;
-    J.R = e->rshift;
+    J.nseg = 1;
+    J.seg[0].row_end = (int)e->rows;
+    J.seg[0].B = e->bias;
+    J.seg[0].R = e->rshift;
     J.njobs = 1;
     return J;
 }
@@ -60,10 +71,15 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         delete c;
         return TRX_ERR_CUDA;
     }
-    if (cudaMemset(c->err, 0, 256) != cudaSuccess || trx::launch_build_lut(c->lut, 0) != TRX_OK ||
+    c->acc_rows = kAccRows;
+    if (cudaMalloc(&c->acc, kAccRows * 16) != cudaSuccess || cudaMalloc(&c->cnt, kAccRows * 4) != cudaSuccess ||
+        cudaMemset(c->acc, 0, kAccRows * 16) != cudaSuccess || cudaMemset(c->cnt, 0, kAccRows * 4) != cudaSuccess ||
+        cudaMemset(c->err, 0, 256) != cudaSuccess || trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
         cudaFree(c->lut);
+        cudaFree(c->acc);
+        cudaFree(c->cnt);
         delete c;
         return TRX_ERR_CUDA;
     }
@@ -75,6 +91,8 @@ trx_status trx_destroy(trx_ctx *ctx) {
     if (!ctx) return TRX_ERR_ARG;
     cudaFree(ctx->err);
     cudaFree(ctx->lut);
+    cudaFree(ctx->acc);
+    cudaFree(ctx->cnt);
     delete ctx;
     return TRX_OK;
 }
@@ -88,6 +106,8 @@ trx_status trx_get_error(trx_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
     if (v && cudaMemsetAsync(ctx->err, 0, 4, stream) != cudaSuccess) return TRX_ERR_CUDA;
     return TRX_OK;
 }
+
+const char *trx_last_cuda_error(void) { return trx::last_cuda_error(); }
 
 uint64_t trx_row_bytes(uint32_t cols, int32_t kind) {
     if (!ternary_kind(kind) || cols == 0 || cols % 128) return 0;
@@ -103,9 +123,9 @@ trx_status trx_matvec_i8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x8 || !d_out || !aligned16(d_packed)) return TRX_ERR_ARG;
-    trx::MvJobs J = base_jobs(e, d_packed);
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x8 = d_x8;
-    J.y = d_out;
+    J.seg[0].y = d_out;
     J.out = trx::OUT_I32;
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
@@ -116,10 +136,10 @@ trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_pa
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x8 || !d_out || nb < 1 || nb > 8 || !aligned16(d_packed)) return TRX_ERR_ARG;
-    trx::MvJobs J = base_jobs(e, d_packed);
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x8 = d_x8;
     J.x_stride = e->cols;
-    J.y = d_out;
+    J.seg[0].y = d_out;
     J.y_stride = e->rows;
     J.w_stride = 0;  // every row of x8 streams the same tensor
     J.njobs = nb;
@@ -139,12 +159,12 @@ trx_status trx_matvec_f(trx_ctx *ctx, const trx_entry *e, const void *d_packed, 
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x || !d_y || !aligned16(d_packed)) return TRX_ERR_ARG;
-    trx::MvJobs J = base_jobs(e, d_packed);
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x = d_x;
     J.norm_w = d_norm_w;
     J.eps = eps;
-    J.resid = d_resid;
-    J.y = d_y;
+    J.seg[0].resid = d_resid;
+    J.seg[0].y = d_y;
     J.out = trx::OUT_F32;
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
@@ -155,9 +175,9 @@ trx_status trx_matvec_fp(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x || !d_y) return TRX_ERR_ARG;
-    trx::MvJobs J = base_jobs(e, d_packed);
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x = d_x;
-    J.y = d_y;
+    J.seg[0].y = d_y;
     J.out = trx::OUT_F32;
     return trx::launch_matvec_fp(J, ctx->err, stream);
 }
@@ -172,14 +192,14 @@ trx_status trx_matvec_swiglu(trx_ctx *ctx, const trx_entry *gate, const void *d_
     if (s) return s;
     if (gate->rows != up->rows || gate->cols != up->cols || gate->kind != up->kind) return TRX_ERR_ARG;
     if (!d_gate || !d_up || !d_x || !d_act || !aligned16(d_gate) || !aligned16(d_up)) return TRX_ERR_ARG;
-    trx::MvJobs J = base_jobs(gate, d_gate);
+    trx::MvJobs J = base_jobs(ctx, gate, d_gate);
     J.w2 = static_cast<const uint8_t *>(d_up);
     J.B2 = up->bias;
     J.R2 = up->rshift;
     J.x = d_x;
     J.norm_w = d_norm_w;
     J.eps = eps;
-    J.y = d_act;
+    J.seg[0].y = d_act;
     J.out = trx::OUT_SWIGLU;
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
@@ -202,9 +222,9 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
     if (s) return s;
     if (!d_packed || !d_x || !d_y || njobs < 1 || !aligned16(d_packed) || (w_stride % 16) != 0)
         return TRX_ERR_ARG;
-    trx::MvJobs J = base_jobs(e, d_packed);
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x = d_x;
-    J.y = d_y;
+    J.seg[0].y = d_y;
     J.w_stride = w_stride;
     J.x_stride = x_stride;
     J.y_stride = y_stride;

@@ -1,6 +1,7 @@
 // Internal launch interface between the C ABI (trx_capi.cu) and the kernels.
 #pragma once
 #include <cstdint>
+#include <cstring>
 #include <cuda_runtime.h>
 
 #include "../../include/trixium_b200.h"
@@ -9,25 +10,54 @@ namespace trx {
 
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_SWIGLU = 2 };
 
+constexpr int kMaxSegs = 4;
+
+// A row segment of a launch: rows [previous row_end, row_end) belong to one tensor with its
+// own fixed point (B, R) and output.  Several tensors that read the same activation (q, k, v)
+// are packed back to back and run as one launch.
+struct MvSeg {
+    int row_end;
+    int B, R;
+    void *y;               // output of this segment (row index relative to the segment)
+    const float *resid;    // residual added to the float result, or nullptr
+};
+
 // One matvec launch: njobs copies of the same tensor geometry, strided (a single job has
-// njobs = 1).  w2/B2/R2: the second tensor of a SwiGLU pair (same geometry).
+// njobs = 1).  w2/B2/R2: the second tensor of a SwiGLU pair (same geometry, one segment).
 struct MvJobs {
     const uint8_t *w;
     const uint8_t *w2;
     const float *x;        // fp32 input, or nullptr when x8 is given
     const int8_t *x8;      // pre-quantised input (OUT_I32 from trx_matvec_i8)
     const float *norm_w;   // RMSNorm weight or nullptr
-    const float *resid;    // residual added to the float result, or nullptr
-    void *y;
     uint64_t w_stride;     // bytes between jobs' tensors
     uint64_t x_stride;     // elements between jobs' inputs
     uint64_t y_stride;     // elements between jobs' outputs
     int rows, cols, kind;
-    int B, R, B2, R2;
+    int B2, R2;
     int out;
     int njobs;
     float eps;
+    int nseg;
+    MvSeg seg[kMaxSegs];
+    unsigned long long *argmax;  // if set: greedy argmax key of the float results (see below)
+    const int *skip;             // if set and *skip != 0, the launch does nothing
+    // Rows split over slabs (K > 4096) are summed in a zeroed global accumulator: acc[2*i] (and
+    // acc[2*i+1] for SwiGLU's up row) and an arrival count cnt[i], i = job*rows + row.  The last
+    // slab to arrive finishes the row and leaves both at zero again.
+    unsigned long long *acc;
+    unsigned *cnt;
+    uint64_t acc_rows;           // capacity of acc/cnt in rows
 };
+
+// Argmax key of (value, row): orderable float bits in the high word, ~row in the low word, so
+// an unsigned max picks the largest value and, on ties, the smallest row (doc/units.md:149).
+__host__ __device__ inline unsigned long long argmax_key(float v, uint32_t row) {
+    uint32_t b;
+    memcpy(&b, &v, 4);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - row);
+}
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);
@@ -35,5 +65,7 @@ trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStrea
 trx_status launch_validate_t5(const uint8_t *w, int rows, int cols, uint32_t *err, cudaStream_t st);
 trx_status launch_build_lut(uint32_t *lut, cudaStream_t st);
 size_t lut_bytes();
+trx_status note_cuda(cudaError_t e);   // TRX_OK, or TRX_ERR_CUDA after recording e
+const char *last_cuda_error();
 
 }  // namespace trx
