@@ -44,7 +44,7 @@ constexpr int kXWordsT5 = 40;                    // 26 dp4a words + 14 dp2a word
 constexpr int kXWords2b = 32;
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxDepth = 8;                     // blocks in flight per warp (ring slots)
-constexpr int kRingTarget = 12 * 1024;           // bytes of ring per warp to aim for
+constexpr int kRingTarget = 14 * 1024;           // bytes of ring per warp to aim for
 constexpr int kMaxNpb = 4;
 
 // Geometry of one launch, derived on the host (plan_matvec) and passed by value.
@@ -252,35 +252,36 @@ __device__ __forceinline__ int gsum_2b(const uint8_t *p, const uint32_t *xw) {
     return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6);
 }
 
-// (gs*m11) shifted by e16+B as int64: one wide multiply in the common case (0 <= sh <= 19,
-// so m11 << sh fits int32), the general floor/left shift otherwise.
-__device__ __forceinline__ long long contrib_fast(int gs, uint32_t sbits, int B) {
-    int m11, e16;
-    fp16_split(sbits, m11, e16);
-    const int sh = e16 + B;
-    if (sh >= 0 && sh <= 19) return (long long)gs * (long long)(m11 << sh);
+// (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Common case: a normal fp16
+// scale with 0 <= e16+B <= 19, where m11 << (e16+B) = scale * 2^B is an integer below 2^30, so the
+// contribution is one wide multiply by F2I(fp32(scale) * 2^B) (both steps exact).  Otherwise the
+// general floor/left shift.
+__device__ __forceinline__ long long contrib_fast(int gs, uint32_t sbits, int B, float pow2B) {
+    const int E = (sbits >> 10) & 31;
+    const int sh = E - 25 + B;
+    if (E != 0 && (unsigned)sh <= 19u)
+        return (long long)gs * (long long)__float2int_rz(__fmul_rn(__half2float(__ushort_as_half((unsigned short)sbits)), pow2B));
     return group_contrib(gs, sbits, B);
 }
 
-// Exact int64 sum over the CW lanes of this lane's slot (CW a power of two <= 32): two 32-bit
-// warp reductions of the split c = hi*2^24 + lo, lo in [0, 2^24).
+// Exact int64 sum over the CW lanes of this lane's slot (CW a power of two <= 32), without
+// divergence: c = hi*2^24 + lo (lo in [0, 2^24)); 32-bit warp reductions of the slot-masked
+// parts (CW >= 16), or xor-shuffles (CW < 16).
 __device__ __forceinline__ long long slot_sum64(long long c, int CW, int lane) {
     if (CW >= 16) {
         const uint32_t lo = (uint32_t)(c & 0xffffffll);
         const int hi = (int)(c >> 24);
-        uint32_t slo;
-        int shi;
         if (CW == 32) {
-            slo = __reduce_add_sync(0xffffffffu, lo);
-            shi = __reduce_add_sync(0xffffffffu, hi);
-        } else if (lane < 16) {
-            slo = __reduce_add_sync(0x0000ffffu, lo);
-            shi = __reduce_add_sync(0x0000ffffu, hi);
-        } else {
-            slo = __reduce_add_sync(0xffff0000u, lo);
-            shi = __reduce_add_sync(0xffff0000u, hi);
+            const uint32_t slo = __reduce_add_sync(0xffffffffu, lo);
+            const int shi = __reduce_add_sync(0xffffffffu, hi);
+            return ((long long)shi << 24) + (long long)slo;
         }
-        return ((long long)shi << 24) + (long long)slo;
+        const bool upper = lane >= 16;
+        const uint32_t lo1 = __reduce_add_sync(0xffffffffu, upper ? lo : 0u);
+        const int hi1 = __reduce_add_sync(0xffffffffu, upper ? hi : 0);
+        const uint32_t lo0 = __reduce_add_sync(0xffffffffu, upper ? 0u : lo);
+        const int hi0 = __reduce_add_sync(0xffffffffu, upper ? 0 : hi);
+        return upper ? ((long long)hi1 << 24) + (long long)lo1 : ((long long)hi0 << 24) + (long long)lo0;
     }
     for (int o = CW >> 1; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
     return c;
@@ -487,6 +488,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
                     xr[i] = xp[g * M.xwords + i];
             }
             const int xs = gvalid ? xsum[g] : 0;
+            const int gi = nck == 1 ? g : gl;  // group index inside a ring row
+            const int code_off = (nck == 1 ? M.sbytes : M.s_len) + (KIND == TRX_KIND_TERNARY5 ? 26 : 32) * gi;
+            const int lane_row = slot * M.srow;  // this lane's row within a pass
             // Prime the ring with the first D-1 blocks.
             for (int d = 0; d < M.D - 1; ++d) {
                 if (d < nmine) {
@@ -496,6 +500,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
                 cp_commit();
             }
             int rs = M.D - 1, cs = 0, cur_seg = -1, Bs = 0, sb0 = 0;
+            float p2B = 1.f;
+            const float p2B2 = pow2f(J.B2);
             RowOut ro{};
             for (int j = 0; j < nmine; ++j) {
                 if (j + M.D - 1 < nmine) {
@@ -516,25 +522,25 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
                         cur_seg = sg;
                         ro = row_out(J, job, sg, e8);
                         Bs = ro.B;
+                        p2B = pow2f(Bs);
                         sb0 = seg_start(J, sg);
                     }
                 }
-                const unsigned char *blk = ring + (size_t)cs * M.slot_bytes;
+                const unsigned char *blk = ring + (size_t)cs * M.slot_bytes + lane_row;
                 for (int pass = 0; pass < M.NPB; ++pass) {
                     const int rr = pass * M.RPW + slot;
                     auto unit = [&](int w) -> long long {
                         long long cc = 0;
-                        if (gvalid && rr < nr) {
-                            const unsigned char *row = blk + ((size_t)w * M.BR + rr) * M.srow;
-                            const unsigned char *codes = row + (nck == 1 ? M.sbytes : M.s_len);
-                            const int gi = nck == 1 ? g : gl;  // group index inside the ring row
+                        if (gvalid) {  // rows past nr decode stale slot bytes; masked below
+                            const unsigned char *row = blk + (w * M.BR + pass * M.RPW) * M.srow;
                             const uint32_t sbits = reinterpret_cast<const uint16_t *>(row)[gi];
                             int gs;
                             if (KIND == TRX_KIND_TERNARY5)
-                                gs = gsum_t5(codes + 26 * gi, gi & 1, lut, lane4, xr, xr + 26) - xs;
+                                gs = gsum_t5(row + code_off, gi & 1, lut, lane4, xr, xr + 26) - xs;
                             else
-                                gs = gsum_2b(codes + 32 * gi, xr) - xs;
-                            cc = contrib_fast(gs, sbits, w ? J.B2 : Bs);
+                                gs = gsum_2b(row + code_off, xr) - xs;
+                            cc = contrib_fast(gs, sbits, w ? J.B2 : Bs, w ? p2B2 : p2B);
+                            cc = rr < nr ? cc : 0ll;
                         }
                         return slot_sum64(cc, CW, lane);
                     };
