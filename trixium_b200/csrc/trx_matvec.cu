@@ -3,29 +3,35 @@
 // with the firmware's float wrapper (quantise -> engine -> scale, firmware/infer_float.c:398)
 // fused in, and the fp-mode projection of model/fastref.py:103-125.
 //
-// Work decomposition:
-//  * Persistent: one CTA of 16 warps per SM, a contiguous range of rows (of one or more jobs).
-//  * A row is split into nck slabs of CW groups (CW a power of two <= 32; one slab when the row
-//    has <= 32 groups).  A warp owns one slab for a whole job: each lane owns one group of it, and
-//    the activation's permuted int8 words for that group live in the lane's registers, so the
-//    inner loop reads only codes (and, for trit5, the byte LUT) from shared memory.
-//  * A block is BR consecutive rows of the warp's slab.  Every warp streams its own blocks
-//    global -> shared through a private D-deep ring with 16-byte cp.async copies (coalesced:
-//    consecutive lanes copy consecutive 16-byte chunks of a row packet), cp.async.wait_group
-//    tracking completion -- no producer warp, no CTA-wide barrier inside the job.  Measured on
-//    B200, 1-D bulk (TMA) copies complete one after another per SM with ~0.8 us exposed each and a
-//    227 KB ring cannot hold enough of them in flight while blocks are decoded; per-warp rings keep
-//    ~100 KB in flight per SM.
-//  * Group sums are exact int32 (dp4a / dp2a); the scale/shift contribution is int64, summed over
-//    the slot's lanes with two 32-bit warp reductions of an exact hi/lo split.  A whole row's sum
-//    is finished by the slot's leader lane (>> R, overflow checks, float scaling, epilogue); a row
-//    split over slabs is summed with 64-bit atomics in a self-cleaning global accumulator and
-//    finished by the last slab to arrive.
+// Work decomposition (row per lane):
+//  * A row block is 32 consecutive output rows; lane l of a warp owns row l of the block for the
+//    whole of it and keeps that row's exact int64 sum in a register, so no cross-lane reduction
+//    exists anywhere on the path.
+//  * A row is cut into chunks of 4 groups (512 weights).  A block is one chunk of the 32 rows:
+//    per row 16 bytes of scales and the chunk's codes (104 bytes of trit5, 128 of 2-bit), laid
+//    out in shared memory at a 144-byte row stride (9 x 16 B, odd: the 32 lanes' 16-byte loads
+//    of their own rows never conflict).
+//  * A task is a row block and a range of its chunks.  The CTA (up to 16 warps, one per SM)
+//    takes a contiguous range of (job, task) space; warp w takes every warps-th task of it and
+//    streams the blocks of its tasks global -> shared through a private ring of D slots with
+//    16-byte cp.async copies (consecutive lanes copy consecutive 16 bytes of a row, so every
+//    copy instruction reads whole 128-byte lines), tracked with cp.async.wait_group: no producer
+//    warp and no CTA-wide barrier inside a job.  Measured on B200, 1-D bulk (TMA) copies complete
+//    one after another per SM (~0.8 us exposed each), and a 227 KB ring cannot keep enough of
+//    them in flight while blocks are decoded; per-warp cp.async rings keep 70-150 KB in flight.
+//  * The quantised activation of the job is built once per CTA in shared memory, permuted per
+//    group into the words the decoders multiply with (read as broadcast 16-byte loads).
+//  * Group sums are exact int32 (dp4a / dp2a).  The scale contribution (gs*m11) << (e16+B) is
+//    one int32 x int32 -> int64 multiply in the common case.  A task that covers a whole row
+//    finishes it in the lane (>> R, overflow checks, float scaling, epilogue); a row split over
+//    tasks (a single matvec too small to fill the GPU) is summed with 64-bit atomics in a
+//    self-cleaning global accumulator and finished by the last task to arrive.
 //  * trit5 decode: a 256-entry byte LUT (digits d0, d1, d2 and d3+3*d4 as bytes), replicated 32x
 //    (one copy per lane, so lookups never bank-conflict), addressed with one PRMT per byte.
 //    dp4a adds d0*x0+d1*x1+d2*x2+(d3+3d4)*x3; the d4 correction d4*(x4-3*x3) is a dp2a on
 //    16-bit activation pairs, d4 = (d3+3d4)/3 computed for four bytes at once.
 //  * 2-bit decode: four masks per word; dp4a on (code << 2p) bytes into four accumulators.
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cuda_runtime.h>
@@ -36,35 +42,34 @@
 namespace trx {
 
 // Launch shape and shared-memory plan --------------------------------------------------------------
-constexpr int kWarpsMv = 16;
-constexpr int kMvThreads = kWarpsMv * 32;
+#ifndef TRX_MV_MAX_WARPS
+#define TRX_MV_MAX_WARPS 16
+#endif
+constexpr int kMaxWarps = TRX_MV_MAX_WARPS;
+constexpr int kMvThreads = 16 * 32;               // launch bound (a launch may use fewer warps)
 constexpr int kLutWords = 256 * 64;              // 256 entries x 256-byte stride (32 replicas used)
 constexpr int kLutBytes = kLutWords * 4;         // 64 KiB
-constexpr int kXWordsT5 = 40;                    // 26 dp4a words + 14 dp2a words per group
-constexpr int kXWords2b = 32;
+constexpr int kXwT5 = 44;    // words per group: 26 dp4a words, 14 dp2a words, sum(x), 3 zero
+constexpr int kXw2b = 36;    // words per group: 32 dp4a words, sum(x), 3 zero
+constexpr int kCG = 4;                           // groups per chunk
+constexpr int kRowStride = 144;                  // ring bytes per row of a block
+constexpr int kBlkBytes = 32 * kRowStride;       // one tensor's block (32 rows x one chunk)
 constexpr int kSmemMax = 227 * 1024;
-constexpr int kMaxDepth = 8;                     // blocks in flight per warp (ring slots)
-constexpr int kRingTarget = 14 * 1024;           // bytes of ring per warp to aim for
-constexpr int kMaxNpb = 4;
 
 // Geometry of one launch, derived on the host (plan_matvec) and passed by value.
 struct MvGeom {
     int G;        // groups per row
-    int CW;       // groups per slab = lanes per slot (power of two <= 32)
-    int nck;      // slabs per row
-    int RPW;      // rows a warp decodes at once (32 / CW slots)
-    int NPB;      // passes (of RPW rows) per block
-    int BR;       // rows per block = RPW * NPB
-    int D;        // ring depth (blocks)
+    int nch;      // chunks per row (the last may hold fewer than kCG groups)
+    int cpt;      // chunks per task
+    int S;        // tasks per row block
+    int nrb;      // row blocks per job
+    int tpj;      // tasks per job (nrb * S)
     int rb;       // row packet bytes in global memory
     int sbytes;   // scale-region bytes of a packet
-    int s_off, s_len;   // slab c's scales: packet bytes [s_off*c, +s_len) (s_len 16-byte rounded)
-    int c_off, c_len;   // slab c's codes: packet bytes [sbytes + c_off*c, +c_len)
-    int srow;     // bytes of one row in the ring (s_len + c_len, or rb for a single slab)
-    int slot_bytes;     // BR * srow * nw
-    int nbj;      // blocks per job (segments are whole blocks, except a single segment's tail)
     int nw;       // tensors per block (2 for SwiGLU)
-    int xwords;   // permuted activation words per group
+    int warps;    // warps per CTA
+    int D;        // ring depth (blocks)
+    int xw;       // activation words per group
     int smem;     // dynamic shared bytes
 };
 
@@ -107,11 +112,11 @@ __device__ float block_sumsq64(const float *x, int n, float *red64) {
     return ss;
 }
 
-// Build the permuted int8 activation of one job in shared memory (all threads).
-// q8: K bytes, xp: G*xwords words, xsum: G ints.  Returns e8.
+// Build the permuted int8 activation of one job in shared memory (all threads of the CTA).
+// q8: K bytes of staging, xp: G * xw words.  Returns e8.
 template <int KIND>
 __device__ int build_activation(const float *x, const int8_t *x8g, const float *nw, float eps, int K, int8_t *q8,
-                                uint32_t *xp, int *xsum, uint32_t *amax_s, float *red64) {
+                                uint32_t *xp, uint32_t *amax_s, float *red64) {
     const int ct = threadIdx.x;
     const int nt = blockDim.x;
     int e8 = 0;
@@ -144,14 +149,17 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
     }
     __syncthreads();
     const int G = K / 128;
-    if (KIND == TRX_KIND_TERNARY5) {
-        // Per group: words 0..25 = bytes (x[5i], x[5i+1], x[5i+2], x[5i+3]);
-        // words 26..39 = 16-bit pairs (y[2j], y[2j+1]) with y[i] = x[5i+4] - 3*x[5i+3];
-        // lanes 128/129 (digits 3/4 of byte 25) see x = 0.
-        for (int idx = ct; idx < G * kXWordsT5; idx += nt) {
-            const int g = idx / kXWordsT5, j = idx % kXWordsT5;
-            const int8_t *qg = q8 + g * 128;
-            uint32_t w = 0;
+    constexpr int XW = KIND == TRX_KIND_TERNARY5 ? kXwT5 : kXw2b;
+    constexpr int XS = KIND == TRX_KIND_TERNARY5 ? 40 : 32;  // the word holding sum(x) of the group
+    for (int idx = ct; idx < G * XW; idx += nt) {
+        const int g = idx / XW, j = idx % XW;
+        const int8_t *qg = q8 + g * 128;
+        uint32_t w = 0;
+        if (j == XS) continue;  // written below
+        if (KIND == TRX_KIND_TERNARY5) {
+            // Words 0..25 = bytes (x[5i], x[5i+1], x[5i+2], x[5i+3]); words 26..39 = 16-bit pairs
+            // (y[2j], y[2j+1]) with y[i] = x[5i+4] - 3*x[5i+3]; lanes 128/129 (digits 3/4 of byte
+            // 25) see x = 0.
             if (j < 26) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -159,7 +167,7 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
                     const uint32_t b = l < 128 ? (uint32_t)(uint8_t)qg[l] : 0u;
                     w |= b << (8 * k);
                 }
-            } else {
+            } else if (j < 40) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int i = 2 * (j - 26) + h;
@@ -172,19 +180,14 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
                     w |= ((uint32_t)y & 0xffffu) << (16 * h);
                 }
             }
-            xp[idx] = w;
-        }
-    } else {
-        // Per group: word (w*4 + p) = bytes x[16w + 4b + p], b = 0..3.
-        for (int idx = ct; idx < G * kXWords2b; idx += nt) {
-            const int g = idx / kXWords2b, j = idx % kXWords2b;
+        } else if (j < 32) {
+            // Word (w*4 + p) = bytes x[16w + 4b + p], b = 0..3: the activations that meet bit
+            // pair p of code bytes 4w..4w+3.
             const int wq = j >> 2, p = j & 3;
-            const int8_t *qg = q8 + g * 128;
-            uint32_t w = 0;
 #pragma unroll
             for (int b = 0; b < 4; ++b) w |= (uint32_t)(uint8_t)qg[16 * wq + 4 * b + p] << (8 * b);
-            xp[idx] = w;
         }
+        xp[idx] = w;
     }
     // Group sums of x8: one warp per group.
     for (int g = ct >> 5; g < G; g += nt >> 5) {
@@ -192,32 +195,38 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
         const int8_t *qg = q8 + g * 128 + 4 * lane;
         int s = (int)qg[0] + (int)qg[1] + (int)qg[2] + (int)qg[3];
         s = __reduce_add_sync(0xffffffffu, s);
-        if (lane == 0) xsum[g] = s;
+        if (lane == 0) xp[g * XW + XS] = (uint32_t)s;
     }
     __syncthreads();
     return e8;
 }
 
 // Group sums -----------------------------------------------------------------------------------------
-// trit5: the 26 code bytes of one group start at `p` (2-byte aligned).  Returns sum(digit*x).
-__device__ __forceinline__ int gsum_t5(const uint8_t *p, int odd, const char *lut, uint32_t lane4,
-                                       const uint32_t *xa, const uint32_t *yy) {
-    const uint32_t *wp = reinterpret_cast<const uint32_t *>(p - 2 * odd);
-    uint32_t w[7];
+// trit5, group g of a chunk whose 104 code bytes start at byte H (0 or 8) of the 28-word window
+// cw.  xg: the group's 44 activation words.  Returns sum((digit - 1) * x).
+template <int H, int g>
+__device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], const char *lut, uint32_t lane4, const uint32_t *xg) {
+    uint32_t xa[kXwT5];
 #pragma unroll
-    for (int i = 0; i < 7; ++i) w[i] = wp[i];
-    const uint32_t sel = odd ? 0x5432u : 0x3210u;
+    for (int i = 0; i < kXwT5 / 4; ++i) {
+        const uint4 v = reinterpret_cast<const uint4 *>(xg)[i];
+        xa[4 * i] = v.x;
+        xa[4 * i + 1] = v.y;
+        xa[4 * i + 2] = v.z;
+        xa[4 * i + 3] = v.w;
+    }
     int acc[4] = {0, 0, 0, 0};  // independent chains (byte position within a quad)
 #pragma unroll
     for (int q = 0; q < 7; ++q) {
-        const uint32_t W = __byte_perm(w[q], q < 6 ? w[q + 1] : w[q], sel);
         const int nb = q < 6 ? 4 : 2;
         uint32_t E[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             if (i < nb) {
+                constexpr int base = H + 26 * g;
+                const int pb = base + 4 * q + i;  // byte of the window (compile time)
                 // a = byte * 256 + lane * 4: this lane's replica of the entry, no bank conflict.
-                const uint32_t a = __byte_perm(W, lane4, 0x5504u | (i << 4));
+                const uint32_t a = __byte_perm(cw[pb >> 2], lane4, 0x5504u | ((pb & 3) << 4));
                 E[i] = *reinterpret_cast<const uint32_t *>(lut + a);
                 acc[i] = dp4a_ss(E[i], xa[4 * q + i], acc[i]);
             }
@@ -225,31 +234,41 @@ __device__ __forceinline__ int gsum_t5(const uint8_t *p, int odd, const char *lu
         if (nb == 4) {
             const uint32_t d01 = __byte_perm(E[0], E[1], 0x0073u);
             const uint32_t d23 = __byte_perm(E[2], E[3], 0x0073u);
-            const uint32_t D = ((__byte_perm(d01, d23, 0x5410u) * 11u) >> 5) & 0x03030303u;
-            acc[q & 3] = dp2a_lo(yy[2 * q], D, acc[q & 3]);
-            acc[(q + 2) & 3] = dp2a_hi(yy[2 * q + 1], D, acc[(q + 2) & 3]);
+            const uint32_t D = __umulhi(__byte_perm(d01, d23, 0x5410u), 11u << 27) & 0x03030303u;
+            acc[q & 3] = dp2a_lo(xa[26 + 2 * q], D, acc[q & 3]);
+            acc[(q + 2) & 3] = dp2a_hi(xa[26 + 2 * q + 1], D, acc[(q + 2) & 3]);
         } else {
-            const uint32_t D = ((__byte_perm(E[0], E[1], 0x0073u) * 11u) >> 5) & 0x03030303u;
-            acc[3] = dp2a_lo(yy[2 * q], D, acc[3]);
+            const uint32_t D = __umulhi(__byte_perm(E[0], E[1], 0x0073u), 11u << 27) & 0x03030303u;
+            acc[3] = dp2a_lo(xa[26 + 2 * q], D, acc[3]);
         }
     }
-    return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    return (acc[0] + acc[1]) + (acc[2] + acc[3]) - (int)xa[40];
 }
 
-// 2-bit: the 32 code bytes of one group at `p` (16-byte aligned).  Returns sum(code*x).
-__device__ __forceinline__ int gsum_2b(const uint8_t *p, const uint32_t *xw) {
-    const uint4 c0 = reinterpret_cast<const uint4 *>(p)[0];
-    const uint4 c1 = reinterpret_cast<const uint4 *>(p)[1];
-    const uint32_t c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+// 2-bit, group g of a chunk: the 32 code bytes at cp (shared, 16-byte aligned).  Returns
+// sum((code - 1) * x).
+__device__ __forceinline__ int gsum_2b(const uint4 *cp, const uint32_t *xg) {
+    uint32_t xw[kXw2b];
+#pragma unroll
+    for (int i = 0; i < kXw2b / 4; ++i) {
+        const uint4 v = reinterpret_cast<const uint4 *>(xg)[i];
+        xw[4 * i] = v.x;
+        xw[4 * i + 1] = v.y;
+        xw[4 * i + 2] = v.z;
+        xw[4 * i + 3] = v.w;
+    }
+    const uint4 c0 = cp[0], c1 = cp[1];
+    const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-        a0 = dp4a_us(c[w] & 0x03030303u, xw[4 * w + 0], a0);
-        a1 = dp4a_us(c[w] & 0x0c0c0c0cu, xw[4 * w + 1], a1);
-        a2 = dp4a_us(c[w] & 0x30303030u, xw[4 * w + 2], a2);
-        a3 = dp4a_us(c[w] & 0xc0c0c0c0u, xw[4 * w + 3], a3);
+        const uint32_t c = cw[w];
+        a0 = dp4a_us(c & 0x03030303u, xw[4 * w + 0], a0);
+        a1 = dp4a_us(c & 0x0c0c0c0cu, xw[4 * w + 1], a1);
+        a2 = dp4a_us(c & 0x30303030u, xw[4 * w + 2], a2);
+        a3 = dp4a_us(c & 0xc0c0c0c0u, xw[4 * w + 3], a3);
     }
-    return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6);
+    return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - (int)xw[32];
 }
 
 // (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Common case: a normal fp16
@@ -264,27 +283,28 @@ __device__ __forceinline__ long long contrib_fast(int gs, uint32_t sbits, int B,
     return group_contrib(gs, sbits, B);
 }
 
-// Exact int64 sum over the CW lanes of this lane's slot (CW a power of two <= 32), without
-// divergence: c = hi*2^24 + lo (lo in [0, 2^24)); 32-bit warp reductions of the slot-masked
-// parts (CW >= 16), or xor-shuffles (CW < 16).
-__device__ __forceinline__ long long slot_sum64(long long c, int CW, int lane) {
-    if (CW >= 16) {
-        const uint32_t lo = (uint32_t)(c & 0xffffffll);
-        const int hi = (int)(c >> 24);
-        if (CW == 32) {
-            const uint32_t slo = __reduce_add_sync(0xffffffffu, lo);
-            const int shi = __reduce_add_sync(0xffffffffu, hi);
-            return ((long long)shi << 24) + (long long)slo;
-        }
-        const bool upper = lane >= 16;
-        const uint32_t lo1 = __reduce_add_sync(0xffffffffu, upper ? lo : 0u);
-        const int hi1 = __reduce_add_sync(0xffffffffu, upper ? hi : 0);
-        const uint32_t lo0 = __reduce_add_sync(0xffffffffu, upper ? 0u : lo);
-        const int hi0 = __reduce_add_sync(0xffffffffu, upper ? 0 : hi);
-        return upper ? ((long long)hi1 << 24) + (long long)lo1 : ((long long)hi0 << 24) + (long long)lo0;
-    }
-    for (int o = CW >> 1; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-    return c;
+__device__ __forceinline__ uint32_t scale_bits(uint2 s, int g) {
+    const uint32_t w = g < 2 ? s.x : s.y;
+    return g & 1 ? w >> 16 : w & 0xffffu;
+}
+
+// The int64 contribution of one chunk of this lane's row (ng <= 4 groups).
+template <int H>
+__device__ __forceinline__ long long chunk_t5(const uint32_t (&cw)[28], uint2 sc, int ng, const uint32_t *xg,
+                                              const char *lut, uint32_t lane4, int B, float p2B) {
+    long long a = contrib_fast(gsum_t5<H, 0>(cw, lut, lane4, xg), scale_bits(sc, 0), B, p2B);
+    if (ng > 1) a += contrib_fast(gsum_t5<H, 1>(cw, lut, lane4, xg + kXwT5), scale_bits(sc, 1), B, p2B);
+    if (ng > 2) a += contrib_fast(gsum_t5<H, 2>(cw, lut, lane4, xg + 2 * kXwT5), scale_bits(sc, 2), B, p2B);
+    if (ng > 3) a += contrib_fast(gsum_t5<H, 3>(cw, lut, lane4, xg + 3 * kXwT5), scale_bits(sc, 3), B, p2B);
+    return a;
+}
+
+__device__ __forceinline__ long long chunk_2b(const uint4 *cp, uint2 sc, int ng, const uint32_t *xg, int B, float p2B) {
+    long long a = contrib_fast(gsum_2b(cp, xg), scale_bits(sc, 0), B, p2B);
+    if (ng > 1) a += contrib_fast(gsum_2b(cp + 2, xg + kXw2b), scale_bits(sc, 1), B, p2B);
+    if (ng > 2) a += contrib_fast(gsum_2b(cp + 4, xg + 2 * kXw2b), scale_bits(sc, 2), B, p2B);
+    if (ng > 3) a += contrib_fast(gsum_2b(cp + 6, xg + 3 * kXw2b), scale_bits(sc, 3), B, p2B);
+    return a;
 }
 
 // The float epilogue value of one finished row (the firmware's int32 -> float scaling).
@@ -366,50 +386,125 @@ __device__ __forceinline__ void argmax_commit(const MvJobs &J, int job, unsigned
 __device__ __forceinline__ void cp16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// Predicated 16-byte copy to shared address dst + OFF.
+template <int OFF>
+__device__ __forceinline__ void cp16p(uint32_t dst, const void *src, bool p) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q cp.async.cg.shared.global [%0+%3], [%1], 16;\n}" ::"r"(dst),
+        "l"(src), "r"((int)p), "n"(OFF)
+        : "memory");
+}
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
-__device__ __forceinline__ void cp_wait_n(int n) {  // n <= kMaxDepth - 1
-    switch (n) {
-        case 0: cp_wait<0>(); break;
-        case 1: cp_wait<1>(); break;
-        case 2: cp_wait<2>(); break;
-        case 3: cp_wait<3>(); break;
-        case 4: cp_wait<4>(); break;
-        case 5: cp_wait<5>(); break;
-        case 6: cp_wait<6>(); break;
-        default: cp_wait<7>(); break;
+
+// Position in a warp's stream of blocks: task `task` (row block rbk, chunks [c, c1)).
+struct Cursor {
+    int task, rbk, c, c1;
+};
+
+__device__ __forceinline__ void cursor_task(const MvGeom &M, int task, Cursor &k) {
+    k.task = task;
+    if (M.S == 1) {
+        k.rbk = task;
+        k.c = 0;
+        k.c1 = M.nch;
+        return;
+    }
+    k.rbk = task / M.S;
+    const int s = task - k.rbk * M.S;
+    k.c = s * M.cpt;
+    k.c1 = min(M.nch, k.c + M.cpt);
+}
+
+__device__ __forceinline__ void cursor_next(const MvGeom &M, Cursor &k, int stride) {
+    if (++k.c == k.c1) cursor_task(M, k.task + stride, k);
+}
+
+// Issue the copies of block (row block rbk, chunk c) of `job` into ring slot `dst`.  Per row,
+// the 16 scale bytes holding the chunk's scales land at ring bytes [0, 16) and the chunk's codes
+// at [16, ...) (trit5: from the 16-byte boundary at or below their start, so an odd chunk's codes
+// begin at byte 8 of the window).  Lane l copies 16-byte piece l%8 of rows l/8, l/8+4, ...: each
+// copy instruction reads 4 rows x 128 contiguous bytes.
+template <int KIND, int NW>
+__device__ __forceinline__ void issue_block(const MvJobs &J, const MvGeom &M, int job, int rbk, int c, uint32_t dst,
+                                            int lane) {
+    const int r0 = rbk * 32;
+    const int nrows = min(32, J.rows - r0);
+    const int ng = min(kCG, M.G - c * kCG);
+    const int sub = lane >> 3, k = lane & 7;
+    const int soff = 16 * (c >> 1);
+    int off, doff;
+    bool pv;
+    if (KIND == TRX_KIND_TERNARY5) {  // piece 0: scales; pieces 1..7: codes
+        const int head = (c & 1) * 8;
+        const int np = (head + 26 * ng + 15) >> 4;
+        off = k ? M.sbytes + 104 * c - head + 16 * (k - 1) : soff;
+        doff = 16 * k;
+        pv = k <= np;
+    } else {                          // pieces 0..7: codes; scales in a pass of their own
+        off = M.sbytes + 128 * c + 16 * k;
+        doff = 16 + 16 * k;
+        pv = k < 2 * ng;
+    }
+    const int nv = pv ? (nrows - sub + 3) >> 2 : 0;  // copies (of rows sub, sub+4, ...) this lane makes
+    const uint64_t jbase = (uint64_t)job * J.w_stride + (uint64_t)r0 * M.rb;
+    const uint64_t rstep = 4ull * M.rb;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const uint8_t *base = (w ? J.w2 : J.w) + jbase;
+        const uint8_t *src = base + (uint64_t)sub * M.rb + off;
+        const uint32_t d = dst + w * kBlkBytes + sub * kRowStride + doff;
+        cp16p<0 * 4 * kRowStride>(d, src, 0 < nv);
+        cp16p<1 * 4 * kRowStride>(d, src + rstep, 1 < nv);
+        cp16p<2 * 4 * kRowStride>(d, src + 2 * rstep, 2 < nv);
+        cp16p<3 * 4 * kRowStride>(d, src + 3 * rstep, 3 < nv);
+        src += 4 * rstep;
+        cp16p<4 * 4 * kRowStride>(d, src, 4 < nv);
+        cp16p<5 * 4 * kRowStride>(d, src + rstep, 5 < nv);
+        cp16p<6 * 4 * kRowStride>(d, src + 2 * rstep, 6 < nv);
+        cp16p<7 * 4 * kRowStride>(d, src + 3 * rstep, 7 < nv);
+        if (KIND != TRX_KIND_TERNARY5)
+            cp16p<0>(dst + w * kBlkBytes + lane * kRowStride, base + (uint64_t)lane * M.rb + soff, lane < nrows);
     }
 }
 
-// Issue the copies of one block (rows [r, r+nr) of slab c) into ring slot `dst`.
-__device__ __forceinline__ void issue_block(const MvJobs &J, const MvGeom &M, int job, int r, int nr, int c,
-                                            unsigned char *dst, int lane) {
-    const uint64_t jbase = (uint64_t)job * J.w_stride;
-    for (int w = 0; w < M.nw; ++w) {
-        const uint8_t *base = (w ? J.w2 : J.w) + jbase;
-        unsigned char *d = dst + (size_t)w * M.BR * M.srow;
-        if (M.nck == 1) {  // whole rows: one contiguous range
-            const int n16 = nr * M.rb / 16;
-            const uint8_t *src = base + (uint64_t)r * M.rb;
-            for (int i = lane; i < n16; i += 32) cp16(d + 16 * i, src + 16 * i);
-        } else {           // per row: the slab's scales, then its codes
-            const int ns = M.s_len / 16, nc = M.c_len / 16, per = ns + nc;
-            for (int i = lane; i < nr * per; i += 32) {
-                const int rr = i / per, j = i - rr * per;
-                const uint8_t *row = base + (uint64_t)(r + rr) * M.rb;
-                const uint8_t *src = j < ns ? row + M.s_off * c + 16 * j : row + M.sbytes + M.c_off * c + 16 * (j - ns);
-                cp16(d + rr * M.srow + 16 * j, src);
-            }
-        }
+// This lane's output context for the row it owns in the current task.
+struct LaneRow {
+    int row;        // row of the packed tensor (or -1 past the end)
+    int srow;       // row within its segment
+    int B;          // scale bias of the row's tensor
+    float p2B;      // 2^B
+    RowOut o;
+};
+
+__device__ __forceinline__ void lane_row(const MvJobs &J, int job, int row, int e8, const LaneRow &one, LaneRow &L) {
+    if (J.nseg == 1) {  // one tensor: the context of segment 0, computed once per job
+        L = one;
+        L.row = row < J.rows ? row : -1;
+        L.srow = row;
+        return;
     }
+    L.row = row < J.rows ? row : -1;
+    int sg = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxSegs - 1; ++i) sg += (i < J.nseg - 1 && row >= J.seg[i].row_end) ? 1 : 0;
+    L.o = row_out(J, job, sg, e8);
+    L.B = L.o.B;
+    L.p2B = pow2f(L.B);
+    L.srow = row - seg_start(J, sg);
 }
 
 // The matvec kernel ---------------------------------------------------------------------------------
+// Ring depth: trit5 shares shared memory with its 64 KiB LUT.
 template <int KIND>
+constexpr int ring_depth() { return KIND == TRX_KIND_TERNARY5 ? 2 : 3; }
+
+template <int KIND, int NW>
 __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, const uint32_t *lut_g, uint32_t *err) {
+    constexpr int D = ring_depth<KIND>();
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -422,167 +517,135 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
         lut = reinterpret_cast<char *>(p);
         p += kLutBytes;
     }
-    unsigned char *const ring = p + (size_t)warp * M.D * M.slot_bytes;
-    p += (size_t)kWarpsMv * M.D * M.slot_bytes;
-    long long *const wred = reinterpret_cast<long long *>(p) + warp * 2 * M.BR;  // this warp's row sums
-    p += kWarpsMv * 2 * M.BR * 8;
+    unsigned char *const rings = p;
+    constexpr int slot_bytes = NW * kBlkBytes;
+    unsigned char *const ring = rings + (size_t)warp * D * slot_bytes;
+    const uint32_t ring_s = smem_u32(ring);
+    p += (size_t)M.warps * D * slot_bytes;
     uint32_t *const xp = reinterpret_cast<uint32_t *>(p);
-    p += M.G * M.xwords * 4;
-    int *const xsum = reinterpret_cast<int *>(p);
-    p += ((M.G * 4 + 15) / 16) * 16;
+    p += M.G * M.xw * 4;
     float *const red64 = reinterpret_cast<float *>(p);
     p += 64 * 4;
     uint32_t *const amax_s = reinterpret_cast<uint32_t *>(p);
-    p += 16;
-    int8_t *const q8 = reinterpret_cast<int8_t *>(p);
+    int8_t *const q8 = reinterpret_cast<int8_t *>(rings);  // staging; the rings are idle then
 
-    // This CTA's share of the (job, block) space; a block is BR rows of one segment.
-    const long long total = (long long)J.njobs * M.nbj;
-    const long long q0 = (long long)blockIdx.x * total / gridDim.x;
-    const long long q1 = (long long)(blockIdx.x + 1) * total / gridDim.x;
-    if (q0 >= q1) return;
+    // This CTA's share of the (job, task) space.
+    const long long total = (long long)J.njobs * M.tpj;
+    const long long t0 = (long long)blockIdx.x * total / gridDim.x;
+    const long long t1 = (long long)(blockIdx.x + 1) * total / gridDim.x;
+    if (t0 >= t1) return;
 
     if (KIND == TRX_KIND_TERNARY5) {  // the trit5 LUT (replicated, 256-byte stride)
         const uint4 *src = reinterpret_cast<const uint4 *>(lut_g);
         uint4 *dst = reinterpret_cast<uint4 *>(lut);
         for (int i = tid; i < kLutBytes / 16; i += blockDim.x) dst[i] = src[i];
     }
-
-    // Warp -> slab(s) and its share of the blocks.
-    const int CW = M.CW, nck = M.nck;
-    int c0, nsub, sub;
-    if (nck <= kWarpsMv) {
-        c0 = warp % nck;
-        sub = warp / nck;
-        nsub = (kWarpsMv - c0 + nck - 1) / nck;
-    } else {
-        c0 = warp;
-        sub = 0;
-        nsub = 1;
-    }
-    const int slot = lane / CW;              // which of the RPW rows of a pass
-    const int gl = lane % CW;                // group within the slab
-    const bool leader = gl == 0;
     const uint32_t lane4 = (uint32_t)lane * 4u;
-    uint32_t xr[kXWordsT5 > kXWords2b ? kXWordsT5 : kXWords2b];
+    const float p2B2 = pow2f(J.B2);
 
-    for (long long q = q0; q < q1;) {
-        const int job = (int)(q / M.nbj);
-        const long long jb0 = (long long)job * M.nbj;
-        const int pb0 = (int)(q - jb0);                                   // first block of the piece
-        const int pb1 = (int)min((long long)M.nbj, q1 - jb0);             // end block of the piece
-        q = jb0 + pb1;
-        __syncthreads();  // the previous job's activation is no longer read
+    for (long long t = t0; t < t1;) {
+        const int job = (int)(t / M.tpj);
+        const long long tjb = (long long)job * M.tpj;
+        const int last = (int)(min(t1, tjb + M.tpj) - tjb);  // end task (exclusive) of this piece
+        const int first = (int)(t - tjb) + warp;             // this warp's first task
+        t = tjb + last;
+        __syncthreads();  // the previous piece's activation and rings are no longer in use
         const float *xj = J.x ? J.x + (uint64_t)job * J.x_stride : nullptr;
         const int8_t *x8j = J.x8 ? J.x8 + (uint64_t)job * J.x_stride : nullptr;
-        const int e8 = build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xp, xsum, amax_s, red64);
+        const int e8 = build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xp, amax_s, red64);
         unsigned long long best = 0ull;
-        const int nmine = pb1 - pb0 > sub ? (pb1 - pb0 - sub + nsub - 1) / nsub : 0;  // this warp's blocks
 
-        for (int c = c0; c < nck; c += kWarpsMv) {
-            const int g = c * CW + gl;
-            const bool gvalid = g < M.G;
-            if (gvalid) {
+        Cursor is, cs;
+        cursor_task(M, first, is);
+        cs = is;
+        // Prime the ring with the first D-1 blocks.
 #pragma unroll
-                for (int i = 0; i < (KIND == TRX_KIND_TERNARY5 ? kXWordsT5 : kXWords2b); ++i)
-                    xr[i] = xp[g * M.xwords + i];
+        for (int d = 0; d < D - 1; ++d) {
+            if (is.task < last) {
+                issue_block<KIND, NW>(J, M, job, is.rbk, is.c, ring_s + d * slot_bytes, lane);
+                cursor_next(M, is, M.warps);
             }
-            const int xs = gvalid ? xsum[g] : 0;
-            const int gi = nck == 1 ? g : gl;  // group index inside a ring row
-            const int code_off = (nck == 1 ? M.sbytes : M.s_len) + (KIND == TRX_KIND_TERNARY5 ? 26 : 32) * gi;
-            const int lane_row = slot * M.srow;  // this lane's row within a pass
-            // Prime the ring with the first D-1 blocks.
-            for (int d = 0; d < M.D - 1; ++d) {
-                if (d < nmine) {
-                    const int r = (pb0 + sub + d * nsub) * M.BR;
-                    issue_block(J, M, job, r, min(M.BR, J.rows - r), c, ring + (size_t)d * M.slot_bytes, lane);
-                }
-                cp_commit();
+            cp_commit();
+        }
+        int rs = D - 1, slot = 0;
+        long long acc0 = 0, acc1 = 0;
+        LaneRow L, one;
+        one.o = row_out(J, job, 0, e8);
+        one.B = one.o.B;
+        one.p2B = pow2f(one.B);
+        bool fresh = true;  // the consume cursor entered a new task
+        while (cs.task < last) {
+            if (is.task < last) {
+                issue_block<KIND, NW>(J, M, job, is.rbk, is.c, ring_s + rs * slot_bytes, lane);
+                cursor_next(M, is, M.warps);
             }
-            int rs = M.D - 1, cs = 0, cur_seg = -1, Bs = 0, sb0 = 0;
-            float p2B = 1.f;
-            const float p2B2 = pow2f(J.B2);
-            RowOut ro{};
-            for (int j = 0; j < nmine; ++j) {
-                if (j + M.D - 1 < nmine) {
-                    const int r = (pb0 + sub + (j + M.D - 1) * nsub) * M.BR;
-                    issue_block(J, M, job, r, min(M.BR, J.rows - r), c, ring + (size_t)rs * M.slot_bytes, lane);
-                }
-                cp_commit();
-                rs = rs + 1 == M.D ? 0 : rs + 1;
-                cp_wait_n(M.D - 1);
-                __syncwarp();
-                const int r = (pb0 + sub + j * nsub) * M.BR;
-                const int nr = min(M.BR, J.rows - r);
-                {  // segment of this block (blocks never straddle segments)
-                    int sg = 0;
+            cp_commit();
+            rs = rs + 1 == D ? 0 : rs + 1;
+            if (fresh) {
+                lane_row(J, job, cs.rbk * 32 + lane, e8, one, L);
+                fresh = false;
+            }
+            cp_wait<D - 1>();
+            __syncwarp();
+            const int c = cs.c;
+            const int ng = min(kCG, M.G - c * kCG);
+            const uint32_t *xg = xp + c * kCG * M.xw;
+            const unsigned char *rp = ring + (size_t)slot * slot_bytes + lane * kRowStride;
 #pragma unroll
-                    for (int i = 0; i < kMaxSegs - 1; ++i) sg += (i < J.nseg - 1 && r >= J.seg[i].row_end) ? 1 : 0;
-                    if (sg != cur_seg) {
-                        cur_seg = sg;
-                        ro = row_out(J, job, sg, e8);
-                        Bs = ro.B;
-                        p2B = pow2f(Bs);
-                        sb0 = seg_start(J, sg);
+            for (int w = 0; w < NW; ++w) {
+                const unsigned char *rw = rp + w * kBlkBytes;
+                const uint2 sc = *reinterpret_cast<const uint2 *>(rw + (c & 1) * 8);
+                const int Bw = w ? J.B2 : L.B;
+                const float pw = w ? p2B2 : L.p2B;
+                long long a;
+                if (KIND == TRX_KIND_TERNARY5) {
+                    uint32_t cw[28];
+#pragma unroll
+                    for (int i = 0; i < 7; ++i) {
+                        const uint4 v = reinterpret_cast<const uint4 *>(rw + 16)[i];
+                        cw[4 * i] = v.x;
+                        cw[4 * i + 1] = v.y;
+                        cw[4 * i + 2] = v.z;
+                        cw[4 * i + 3] = v.w;
                     }
+                    a = (c & 1) ? chunk_t5<8>(cw, sc, ng, xg, lut, lane4, Bw, pw)
+                                : chunk_t5<0>(cw, sc, ng, xg, lut, lane4, Bw, pw);
+                } else {
+                    a = chunk_2b(reinterpret_cast<const uint4 *>(rw + 16), sc, ng, xg, Bw, pw);
                 }
-                const unsigned char *blk = ring + (size_t)cs * M.slot_bytes + lane_row;
-                for (int pass = 0; pass < M.NPB; ++pass) {
-                    const int rr = pass * M.RPW + slot;
-                    auto unit = [&](int w) -> long long {
-                        long long cc = 0;
-                        if (gvalid) {  // rows past nr decode stale slot bytes; masked below
-                            const unsigned char *row = blk + (w * M.BR + pass * M.RPW) * M.srow;
-                            const uint32_t sbits = reinterpret_cast<const uint16_t *>(row)[gi];
-                            int gs;
-                            if (KIND == TRX_KIND_TERNARY5)
-                                gs = gsum_t5(row + code_off, gi & 1, lut, lane4, xr, xr + 26) - xs;
-                            else
-                                gs = gsum_2b(row + code_off, xr) - xs;
-                            cc = contrib_fast(gs, sbits, w ? J.B2 : Bs, w ? p2B2 : p2B);
-                            cc = rr < nr ? cc : 0ll;
-                        }
-                        return slot_sum64(cc, CW, lane);
-                    };
-                    const long long sum0 = unit(0);
-                    if (leader) wred[rr] = sum0;
-                    if (M.nw == 2) {
-                        const long long sum1 = unit(1);
-                        if (leader) wred[M.BR + rr] = sum1;
-                    }
-                }
-                __syncwarp();  // every lane is done with the slot; the row sums are in wred
-                cs = cs + 1 == M.D ? 0 : cs + 1;
-                // Finish the block's rows, one lane per row.
-                for (int rr = lane; rr < nr; rr += 32) {
-                    const int row = r + rr;
-                    const long long a = wred[rr];
-                    const long long a2 = M.nw == 2 ? wred[M.BR + rr] : 0ll;
-                    if (nck == 1) {
-                        const unsigned long long k = finish_row(J, ro, row, row - sb0, a, a2, err);
+                if (w) acc1 += a;
+                else acc0 += a;
+            }
+            __syncwarp();  // every lane is done with the slot before it is refilled
+            slot = slot + 1 == D ? 0 : slot + 1;
+            if (c + 1 == cs.c1) {  // the task's last chunk: finish or hand over this lane's row
+                if (L.row >= 0) {
+                    if (M.S == 1) {
+                        const unsigned long long k = finish_row(J, L.o, L.row, L.srow, acc0, acc1, err);
                         best = k > best ? k : best;
                     } else {
-                        // Split row: add this slab's sums; the last slab to arrive finishes it.
-                        const uint64_t ix = (uint64_t)job * J.rows + row;
+                        const uint64_t ix = (uint64_t)job * J.rows + L.row;
                         unsigned long long *acc = J.acc + 2 * ix;
-                        atomicAdd(acc, (unsigned long long)a);
-                        if (M.nw == 2) atomicAdd(acc + 1, (unsigned long long)a2);
+                        atomicAdd(acc, (unsigned long long)acc0);
+                        if (NW == 2) atomicAdd(acc + 1, (unsigned long long)acc1);
                         __threadfence();
-                        if (atomicAdd(J.cnt + ix, 1u) == (unsigned)(nck - 1)) {
+                        if (atomicAdd(J.cnt + ix, 1u) == (unsigned)(M.S - 1)) {
                             __threadfence();
-                            const long long t = (long long)atomicExch(acc, 0ull);
-                            const long long t2 = M.nw == 2 ? (long long)atomicExch(acc + 1, 0ull) : 0ll;
+                            const long long tt = (long long)atomicExch(acc, 0ull);
+                            const long long t2 = NW == 2 ? (long long)atomicExch(acc + 1, 0ull) : 0ll;
                             J.cnt[ix] = 0u;
-                            const unsigned long long k = finish_row(J, ro, row, row - sb0, t, t2, err);
+                            const unsigned long long k = finish_row(J, L.o, L.row, L.srow, tt, t2, err);
                             best = k > best ? k : best;
                         }
                     }
                 }
-                __syncwarp();  // wred is reused by the next block
+                acc0 = acc1 = 0;
+                fresh = true;
             }
-            cp_wait<0>();
-            __syncwarp();
+            cursor_next(M, cs, M.warps);
         }
+        cp_wait<0>();
+        __syncwarp();
         if (J.argmax) argmax_commit(J, job, best, lane);
     }
 }
@@ -694,69 +757,6 @@ trx_status note_cuda(cudaError_t e) {
 
 const char *last_cuda_error() { return cudaGetErrorString(g_last_cuda); }
 
-static int round_pow2(int v) {
-    int p = 1;
-    while (p < v) p <<= 1;
-    return p;
-}
-
-// Plan a launch.  Rows with more than 32 groups are split into equal slabs of CW groups (a power
-// of two >= 8 dividing G, so every slab starts on a 16-byte boundary); others are one slab.
-bool plan_matvec(const MvJobs &J, int cols, int kind, int nw, MvGeom &M) {
-    M.G = cols / 128;
-    if (M.G <= 32) {
-        M.CW = round_pow2(M.G);
-        M.nck = 1;
-    } else {
-        int cw = M.G & -M.G;
-        if (cw > 32) cw = 32;
-        if (cw < 8) return false;  // K > 4096 must be a multiple of 1024
-        M.CW = cw;
-        M.nck = M.G / cw;
-    }
-    M.RPW = 32 / M.CW;
-    M.sbytes = (M.G + 15) / 16 * 32;
-    const int gb = kind == TRX_KIND_TERNARY5 ? 26 : 32;
-    M.rb = M.sbytes + (gb * M.G + 31) / 32 * 32;
-    M.nw = nw;
-    M.xwords = kind == TRX_KIND_TERNARY5 ? kXWordsT5 : kXWords2b;
-    if (M.nck == 1) {
-        M.s_off = M.s_len = M.c_off = M.c_len = 0;
-        M.srow = M.rb;
-    } else {
-        M.s_off = 2 * M.CW;
-        M.s_len = (2 * M.CW + 15) / 16 * 16;
-        M.c_off = gb * M.CW;
-        M.c_len = (gb * M.CW + 15) / 16 * 16;
-        M.srow = M.s_len + M.c_len;
-    }
-    // Passes per block: blocks of about 4 KiB (2 KiB beside the trit5 LUT), and in a launch of
-    // several segments, a block size that divides every segment.
-    int npb = (kind == TRX_KIND_TERNARY5 ? 2048 : 4096) / (M.RPW * M.srow * nw);
-    npb = npb < 1 ? 1 : (npb > kMaxNpb ? kMaxNpb : npb);
-    for (; npb > 1; --npb) {
-        bool ok = true;
-        for (int i = 0; i < J.nseg - 1 && J.nseg > 1; ++i)
-            if ((J.seg[i].row_end - (i ? J.seg[i - 1].row_end : 0)) % (M.RPW * npb)) ok = false;
-        if (ok) break;
-    }
-    M.NPB = npb;
-    M.BR = M.RPW * M.NPB;
-    for (int i = 0; i < J.nseg - 1; ++i)
-        if ((J.seg[i].row_end - (i ? J.seg[i - 1].row_end : 0)) % M.BR) return false;
-    M.nbj = (J.rows + M.BR - 1) / M.BR;
-    M.slot_bytes = M.BR * M.srow * nw;
-    const int fixed = (kind == TRX_KIND_TERNARY5 ? kLutBytes : 0) + kWarpsMv * 2 * M.BR * 8 + M.G * M.xwords * 4 +
-                      ((M.G * 4 + 15) / 16) * 16 + 64 * 4 + 16 + cols + 128;
-    int d = kRingTarget / M.slot_bytes;
-    if (d > kMaxDepth) d = kMaxDepth;
-    if (d < 2) d = 2;
-    while (d > 2 && fixed + kWarpsMv * d * M.slot_bytes > kSmemMax) --d;
-    M.D = d;
-    M.smem = (fixed + kWarpsMv * d * M.slot_bytes + 127) / 128 * 128;
-    return M.smem <= kSmemMax;
-}
-
 static int g_num_sms = 0;
 
 static int num_sms() {
@@ -769,30 +769,64 @@ static int num_sms() {
     return g_num_sms;
 }
 
-template <int KIND>
+// Plan a launch: chunks, tasks (rows split over tasks only when the launch has too few row blocks
+// to give every warp slot of the GPU one), warps and ring depth that fit shared memory.
+bool plan_matvec(const MvJobs &J, int nw, int sms, MvGeom &M) {
+    const int kind = J.kind;
+    M.G = J.cols / 128;
+    M.nch = (M.G + kCG - 1) / kCG;
+    M.sbytes = (M.G + 15) / 16 * 32;
+    M.rb = M.sbytes + ((kind == TRX_KIND_TERNARY5 ? 26 : 32) * M.G + 31) / 32 * 32;
+    M.nw = nw;
+    M.xw = kind == TRX_KIND_TERNARY5 ? kXwT5 : kXw2b;
+    M.nrb = (J.rows + 31) / 32;
+    const long long rbs = (long long)J.njobs * M.nrb;
+    const long long want = (long long)sms * kMaxWarps;
+    int S = 1;
+    if (rbs < want) S = (int)std::min<long long>(M.nch, (want + rbs - 1) / rbs);
+    if (S > 1 && (!J.acc || !J.cnt || (uint64_t)J.njobs * (uint64_t)J.rows > J.acc_rows)) S = 1;
+    M.cpt = (M.nch + S - 1) / S;
+    M.S = (M.nch + M.cpt - 1) / M.cpt;
+    M.tpj = M.nrb * M.S;
+    const int fixed = (kind == TRX_KIND_TERNARY5 ? kLutBytes : 0) + M.G * M.xw * 4 + 64 * 4 + 16;
+    const int ring = (kind == TRX_KIND_TERNARY5 ? 2 : 3) * nw * kBlkBytes;  // one warp's ring
+    M.D = kind == TRX_KIND_TERNARY5 ? 2 : 3;
+    M.warps = std::min(kMaxWarps, (kSmemMax - fixed) / ring);
+    if (M.warps < 4) return false;
+    if (M.warps * ring < J.cols) return false;  // the q8 staging lives in the rings
+    M.smem = (fixed + M.warps * ring + 127) / 128 * 128;
+    return M.smem <= kSmemMax;
+}
+
+template <int KIND, int NW>
 static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, int grid, const uint32_t *lut, uint32_t *err,
                              cudaStream_t st) {
-    static int configured = 0;
-    if (M.smem > configured) {
+    static unsigned long long configured = 0;  // devices whose attribute is set
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(configured & bit)) {
         const cudaError_t e =
-            cudaFuncSetAttribute(tmv_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+            cudaFuncSetAttribute(tmv_kernel<KIND, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return note_cuda(e);
-        configured = kSmemMax;
+        configured |= bit;
     }
-    tmv_kernel<KIND><<<grid, kMvThreads, M.smem, st>>>(J, M, lut, err);
+    tmv_kernel<KIND, NW><<<grid, M.warps * 32, M.smem, st>>>(J, M, lut, err);
     return note_cuda(cudaGetLastError());
 }
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st) {
     MvGeom M;
-    if (!plan_matvec(J, J.cols, J.kind, J.w2 ? 2 : 1, M)) return TRX_ERR_UNSUPPORTED;
-    if (M.nck > 1 && (!J.acc || !J.cnt || (uint64_t)J.njobs * (uint64_t)J.rows > J.acc_rows))
-        return TRX_ERR_UNSUPPORTED;
-    long long want = ((long long)J.njobs * M.nbj + 1) / 2;  // at least a couple of blocks per CTA
-    int grid = num_sms();
-    if (want < grid) grid = (int)(want < 1 ? 1 : want);
-    if (J.kind == TRX_KIND_TERNARY5) return launch_tmv<TRX_KIND_TERNARY5>(J, M, grid, lut, err, st);
-    return launch_tmv<TRX_KIND_TERNARY>(J, M, grid, lut, err, st);
+    const int sms = num_sms();
+    const int nw = J.w2 ? 2 : 1;
+    if (!plan_matvec(J, nw, sms, M)) return TRX_ERR_UNSUPPORTED;
+    const long long tasks = (long long)J.njobs * M.tpj;
+    const int grid = (int)std::min<long long>(sms, tasks);
+    if (J.kind == TRX_KIND_TERNARY5)
+        return nw == 2 ? launch_tmv<TRX_KIND_TERNARY5, 2>(J, M, grid, lut, err, st)
+                       : launch_tmv<TRX_KIND_TERNARY5, 1>(J, M, grid, lut, err, st);
+    return nw == 2 ? launch_tmv<TRX_KIND_TERNARY, 2>(J, M, grid, lut, err, st)
+                   : launch_tmv<TRX_KIND_TERNARY, 1>(J, M, grid, lut, err, st);
 }
 
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st) {
