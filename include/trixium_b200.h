@@ -39,6 +39,7 @@ typedef int trx_status;
 #define TRX_DEV_OVERFLOW   0x1u
 #define TRX_DEV_BADBYTE    0x2u
 #define TRX_DEV_TIMEOUT    0x4u
+#define TRX_DEV_INTERNAL   0x8u   /* a launch found shared memory laid out unlike its plan */
 
 #define TRX_KIND_TERNARY   0    /* KIND_TERNARY,  model/layout.py:46 */
 #define TRX_KIND_TERNARY5  5    /* KIND_TERNARY5, model/layout.py:50 */

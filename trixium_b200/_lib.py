@@ -15,7 +15,7 @@ ERRORS = {
     -1: "TRX_ERR_ARG", -2: "TRX_ERR_LAYOUT", -3: "TRX_ERR_OVERFLOW", -4: "TRX_ERR_CUDA",
     -5: "TRX_ERR_TIMEOUT", -6: "TRX_ERR_UNSUPPORTED",
 }
-DEV_OVERFLOW, DEV_BADBYTE, DEV_TIMEOUT = 0x1, 0x2, 0x4
+DEV_OVERFLOW, DEV_BADBYTE, DEV_TIMEOUT, DEV_INTERNAL = 0x1, 0x2, 0x4, 0x8
 
 # Every symbol the header declares (tests check the library exports all of them).
 SYMBOLS = (
@@ -35,7 +35,8 @@ class TrxDeviceError(RuntimeError):
     def __init__(self, bits):
         self.bits = bits
         names = [n for b, n in ((DEV_OVERFLOW, "overflow"), (DEV_BADBYTE, "invalid trit5 byte"),
-                                (DEV_TIMEOUT, "bounded wait timed out")) if bits & b]
+                                (DEV_TIMEOUT, "bounded wait timed out"),
+                                (DEV_INTERNAL, "shared-memory layout mismatch")) if bits & b]
         super().__init__("device error: " + ", ".join(names or [hex(bits)]))
 
 

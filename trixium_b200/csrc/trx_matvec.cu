@@ -70,6 +70,10 @@ struct MvGeom {
     int warps;    // warps per CTA
     int D;        // ring depth (blocks)
     int xw;       // activation words per group
+    int fixed;    // bytes of activation words and reductions (128-byte rounded): rings A start here
+    int na;       // warps whose ring lies in region A (the rest: region C, after the trit5 LUT)
+    int q8c;      // the quantiser's staging lies in region C
+    int base;     // shared-window address of the dynamic shared memory the plan assumes
     int smem;     // dynamic shared bytes
 };
 
@@ -205,7 +209,7 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
 // trit5, group g of a chunk whose 104 code bytes start at byte H (0 or 8) of the 28-word window
 // cw.  xg: the group's 44 activation words.  Returns sum((digit - 1) * x).
 template <int H, int g>
-__device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], const char *lut, uint32_t lane4, const uint32_t *xg) {
+__device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], uint32_t lane4x, const uint32_t *xg) {
     uint32_t xa[kXwT5];
 #pragma unroll
     for (int i = 0; i < kXwT5 / 4; ++i) {
@@ -225,9 +229,10 @@ __device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], const char *lut
             if (i < nb) {
                 constexpr int base = H + 26 * g;
                 const int pb = base + 4 * q + i;  // byte of the window (compile time)
-                // a = byte * 256 + lane * 4: this lane's replica of the entry, no bank conflict.
-                const uint32_t a = __byte_perm(cw[pb >> 2], lane4, 0x5504u | ((pb & 3) << 4));
-                E[i] = *reinterpret_cast<const uint32_t *>(lut + a);
+                // a = 0x10000 + byte * 256 + lane * 4: the shared address of this lane's replica of
+                // the entry (the LUT sits at window address 0x10000), no bank conflict.
+                const uint32_t a = __byte_perm(cw[pb >> 2], lane4x, 0x7604u | ((pb & 3) << 4));
+                asm("ld.shared.u32 %0, [%1];" : "=r"(E[i]) : "r"(a));
                 acc[i] = dp4a_ss(E[i], xa[4 * q + i], acc[i]);
             }
         }
@@ -271,16 +276,23 @@ __device__ __forceinline__ int gsum_2b(const uint4 *cp, const uint32_t *xg) {
     return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - (int)xw[32];
 }
 
-// (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Common case: a normal fp16
-// scale with 0 <= e16+B <= 19, where m11 << (e16+B) = scale * 2^B is an integer below 2^30, so the
-// contribution is one wide multiply by F2I(fp32(scale) * 2^B) (both steps exact).  Otherwise the
-// general floor/left shift.
-__device__ __forceinline__ long long contrib_fast(int gs, uint32_t sbits, int B, float pow2B) {
-    const int E = (sbits >> 10) & 31;
-    const int sh = E - 25 + B;
-    if (E != 0 && (unsigned)sh <= 19u)
-        return (long long)gs * (long long)__float2int_rz(__fmul_rn(__half2float(__ushort_as_half((unsigned short)sbits)), pow2B));
-    return group_contrib(gs, sbits, B);
+// (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Fast range: a normal fp16
+// scale (biased exponent E in [1, 30]) with 0 <= e16+B = E-25+B <= 19, where m11 << (e16+B) =
+// scale * 2^B is an integer below 2^30: the contribution is gs * F2I(fp32(scale) * 2^B) (both
+// steps exact, the sign carried by the float), one 32x32->64 multiply.  Other scales (tiny or
+// subnormal ones, far below the tensor's largest) take the general floor/left shift.
+struct ScaleFast {
+    int lo, span;  // fast iff E - lo in [0, span]
+    float p2B;     // 2^B
+};
+
+__device__ __forceinline__ ScaleFast scale_fast(int B) {
+    ScaleFast f;
+    const int lo = max(1, 25 - B), hi = min(30, 44 - B);
+    f.lo = hi >= lo ? lo : 64;  // an empty range: E - 64 < 0 fails the unsigned test below
+    f.span = hi >= lo ? hi - lo : 0;
+    f.p2B = pow2f(B);
+    return f;
 }
 
 __device__ __forceinline__ uint32_t scale_bits(uint2 s, int g) {
@@ -288,22 +300,29 @@ __device__ __forceinline__ uint32_t scale_bits(uint2 s, int g) {
     return g & 1 ? w >> 16 : w & 0xffffu;
 }
 
-// The int64 contribution of one chunk of this lane's row (ng <= 4 groups).
+__device__ __forceinline__ long long contrib(int gs, uint32_t sb, int B, const ScaleFast &F) {
+    if ((unsigned)((int)((sb >> 10) & 31u) - F.lo) <= (unsigned)F.span)
+        return (long long)gs * (long long)__float2int_rz(__fmul_rn(__half2float(__ushort_as_half((unsigned short)sb)), F.p2B));
+    return group_contrib(gs, sb, B);
+}
+
+// The int64 sum of one chunk (ng <= 4 groups) of this lane's row.
 template <int H>
 __device__ __forceinline__ long long chunk_t5(const uint32_t (&cw)[28], uint2 sc, int ng, const uint32_t *xg,
-                                              const char *lut, uint32_t lane4, int B, float p2B) {
-    long long a = contrib_fast(gsum_t5<H, 0>(cw, lut, lane4, xg), scale_bits(sc, 0), B, p2B);
-    if (ng > 1) a += contrib_fast(gsum_t5<H, 1>(cw, lut, lane4, xg + kXwT5), scale_bits(sc, 1), B, p2B);
-    if (ng > 2) a += contrib_fast(gsum_t5<H, 2>(cw, lut, lane4, xg + 2 * kXwT5), scale_bits(sc, 2), B, p2B);
-    if (ng > 3) a += contrib_fast(gsum_t5<H, 3>(cw, lut, lane4, xg + 3 * kXwT5), scale_bits(sc, 3), B, p2B);
+                                              uint32_t lane4x, int B, const ScaleFast &F) {
+    long long a = contrib(gsum_t5<H, 0>(cw, lane4x, xg), scale_bits(sc, 0), B, F);
+    if (ng > 1) a += contrib(gsum_t5<H, 1>(cw, lane4x, xg + kXwT5), scale_bits(sc, 1), B, F);
+    if (ng > 2) a += contrib(gsum_t5<H, 2>(cw, lane4x, xg + 2 * kXwT5), scale_bits(sc, 2), B, F);
+    if (ng > 3) a += contrib(gsum_t5<H, 3>(cw, lane4x, xg + 3 * kXwT5), scale_bits(sc, 3), B, F);
     return a;
 }
 
-__device__ __forceinline__ long long chunk_2b(const uint4 *cp, uint2 sc, int ng, const uint32_t *xg, int B, float p2B) {
-    long long a = contrib_fast(gsum_2b(cp, xg), scale_bits(sc, 0), B, p2B);
-    if (ng > 1) a += contrib_fast(gsum_2b(cp + 2, xg + kXw2b), scale_bits(sc, 1), B, p2B);
-    if (ng > 2) a += contrib_fast(gsum_2b(cp + 4, xg + 2 * kXw2b), scale_bits(sc, 2), B, p2B);
-    if (ng > 3) a += contrib_fast(gsum_2b(cp + 6, xg + 3 * kXw2b), scale_bits(sc, 3), B, p2B);
+__device__ __forceinline__ long long chunk_2b(const uint4 *cp, uint2 sc, int ng, const uint32_t *xg, int B,
+                                              const ScaleFast &F) {
+    long long a = contrib(gsum_2b(cp, xg), scale_bits(sc, 0), B, F);
+    if (ng > 1) a += contrib(gsum_2b(cp + 2, xg + kXw2b), scale_bits(sc, 1), B, F);
+    if (ng > 2) a += contrib(gsum_2b(cp + 4, xg + 2 * kXw2b), scale_bits(sc, 2), B, F);
+    if (ng > 3) a += contrib(gsum_2b(cp + 6, xg + 3 * kXw2b), scale_bits(sc, 3), B, F);
     return a;
 }
 
@@ -476,7 +495,7 @@ struct LaneRow {
     int row;        // row of the packed tensor (or -1 past the end)
     int srow;       // row within its segment
     int B;          // scale bias of the row's tensor
-    float p2B;      // 2^B
+    ScaleFast F;    // its fast scale range
     RowOut o;
 };
 
@@ -493,7 +512,7 @@ __device__ __forceinline__ void lane_row(const MvJobs &J, int job, int row, int 
     for (int i = 0; i < kMaxSegs - 1; ++i) sg += (i < J.nseg - 1 && row >= J.seg[i].row_end) ? 1 : 0;
     L.o = row_out(J, job, sg, e8);
     L.B = L.o.B;
-    L.p2B = pow2f(L.B);
+    L.F = scale_fast(L.B);
     L.srow = row - seg_start(J, sg);
 }
 
@@ -510,24 +529,26 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
     const int warp = tid >> 5, lane = tid & 31;
     if (J.skip && *J.skip) return;
 
-    // Carve shared memory (must match plan_matvec).
-    unsigned char *p = smem;
-    char *lut = nullptr;
-    if (KIND == TRX_KIND_TERNARY5) {
-        lut = reinterpret_cast<char *>(p);
-        p += kLutBytes;
-    }
-    unsigned char *const rings = p;
+    // Carve shared memory (must match plan_matvec): [activation words, reductions][rings A]
+    // [trit5 LUT at window address 0x10000][rings C]; 2-bit: one ring region, no LUT.
+    constexpr int RING = D * NW * kBlkBytes;  // one warp's ring
     constexpr int slot_bytes = NW * kBlkBytes;
-    unsigned char *const ring = rings + (size_t)warp * D * slot_bytes;
-    const uint32_t ring_s = smem_u32(ring);
-    p += (size_t)M.warps * D * slot_bytes;
-    uint32_t *const xp = reinterpret_cast<uint32_t *>(p);
-    p += M.G * M.xw * 4;
+    uint32_t *const xp = reinterpret_cast<uint32_t *>(smem);
+    unsigned char *p = smem + M.G * M.xw * 4;
     float *const red64 = reinterpret_cast<float *>(p);
     p += 64 * 4;
     uint32_t *const amax_s = reinterpret_cast<uint32_t *>(p);
-    int8_t *const q8 = reinterpret_cast<int8_t *>(rings);  // staging; the rings are idle then
+    // Offsets (not pointers chosen between regions) keep every access provably shared.
+    const int lut_off = 0x10000 - M.base, c_off = lut_off + kLutBytes;
+    if (KIND == TRX_KIND_TERNARY5 && smem_u32(smem) != (uint32_t)M.base) {
+        if (tid == 0) atomicOr(err, TRX_DEV_INTERNAL);  // the window is not where the plan put the LUT
+        return;
+    }
+    unsigned char *const lut = smem + lut_off;  // trit5 only
+    const int ring_off = warp < M.na ? M.fixed + warp * RING : c_off + (warp - M.na) * RING;
+    unsigned char *const ring = smem + ring_off;
+    const uint32_t ring_s = smem_u32(ring);
+    int8_t *const q8 = reinterpret_cast<int8_t *>(smem + (M.q8c ? c_off : M.fixed));  // staging; rings idle then
 
     // This CTA's share of the (job, task) space.
     const long long total = (long long)J.njobs * M.tpj;
@@ -540,8 +561,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
         uint4 *dst = reinterpret_cast<uint4 *>(lut);
         for (int i = tid; i < kLutBytes / 16; i += blockDim.x) dst[i] = src[i];
     }
-    const uint32_t lane4 = (uint32_t)lane * 4u;
-    const float p2B2 = pow2f(J.B2);
+    const uint32_t lane4x = 0x10000u | ((uint32_t)lane * 4u);
+    const ScaleFast F2 = scale_fast(J.B2);
 
     for (long long t = t0; t < t1;) {
         const int job = (int)(t / M.tpj);
@@ -572,7 +593,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
         LaneRow L, one;
         one.o = row_out(J, job, 0, e8);
         one.B = one.o.B;
-        one.p2B = pow2f(one.B);
+        one.F = scale_fast(one.B);
         bool fresh = true;  // the consume cursor entered a new task
         while (cs.task < last) {
             if (is.task < last) {
@@ -596,7 +617,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
                 const unsigned char *rw = rp + w * kBlkBytes;
                 const uint2 sc = *reinterpret_cast<const uint2 *>(rw + (c & 1) * 8);
                 const int Bw = w ? J.B2 : L.B;
-                const float pw = w ? p2B2 : L.p2B;
+                const ScaleFast &Fw = w ? F2 : L.F;
                 long long a;
                 if (KIND == TRX_KIND_TERNARY5) {
                     uint32_t cw[28];
@@ -608,10 +629,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
                         cw[4 * i + 2] = v.z;
                         cw[4 * i + 3] = v.w;
                     }
-                    a = (c & 1) ? chunk_t5<8>(cw, sc, ng, xg, lut, lane4, Bw, pw)
-                                : chunk_t5<0>(cw, sc, ng, xg, lut, lane4, Bw, pw);
+                    a = (c & 1) ? chunk_t5<8>(cw, sc, ng, xg, lane4x, Bw, Fw)
+                                : chunk_t5<0>(cw, sc, ng, xg, lane4x, Bw, Fw);
                 } else {
-                    a = chunk_2b(reinterpret_cast<const uint4 *>(rw + 16), sc, ng, xg, Bw, pw);
+                    a = chunk_2b(reinterpret_cast<const uint4 *>(rw + 16), sc, ng, xg, Bw, Fw);
                 }
                 if (w) acc1 += a;
                 else acc0 += a;
@@ -757,21 +778,34 @@ trx_status note_cuda(cudaError_t e) {
 
 const char *last_cuda_error() { return cudaGetErrorString(g_last_cuda); }
 
-static int g_num_sms = 0;
+// Per-device launch facts: SM count and the shared memory the driver reserves per block (the
+// dynamic shared memory starts at that window address).
+struct DevInfo {
+    int sms, reserved;
+};
 
-static int num_sms() {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
+static DevInfo dev_info() {
+    static DevInfo info[64];
+    static bool have[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    dev &= 63;
+    if (!have[dev]) {
+        int v = 0;
+        info[dev].sms = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+        v = 0;
+        info[dev].reserved =
+            cudaDeviceGetAttribute(&v, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess ? v : 1024;
+        have[dev] = true;
     }
-    return g_num_sms;
+    return info[dev];
 }
+
+static int num_sms() { return dev_info().sms; }
 
 // Plan a launch: chunks, tasks (rows split over tasks only when the launch has too few row blocks
 // to give every warp slot of the GPU one), warps and ring depth that fit shared memory.
-bool plan_matvec(const MvJobs &J, int nw, int sms, MvGeom &M) {
+bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     const int kind = J.kind;
     M.G = J.cols / 128;
     M.nch = (M.G + kCG - 1) / kCG;
@@ -788,13 +822,34 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, MvGeom &M) {
     M.cpt = (M.nch + S - 1) / S;
     M.S = (M.nch + M.cpt - 1) / M.cpt;
     M.tpj = M.nrb * M.S;
-    const int fixed = (kind == TRX_KIND_TERNARY5 ? kLutBytes : 0) + M.G * M.xw * 4 + 64 * 4 + 16;
-    const int ring = (kind == TRX_KIND_TERNARY5 ? 2 : 3) * nw * kBlkBytes;  // one warp's ring
+    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 127) / 128 * 128;
     M.D = kind == TRX_KIND_TERNARY5 ? 2 : 3;
-    M.warps = std::min(kMaxWarps, (kSmemMax - fixed) / ring);
+    const int ring = M.D * nw * kBlkBytes;  // one warp's ring
+    if (kind == TRX_KIND_TERNARY5) {
+        // The LUT sits at shared-window address 0x10000 (its PRMT-built addresses need no add):
+        // region A below it, region C above it.
+        M.base = reserved;
+        const int lut_off = 0x10000 - reserved;
+        if (M.fixed > lut_off) return false;
+        const int na_max = (lut_off - M.fixed) / ring;
+        const int c_off = lut_off + kLutBytes;
+        const int nc_max = (kSmemMax - c_off) / ring;
+        M.warps = std::min(kMaxWarps, na_max + nc_max);
+        M.na = std::min(na_max, M.warps);
+        const int nc = M.warps - M.na;
+        M.smem = c_off + nc * ring;
+        if (M.na * ring >= J.cols) M.q8c = 0;
+        else if (nc * ring >= J.cols) M.q8c = 1;
+        else return false;  // no ring region holds the quantiser's staging
+    } else {
+        M.base = 0;
+        M.warps = std::min(kMaxWarps, (kSmemMax - M.fixed) / ring);
+        M.na = M.warps;
+        M.q8c = 0;
+        M.smem = M.fixed + M.warps * ring;
+        if (M.warps * ring < J.cols) return false;
+    }
     if (M.warps < 4) return false;
-    if (M.warps * ring < J.cols) return false;  // the q8 staging lives in the rings
-    M.smem = (fixed + M.warps * ring + 127) / 128 * 128;
     return M.smem <= kSmemMax;
 }
 
@@ -817,9 +872,10 @@ static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, int grid, const u
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st) {
     MvGeom M;
-    const int sms = num_sms();
+    const DevInfo di = dev_info();
+    const int sms = di.sms;
     const int nw = J.w2 ? 2 : 1;
-    if (!plan_matvec(J, nw, sms, M)) return TRX_ERR_UNSUPPORTED;
+    if (!plan_matvec(J, nw, sms, di.reserved, M)) return TRX_ERR_UNSUPPORTED;
     const long long tasks = (long long)J.njobs * M.tpj;
     const int grid = (int)std::min<long long>(sms, tasks);
     if (J.kind == TRX_KIND_TERNARY5)
