@@ -194,3 +194,54 @@ def sigmoid(x):
 def argmax_first(v):
     """Greedy argmax, ties to the smallest index (doc/units.md:149)."""
     return int(np.argmax(np.asarray(v)))
+
+
+# Decode attention --------------------------------------------------------------------------------
+
+def rope_freq(rope_n, theta):
+    """model/mirror.py:754: theta^(-2i/rope_n) per pair, in fp32."""
+    return np.array([f32(f32(theta) ** f32(-2.0 * i / rope_n)) for i in range(rope_n // 2)], dtype=f32)
+
+
+def rope_neox(vh, pos, freq):
+    """model/mirror.py:956-961: neox pairs (i, i + rope_n/2) over the first rope_n dims, cos/sin of
+    fp32(pos * freq) in fp32; the rest passes through."""
+    vh = np.array(vh, dtype=f32)
+    half = len(freq)
+    ang = (f32(pos) * freq).astype(f32)
+    c, s = np.cos(ang, dtype=f32), np.sin(ang, dtype=f32)
+    x0, x1 = vh[:half].copy(), vh[half:2 * half].copy()
+    vh[:half] = (x0 * c - x1 * s).astype(f32)
+    vh[half:2 * half] = (x0 * s + x1 * c).astype(f32)
+    return vh
+
+
+def attn_decode(q, k, v, kcache, vcache, pos, qn_w, kn_w, eps, freq, gate=None):
+    """One decode step of GQA attention (model/mirror.py:945-996; model/golden.py:361-398).
+
+    q (H, hd), k/v (Hkv, hd) fp32: this token's projections (gate (H, hd) or None).
+    kcache/vcache (T, Hkv, hd) fp16: positions [0, pos) already filled; this step writes
+    position pos (QK-RMSNorm'd, RoPE'd k; v as is), rounded to fp16 (the build's cache type).
+    Returns out (H, hd) fp32; kcache/vcache updated in place."""
+    H, hd = q.shape
+    Hkv = k.shape[0]
+    rep = H // Hkv
+    qn = np.stack([rope_neox(rmsnorm(q[h], qn_w, eps), pos, freq) for h in range(H)])
+    kn = np.stack([rope_neox(rmsnorm(k[h], kn_w, eps), pos, freq) for h in range(Hkv)])
+    kcache[pos] = kn.astype(np.float16)
+    vcache[pos] = np.asarray(v, dtype=f32).astype(np.float16)
+    T = pos + 1
+    K = kcache[:T].astype(f32)
+    V = vcache[:T].astype(f32)
+    scale = f32(1.0 / np.sqrt(hd))
+    out = np.zeros((H, hd), dtype=f32)
+    for h in range(H):
+        kvh = h // rep
+        sc = ((K[:, kvh, :] @ qn[h]).astype(f32) * scale).astype(f32)
+        ex = np.exp((sc - sc.max()).astype(f32), dtype=f32)
+        inv = f32(f32(1) / ex.sum(dtype=f32))
+        o = ((ex * inv).astype(f32) @ V[:, kvh, :]).astype(f32)
+        if gate is not None:
+            o = (o * sigmoid(gate[h])).astype(f32)
+        out[h] = o
+    return out
