@@ -40,6 +40,7 @@ typedef int trx_status;
 #define TRX_DEV_BADBYTE    0x2u
 #define TRX_DEV_TIMEOUT    0x4u
 #define TRX_DEV_INTERNAL   0x8u   /* a launch found shared memory laid out unlike its plan */
+#define TRX_DEV_RANGE      0x10u  /* an index read from device memory (a position) was out of range */
 
 #define TRX_KIND_TERNARY   0    /* KIND_TERNARY,  model/layout.py:46 */
 #define TRX_KIND_TERNARY5  5    /* KIND_TERNARY5, model/layout.py:50 */
@@ -135,6 +136,35 @@ trx_status trx_validate_packed(trx_ctx *ctx, const trx_entry *e, const void *d_p
 trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
                               uint64_t w_stride, const float *d_x, uint64_t x_stride,
                               float *d_y, uint64_t y_stride, int njobs, cudaStream_t stream);
+
+/* Shape of one attention layer (model/configs.py head counts; mirror.py:945-996). */
+typedef struct trx_attn_shape {
+    uint32_t n_head;     /* query heads H                                              */
+    uint32_t n_kv;       /* kv heads (H % n_kv == 0; query head h reads kv head h/(H/n_kv)) */
+    uint32_t head_dim;   /* hd, a multiple of 8, <= 512                                 */
+    uint32_t rope_dims;  /* rotated dims per head (even, <= hd; neox pairs inside them)  */
+    uint32_t max_pos;    /* cache capacity in positions                                 */
+    int32_t  gated;      /* q holds [q | gate] per head (2*hd floats): out *= sigmoid(gate) */
+    float    eps;        /* epsilon of the q/k RMSNorms                                 */
+} trx_attn_shape;
+
+/*
+ * One decode step of GQA attention over an fp16 KV cache (model/mirror.py:945-996,
+ * model/golden.py:361-398), in one launch:
+ *   q[h] = RoPE(RMSNorm(q[h]) * qnorm_w), k = RoPE(RMSNorm(k) * knorm_w) (neox pairs over the
+ *   first rope_dims, angle fp32(pos * rope_freq[i])); k and v (rounded to fp16) are written to
+ *   the caches at position *d_pos; out[h] = softmax(q[h].K^T / sqrt(hd)) V over positions
+ *   0..pos, times sigmoid(gate[h]) when gated.
+ * d_q: H * (gated ? 2 : 1) * hd floats; d_k, d_v: n_kv * hd; d_qnorm_w, d_knorm_w: hd;
+ * d_rope_freq: rope_dims/2 floats; caches: [max_pos][n_kv][hd] fp16 (16-byte aligned);
+ * d_pos: one int32 on the device (read by the kernel, so a captured graph replays every step);
+ * d_out: H * hd floats.  A position outside [0, max_pos) sets TRX_DEV_RANGE and does nothing.
+ * Launches on the context's scratch: calls on one context must not overlap.
+ */
+trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const float *d_q, const float *d_k,
+                           const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                           const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                           float *d_out, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -216,20 +216,25 @@ def rope_neox(vh, pos, freq):
     return vh
 
 
-def attn_decode(q, k, v, kcache, vcache, pos, qn_w, kn_w, eps, freq, gate=None):
+def attn_new_rows(k, v, pos, kn_w, eps, freq):
+    """model/mirror.py:963-965: this token's cache rows, RMSNorm'd and RoPE'd k and v, rounded to
+    fp16 (the build's cache type)."""
+    kn = np.stack([rope_neox(rmsnorm(k[h], kn_w, eps), pos, freq) for h in range(k.shape[0])])
+    return kn.astype(np.float16), np.asarray(v, dtype=f32).astype(np.float16)
+
+
+def attn_decode(q, k, v, kcache, vcache, pos, qn_w, kn_w, eps, freq, gate=None, rows=None):
     """One decode step of GQA attention (model/mirror.py:945-996; model/golden.py:361-398).
 
     q (H, hd), k/v (Hkv, hd) fp32: this token's projections (gate (H, hd) or None).
     kcache/vcache (T, Hkv, hd) fp16: positions [0, pos) already filled; this step writes
-    position pos (QK-RMSNorm'd, RoPE'd k; v as is), rounded to fp16 (the build's cache type).
+    position pos (attn_new_rows, or `rows` = (k_row, v_row) given).
     Returns out (H, hd) fp32; kcache/vcache updated in place."""
     H, hd = q.shape
     Hkv = k.shape[0]
     rep = H // Hkv
     qn = np.stack([rope_neox(rmsnorm(q[h], qn_w, eps), pos, freq) for h in range(H)])
-    kn = np.stack([rope_neox(rmsnorm(k[h], kn_w, eps), pos, freq) for h in range(Hkv)])
-    kcache[pos] = kn.astype(np.float16)
-    vcache[pos] = np.asarray(v, dtype=f32).astype(np.float16)
+    kcache[pos], vcache[pos] = rows if rows is not None else attn_new_rows(k, v, pos, kn_w, eps, freq)
     T = pos + 1
     K = kcache[:T].astype(f32)
     V = vcache[:T].astype(f32)

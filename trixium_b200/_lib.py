@@ -15,13 +15,13 @@ ERRORS = {
     -1: "TRX_ERR_ARG", -2: "TRX_ERR_LAYOUT", -3: "TRX_ERR_OVERFLOW", -4: "TRX_ERR_CUDA",
     -5: "TRX_ERR_TIMEOUT", -6: "TRX_ERR_UNSUPPORTED",
 }
-DEV_OVERFLOW, DEV_BADBYTE, DEV_TIMEOUT, DEV_INTERNAL = 0x1, 0x2, 0x4, 0x8
+DEV_OVERFLOW, DEV_BADBYTE, DEV_TIMEOUT, DEV_INTERNAL, DEV_RANGE = 0x1, 0x2, 0x4, 0x8, 0x10
 
 # Every symbol the header declares (tests check the library exports all of them).
 SYMBOLS = (
     "trx_create", "trx_destroy", "trx_get_error", "trx_last_cuda_error", "trx_row_bytes", "trx_matvec_i8",
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
-    "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch",
+    "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
 )
 
 
@@ -36,8 +36,16 @@ class TrxDeviceError(RuntimeError):
         self.bits = bits
         names = [n for b, n in ((DEV_OVERFLOW, "overflow"), (DEV_BADBYTE, "invalid trit5 byte"),
                                 (DEV_TIMEOUT, "bounded wait timed out"),
-                                (DEV_INTERNAL, "shared-memory layout mismatch")) if bits & b]
+                                (DEV_INTERNAL, "shared-memory layout mismatch"),
+                                (DEV_RANGE, "device-side index out of range")) if bits & b]
         super().__init__("device error: " + ", ".join(names or [hex(bits)]))
+
+
+class AttnShape(ctypes.Structure):
+    """trx_attn_shape: one attention layer's geometry."""
+    _fields_ = [("n_head", ctypes.c_uint32), ("n_kv", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+                ("rope_dims", ctypes.c_uint32), ("max_pos", ctypes.c_uint32), ("gated", ctypes.c_int32),
+                ("eps", ctypes.c_float)]
 
 
 class Entry(ctypes.Structure):
@@ -72,6 +80,7 @@ def lib():
             "trx_validate_packed": ([_vp, E, _vp, _vp], ctypes.c_int),
             "trx_matvec_f_batch": ([_vp, E, _vp, ctypes.c_uint64, _vp, ctypes.c_uint64, _vp,
                                     ctypes.c_uint64, ctypes.c_int, _vp], ctypes.c_int),
+            "trx_attn_decode": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

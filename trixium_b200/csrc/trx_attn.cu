@@ -1,0 +1,237 @@
+// GQA decode attention for B200 (sm_100a): one new token against the fp16 KV cache, the decode
+// step of model/mirror.py:945-996 (model/golden.py:361-398).
+//
+// One launch does the whole step:
+//  * per query head: RMSNorm with the canonical 64-partial sum of squares (mirror.py:576-591,
+//    :697-700), then neox RoPE over the first rope_n dims with cos/sin of fp32(pos * freq)
+//    (mirror.py:954-961);
+//  * the new key (normalised, rotated) and value are rounded to fp16 and written to the cache at
+//    position pos by the CTA whose chunk holds pos;
+//  * split-K over the cache: CTA (s, kv head) owns positions [s*chunk, (s+1)*chunk) and every query
+//    head of its group (GQA: head h reads kv head h / (H/Hkv)).  It stages the K and V rows of its
+//    chunk in shared memory with cp.async, forms the scores q.k * 1/sqrt(hd), the chunk's max and
+//    exp-sum and the exp-weighted sum of V rows, and writes (max, sum, o) to a scratch partial;
+//  * the last CTA of a kv head to arrive (an atomic count, reset by that CTA) merges the partials:
+//    o = sum_s e^(m_s-M) o_s * 1/(sum_s e^(m_s-M) l_s) (one reciprocal per head, as mirror.py:984
+//    and ggml), times sigmoid(gate) for gated heads (mirror.py:992-993).
+// The position is read from device memory, so a captured CUDA graph replays every step.  CTAs
+// past the position only arrive at the count.  Memory-bound on the KV stream: 4*hd bytes per
+// (position, kv head) read once.
+#include <cstdint>
+#include <cstring>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "trx_common.cuh"
+#include "trx_internal.h"
+
+namespace trx {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+// Canonical RMSNorm of one head vector in shared memory, by one warp: partial j (j < 64) sums
+// v[i]^2 over i = j, j+64, ... in order, then the halving tree; r = 1/sqrt(ss/n + eps) in fp32;
+// v = (v*r)*w.
+__device__ void head_rmsnorm(float *v, int hd, const float *w, float eps, int lane) {
+    float p0 = 0.f, p1 = 0.f;
+    for (int i = lane; i < hd; i += 64) p0 = __fadd_rn(p0, __fmul_rn(v[i], v[i]));
+    for (int i = lane + 32; i < hd; i += 64) p1 = __fadd_rn(p1, __fmul_rn(v[i], v[i]));
+    float a = __fadd_rn(p0, p1);
+    for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
+    const float ss = __shfl_sync(0xffffffffu, a, 0);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(__fmul_rn(v[i], r), w ? __ldg(w + i) : 1.0f);
+    __syncwarp();
+}
+
+// neox RoPE over dims [0, 2*half): pairs (d, d + half), angle fp32(pos * freq[d]).
+__device__ void head_rope(float *v, int half, const float *freq, int pos, int lane) {
+    for (int d = lane; d < half; d += 32) {
+        const float ang = __fmul_rn((float)pos, __ldg(freq + d));
+        const float c = cosf(ang), s = sinf(ang);
+        const float x0 = v[d], x1 = v[d + half];
+        v[d] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        v[d + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t u) {
+    __half2 h;
+    memcpy(&h, &u, 4);
+    return __half22float2(h);
+}
+
+__device__ __forceinline__ void cp16_attn(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, uint32_t *err) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int s = blockIdx.x, kh = blockIdx.y;
+    const int hd = A.hd, rep = A.H / A.Hkv, chunk = A.chunk;
+    const int pos = *A.pos;
+    if (pos < 0 || pos >= A.max_pos) {  // every CTA reads the same position: all leave together
+        if (tid == 0 && s == 0 && kh == 0) atomicOr(err, TRX_DEV_RANGE);
+        return;
+    }
+    const int rowh = hd + 8;  // halves per staged row (16 bytes of padding: conflict-free rows)
+    __half *kt = reinterpret_cast<__half *>(smem);
+    __half *vt = kt + chunk * rowh;
+    float *qs = reinterpret_cast<float *>(vt + chunk * rowh);  // [rep][hd]
+    float *knew = qs + rep * hd;                                // [hd]
+    float *sc = knew + hd;                                      // [rep][chunk]
+    float *mrow = sc + rep * chunk;                             // [rep]
+    float *lrow = mrow + rep;                                   // [rep]
+    __shared__ int last_s;
+
+    const int t0 = s * chunk;
+    const int n = min(chunk, pos + 1 - t0);  // positions of this chunk in use (<= 0: none)
+    const int stride_t = A.Hkv * hd;         // halves between positions in the cache
+    float *part = A.part + (size_t)(kh * A.nsplit + s) * rep * (hd + 2);
+    if (n > 0) {
+        // Query heads of this group: RMSNorm + RoPE, one warp per head.
+        for (int r = warp; r < rep; r += kAttnWarps) {
+            const float *qh = A.q + (size_t)(kh * rep + r) * A.qstride;
+            float *v = qs + r * hd;
+            for (int i = lane; i < hd; i += 32) v[i] = __ldg(qh + i);
+            __syncwarp();
+            head_rmsnorm(v, hd, A.qn, A.eps, lane);
+            head_rope(v, A.rope_half, A.freq, pos, lane);
+        }
+        // The new key and value: into the cache (fp16), by the CTA whose chunk holds pos.
+        if (pos >= t0 && pos < t0 + chunk && warp == kAttnWarps - 1) {
+            const float *kg = A.k + (size_t)kh * hd;
+            for (int i = lane; i < hd; i += 32) knew[i] = __ldg(kg + i);
+            __syncwarp();
+            head_rmsnorm(knew, hd, A.kn, A.eps, lane);
+            head_rope(knew, A.rope_half, A.freq, pos, lane);
+            __half *kc = A.kc + (size_t)pos * stride_t + (size_t)kh * hd;
+            __half *vc = A.vc + (size_t)pos * stride_t + (size_t)kh * hd;
+            const float *vg = A.v + (size_t)kh * hd;
+            for (int i = lane; i < hd; i += 32) {
+                kc[i] = __float2half_rn(knew[i]);
+                vc[i] = __float2half_rn(__ldg(vg + i));
+            }
+        }
+        __syncthreads();  // queries ready; the new cache row is visible to this CTA's copies
+        // Stage K and V rows [t0, t0 + n).
+        const int pieces = hd / 8;  // 16-byte pieces per row
+        for (int i = tid; i < n * pieces; i += kAttnThreads) {
+            const int t = i / pieces, j = i - t * pieces;
+            const size_t g = (size_t)(t0 + t) * stride_t + (size_t)kh * hd + 8 * j;
+            cp16_attn(kt + t * rowh + 8 * j, A.kc + g);
+            cp16_attn(vt + t * rowh + 8 * j, A.vc + g);
+        }
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        // Scores.
+        for (int i = tid; i < rep * n; i += kAttnThreads) {
+            const int r = i / n, t = i - r * n;
+            const float *qv = qs + r * hd;
+            const uint4 *kr = reinterpret_cast<const uint4 *>(kt + t * rowh);
+            float acc = 0.f;
+            for (int j = 0; j < pieces; ++j) {
+                const uint4 w = kr[j];
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = h2_to_f2(u[e]);
+                    acc = fmaf(qv[8 * j + 2 * e], f.x, acc);
+                    acc = fmaf(qv[8 * j + 2 * e + 1], f.y, acc);
+                }
+            }
+            sc[r * chunk + t] = __fmul_rn(acc, A.scale);
+        }
+        __syncthreads();
+        // Chunk max and exp-sum per head, one warp per head.
+        for (int r = warp; r < rep; r += kAttnWarps) {
+            float m = -INFINITY;
+            for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[r * chunk + t]);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float l = 0.f;
+            for (int t = lane; t < n; t += 32) {
+                const float e = expf(__fsub_rn(sc[r * chunk + t], m));
+                sc[r * chunk + t] = e;
+                l += e;
+            }
+            for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (lane == 0) {
+                mrow[r] = m;
+                lrow[r] = l;
+            }
+        }
+        __syncthreads();
+        // Exp-weighted sum of V rows, two dims per thread.
+        const int hp = hd / 2;
+        for (int i = tid; i < rep * hp; i += kAttnThreads) {
+            const int r = i / hp, dp = i - r * hp;
+            const float *e = sc + r * chunk;
+            float ax = 0.f, ay = 0.f;
+            for (int t = 0; t < n; ++t) {
+                const float2 f = __half22float2(reinterpret_cast<const __half2 *>(vt + t * rowh)[dp]);
+                ax = fmaf(e[t], f.x, ax);
+                ay = fmaf(e[t], f.y, ay);
+            }
+            reinterpret_cast<float2 *>(part + r * (hd + 2) + 2)[dp] = make_float2(ax, ay);
+        }
+        if (tid < rep) {
+            part[tid * (hd + 2)] = mrow[tid];
+            part[tid * (hd + 2) + 1] = lrow[tid];
+        }
+    }
+    // Arrive; the last CTA of this kv head merges the active chunks.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_s = atomicAdd(A.cnt + kh, 1u) == (unsigned)(A.nsplit - 1);
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    const int ns = pos / chunk + 1;
+    const float *pk = A.part + (size_t)kh * A.nsplit * rep * (hd + 2);
+    for (int i = tid; i < rep * hd; i += kAttnThreads) {
+        const int r = i / hd, d = i - r * hd;
+        float M = -INFINITY;
+        for (int j = 0; j < ns; ++j) M = fmaxf(M, __ldcg(pk + (size_t)(j * rep + r) * (hd + 2)));
+        float L = 0.f, O = 0.f;
+        for (int j = 0; j < ns; ++j) {
+            const float *pj = pk + (size_t)(j * rep + r) * (hd + 2);
+            const float w = expf(__fsub_rn(__ldcg(pj), M));
+            L = fmaf(w, __ldcg(pj + 1), L);
+            O = fmaf(w, __ldcg(pj + 2 + d), O);
+        }
+        float o = __fmul_rn(O, __fdiv_rn(1.0f, L));
+        const int h = kh * rep + r;
+        if (A.gated) {
+            const float g = __ldg(A.q + (size_t)h * A.qstride + hd + d);
+            o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+        }
+        A.out[(size_t)h * hd + d] = o;
+    }
+    if (tid == 0) A.cnt[kh] = 0u;
+}
+
+size_t attn_smem_bytes(int hd, int rep, int chunk) {
+    return (size_t)2 * chunk * (hd + 8) * 2 + ((size_t)rep * hd + hd + (size_t)rep * chunk + 2 * rep) * 4;
+}
+
+trx_status launch_attn_decode(const AttnArgs &A, uint32_t *err, cudaStream_t st) {
+    const size_t smem = attn_smem_bytes(A.hd, A.H / A.Hkv, A.chunk);
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(configured & bit)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
+        if (e != cudaSuccess) return note_cuda(e);
+        configured |= bit;
+    }
+    attn_decode_kernel<<<dim3(A.nsplit, A.Hkv), kAttnThreads, smem, st>>>(A, err);
+    return note_cuda(cudaGetLastError());
+}
+
+}  // namespace trx

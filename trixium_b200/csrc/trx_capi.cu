@@ -15,9 +15,14 @@ struct trx_ctx {
     unsigned long long *acc;
     unsigned *cnt;
     uint64_t acc_rows;
+    // Decode-attention partials and per-kv-head arrival counts (zero between launches).
+    float *attn_part;
+    unsigned *attn_cnt;
 };
 
 static const uint64_t kAccRows = 1ull << 20;  // rows (x jobs) a split-row launch may cover
+static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
+static const uint32_t kAttnMaxKv = 1024;
 
 namespace {
 
@@ -74,12 +79,17 @@ trx_status trx_create(trx_ctx **ctx, int device) {
     c->acc_rows = kAccRows;
     if (cudaMalloc(&c->acc, kAccRows * 16) != cudaSuccess || cudaMalloc(&c->cnt, kAccRows * 4) != cudaSuccess ||
         cudaMemset(c->acc, 0, kAccRows * 16) != cudaSuccess || cudaMemset(c->cnt, 0, kAccRows * 4) != cudaSuccess ||
-        cudaMemset(c->err, 0, 256) != cudaSuccess || trx::launch_build_lut(c->lut, 0) != TRX_OK ||
+        cudaMemset(c->err, 0, 256) != cudaSuccess ||
+        cudaMalloc(&c->attn_part, kAttnPartFloats * 4) != cudaSuccess ||
+        cudaMalloc(&c->attn_cnt, kAttnMaxKv * 4) != cudaSuccess || cudaMemset(c->attn_cnt, 0, kAttnMaxKv * 4) != cudaSuccess ||
+        trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
         cudaFree(c->lut);
         cudaFree(c->acc);
         cudaFree(c->cnt);
+        cudaFree(c->attn_part);
+        cudaFree(c->attn_cnt);
         delete c;
         return TRX_ERR_CUDA;
     }
@@ -93,6 +103,8 @@ trx_status trx_destroy(trx_ctx *ctx) {
     cudaFree(ctx->lut);
     cudaFree(ctx->acc);
     cudaFree(ctx->cnt);
+    cudaFree(ctx->attn_part);
+    cudaFree(ctx->attn_cnt);
     delete ctx;
     return TRX_OK;
 }
@@ -231,6 +243,48 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
     J.njobs = njobs;
     J.out = trx::OUT_F32;
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
+                           const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                           const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                           float *d_out, cudaStream_t stream) {
+    if (!ctx || !sh) return TRX_ERR_ARG;
+    const uint32_t H = sh->n_head, Hkv = sh->n_kv, hd = sh->head_dim;
+    if (H == 0 || Hkv == 0 || H % Hkv || Hkv > kAttnMaxKv || hd == 0 || hd % 8 || hd > 512) return TRX_ERR_ARG;
+    if (sh->rope_dims % 2 || sh->rope_dims > hd || sh->max_pos == 0 || sh->max_pos > (1u << 24)) return TRX_ERR_ARG;
+    if (!(sh->eps >= 0.f)) return TRX_ERR_ARG;
+    if (!d_q || !d_k || !d_v || !d_qnorm_w || !d_knorm_w || !d_kcache || !d_vcache || !d_pos || !d_out)
+        return TRX_ERR_ARG;
+    if ((sh->rope_dims && !d_rope_freq) || !aligned16(d_kcache) || !aligned16(d_vcache)) return TRX_ERR_ARG;
+    trx::AttnArgs A{};
+    A.H = (int)H;
+    A.Hkv = (int)Hkv;
+    A.hd = (int)hd;
+    A.rope_half = (int)sh->rope_dims / 2;
+    A.gated = sh->gated ? 1 : 0;
+    A.qstride = (int)hd * (A.gated ? 2 : 1);
+    A.max_pos = (int)sh->max_pos;
+    A.chunk = sh->max_pos <= 2048 ? 64 : 128;
+    A.nsplit = (A.max_pos + A.chunk - 1) / A.chunk;
+    A.eps = sh->eps;
+    A.scale = 1.0f / sqrtf((float)hd);
+    const uint32_t rep = H / Hkv;
+    if ((uint64_t)Hkv * A.nsplit * rep * (hd + 2) > kAttnPartFloats) return TRX_ERR_UNSUPPORTED;
+    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u) return TRX_ERR_UNSUPPORTED;
+    A.q = d_q;
+    A.k = d_k;
+    A.v = d_v;
+    A.qn = d_qnorm_w;
+    A.kn = d_knorm_w;
+    A.freq = d_rope_freq;
+    A.pos = d_pos;
+    A.kc = static_cast<__half *>(d_kcache);
+    A.vc = static_cast<__half *>(d_vcache);
+    A.out = d_out;
+    A.part = ctx->attn_part;
+    A.cnt = ctx->attn_cnt;
+    return trx::launch_attn_decode(A, ctx->err, stream);
 }
 
 }  // extern "C"

@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include <cstring>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "../../include/trixium_b200.h"
@@ -58,6 +59,21 @@ __host__ __device__ inline unsigned long long argmax_key(float v, uint32_t row) 
     b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
     return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - row);
 }
+
+// One decode-attention launch (trx_attn.cu).
+struct AttnArgs {
+    const float *q, *k, *v, *qn, *kn, *freq;
+    const int *pos;
+    __half *kc, *vc;
+    float *out;
+    float *part;        // scratch partials: [Hkv][nsplit][H/Hkv][hd + 2]
+    unsigned *cnt;      // [Hkv] arrival counts, zero between launches
+    int H, Hkv, hd, rope_half, qstride, gated, max_pos, chunk, nsplit;
+    float eps, scale;
+};
+
+trx_status launch_attn_decode(const AttnArgs &A, uint32_t *err, cudaStream_t st);
+size_t attn_smem_bytes(int hd, int rep, int chunk);
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);

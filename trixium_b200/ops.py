@@ -176,9 +176,34 @@ def matvec_f_batch(ctx, w: DeviceTensor, w_stride, x, x_stride, y, y_stride, njo
     return y
 
 
+def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, out=None):
+    """One decode step of GQA attention (trx_attn_decode).  shape: _lib.AttnShape; q (H*(1+gated)*hd),
+    k/v (n_kv*hd) float32; caches [max_pos, n_kv, hd] float16; pos: int32 device tensor of one
+    element (the position written and attended up to)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (q_norm, "q_norm"), (k_norm, "k_norm")):
+        _need(t, torch.float32, n)
+    _need(kcache, torch.float16, "kcache")
+    _need(vcache, torch.float16, "vcache")
+    _need(pos, torch.int32, "pos")
+    if rope_freq is not None:
+        _need(rope_freq, torch.float32, "rope_freq")
+    if out is None:
+        out = torch.empty(shape.n_head * shape.head_dim, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().trx_attn_decode(ctx.h, ctypes.byref(shape), _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
+                                          _ptr(k_norm), _ptr(rope_freq), _ptr(kcache), _ptr(vcache), _ptr(pos),
+                                          _ptr(out), _stream()), "trx_attn_decode")
+    return out
+
+
+def attn_shape(n_head, n_kv, head_dim, max_pos, rope_dims=None, gated=False, eps=1e-6):
+    return _lib.AttnShape(n_head, n_kv, head_dim, head_dim if rope_dims is None else rope_dims, max_pos,
+                          1 if gated else 0, eps)
+
+
 def row_bytes(cols, kind):
     return int(_lib.lib().trx_row_bytes(cols, kind))
 
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
-           "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "row_bytes", "L"]
+           "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_shape",
+           "row_bytes", "L"]
