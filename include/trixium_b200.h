@@ -166,6 +166,36 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const floa
                            const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
                            float *d_out, cudaStream_t stream);
 
+/* Shape of one gated-DeltaNet layer (model/configs.py dn_* fields). */
+typedef struct trx_deltanet_shape {
+    uint32_t n_k_heads;    /* nk                                                    */
+    uint32_t k_head_dim;   /* hk: 32, 64, 128 or 256                                 */
+    uint32_t n_v_heads;    /* nv, a multiple of nk (value head h uses key head h % nk) */
+    uint32_t v_head_dim;   /* hv <= 1024                                             */
+    uint32_t conv_kernel;  /* K taps of the causal conv, 2..8                        */
+    float    eps;          /* epsilon of the L2 norms and the output RMSNorm         */
+} trx_deltanet_shape;
+
+/*
+ * One decode step of a gated-DeltaNet layer after its projections (model/mirror.py:892-943,
+ * mathematical profile), in one launch:
+ *   causal conv over the last K inputs of each of the C = 2*nk*hk + nv*hv qkv channels, SiLU;
+ *   q, k L2-normalised per key head; per value head h (key head h % nk):
+ *   M *= exp(softplus(alpha+dt_bias)*a); delta = (v - M k)*sigmoid(beta); M += delta k^T;
+ *   o = M q / sqrt(hk); out[grouped position of h] = RMSNorm(o)*norm_w*silu(z_h).
+ * d_qkv: C floats; d_z: nv*hv; d_beta, d_alpha (pre-activation), d_dt_bias, d_ssm_a: nv;
+ * d_conv_w: [C][K]; d_norm_w: hv; d_conv_ring: [K][C] floats, zero before the first step, slot
+ * pos % K receives this step's qkv; d_state: [nv][hv][hk] fp32, updated in place; d_pos: one int32
+ * on the device, the step's position (0 for the first token); d_out: nv*hv floats, value head h
+ * at (h % nk)*(nv/nk) + h/nk (mirror.py:941-942).  Uses the context's scratch: calls on one
+ * context must not overlap.
+ */
+trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *shape, const float *d_qkv, const float *d_z,
+                             const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                             const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                             float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                             cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

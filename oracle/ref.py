@@ -250,3 +250,57 @@ def attn_decode(q, k, v, kcache, vcache, pos, qn_w, kn_w, eps, freq, gate=None, 
             o = (o * sigmoid(gate[h])).astype(f32)
         out[h] = o
     return out
+
+
+# Gated DeltaNet step -----------------------------------------------------------------------------
+
+def softplus(x):
+    """model/mirror.py:714: x for x > 20, else log1p(exp(x)), in fp32."""
+    x = np.asarray(x, dtype=f32)
+    return np.where(x > 20, x, np.log1p(np.exp(x, dtype=f32), dtype=f32)).astype(f32)
+
+
+def deltanet_step(qkv, z, beta_raw, alpha, dt_bias, ssm_a, conv_w, win, S, norm_w, eps, nk, hk, nv, hv):
+    """One decode step of a gated-DeltaNet layer after its projections (model/mirror.py:892-943,
+    mathematical profile; model/golden.py:400-434).
+
+    qkv (2*nk*hk + nv*hv), z (nv*hv), beta_raw/alpha (nv) fp32: this token's projections;
+    dt_bias, ssm_a (nv); conv_w (C, K); win (K-1, C): the previous K-1 conv inputs, oldest
+    first; S (nv, hv, hk): the recurrent state.  win and S are updated in place.
+    Returns og (nv*hv): RMSNorm(o_h)*silu(z_h) per value head, in the grouped head order
+    (value head h at position (h % nk)*(nv/nk) + h // nk, mirror.py:941-942)."""
+    nq = nk * hk
+    C = 2 * nq + nv * hv
+    K = conv_w.shape[1]
+    beta = sigmoid(np.asarray(beta_raw, dtype=f32))
+    g = (softplus(np.asarray(alpha, dtype=f32) + np.asarray(dt_bias, dtype=f32)) * np.asarray(ssm_a, dtype=f32)).astype(f32)
+    conv = np.empty(C, dtype=f32)
+    for c in range(C):
+        acc = f32(0.0)
+        for i in range(K - 1):
+            acc = f32(acc + f32(conv_w[c, i] * win[i, c]))
+        conv[c] = f32(acc + f32(conv_w[c, K - 1] * qkv[c]))
+    conv = silu(conv)
+    win[:-1] = win[1:]
+    win[-1] = qkv
+    q = conv[:nq].copy()
+    k = conv[nq:2 * nq].copy()
+    v = conv[2 * nq:].copy()
+    for h in range(nk):
+        q[h * hk:(h + 1) * hk] = l2norm(q[h * hk:(h + 1) * hk], eps)
+        k[h * hk:(h + 1) * hk] = l2norm(k[h * hk:(h + 1) * hk], eps)
+    rep = nv // nk
+    scale = f32(1.0 / np.sqrt(hk))
+    og = np.zeros(nv * hv, dtype=f32)
+    for h in range(nv):
+        kh = h % nk
+        qh, kk, vh = q[kh * hk:(kh + 1) * hk], k[kh * hk:(kh + 1) * hk], v[h * hv:(h + 1) * hv]
+        decay = f32(np.exp(f32(g[h]), dtype=f32))
+        M = S[h]
+        M *= decay
+        delta = ((vh - (M @ kk).astype(f32)).astype(f32) * f32(beta[h])).astype(f32)
+        M += (delta[:, None] * kk[None, :]).astype(f32)
+        oh = ((M @ qh).astype(f32) * scale).astype(f32)
+        gpos = kh * rep + h // nk
+        og[gpos * hv:(gpos + 1) * hv] = (rmsnorm(oh, norm_w, eps) * silu(z[h * hv:(h + 1) * hv])).astype(f32)
+    return og

@@ -22,6 +22,7 @@ SYMBOLS = (
     "trx_create", "trx_destroy", "trx_get_error", "trx_last_cuda_error", "trx_row_bytes", "trx_matvec_i8",
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
     "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
+    "trx_deltanet_step",
 )
 
 
@@ -46,6 +47,12 @@ class AttnShape(ctypes.Structure):
     _fields_ = [("n_head", ctypes.c_uint32), ("n_kv", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
                 ("rope_dims", ctypes.c_uint32), ("max_pos", ctypes.c_uint32), ("gated", ctypes.c_int32),
                 ("eps", ctypes.c_float)]
+
+
+class DeltaNetShape(ctypes.Structure):
+    """trx_deltanet_shape: one gated-DeltaNet layer's geometry."""
+    _fields_ = [("n_k_heads", ctypes.c_uint32), ("k_head_dim", ctypes.c_uint32), ("n_v_heads", ctypes.c_uint32),
+                ("v_head_dim", ctypes.c_uint32), ("conv_kernel", ctypes.c_uint32), ("eps", ctypes.c_float)]
 
 
 class Entry(ctypes.Structure):
@@ -81,6 +88,7 @@ def lib():
             "trx_matvec_f_batch": ([_vp, E, _vp, ctypes.c_uint64, _vp, ctypes.c_uint64, _vp,
                                     ctypes.c_uint64, ctypes.c_int, _vp], ctypes.c_int),
             "trx_attn_decode": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
+            "trx_deltanet_step": ([_vp, ctypes.POINTER(DeltaNetShape)] + [_vp] * 13, ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

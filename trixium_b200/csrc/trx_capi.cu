@@ -287,4 +287,51 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *
     return trx::launch_attn_decode(A, ctx->err, stream);
 }
 
+trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, const float *d_qkv, const float *d_z,
+                             const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                             const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                             float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                             cudaStream_t stream) {
+    if (!ctx || !sh) return TRX_ERR_ARG;
+    const uint32_t nk = sh->n_k_heads, hk = sh->k_head_dim, nv = sh->n_v_heads, hv = sh->v_head_dim;
+    const uint32_t K = sh->conv_kernel;
+    if (nk == 0 || nv == 0 || nv % nk || nv > kAttnMaxKv) return TRX_ERR_ARG;
+    if (!(hk == 32 || hk == 64 || hk == 128 || hk == 256) || hv == 0 || hv > 1024 || K < 2 || K > 8) return TRX_ERR_ARG;
+    if (!(sh->eps >= 0.f)) return TRX_ERR_ARG;
+    if (!d_qkv || !d_z || !d_beta || !d_alpha || !d_dt_bias || !d_ssm_a || !d_conv_w || !d_norm_w || !d_conv_ring ||
+        !d_state || !d_pos || !d_out)
+        return TRX_ERR_ARG;
+    if ((uint64_t)nv * hv > kAttnPartFloats) return TRX_ERR_UNSUPPORTED;
+    trx::DnArgs A{};
+    A.nk = (int)nk;
+    A.hk = (int)hk;
+    A.nv = (int)nv;
+    A.hv = (int)hv;
+    A.K = (int)K;
+    A.C = (int)(2 * nk * hk + nv * hv);
+    // Rows per CTA: about two CTAs per SM over all heads, at least 8 rows each.
+    int nsplit = (int)((2 * 148 + nv - 1) / nv);
+    int rows = (int)((hv + nsplit - 1) / nsplit);
+    if (rows < 8) rows = 8;
+    A.rows = rows;
+    A.nsplit = (int)((hv + rows - 1) / rows);
+    A.eps = sh->eps;
+    A.scale = 1.0f / sqrtf((float)hk);
+    A.qkv = d_qkv;
+    A.z = d_z;
+    A.beta = d_beta;
+    A.alpha = d_alpha;
+    A.dt_bias = d_dt_bias;
+    A.ssm_a = d_ssm_a;
+    A.conv_w = d_conv_w;
+    A.norm_w = d_norm_w;
+    A.pos = d_pos;
+    A.win = d_conv_ring;
+    A.S = d_state;
+    A.out = d_out;
+    A.part = ctx->attn_part;
+    A.cnt = ctx->attn_cnt;
+    return trx::launch_deltanet(A, ctx->err, stream);
+}
+
 }  // extern "C"

@@ -73,6 +73,21 @@ struct AttnArgs {
 };
 
 trx_status launch_attn_decode(const AttnArgs &A, uint32_t *err, cudaStream_t st);
+
+// One gated-DeltaNet step launch (trx_deltanet.cu).
+struct DnArgs {
+    const float *qkv, *z, *beta, *alpha, *dt_bias, *ssm_a, *conv_w, *norm_w;
+    const int *pos;
+    float *win;         // conv input ring [K][C]
+    float *S;           // state [nv][hv][hk]
+    float *out;         // [nv*hv], grouped head order
+    float *part;        // scratch [nv][hv]
+    unsigned *cnt;      // [nv] arrival counts, zero between launches
+    int nk, hk, nv, hv, K, C, rows, nsplit;
+    float eps, scale;
+};
+
+trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
 size_t attn_smem_bytes(int hd, int rep, int chunk);
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);

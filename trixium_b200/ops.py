@@ -200,10 +200,29 @@ def attn_shape(n_head, n_kv, head_dim, max_pos, rope_dims=None, gated=False, eps
                           1 if gated else 0, eps)
 
 
+def deltanet_shape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel=4, eps=1e-6):
+    return _lib.DeltaNetShape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel, eps)
+
+
+def deltanet_step(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, norm_w, conv_ring, state, pos, out=None):
+    """One gated-DeltaNet decode step (trx_deltanet_step); conv_ring [K, C] and state [nv, hv, hk]
+    float32 are updated in place; pos: int32 device tensor of one element."""
+    for t, n in ((qkv, "qkv"), (z, "z"), (beta, "beta"), (alpha, "alpha"), (dt_bias, "dt_bias"), (ssm_a, "ssm_a"),
+                 (conv_w, "conv_w"), (norm_w, "norm_w"), (conv_ring, "conv_ring"), (state, "state")):
+        _need(t, torch.float32, n)
+    _need(pos, torch.int32, "pos")
+    if out is None:
+        out = torch.empty(shape.n_v_heads * shape.v_head_dim, dtype=torch.float32, device=qkv.device)
+    _lib.check(_lib.lib().trx_deltanet_step(ctx.h, ctypes.byref(shape), _ptr(qkv), _ptr(z), _ptr(beta), _ptr(alpha),
+                                            _ptr(dt_bias), _ptr(ssm_a), _ptr(conv_w), _ptr(norm_w), _ptr(conv_ring),
+                                            _ptr(state), _ptr(pos), _ptr(out), _stream()), "trx_deltanet_step")
+    return out
+
+
 def row_bytes(cols, kind):
     return int(_lib.lib().trx_row_bytes(cols, kind))
 
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
            "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_shape",
-           "row_bytes", "L"]
+           "deltanet_shape", "deltanet_step", "row_bytes", "L"]
