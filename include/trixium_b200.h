@@ -137,6 +137,16 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
                               uint64_t w_stride, const float *d_x, uint64_t x_stride,
                               float *d_y, uint64_t y_stride, int njobs, cudaStream_t stream);
 
+/*
+ * LM head + greedy token (model/mirror.py:1027-1034; doc/units.md:148-149): the float projection of
+ * trx_matvec_f (with the final RMSNorm fused when d_norm_w is set), and the index of its largest
+ * value, ties to the smallest row, written to *d_token (one int32 on the device) by the same
+ * launch.  d_logits may be NULL (the logits are then not stored).
+ */
+trx_status trx_lmhead_argmax(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                             const float *d_norm_w, float eps, float *d_logits, int32_t *d_token,
+                             cudaStream_t stream);
+
 /* Shape of one attention layer (model/configs.py head counts; mirror.py:945-996). */
 typedef struct trx_attn_shape {
     uint32_t n_head;     /* query heads H                                              */

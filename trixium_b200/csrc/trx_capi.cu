@@ -18,11 +18,15 @@ struct trx_ctx {
     // Decode-attention partials and per-kv-head arrival counts (zero between launches).
     float *attn_part;
     unsigned *attn_cnt;
+    // Greedy-argmax keys (one per job) and the matvec's arrival count (zero between launches).
+    unsigned long long *amax_key;
+    unsigned *amax_cnt;
 };
 
 static const uint64_t kAccRows = 1ull << 20;  // rows (x jobs) a split-row launch may cover
 static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
 static const uint32_t kAttnMaxKv = 1024;
+static const int kMaxArgmaxJobs = 64;
 
 namespace {
 
@@ -82,6 +86,9 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaMemset(c->err, 0, 256) != cudaSuccess ||
         cudaMalloc(&c->attn_part, kAttnPartFloats * 4) != cudaSuccess ||
         cudaMalloc(&c->attn_cnt, kAttnMaxKv * 4) != cudaSuccess || cudaMemset(c->attn_cnt, 0, kAttnMaxKv * 4) != cudaSuccess ||
+        cudaMalloc(&c->amax_key, kMaxArgmaxJobs * 8) != cudaSuccess ||
+        cudaMemset(c->amax_key, 0, kMaxArgmaxJobs * 8) != cudaSuccess ||
+        cudaMalloc(&c->amax_cnt, 16) != cudaSuccess || cudaMemset(c->amax_cnt, 0, 16) != cudaSuccess ||
         trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
@@ -90,6 +97,8 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaFree(c->cnt);
         cudaFree(c->attn_part);
         cudaFree(c->attn_cnt);
+        cudaFree(c->amax_key);
+        cudaFree(c->amax_cnt);
         delete c;
         return TRX_ERR_CUDA;
     }
@@ -105,6 +114,8 @@ trx_status trx_destroy(trx_ctx *ctx) {
     cudaFree(ctx->cnt);
     cudaFree(ctx->attn_part);
     cudaFree(ctx->attn_cnt);
+    cudaFree(ctx->amax_key);
+    cudaFree(ctx->amax_cnt);
     delete ctx;
     return TRX_OK;
 }
@@ -242,6 +253,25 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
     J.y_stride = y_stride;
     J.njobs = njobs;
     J.out = trx::OUT_F32;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_lmhead_argmax(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                             const float *d_norm_w, float eps, float *d_logits, int32_t *d_token,
+                             cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_token || !aligned16(d_packed)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
+    J.x = d_x;
+    J.norm_w = d_norm_w;
+    J.eps = eps;
+    J.seg[0].y = d_logits;
+    J.out = trx::OUT_F32;
+    J.argmax = ctx->amax_key;
+    J.token = d_token;
+    J.arg_cnt = ctx->amax_cnt;
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
 

@@ -42,6 +42,8 @@ struct MvJobs {
     int nseg;
     MvSeg seg[kMaxSegs];
     unsigned long long *argmax;  // if set: greedy argmax key of the float results (see below)
+    int *token;                  // if set (with argmax): per job, the argmax row; the keys and
+    unsigned *arg_cnt;           // the arrival count arg_cnt are left at zero again
     const int *skip;             // if set and *skip != 0, the launch does nothing
     // Rows split over slabs (K > 4096) are summed in a zeroed global accumulator: acc[2*i] (and
     // acc[2*i+1] for SwiGLU's up row) and an arrival count cnt[i], i = job*rows + row.  The last

@@ -669,6 +669,22 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
         __syncwarp();
         if (J.argmax) argmax_commit(J, job, best, lane);
     }
+    if (J.token) {  // greedy tokens: the last CTA to arrive turns each job's key into its row
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            amax_s[1] = atomicAdd(J.arg_cnt, 1u) == gridDim.x - 1 ? 1u : 0u;
+        }
+        __syncthreads();
+        if (amax_s[1]) {
+            __threadfence();
+            for (int j = tid; j < J.njobs; j += blockDim.x) {
+                const unsigned long long k = atomicExch(J.argmax + j, 0ull);
+                J.token[j] = k ? (int)(0xffffffffu - (uint32_t)k) : -1;
+            }
+            if (tid == 0) *J.arg_cnt = 0u;
+        }
+    }
 }
 
 // fp-mode kernel (model/fastref.py:103-125): thread per (row, group); x fp32 in shared memory;

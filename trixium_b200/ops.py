@@ -200,6 +200,23 @@ def attn_shape(n_head, n_kv, head_dim, max_pos, rope_dims=None, gated=False, eps
                           1 if gated else 0, eps)
 
 
+def lmhead_argmax(ctx, w: DeviceTensor, x, token=None, logits=None, norm_w=None, eps=1e-6):
+    """Greedy token of the LM head (trx_lmhead_argmax): token (int32 device tensor of one
+    element) = argmax over rows of the float projection of (optionally RMS-normalised) x."""
+    _need(x, torch.float32, "x")
+    if token is None:
+        token = torch.empty(1, dtype=torch.int32, device=x.device)
+    _need(token, torch.int32, "token")
+    if logits is not None:
+        _need(logits, torch.float32, "logits")
+    if norm_w is not None:
+        _need(norm_w, torch.float32, "norm_w")
+    _lib.check(_lib.lib().trx_lmhead_argmax(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(norm_w),
+                                            ctypes.c_float(eps), _ptr(logits), _ptr(token), _stream()),
+               "trx_lmhead_argmax")
+    return token
+
+
 def deltanet_shape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel=4, eps=1e-6):
     return _lib.DeltaNetShape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel, eps)
 
@@ -225,4 +242,4 @@ def row_bytes(cols, kind):
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
            "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_shape",
-           "deltanet_shape", "deltanet_step", "row_bytes", "L"]
+           "deltanet_shape", "deltanet_step", "lmhead_argmax", "row_bytes", "L"]
