@@ -138,6 +138,27 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
                               float *d_y, uint64_t y_stride, int njobs, cudaStream_t stream);
 
 /*
+ * Several tensors on one input in one launch (q/k/v of an attention layer, qkv/z/beta/alpha of a
+ * DeltaNet layer): nseg <= 4 entries with the same cols and kind, their row packets back to back
+ * in d_packed (segment i after the rows of segments 0..i-1).  Each segment is trx_matvec_f of its
+ * entry on the same (optionally RMS-normalised) x (mirror.py proj(): every projection quantises the
+ * same input, so the quantisation is shared exactly); d_y[i] (device pointers, given in a host
+ * array) receives segment i's rows; d_resid, if not NULL, is a host array of nseg device pointers
+ * or NULLs added to the results.
+ */
+trx_status trx_matvec_f_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
+                              const float *d_x, const float *d_norm_w, float eps, float *const *d_y,
+                              const float *const *d_resid, cudaStream_t stream);
+
+/* x = table[*d_token] as fp32 (table [vocab][dim], fp16 when f16 != 0, else fp32); a token
+ * outside [0, vocab) sets TRX_DEV_RANGE and writes zeros (model/mirror.py:1003 embed_row). */
+trx_status trx_embed_lookup(trx_ctx *ctx, const void *d_table, uint32_t vocab, uint32_t dim, int32_t f16,
+                            const int32_t *d_token, float *d_x, cudaStream_t stream);
+
+/* *d_pos += n on the device (the decode loop's position, read by the attention and DeltaNet steps). */
+trx_status trx_advance_position(trx_ctx *ctx, int32_t *d_pos, int32_t n, cudaStream_t stream);
+
+/*
  * LM head + greedy token (model/mirror.py:1027-1034; doc/units.md:148-149): the float projection of
  * trx_matvec_f (with the final RMSNorm fused when d_norm_w is set), and the index of its largest
  * value, ties to the smallest row, written to *d_token (one int32 on the device) by the same

@@ -22,7 +22,7 @@ SYMBOLS = (
     "trx_create", "trx_destroy", "trx_get_error", "trx_last_cuda_error", "trx_row_bytes", "trx_matvec_i8",
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
     "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
-    "trx_deltanet_step", "trx_lmhead_argmax",
+    "trx_deltanet_step", "trx_lmhead_argmax", "trx_matvec_f_multi", "trx_embed_lookup", "trx_advance_position",
 )
 
 
@@ -90,6 +90,11 @@ def lib():
             "trx_attn_decode": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
             "trx_deltanet_step": ([_vp, ctypes.POINTER(DeltaNetShape)] + [_vp] * 13, ctypes.c_int),
             "trx_lmhead_argmax": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f_multi": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp],
+                                   ctypes.c_int),
+            "trx_embed_lookup": ([_vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32, _vp, _vp, _vp],
+                                 ctypes.c_int),
+            "trx_advance_position": ([_vp, _vp, ctypes.c_int32, _vp], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

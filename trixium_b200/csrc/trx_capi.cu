@@ -256,6 +256,50 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
 
+trx_status trx_matvec_f_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
+                              const float *d_x, const float *d_norm_w, float eps, float *const *d_y,
+                              const float *const *d_resid, cudaStream_t stream) {
+    if (!ctx || !entries || nseg < 1 || nseg > trx::kMaxSegs || !d_y) return TRX_ERR_ARG;
+    uint64_t rows = 0;
+    for (int i = 0; i < nseg; ++i) {
+        trx_status s = check_entry(&entries[i]);
+        if (s) return s;
+        if (entries[i].cols != entries[0].cols || entries[i].kind != entries[0].kind || !d_y[i]) return TRX_ERR_ARG;
+        rows += entries[i].rows;
+    }
+    if (rows > (1u << 30)) return TRX_ERR_UNSUPPORTED;
+    if (!d_packed || !d_x || !aligned16(d_packed)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(ctx, &entries[0], d_packed);
+    J.rows = (int)rows;
+    J.nseg = nseg;
+    int end = 0;
+    for (int i = 0; i < nseg; ++i) {
+        end += (int)entries[i].rows;
+        J.seg[i].row_end = end;
+        J.seg[i].B = entries[i].bias;
+        J.seg[i].R = entries[i].rshift;
+        J.seg[i].y = d_y[i];
+        J.seg[i].resid = d_resid ? d_resid[i] : nullptr;
+    }
+    J.x = d_x;
+    J.norm_w = d_norm_w;
+    J.eps = eps;
+    J.out = trx::OUT_F32;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_embed_lookup(trx_ctx *ctx, const void *d_table, uint32_t vocab, uint32_t dim, int32_t f16,
+                            const int32_t *d_token, float *d_x, cudaStream_t stream) {
+    if (!ctx || !d_table || !d_token || !d_x || vocab == 0 || dim == 0 || vocab > (1u << 30) || dim > (1u << 20))
+        return TRX_ERR_ARG;
+    return trx::launch_embed(d_table, (int)vocab, (int)dim, f16 ? 1 : 0, d_token, d_x, ctx->err, stream);
+}
+
+trx_status trx_advance_position(trx_ctx *ctx, int32_t *d_pos, int32_t n, cudaStream_t stream) {
+    if (!ctx || !d_pos) return TRX_ERR_ARG;
+    return trx::launch_advance(d_pos, n, stream);
+}
+
 trx_status trx_lmhead_argmax(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
                              const float *d_norm_w, float eps, float *d_logits, int32_t *d_token,
                              cudaStream_t stream) {

@@ -92,6 +92,10 @@ struct DnArgs {
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
 size_t attn_smem_bytes(int hd, int rep, int chunk);
 
+trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
+                        cudaStream_t st);
+trx_status launch_advance(int *pos, int n, cudaStream_t st);
+
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);
 trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStream_t st);

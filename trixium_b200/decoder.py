@@ -1,0 +1,340 @@
+"""Batch-1 greedy decoding of the TriXium model families on the B200.
+
+The token step follows model/mirror.py:1002-1034 (`forward`):
+
+    x = embed(token)
+    per layer: hn = RMSNorm(x);  y = DeltaNet(hn) or Attention(hn);  x += y
+               hn = RMSNorm(x);  x += down(silu(gate(hn)) * up(hn))
+    token = argmax(lm_head(RMSNorm(x)))
+
+Every operation is a kernel of libtrixium_b200.so:
+- projections sharing an input run as one segmented launch with the RMSNorm fused in front;
+- residual adds are fused into the projection that produces y;
+- gate/up run as one SwiGLU launch;
+- the greedy token is written on the device by the LM-head launch;
+- the position advances on the device.
+
+One step is captured as a CUDA graph and replayed per token, and the token feeds back through
+device memory, so decoding makes no host round trip.
+
+Weights are synthetic and random-init. Every matrix is group-128 ternary in the converter's row
+packets, drawn from the config-0 distribution (P(w=0)=0.4, fp16 scales |N(0,1)|*0.02). DeltaNet's
+conv taps, A and dt bias follow model/tinygen.py:107-113.
+"""
+
+from dataclasses import dataclass
+import math
+
+import numpy as np
+import torch
+
+from . import _lib, ops
+from . import layout as L
+from .image import pack_rows_torch, synthetic_codes_scales_torch
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    name: str
+    n_layer: int
+    hidden: int
+    n_head: int
+    n_kv: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    kind: int = L.KIND_TERNARY5
+    rope_theta: float = 1e6
+    rope_dims: int = 0            # rotated dims per head (0: all)
+    attn_gated: bool = False      # q projection also emits a per-head output gate (Qwen3.5)
+    pattern: str = ""             # per layer 'd' (gated DeltaNet) or 'a' (attention); "" = all 'a'
+    dn_nk: int = 0
+    dn_hk: int = 0
+    dn_nv: int = 0
+    dn_hv: int = 0
+    dn_conv: int = 4
+    eps: float = 1e-6
+
+    def layer_type(self, l):
+        return self.pattern[l] if self.pattern else "a"
+
+    @property
+    def q_rows(self):
+        return self.n_head * self.head_dim * (2 if self.attn_gated else 1)
+
+    @property
+    def kv_rows(self):
+        return self.n_kv * self.head_dim
+
+    @property
+    def dn_channels(self):
+        return 2 * self.dn_nk * self.dn_hk + self.dn_nv * self.dn_hv
+
+    def weight_bytes_per_token(self):
+        """Bytes of ternary weights + scales streamed per token (row packets, padding included)."""
+        rb = lambda cols: L.row_bytes(cols, self.kind)
+        E, total = self.hidden, 0
+        for l in range(self.n_layer):
+            if self.layer_type(l) == "d":
+                total += (self.dn_channels + 2 * self.dn_nv + self.dn_nv * self.dn_hv) * rb(E)
+                total += E * rb(self.dn_nv * self.dn_hv)
+            else:
+                total += (self.q_rows + 2 * self.kv_rows) * rb(E) + E * rb(self.n_head * self.head_dim)
+            total += 2 * self.ffn * rb(E) + E * rb(self.ffn)
+        return total + self.vocab * rb(E)
+
+
+def _hybrid_pattern(n_layer):
+    return "".join("a" if (l % 4) == 3 else "d" for l in range(n_layer))
+
+
+CONFIGS = {
+    # Qwen3-1.7B shape, trit5.
+    "qwen3-1.7b": DecoderConfig("qwen3-1.7b", 28, 2048, 16, 8, 128, 6144, 151936, L.KIND_TERNARY5),
+    # Qwen3-8B shape, 2-bit image.
+    "qwen3-8b": DecoderConfig("qwen3-8b", 36, 4096, 32, 8, 128, 12288, 151936, L.KIND_TERNARY),
+    # Qwen3.5-style hybrid 2B: 3 DeltaNet : 1 attention, trit5.
+    "hybrid-2b": DecoderConfig("hybrid-2b", 24, 2048, 16, 4, 256, 6144, 151936, L.KIND_TERNARY5,
+                               rope_theta=1e7, rope_dims=64, attn_gated=True, pattern=_hybrid_pattern(24),
+                               dn_nk=16, dn_hk=128, dn_nv=16, dn_hv=128, dn_conv=4),
+    # Qwen3.5-style hybrid 27B, 2-bit image.
+    "hybrid-27b": DecoderConfig("hybrid-27b", 64, 5120, 24, 4, 256, 17408, 151936, L.KIND_TERNARY,
+                                rope_theta=1e7, rope_dims=64, attn_gated=True, pattern=_hybrid_pattern(64),
+                                dn_nk=16, dn_hk=128, dn_nv=48, dn_hv=128, dn_conv=4),
+    # Small shapes for parity tests against the oracle model.
+    "tiny": DecoderConfig("tiny", 2, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY5),
+    "tiny-hybrid": DecoderConfig("tiny-hybrid", 4, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY, rope_dims=32,
+                                 attn_gated=True, pattern="dda" + "a", dn_nk=2, dn_hk=64, dn_nv=4, dn_hv=64,
+                                 dn_conv=4),
+}
+
+
+# Weights --------------------------------------------------------------------------------------------
+
+def _fp16_parts_torch(scales):
+    b = scales.contiguous().view(torch.int16).to(torch.int32) & 0xFFFF
+    E = (b >> 10) & 31
+    mant = b & 0x3FF
+    m11 = torch.where(E == 0, mant, mant | 0x400)
+    e16 = torch.where(E == 0, torch.full_like(E, -24), E - 25)
+    return m11, e16
+
+
+def _bias_rshift(scales_list, gs_max=128 * 127, target_top=12):
+    """model/bitexact.py:77-97 (choose_scale_bias / choose_result_shift) over device scales."""
+    B = target_top - max(int(_fp16_parts_torch(s)[1].max()) for s in scales_list)
+    bound = 0.0
+    for s in scales_list:
+        m11, e16 = _fp16_parts_torch(s)
+        per = torch.ceil(m11.double() * gs_max * torch.exp2((e16 + B).double()))
+        bound = max(bound, float(per.sum(dim=-1).max()))
+    R = 0
+    while bound / float(1 << R) >= 2.0 ** 31:
+        R += 1
+    return B, R
+
+
+class Packed:
+    """Tensors sharing one input, their row packets back to back (one segmented launch)."""
+
+    def __init__(self, gen, segments, cols, kind, device, chunk_rows=16384):
+        self.names = [n for n, _ in segments]
+        self.rows = [r for _, r in segments]
+        self.cols, self.kind = cols, kind
+        rb = L.row_bytes(cols, kind)
+        self.data = torch.empty(sum(self.rows) * rb, dtype=torch.uint8, device=device)
+        self.entries, off = [], 0
+        for _, rows in segments:
+            scales = []
+            for r0 in range(0, rows, chunk_rows):
+                n = min(chunk_rows, rows - r0)
+                codes, sc = synthetic_codes_scales_torch(gen, n, cols, device)
+                self.data[(off + r0) * rb:(off + r0 + n) * rb] = pack_rows_torch(sc, codes, kind)
+                scales.append(sc)
+            B, R = _bias_rshift(scales)
+            self.entries.append(_lib.Entry(rows, cols, kind, B, R))
+            off += rows
+
+    def tensor(self, i):
+        """Segment i as a DeviceTensor (a view of the shared allocation)."""
+        rb = L.row_bytes(self.cols, self.kind)
+        off = sum(self.rows[:i]) * rb
+        e = self.entries[i]
+        return ops.DeviceTensor.from_packed(self.data[off:off + self.rows[i] * rb], e.rows, e.cols, e.kind,
+                                            e.bias, e.rshift)
+
+
+class SyntheticWeights:
+    """Random-init weights of a DecoderConfig, resident on the device."""
+
+    def __init__(self, cfg: DecoderConfig, seed=0, device="cuda"):
+        self.cfg = cfg
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        rng = np.random.default_rng(seed)
+        E, kind = cfg.hidden, cfg.kind
+        norm = lambda n: torch.from_numpy((1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)).to(dev)
+        self.emb = (torch.randn(cfg.vocab, E, generator=gen, device=dev)).to(torch.float16)
+        self.layers = []
+        for l in range(cfg.n_layer):
+            w = {"attn_norm": norm(E), "ffn_norm": norm(E)}
+            if cfg.layer_type(l) == "d":
+                nv, hv, C = cfg.dn_nv, cfg.dn_hv, cfg.dn_channels
+                w["in"] = Packed(gen, [("qkv", C), ("z", nv * hv), ("beta", nv), ("alpha", nv)], E, kind, dev)
+                w["out"] = Packed(gen, [("ssm_out", E)], nv * hv, kind, dev).tensor(0)
+                f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+                w["conv_w"] = f32(rng.uniform(-0.5, 0.5, (C, cfg.dn_conv)))
+                w["ssm_a"] = f32(-np.exp(rng.uniform(-1.5, 0.5, nv)))
+                w["dt_bias"] = f32(rng.uniform(-2.0, 0.5, nv))
+                w["ssm_norm"] = norm(hv)
+            else:
+                w["in"] = Packed(gen, [("q", cfg.q_rows), ("k", cfg.kv_rows), ("v", cfg.kv_rows)], E, kind, dev)
+                w["out"] = Packed(gen, [("o", E)], cfg.n_head * cfg.head_dim, kind, dev).tensor(0)
+                w["q_norm"] = norm(cfg.head_dim)
+                w["k_norm"] = norm(cfg.head_dim)
+            ffn = Packed(gen, [("gate", cfg.ffn), ("up", cfg.ffn)], E, kind, dev)
+            w["gate"], w["up"] = ffn.tensor(0), ffn.tensor(1)
+            w["ffn_packed"] = ffn
+            w["down"] = Packed(gen, [("down", E)], cfg.ffn, kind, dev).tensor(0)
+            self.layers.append(w)
+        self.out_norm = norm(E)
+        self.lm_head = Packed(gen, [("lm_head", cfg.vocab)], E, kind, dev).tensor(0)
+        rope_n = cfg.rope_dims or cfg.head_dim
+        self.rope_freq = torch.from_numpy(np.array(
+            [np.float32(np.float32(cfg.rope_theta) ** np.float32(-2.0 * i / rope_n)) for i in range(rope_n // 2)],
+            dtype=np.float32)).to(dev)
+
+
+# The decoder ------------------------------------------------------------------------------------------
+
+class Decoder:
+    """Greedy batch-1 decoding over SyntheticWeights (or any weights of the same layout)."""
+
+    def __init__(self, weights: SyntheticWeights, ctx=None, max_pos=4096):
+        cfg = self.cfg = weights.cfg
+        self.w = weights
+        self.ctx = ctx or ops.default_context()
+        dev = weights.emb.device
+        f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)
+        E = cfg.hidden
+        self.max_pos = max_pos
+        self.x = f32(E)
+        self.q, self.k, self.v = f32(cfg.q_rows), f32(cfg.kv_rows), f32(cfg.kv_rows)
+        self.attn = f32(cfg.n_head * cfg.head_dim)
+        self.act = f32(cfg.ffn)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.attn_shape = ops.attn_shape(cfg.n_head, cfg.n_kv, cfg.head_dim, max_pos,
+                                         rope_dims=cfg.rope_dims or cfg.head_dim, gated=cfg.attn_gated, eps=cfg.eps)
+        self.kc, self.vc, self.ring, self.state = {}, {}, {}, {}
+        for l in range(cfg.n_layer):
+            if cfg.layer_type(l) == "d":
+                self.ring[l] = f32(cfg.dn_conv * cfg.dn_channels).view(cfg.dn_conv, cfg.dn_channels)
+                self.state[l] = f32(cfg.dn_nv * cfg.dn_hv * cfg.dn_hk).view(cfg.dn_nv, cfg.dn_hv, cfg.dn_hk)
+            else:
+                self.kc[l] = torch.zeros(max_pos, cfg.n_kv, cfg.head_dim, dtype=torch.float16, device=dev)
+                self.vc[l] = torch.zeros_like(self.kc[l])
+        if any(cfg.layer_type(l) == "d" for l in range(cfg.n_layer)):
+            self.dn_shape = ops.deltanet_shape(cfg.dn_nk, cfg.dn_hk, cfg.dn_nv, cfg.dn_hv, cfg.dn_conv, cfg.eps)
+            self.qkv, self.z = f32(cfg.dn_channels), f32(cfg.dn_nv * cfg.dn_hv)
+            self.beta, self.alpha = f32(cfg.dn_nv), f32(cfg.dn_nv)
+            self.og = f32(cfg.dn_nv * cfg.dn_hv)
+        self.graph = None
+
+    def _mutable(self):
+        return [self.tok, self.pos] + list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + \
+            list(self.state.values())
+
+    def reset(self):
+        """Empty caches and states, position 0."""
+        self.pos.zero_()
+        for t in list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + list(self.state.values()):
+            t.zero_()
+
+    def set_states(self, seed=0):
+        """Random DeltaNet states ~N(0,1)/sqrt(hk) (BASELINE's recurrent init)."""
+        g = torch.Generator(device=self.tok.device)
+        g.manual_seed(seed)
+        for t in self.state.values():
+            t.copy_(torch.randn(t.shape, generator=g, device=t.device) / math.sqrt(self.cfg.dn_hk))
+
+    def fill_context(self, n, seed=0):
+        """Synthetic context of n positions: random fp16 K/V rows in every attention cache (of the
+        scale the step's normalised keys have) and the position set to n."""
+        g = torch.Generator(device=self.tok.device)
+        g.manual_seed(seed)
+        for l in self.kc:
+            self.kc[l][:n] = torch.randn(self.kc[l][:n].shape, generator=g, device=self.tok.device).half()
+            self.vc[l][:n] = torch.randn(self.vc[l][:n].shape, generator=g, device=self.tok.device).half()
+        self.pos.fill_(n)
+
+    def enqueue_step(self):
+        """One token's kernels on the current stream: reads self.tok and self.pos, writes the next
+        token into self.tok and advances self.pos."""
+        cfg, w, ctx = self.cfg, self.w, self.ctx
+        ops.embed_lookup(ctx, w.emb, self.tok, self.x)
+        for l, lw in enumerate(w.layers):
+            p = lw["in"]
+            if cfg.layer_type(l) == "d":
+                ops.matvec_f_multi(ctx, p.entries, p.data, self.x, [self.qkv, self.z, self.beta, self.alpha],
+                                   norm_w=lw["attn_norm"], eps=cfg.eps)
+                ops.deltanet_step(ctx, self.dn_shape, self.qkv, self.z, self.beta, self.alpha, lw["dt_bias"],
+                                  lw["ssm_a"], lw["conv_w"], lw["ssm_norm"], self.ring[l], self.state[l], self.pos,
+                                  self.og)
+                ops.matvec_f(ctx, lw["out"], self.og, y=self.x, resid=self.x)
+            else:
+                ops.matvec_f_multi(ctx, p.entries, p.data, self.x, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
+                                   eps=cfg.eps)
+                ops.attn_decode(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"], w.rope_freq,
+                                self.kc[l], self.vc[l], self.pos, self.attn)
+                ops.matvec_f(ctx, lw["out"], self.attn, y=self.x, resid=self.x)
+            ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x, act=self.act, norm_w=lw["ffn_norm"], eps=cfg.eps)
+            ops.matvec_f(ctx, lw["down"], self.act, y=self.x, resid=self.x)
+        ops.lmhead_argmax(ctx, w.lm_head, self.x, token=self.tok, norm_w=w.out_norm, eps=cfg.eps)
+        ops.advance_position(ctx, self.pos)
+
+    def launches_per_step(self):
+        n_attn = sum(1 for l in range(self.cfg.n_layer) if self.cfg.layer_type(l) == "a")
+        n_dn = self.cfg.n_layer - n_attn
+        return 1 + 5 * (n_attn + n_dn) + 2
+
+    def capture(self):
+        """Capture one step as a CUDA graph (the kernels read the position on the device)."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        live = self._mutable()
+        saved = [t.clone() for t in live]
+        with torch.cuda.stream(s):
+            self.enqueue_step()          # warm-up outside the capture, then every buffer restored
+            torch.cuda.synchronize()
+        for t, c in zip(live, saved):
+            t.copy_(c)
+        del saved
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(self.graph, stream=s):
+                self.enqueue_step()
+        torch.cuda.synchronize()
+        return self.graph
+
+    def step(self, token=None):
+        """One token: feed `token` (teacher forcing) or the previous step's greedy token."""
+        if token is not None:
+            self.tok.fill_(int(token))
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.enqueue_step()
+
+    def generate(self, prompt, n_new):
+        """Greedy decode: the prompt, then n_new tokens (mirror.py:1036-1042).  Returns the new ids."""
+        for t in prompt:
+            self.step(t)
+        out = torch.empty(n_new, dtype=torch.int32, device=self.tok.device)
+        for i in range(n_new):
+            out[i:i + 1].copy_(self.tok)
+            if i + 1 < n_new:  # no unused step after the final output (mirror.py:1042)
+                self.step()
+        self.ctx.raise_on_error()
+        return out.cpu().tolist()

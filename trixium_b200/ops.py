@@ -200,6 +200,37 @@ def attn_shape(n_head, n_kv, head_dim, max_pos, rope_dims=None, gated=False, eps
                           1 if gated else 0, eps)
 
 
+def matvec_f_multi(ctx, entries, packed, x, ys, norm_w=None, eps=1e-6, resids=None):
+    """Segments sharing one input (trx_matvec_f_multi): entries (list of _lib.Entry), packed (their row
+    packets back to back, uint8 CUDA tensor), ys (one float32 output per segment)."""
+    n = len(entries)
+    _need(x, torch.float32, "x")
+    arr = (_lib.Entry * n)(*entries)
+    yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    rp = None
+    if resids is not None:
+        rp = (ctypes.c_void_p * n)(*[(r.data_ptr() if r is not None else None) for r in resids])
+    _lib.check(_lib.lib().trx_matvec_f_multi(ctx.h, arr, n, _ptr(packed), _ptr(x), _ptr(norm_w), ctypes.c_float(eps),
+                                             yp, rp, _stream()), "trx_matvec_f_multi")
+    return ys
+
+
+def embed_lookup(ctx, table, token, x):
+    """x = table[token] (float16 or float32 table [vocab, dim]; token: int32 device tensor)."""
+    _need(token, torch.int32, "token")
+    _need(x, torch.float32, "x")
+    f16 = table.dtype == torch.float16
+    _need(table, torch.float16 if f16 else torch.float32, "table")
+    _lib.check(_lib.lib().trx_embed_lookup(ctx.h, _ptr(table), table.shape[0], table.shape[1], 1 if f16 else 0,
+                                           _ptr(token), _ptr(x), _stream()), "trx_embed_lookup")
+    return x
+
+
+def advance_position(ctx, pos, n=1):
+    _need(pos, torch.int32, "pos")
+    _lib.check(_lib.lib().trx_advance_position(ctx.h, _ptr(pos), n, _stream()), "trx_advance_position")
+
+
 def lmhead_argmax(ctx, w: DeviceTensor, x, token=None, logits=None, norm_w=None, eps=1e-6):
     """Greedy token of the LM head (trx_lmhead_argmax): token (int32 device tensor of one
     element) = argmax over rows of the float projection of (optionally RMS-normalised) x."""
@@ -242,4 +273,5 @@ def row_bytes(cols, kind):
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
            "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_shape",
-           "deltanet_shape", "deltanet_step", "lmhead_argmax", "row_bytes", "L"]
+           "deltanet_shape", "deltanet_step", "lmhead_argmax", "matvec_f_multi", "embed_lookup",
+           "advance_position", "row_bytes", "L"]
