@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x, kh = blockIdx.y;
     const int hd = A.hd, rep = A.H / A.Hkv, chunk = A.chunk;
+    pdl_trigger();
+    pdl_wait();
     const int pos = *A.pos;
     if (pos < 0 || pos >= A.max_pos) {  // every CTA reads the same position: all leave together
         if (tid == 0 && s == 0 && kh == 0) atomicOr(err, TRX_DEV_RANGE);
@@ -192,18 +194,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
     __threadfence();
     const int ns = pos / chunk + 1;
     const float *pk = A.part + (size_t)kh * A.nsplit * rep * (hd + 2);
+    // Chunk weights per head: w_j = e^(m_j - M) / sum_j e^(m_j - M) l_j, staged in shared memory
+    // (reusing the score area: rep * chunk >= rep * ns floats... ns may exceed chunk, so use kt).
+    float *wts = reinterpret_cast<float *>(smem);  // [rep][ns], the K tile is no longer needed
+    for (int i = tid; i < rep * ns; i += kAttnThreads) {
+        const int r = i / ns, j = i - r * ns;
+        wts[i] = __ldcg(pk + (size_t)(j * rep + r) * (hd + 2));
+    }
+    __syncthreads();
+    for (int r = warp; r < rep; r += kAttnWarps) {
+        float M = -INFINITY;
+        for (int j = lane; j < ns; j += 32) M = fmaxf(M, wts[r * ns + j]);
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.f;
+        for (int j = lane; j < ns; j += 32) {
+            const float w = expf(__fsub_rn(wts[r * ns + j], M));
+            wts[r * ns + j] = w;
+            L = fmaf(w, __ldcg(pk + (size_t)(j * rep + r) * (hd + 2) + 1), L);
+        }
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = __fdiv_rn(1.0f, L);  // one reciprocal per head
+        __syncwarp();
+        for (int j = lane; j < ns; j += 32) wts[r * ns + j] = __fmul_rn(wts[r * ns + j], inv);
+    }
+    __syncthreads();
     for (int i = tid; i < rep * hd; i += kAttnThreads) {
         const int r = i / hd, d = i - r * hd;
-        float M = -INFINITY;
-        for (int j = 0; j < ns; ++j) M = fmaxf(M, __ldcg(pk + (size_t)(j * rep + r) * (hd + 2)));
-        float L = 0.f, O = 0.f;
-        for (int j = 0; j < ns; ++j) {
-            const float *pj = pk + (size_t)(j * rep + r) * (hd + 2);
-            const float w = expf(__fsub_rn(__ldcg(pj), M));
-            L = fmaf(w, __ldcg(pj + 1), L);
-            O = fmaf(w, __ldcg(pj + 2 + d), O);
+        const float *w = wts + r * ns;
+        const float *pd = pk + (size_t)r * (hd + 2) + 2 + d;
+        const size_t step = (size_t)rep * (hd + 2);
+        float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+        int j = 0;
+        for (; j + 4 <= ns; j += 4) {  // four independent L2 loads in flight
+            const float a0 = __ldcg(pd + j * step), a1 = __ldcg(pd + (j + 1) * step);
+            const float a2 = __ldcg(pd + (j + 2) * step), a3 = __ldcg(pd + (j + 3) * step);
+            O0 = fmaf(w[j], a0, O0);
+            O1 = fmaf(w[j + 1], a1, O1);
+            O2 = fmaf(w[j + 2], a2, O2);
+            O3 = fmaf(w[j + 3], a3, O3);
         }
-        float o = __fmul_rn(O, __fdiv_rn(1.0f, L));
+        for (; j < ns; ++j) O0 = fmaf(w[j], __ldcg(pd + j * step), O0);
+        float o = (O0 + O1) + (O2 + O3);
         const int h = kh * rep + r;
         if (A.gated) {
             const float g = __ldg(A.q + (size_t)h * A.qstride + hd + d);
@@ -230,8 +261,7 @@ trx_status launch_attn_decode(const AttnArgs &A, uint32_t *err, cudaStream_t st)
         if (e != cudaSuccess) return note_cuda(e);
         configured |= bit;
     }
-    attn_decode_kernel<<<dim3(A.nsplit, A.Hkv), kAttnThreads, smem, st>>>(A, err);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(attn_decode_kernel, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
 }
 
 }  // namespace trx

@@ -11,10 +11,6 @@ struct trx_ctx {
     int device;
     uint32_t *err;    // device error word
     uint32_t *lut;    // replicated trit5 byte LUT (64 KiB), copied into each CTA's shared memory
-    // Split-row accumulator of matvecs with K > 4096 (zero between launches).
-    unsigned long long *acc;
-    unsigned *cnt;
-    uint64_t acc_rows;
     // Decode-attention partials and per-kv-head arrival counts (zero between launches).
     float *attn_part;
     unsigned *attn_cnt;
@@ -23,10 +19,16 @@ struct trx_ctx {
     unsigned *amax_cnt;
 };
 
-static const uint64_t kAccRows = 1ull << 20;  // rows (x jobs) a split-row launch may cover
 static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
 static const uint32_t kAttnMaxKv = 1024;
 static const int kMaxArgmaxJobs = 64;
+
+namespace trx {
+bool pdl_enabled() {
+    static const bool on = std::getenv("TRX_NO_PDL") == nullptr;
+    return on;
+}
+}  // namespace trx
 
 namespace {
 
@@ -45,9 +47,6 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 trx::MvJobs base_jobs(const trx_ctx *ctx, const trx_entry *e, const void *packed) {
     trx::MvJobs J{};
-    J.acc = ctx->acc;
-    J.cnt = ctx->cnt;
-    J.acc_rows = ctx->acc_rows;
     J.w = static_cast<const uint8_t *>(packed);
     J.rows = (int)e->rows;
     J.cols = (int)e->cols;
@@ -80,10 +79,7 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         delete c;
         return TRX_ERR_CUDA;
     }
-    c->acc_rows = kAccRows;
-    if (cudaMalloc(&c->acc, kAccRows * 16) != cudaSuccess || cudaMalloc(&c->cnt, kAccRows * 4) != cudaSuccess ||
-        cudaMemset(c->acc, 0, kAccRows * 16) != cudaSuccess || cudaMemset(c->cnt, 0, kAccRows * 4) != cudaSuccess ||
-        cudaMemset(c->err, 0, 256) != cudaSuccess ||
+    if (cudaMemset(c->err, 0, 256) != cudaSuccess ||
         cudaMalloc(&c->attn_part, kAttnPartFloats * 4) != cudaSuccess ||
         cudaMalloc(&c->attn_cnt, kAttnMaxKv * 4) != cudaSuccess || cudaMemset(c->attn_cnt, 0, kAttnMaxKv * 4) != cudaSuccess ||
         cudaMalloc(&c->amax_key, kMaxArgmaxJobs * 8) != cudaSuccess ||
@@ -93,8 +89,6 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
         cudaFree(c->lut);
-        cudaFree(c->acc);
-        cudaFree(c->cnt);
         cudaFree(c->attn_part);
         cudaFree(c->attn_cnt);
         cudaFree(c->amax_key);
@@ -110,8 +104,6 @@ trx_status trx_destroy(trx_ctx *ctx) {
     if (!ctx) return TRX_ERR_ARG;
     cudaFree(ctx->err);
     cudaFree(ctx->lut);
-    cudaFree(ctx->acc);
-    cudaFree(ctx->cnt);
     cudaFree(ctx->attn_part);
     cudaFree(ctx->attn_cnt);
     cudaFree(ctx->amax_key);

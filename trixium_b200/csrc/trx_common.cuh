@@ -140,4 +140,11 @@ __device__ __forceinline__ int frexp_exp(float a) {
     return e;
 }
 
+// Programmatic dependent launch (sm_90+): every kernel of the library releases its successor as
+// soon as it starts (the successor's CTAs take SMs as this kernel's CTAs leave) and waits for its
+// predecessor's completion before it reads anything a kernel may have written.  Both are no-ops
+// for a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace trx

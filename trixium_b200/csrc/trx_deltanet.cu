@@ -57,6 +57,8 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_kernel(DnArgs A, uint32_t
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x, h = blockIdx.y;
     const int hk = A.hk, hv = A.hv, nk = A.nk, nq = A.nk * A.hk;
+    pdl_trigger();
+    pdl_wait();
     const int pos = *A.pos;
     if (pos < 0) {
         if (tid == 0 && s == 0 && h == 0) atomicOr(err, TRX_DEV_RANGE);
@@ -166,8 +168,7 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_kernel(DnArgs A, uint32_t
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st) {
     const size_t smem = (size_t)(2 * A.hk + (A.rows > A.hv ? A.rows : A.hv)) * 4;
-    deltanet_kernel<<<dim3(A.nsplit, A.nv), kDnThreads, smem, st>>>(A, err);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(deltanet_kernel, dim3(A.nsplit, A.nv), dim3(kDnThreads), smem, st, A, err));
 }
 
 }  // namespace trx

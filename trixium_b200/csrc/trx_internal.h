@@ -9,6 +9,27 @@
 
 namespace trx {
 
+// Whether launches carry the programmatic-stream-serialization attribute (set TRX_NO_PDL in the
+// environment to launch plainly).
+bool pdl_enabled();
+
+// Launch `k` on `st`, as a programmatic dependent of the stream's previous kernel when enabled.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_SWIGLU = 2 };
 
 constexpr int kMaxSegs = 4;
@@ -45,12 +66,6 @@ struct MvJobs {
     int *token;                  // if set (with argmax): per job, the argmax row; the keys and
     unsigned *arg_cnt;           // the arrival count arg_cnt are left at zero again
     const int *skip;             // if set and *skip != 0, the launch does nothing
-    // Rows split over slabs (K > 4096) are summed in a zeroed global accumulator: acc[2*i] (and
-    // acc[2*i+1] for SwiGLU's up row) and an arrival count cnt[i], i = job*rows + row.  The last
-    // slab to arrive finishes the row and leaves both at zero again.
-    unsigned long long *acc;
-    unsigned *cnt;
-    uint64_t acc_rows;           // capacity of acc/cnt in rows
 };
 
 // Argmax key of (value, row): orderable float bits in the high word, ~row in the low word, so

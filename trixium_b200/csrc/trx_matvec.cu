@@ -60,10 +60,10 @@ constexpr int kSmemMax = 227 * 1024;
 struct MvGeom {
     int G;        // groups per row
     int nch;      // chunks per row (the last may hold fewer than kCG groups)
-    int cpt;      // chunks per task
-    int S;        // tasks per row block
+    int cpt;      // chunks per warp per row block
+    int S;        // warps sharing a row block (a power of two; 1: a warp owns whole row blocks)
     int nrb;      // row blocks per job
-    int tpj;      // tasks per job (nrb * S)
+    int grid;     // CTAs
     int rb;       // row packet bytes in global memory
     int sbytes;   // scale-region bytes of a packet
     int nw;       // tensors per block (2 for SwiGLU)
@@ -73,6 +73,7 @@ struct MvGeom {
     int fixed;    // bytes of activation words and reductions (128-byte rounded): rings A start here
     int na;       // warps whose ring lies in region A (the rest: region C, after the trit5 LUT)
     int q8c;      // the quantiser's staging lies in region C
+    int stage;    // bytes of that staging region
     int base;     // shared-window address of the dynamic shared memory the plan assumes
     int smem;     // dynamic shared bytes
 };
@@ -117,15 +118,65 @@ __device__ float block_sumsq64(const float *x, int n, float *red64) {
 }
 
 // Build the permuted int8 activation of one job in shared memory (all threads of the CTA).
-// q8: K bytes of staging, xp: G * xw words.  Returns e8.
+// q8: K bytes of staging, xp: G * xw words.  xs (or NULL): 4K bytes of shared staging for x, so x
+// and the norm weight are read from global memory once.  Returns e8.
 template <int KIND>
 __device__ int build_activation(const float *x, const int8_t *x8g, const float *nw, float eps, int K, int8_t *q8,
-                                uint32_t *xp, uint32_t *amax_s, float *red64) {
+                                float *xs, uint32_t *xp, uint32_t *amax_s, float *red64) {
     const int ct = threadIdx.x;
     const int nt = blockDim.x;
     int e8 = 0;
     if (x8g) {
         for (int k = ct; k < K; k += nt) q8[k] = x8g[k];
+    } else if (xs) {
+        // x -> shared (one coalesced pass), then the canonical sum of squares, the prologue values
+        // (x*r)*w in place with their max, and the quantiser, all from shared memory.
+        for (int i = ct; i < K / 4; i += nt)
+            reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        if (ct == 0) *amax_s = 0u;
+        __syncthreads();
+        float r = 0.f;
+        if (nw) {
+            if (ct < 64) {  // partial j: x[j]^2 + x[j+64]^2 + ... in index order (model/mirror.py:576-591)
+                float p = 0.f;
+                for (int i = ct; i < K; i += 64) p = __fadd_rn(p, __fmul_rn(xs[i], xs[i]));
+                red64[ct] = p;
+            }
+            __syncthreads();
+            if (ct < 32) {  // the halving tree: red[j] + red[j+32], then 16, 8, ... in one warp
+                float a = __fadd_rn(red64[ct], red64[ct + 32]);
+                for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
+                if (ct == 0) red64[0] = a;
+            }
+            __syncthreads();
+            r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red64[0], (float)K), eps)));
+        }
+        uint32_t m = 0;
+        for (int i = ct; i < K / 4; i += nt) {
+            float4 v = reinterpret_cast<float4 *>(xs)[i];
+            if (nw) {
+                const float4 wv = __ldg(reinterpret_cast<const float4 *>(nw) + i);
+                v.x = __fmul_rn(__fmul_rn(v.x, r), wv.x);
+                v.y = __fmul_rn(__fmul_rn(v.y, r), wv.y);
+                v.z = __fmul_rn(__fmul_rn(v.z, r), wv.z);
+                v.w = __fmul_rn(__fmul_rn(v.w, r), wv.w);
+                reinterpret_cast<float4 *>(xs)[i] = v;
+            }
+            const uint32_t a = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                                   max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+            m = a > m ? a : m;
+        }
+        m = __reduce_max_sync(0xffffffffu, m);
+        if ((ct & 31) == 0) atomicMax(amax_s, m);
+        __syncthreads();
+        const uint32_t amax = *amax_s;
+        if (amax == 0u) {
+            for (int k = ct; k < K; k += nt) q8[k] = 0;
+        } else {
+            e8 = frexp_exp(__uint_as_float(amax)) - 7;
+            const float inv = pow2f(-e8);
+            for (int k = ct; k < K; k += nt) q8[k] = quant_one(xs[k], inv);
+        }
     } else {
         float r = 0.f;
         if (nw) {
@@ -419,29 +470,6 @@ __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Position in a warp's stream of blocks: task `task` (row block rbk, chunks [c, c1)).
-struct Cursor {
-    int task, rbk, c, c1;
-};
-
-__device__ __forceinline__ void cursor_task(const MvGeom &M, int task, Cursor &k) {
-    k.task = task;
-    if (M.S == 1) {
-        k.rbk = task;
-        k.c = 0;
-        k.c1 = M.nch;
-        return;
-    }
-    k.rbk = task / M.S;
-    const int s = task - k.rbk * M.S;
-    k.c = s * M.cpt;
-    k.c1 = min(M.nch, k.c + M.cpt);
-}
-
-__device__ __forceinline__ void cursor_next(const MvGeom &M, Cursor &k, int stride) {
-    if (++k.c == k.c1) cursor_task(M, k.task + stride, k);
-}
-
 // Issue the copies of block (row block rbk, chunk c) of `job` into ring slot `dst`.  Per row,
 // the 16 scale bytes holding the chunk's scales land at ring bytes [0, 16) and the chunk's codes
 // at [16, ...) (trit5: from the 16-byte boundary at or below their start, so an odd chunk's codes
@@ -522,12 +550,12 @@ template <int KIND>
 constexpr int ring_depth() { return KIND == TRX_KIND_TERNARY5 ? 2 : 3; }
 
 template <int KIND, int NW>
-__global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, const uint32_t *lut_g, uint32_t *err) {
+__global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, const uint32_t *lut_g, uint32_t *err) {
     constexpr int D = ring_depth<KIND>();
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    if (J.skip && *J.skip) return;
+    pdl_trigger();
 
     // Carve shared memory (must match plan_matvec): [activation words, reductions][rings A]
     // [trit5 LUT at window address 0x10000][rings C]; 2-bit: one ring region, no LUT.
@@ -541,6 +569,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
     // Offsets (not pointers chosen between regions) keep every access provably shared.
     const int lut_off = 0x10000 - M.base, c_off = lut_off + kLutBytes;
     if (KIND == TRX_KIND_TERNARY5 && smem_u32(smem) != (uint32_t)M.base) {
+        pdl_wait();
         if (tid == 0) atomicOr(err, TRX_DEV_INTERNAL);  // the window is not where the plan put the LUT
         return;
     }
@@ -550,120 +579,152 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
     const uint32_t ring_s = smem_u32(ring);
     int8_t *const q8 = reinterpret_cast<int8_t *>(smem + (M.q8c ? c_off : M.fixed));  // staging; rings idle then
 
-    // This CTA's share of the (job, task) space.
-    const long long total = (long long)J.njobs * M.tpj;
+    // Combine area of warps sharing a row block: [2 parities][warps][32 lanes][NW] int64.
+    long long *const red = reinterpret_cast<long long *>(smem + M.fixed - (M.S > 1 ? 8192 : 0));
+
+    // This CTA's share of the (job, row block) space.
+    const long long total = (long long)J.njobs * M.nrb;
     const long long t0 = (long long)blockIdx.x * total / gridDim.x;
     const long long t1 = (long long)(blockIdx.x + 1) * total / gridDim.x;
-    if (t0 >= t1) return;
+    if (t0 >= t1) {
+        pdl_wait();
+        return;
+    }
 
-    if (KIND == TRX_KIND_TERNARY5) {  // the trit5 LUT (replicated, 256-byte stride)
-        const uint4 *src = reinterpret_cast<const uint4 *>(lut_g);
-        uint4 *dst = reinterpret_cast<uint4 *>(lut);
-        for (int i = tid; i < kLutBytes / 16; i += blockDim.x) dst[i] = src[i];
+    if (KIND == TRX_KIND_TERNARY5) {  // the trit5 LUT: entry b at b*256, one replica per lane
+        (void)lut_g;
+        for (int b = warp; b < 256; b += blockDim.x >> 5)
+            reinterpret_cast<uint32_t *>(lut + b * 256)[lane] = trit5_lut_entry((uint32_t)b);
     }
     const uint32_t lane4x = 0x10000u | ((uint32_t)lane * 4u);
     const ScaleFast F2 = scale_fast(J.B2);
+    // Warp w: group gi = w / S (row block gi of each round of R = warps/S row blocks), chunks
+    // [cA, cB) of that row block.
+    const int R = M.warps / M.S;
+    const int gi = warp / M.S, sub = warp - gi * M.S;
+    const int cA = sub * M.cpt, cB = min(M.nch, cA + M.cpt);
+    const int nc = cB > cA ? cB - cA : 0;
+    float *const xs = M.stage >= ((J.cols + 15) / 16) * 16 + 4 * J.cols
+                          ? reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(q8) + ((J.cols + 15) / 16) * 16)
+                          : nullptr;
+
+    // Issue cursor of the current piece: (round, chunk) and blocks issued, of `nitems`.
+    int job = 0, pa = 0, pb = 0, kval = 0, nitems = 0, ik = 0, ic = 0, issued = 0;
+    auto piece_begin = [&](long long t) {
+        job = (int)(t / M.nrb);
+        const long long jb = (long long)job * M.nrb;
+        pa = (int)(t - jb);                          // this piece: row blocks [pa, pb) of `job`
+        pb = (int)(min(t1, jb + M.nrb) - jb);
+        kval = pb - pa > gi ? (pb - pa - gi + R - 1) / R : 0;  // rounds with a row block for gi
+        nitems = kval * nc;                                     // blocks this warp streams
+        ik = ic = issued = 0;
+    };
+    auto issue_next = [&](uint32_t dst) {
+        if (issued < nitems) {
+            issue_block<KIND, NW>(J, M, job, pa + ik * R + gi, cA + ic, dst, lane);
+            if (++ic == nc) {
+                ic = 0;
+                ++ik;
+            }
+            ++issued;
+        }
+        cp_commit();
+    };
+    // The first piece's first blocks (weights: written by no kernel) are requested before waiting
+    // for the predecessor, by the warps whose ring is not the quantiser's staging area.
+    const int stage_off = M.q8c ? c_off : M.fixed;
+    const int stage_end = stage_off + ((J.cols + 15) / 16) * 16 + (xs ? 4 * J.cols : 0);
+    const bool early = ring_off + RING <= stage_off || ring_off >= stage_end;
+    piece_begin(t0);
+    if (early) {
+#pragma unroll
+        for (int d = 0; d < D - 1; ++d) issue_next(ring_s + d * slot_bytes);
+    }
+    pdl_wait();
+    if (J.skip && *J.skip) {
+        cp_wait<0>();
+        return;
+    }
 
     for (long long t = t0; t < t1;) {
-        const int job = (int)(t / M.tpj);
-        const long long tjb = (long long)job * M.tpj;
-        const int last = (int)(min(t1, tjb + M.tpj) - tjb);  // end task (exclusive) of this piece
-        const int first = (int)(t - tjb) + warp;             // this warp's first task
-        t = tjb + last;
+        const bool first = t == t0;
+        if (!first) piece_begin(t);
+        t = (long long)job * M.nrb + pb;
         __syncthreads();  // the previous piece's activation and rings are no longer in use
         const float *xj = J.x ? J.x + (uint64_t)job * J.x_stride : nullptr;
         const int8_t *x8j = J.x8 ? J.x8 + (uint64_t)job * J.x_stride : nullptr;
-        const int e8 = build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xp, amax_s, red64);
+        const int e8 = build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
         unsigned long long best = 0ull;
 
-        Cursor is, cs;
-        cursor_task(M, first, is);
-        cs = is;
-        // Prime the ring with the first D-1 blocks.
+        const int rounds = (pb - pa + R - 1) / R;
+        if (!(first && early)) {
 #pragma unroll
-        for (int d = 0; d < D - 1; ++d) {
-            if (is.task < last) {
-                issue_block<KIND, NW>(J, M, job, is.rbk, is.c, ring_s + d * slot_bytes, lane);
-                cursor_next(M, is, M.warps);
-            }
-            cp_commit();
+            for (int d = 0; d < D - 1; ++d) issue_next(ring_s + d * slot_bytes);
         }
         int rs = D - 1, slot = 0;
-        long long acc0 = 0, acc1 = 0;
         LaneRow L, one;
         one.o = row_out(J, job, 0, e8);
         one.B = one.o.B;
         one.F = scale_fast(one.B);
-        bool fresh = true;  // the consume cursor entered a new task
-        while (cs.task < last) {
-            if (is.task < last) {
-                issue_block<KIND, NW>(J, M, job, is.rbk, is.c, ring_s + rs * slot_bytes, lane);
-                cursor_next(M, is, M.warps);
-            }
-            cp_commit();
-            rs = rs + 1 == D ? 0 : rs + 1;
-            if (fresh) {
-                lane_row(J, job, cs.rbk * 32 + lane, e8, one, L);
-                fresh = false;
-            }
-            cp_wait<D - 1>();
-            __syncwarp();
-            const int c = cs.c;
-            const int ng = min(kCG, M.G - c * kCG);
-            const uint32_t *xg = xp + c * kCG * M.xw;
-            const unsigned char *rp = ring + (size_t)slot * slot_bytes + lane * kRowStride;
+        for (int k = 0; k < rounds; ++k) {
+            const int rbk = pa + k * R + gi;
+            const bool valid = k < kval;
+            long long acc0 = 0, acc1 = 0;
+            if (valid) lane_row(J, job, rbk * 32 + lane, e8, one, L);
+            for (int c = cA; valid && c < cB; ++c) {
+                issue_next(ring_s + rs * slot_bytes);
+                rs = rs + 1 == D ? 0 : rs + 1;
+                cp_wait<D - 1>();
+                __syncwarp();
+                const int ng = min(kCG, M.G - c * kCG);
+                const uint32_t *xg = xp + c * kCG * M.xw;
+                const unsigned char *rp = ring + (size_t)slot * slot_bytes + lane * kRowStride;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                const unsigned char *rw = rp + w * kBlkBytes;
-                const uint2 sc = *reinterpret_cast<const uint2 *>(rw + (c & 1) * 8);
-                const int Bw = w ? J.B2 : L.B;
-                const ScaleFast &Fw = w ? F2 : L.F;
-                long long a;
-                if (KIND == TRX_KIND_TERNARY5) {
-                    uint32_t cw[28];
+                for (int w = 0; w < NW; ++w) {
+                    const unsigned char *rw = rp + w * kBlkBytes;
+                    const uint2 sc = *reinterpret_cast<const uint2 *>(rw + (c & 1) * 8);
+                    const int Bw = w ? J.B2 : L.B;
+                    const ScaleFast &Fw = w ? F2 : L.F;
+                    long long a;
+                    if (KIND == TRX_KIND_TERNARY5) {
+                        uint32_t cw[28];
 #pragma unroll
-                    for (int i = 0; i < 7; ++i) {
-                        const uint4 v = reinterpret_cast<const uint4 *>(rw + 16)[i];
-                        cw[4 * i] = v.x;
-                        cw[4 * i + 1] = v.y;
-                        cw[4 * i + 2] = v.z;
-                        cw[4 * i + 3] = v.w;
-                    }
-                    a = (c & 1) ? chunk_t5<8>(cw, sc, ng, xg, lane4x, Bw, Fw)
-                                : chunk_t5<0>(cw, sc, ng, xg, lane4x, Bw, Fw);
-                } else {
-                    a = chunk_2b(reinterpret_cast<const uint4 *>(rw + 16), sc, ng, xg, Bw, Fw);
-                }
-                if (w) acc1 += a;
-                else acc0 += a;
-            }
-            __syncwarp();  // every lane is done with the slot before it is refilled
-            slot = slot + 1 == D ? 0 : slot + 1;
-            if (c + 1 == cs.c1) {  // the task's last chunk: finish or hand over this lane's row
-                if (L.row >= 0) {
-                    if (M.S == 1) {
-                        const unsigned long long k = finish_row(J, L.o, L.row, L.srow, acc0, acc1, err);
-                        best = k > best ? k : best;
-                    } else {
-                        const uint64_t ix = (uint64_t)job * J.rows + L.row;
-                        unsigned long long *acc = J.acc + 2 * ix;
-                        atomicAdd(acc, (unsigned long long)acc0);
-                        if (NW == 2) atomicAdd(acc + 1, (unsigned long long)acc1);
-                        __threadfence();
-                        if (atomicAdd(J.cnt + ix, 1u) == (unsigned)(M.S - 1)) {
-                            __threadfence();
-                            const long long tt = (long long)atomicExch(acc, 0ull);
-                            const long long t2 = NW == 2 ? (long long)atomicExch(acc + 1, 0ull) : 0ll;
-                            J.cnt[ix] = 0u;
-                            const unsigned long long k = finish_row(J, L.o, L.row, L.srow, tt, t2, err);
-                            best = k > best ? k : best;
+                        for (int i = 0; i < 7; ++i) {
+                            const uint4 v = reinterpret_cast<const uint4 *>(rw + 16)[i];
+                            cw[4 * i] = v.x;
+                            cw[4 * i + 1] = v.y;
+                            cw[4 * i + 2] = v.z;
+                            cw[4 * i + 3] = v.w;
                         }
+                        a = (c & 1) ? chunk_t5<8>(cw, sc, ng, xg, lane4x, Bw, Fw)
+                                    : chunk_t5<0>(cw, sc, ng, xg, lane4x, Bw, Fw);
+                    } else {
+                        a = chunk_2b(reinterpret_cast<const uint4 *>(rw + 16), sc, ng, xg, Bw, Fw);
+                    }
+                    if (w) acc1 += a;
+                    else acc0 += a;
+                }
+                __syncwarp();  // every lane is done with the slot before it is refilled
+                slot = slot + 1 == D ? 0 : slot + 1;
+            }
+            if (M.S > 1) {
+                // The S warps of the group add their partial sums in a fixed order (exact int64).
+                long long *rd = red + (size_t)(k & 1) * M.warps * 32 * NW;
+                rd[(warp * 32 + lane) * NW] = acc0;
+                if (NW == 2) rd[(warp * 32 + lane) * NW + 1] = acc1;
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + gi), "r"(M.S * 32) : "memory");
+                if (sub == 0 && valid) {
+                    acc0 = acc1 = 0;
+                    for (int s2 = 0; s2 < M.S; ++s2) {
+                        acc0 += rd[((gi * M.S + s2) * 32 + lane) * NW];
+                        if (NW == 2) acc1 += rd[((gi * M.S + s2) * 32 + lane) * NW + 1];
                     }
                 }
-                acc0 = acc1 = 0;
-                fresh = true;
             }
-            cursor_next(M, cs, M.warps);
+            if (valid && sub == 0 && L.row >= 0) {
+                const unsigned long long key = finish_row(J, L.o, L.row, L.srow, acc0, acc1, err);
+                best = key > best ? key : best;
+            }
         }
         cp_wait<0>();
         __syncwarp();
@@ -692,6 +753,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, 
 template <int KIND>
 __global__ void __launch_bounds__(256) tmv_fp_kernel(MvJobs J, int TR, uint32_t *err) {
     extern __shared__ __align__(128) unsigned char smem[];
+    pdl_trigger();
+    pdl_wait();
     float *xs = reinterpret_cast<float *>(smem);
     float *part = xs + J.cols;  // [TR][G+1]
     const int G = J.cols / 128, K = J.cols;
@@ -742,6 +805,8 @@ __global__ void __launch_bounds__(256) tmv_fp_kernel(MvJobs J, int TR, uint32_t 
 // Standalone quantiser (trx_quantize_pow2): one CTA, grid-stride.
 __global__ void __launch_bounds__(1024) quantize_kernel(const float *x, int n, int8_t *x8, int *e8_out) {
     __shared__ uint32_t amax_s;
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x == 0) amax_s = 0;
     __syncthreads();
     uint32_t m = 0;
@@ -764,6 +829,8 @@ __global__ void __launch_bounds__(1024) quantize_kernel(const float *x, int n, i
 
 // Validation of trit5 bytes (> 242 is invalid).
 __global__ void validate_t5_kernel(const uint8_t *w, int rows, int rb, int sbytes, int G, uint32_t *err) {
+    pdl_trigger();
+    pdl_wait();
     const int cb = 26 * G;
     const long long total = (long long)rows * cb;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -830,42 +897,50 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     M.nw = nw;
     M.xw = kind == TRX_KIND_TERNARY5 ? kXwT5 : kXw2b;
     M.nrb = (J.rows + 31) / 32;
-    const long long rbs = (long long)J.njobs * M.nrb;
-    const long long want = (long long)sms * kMaxWarps;
-    int S = 1;
-    if (rbs < want) S = (int)std::min<long long>(M.nch, (want + rbs - 1) / rbs);
-    if (S > 1 && (!J.acc || !J.cnt || (uint64_t)J.njobs * (uint64_t)J.rows > J.acc_rows)) S = 1;
-    M.cpt = (M.nch + S - 1) / S;
-    M.S = (M.nch + M.cpt - 1) / M.cpt;
-    M.tpj = M.nrb * M.S;
-    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 127) / 128 * 128;
+    // Row blocks are dealt to CTAs; when a CTA gets fewer row blocks than it has warps, the warps
+    // share row blocks (S per row block, chunks split between them, sums combined in shared memory).
+    const long long rbt = (long long)J.njobs * M.nrb;
+    M.grid = (int)std::min<long long>(sms, rbt);
+    const long long rbc = (rbt + M.grid - 1) / M.grid;
+    const bool split = rbc < kMaxWarps && M.nch > 1;
+    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 127) / 128 * 128 + (split ? 8192 : 0);
     M.D = kind == TRX_KIND_TERNARY5 ? 2 : 3;
     const int ring = M.D * nw * kBlkBytes;  // one warp's ring
+    // The trit5 LUT sits at shared-window address 0x10000 (its PRMT-built addresses need no add):
+    // ring region A below it, region C above it.  2-bit: region A only.
+    const int lut_off = 0x10000 - reserved, c_off = lut_off + kLutBytes;
+    int na_max, nc_max;
     if (kind == TRX_KIND_TERNARY5) {
-        // The LUT sits at shared-window address 0x10000 (its PRMT-built addresses need no add):
-        // region A below it, region C above it.
-        M.base = reserved;
-        const int lut_off = 0x10000 - reserved;
         if (M.fixed > lut_off) return false;
-        const int na_max = (lut_off - M.fixed) / ring;
-        const int c_off = lut_off + kLutBytes;
-        const int nc_max = (kSmemMax - c_off) / ring;
-        M.warps = std::min(kMaxWarps, na_max + nc_max);
-        M.na = std::min(na_max, M.warps);
-        const int nc = M.warps - M.na;
-        M.smem = c_off + nc * ring;
-        if (M.na * ring >= J.cols) M.q8c = 0;
-        else if (nc * ring >= J.cols) M.q8c = 1;
-        else return false;  // no ring region holds the quantiser's staging
+        na_max = (lut_off - M.fixed) / ring;
+        nc_max = (kSmemMax - c_off) / ring;
     } else {
-        M.base = 0;
-        M.warps = std::min(kMaxWarps, (kSmemMax - M.fixed) / ring);
-        M.na = M.warps;
-        M.q8c = 0;
-        M.smem = M.fixed + M.warps * ring;
-        if (M.warps * ring < J.cols) return false;
+        na_max = (kSmemMax - M.fixed) / ring;
+        nc_max = 0;
     }
+    M.warps = std::min(nw == 2 ? kMaxWarps / 2 : kMaxWarps, na_max + nc_max);
     if (M.warps < 4) return false;
+    M.S = 1;
+    if (split) {
+        int w = 1;
+        while (w * 2 <= M.warps) w *= 2;  // sharing groups need a power-of-two warp count
+        M.warps = w;
+        int R = 1;
+        while (R * 2 <= M.warps && R * 2 <= rbc) R *= 2;
+        M.S = M.warps / R;
+        while (M.S > 1 && M.S > M.nch) M.S /= 2;  // more sharers than chunks would only idle
+    }
+    M.cpt = (M.nch + M.S - 1) / M.S;
+    M.na = std::min(na_max, M.warps);
+    const int nc = M.warps - M.na;
+    M.base = kind == TRX_KIND_TERNARY5 ? reserved : 0;
+    M.smem = kind == TRX_KIND_TERNARY5 ? c_off + nc * ring : M.fixed + M.warps * ring;
+    // The quantiser's staging (q8, then x as fp32) lives in the larger ring region, idle then.
+    M.q8c = nc > M.na ? 1 : 0;
+    M.stage = (M.q8c ? nc : M.na) * ring;
+    if (M.stage < J.cols) return false;
+    if ((reinterpret_cast<uintptr_t>(J.x) & 15) || (reinterpret_cast<uintptr_t>(J.norm_w) & 15) || (J.x_stride & 3))
+        M.stage = J.cols;  // float4 loads need 16-byte aligned rows: the global prologue path
     return M.smem <= kSmemMax;
 }
 
@@ -882,8 +957,7 @@ static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, int grid, const u
         if (e != cudaSuccess) return note_cuda(e);
         configured |= bit;
     }
-    tmv_kernel<KIND, NW><<<grid, M.warps * 32, M.smem, st>>>(J, M, lut, err);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(tmv_kernel<KIND, NW>, dim3(grid), dim3(M.warps * 32), M.smem, st, J, M, lut, err));
 }
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st) {
@@ -892,8 +966,7 @@ trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cu
     const int sms = di.sms;
     const int nw = J.w2 ? 2 : 1;
     if (!plan_matvec(J, nw, sms, di.reserved, M)) return TRX_ERR_UNSUPPORTED;
-    const long long tasks = (long long)J.njobs * M.tpj;
-    const int grid = (int)std::min<long long>(sms, tasks);
+    const int grid = M.grid;
     if (J.kind == TRX_KIND_TERNARY5)
         return nw == 2 ? launch_tmv<TRX_KIND_TERNARY5, 2>(J, M, grid, lut, err, st)
                        : launch_tmv<TRX_KIND_TERNARY5, 1>(J, M, grid, lut, err, st);
@@ -912,18 +985,17 @@ trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st) {
     if (J.kind == TRX_KIND_TERNARY5) {
         e = cudaFuncSetAttribute(tmv_fp_kernel<TRX_KIND_TERNARY5>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return note_cuda(e);
-        tmv_fp_kernel<TRX_KIND_TERNARY5><<<grid, 256, smem, st>>>(J, TR, err);
+        e = launch_kernel(tmv_fp_kernel<TRX_KIND_TERNARY5>, dim3(grid), dim3(256), smem, st, J, TR, err);
     } else {
         e = cudaFuncSetAttribute(tmv_fp_kernel<TRX_KIND_TERNARY>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return note_cuda(e);
-        tmv_fp_kernel<TRX_KIND_TERNARY><<<grid, 256, smem, st>>>(J, TR, err);
+        e = launch_kernel(tmv_fp_kernel<TRX_KIND_TERNARY>, dim3(grid), dim3(256), smem, st, J, TR, err);
     }
-    return note_cuda(cudaGetLastError());
+    return note_cuda(e);
 }
 
 trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStream_t st) {
-    quantize_kernel<<<1, 1024, 0, st>>>(x, n, x8, e8);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(quantize_kernel, dim3(1), dim3(1024), 0, st, x, n, x8, e8));
 }
 
 trx_status launch_validate_t5(const uint8_t *w, int rows, int cols, uint32_t *err, cudaStream_t st) {
@@ -934,8 +1006,7 @@ trx_status launch_validate_t5(const uint8_t *w, int rows, int cols, uint32_t *er
     int grid = (int)((total + 255) / 256);
     if (grid > num_sms() * 8) grid = num_sms() * 8;
     if (grid < 1) grid = 1;
-    validate_t5_kernel<<<grid, 256, 0, st>>>(w, rows, rb, sb, G, err);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(validate_t5_kernel, dim3(grid), dim3(256), 0, st, w, rows, rb, sb, G, err));
 }
 
 trx_status launch_build_lut(uint32_t *lut, cudaStream_t st) {

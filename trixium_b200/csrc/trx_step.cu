@@ -14,6 +14,8 @@ namespace trx {
 // TRX_DEV_RANGE and writes zeros.
 __global__ void embed_kernel(const void *table, int vocab, int dim, int f16, const int *token, float *x,
                              uint32_t *err) {
+    pdl_trigger();
+    pdl_wait();
     const int t = *token;
     const bool ok = t >= 0 && t < vocab;
     if (!ok && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, TRX_DEV_RANGE);
@@ -26,18 +28,20 @@ __global__ void embed_kernel(const void *table, int vocab, int dim, int f16, con
     }
 }
 
-__global__ void advance_kernel(int *pos, int n) { *pos += n; }
+__global__ void advance_kernel(int *pos, int n) {
+    pdl_trigger();
+    pdl_wait();
+    *pos += n;
+}
 
 trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
                         cudaStream_t st) {
     const int blocks = (dim + 255) / 256 < 16 ? (dim + 255) / 256 : 16;
-    embed_kernel<<<blocks, 256, 0, st>>>(table, vocab, dim, f16, token, x, err);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(embed_kernel, dim3(blocks), dim3(256), 0, st, table, vocab, dim, f16, token, x, err));
 }
 
 trx_status launch_advance(int *pos, int n, cudaStream_t st) {
-    advance_kernel<<<1, 1, 0, st>>>(pos, n);
-    return note_cuda(cudaGetLastError());
+    return note_cuda(launch_kernel(advance_kernel, dim3(1), dim3(1), 0, st, pos, n));
 }
 
 }  // namespace trx
