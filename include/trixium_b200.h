@@ -197,6 +197,22 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const floa
                            const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
                            float *d_out, cudaStream_t stream);
 
+/*
+ * trx_attn_decode without a context, for callers that cannot allocate device memory while they
+ * run (a serving loop that reserved the device's memory up front, a host runtime whose allocator
+ * belongs to another framework).  No counterpart in the reference.  Same computation and
+ * arguments as trx_attn_decode; the partials and arrival counts live in the library's static
+ * device arrays (limits: n_kv <= 64 and n_kv * splits * (H/n_kv) * (head_dim + 2) floats <= 2^20,
+ * splits = ceil(max_pos / (max_pos <= 2048 ? 64 : 128)); larger shapes return
+ * TRX_ERR_UNSUPPORTED), so the library allocates nothing.  Device error bits are OR'd into *d_err
+ * (a caller-owned device word).  The first call on a device sets the arrays up and should come
+ * before any other work on that device's streams; calls that overlap in time race on the arrays.
+ */
+trx_status trx_attn_decode_static(const trx_attn_shape *shape, const float *d_q, const float *d_k,
+                                  const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                                  const float *d_rope_freq, void *d_kcache, void *d_vcache,
+                                  const int32_t *d_pos, float *d_out, uint32_t *d_err, cudaStream_t stream);
+
 /* Shape of one gated-DeltaNet layer (model/configs.py dn_* fields). */
 typedef struct trx_deltanet_shape {
     uint32_t n_k_heads;    /* nk                                                    */

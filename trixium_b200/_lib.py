@@ -23,6 +23,7 @@ SYMBOLS = (
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
     "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
     "trx_deltanet_step", "trx_lmhead_argmax", "trx_matvec_f_multi", "trx_embed_lookup", "trx_advance_position",
+    "trx_attn_decode_static",
 )
 
 
@@ -95,6 +96,7 @@ def lib():
             "trx_embed_lookup": ([_vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32, _vp, _vp, _vp],
                                  ctypes.c_int),
             "trx_advance_position": ([_vp, _vp, ctypes.c_int32, _vp], ctypes.c_int),
+            "trx_attn_decode_static": ([ctypes.POINTER(AttnShape)] + [_vp] * 12, ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -19,6 +19,7 @@
 // (position, kv head) read once.
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -265,3 +266,103 @@ trx_status launch_attn_decode(const AttnArgs &A, uint32_t *err, cudaStream_t st)
 }
 
 }  // namespace trx
+
+// Context-free decode attention ---------------------------------------------------------------
+// For callers that cannot allocate device memory while they run: a serving loop that reserved
+// all of the device's memory before it started, or a host runtime whose device allocator belongs
+// to another framework.  The partials and arrival counts live in this file's static device arrays
+// instead of a trx_ctx's scratch; the library allocates nothing.  The first call on a device sets
+// up (symbol addresses, counts zeroed) and should come before any other work on that device's
+// streams; calls that overlap in time race on the one array per device.
+namespace trx {
+namespace {
+
+constexpr size_t kStaticPartFloats = size_t(1) << 20;  // 4 MiB: [n_kv][splits][H/n_kv][hd + 2]
+constexpr uint32_t kStaticMaxKv = 64;
+__device__ __align__(256) float g_static_part[kStaticPartFloats];
+__device__ __align__(256) unsigned g_static_cnt[kStaticMaxKv];  // must start at zero
+
+struct StaticScratch {
+    bool ready;
+    float *part;
+    unsigned *cnt;
+};
+StaticScratch g_static[64];
+std::mutex g_static_mu;
+
+trx_status static_scratch(StaticScratch &out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TRX_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    StaticScratch &s = g_static[dev];
+    if (!s.ready) {
+        void *p = nullptr, *c = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_part);
+        if (e != cudaSuccess) return note_cuda(e);
+        e = cudaGetSymbolAddress(&c, g_static_cnt);
+        if (e != cudaSuccess) return note_cuda(e);
+        e = cudaMemset(c, 0, sizeof(g_static_cnt));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return note_cuda(e);
+        s.part = static_cast<float *>(p);
+        s.cnt = static_cast<unsigned *>(c);
+        s.ready = true;
+    }
+    out = s;
+    return TRX_OK;
+}
+
+}  // namespace
+}  // namespace trx
+
+extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const float *d_q, const float *d_k,
+                                             const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                                             const float *d_rope_freq, void *d_kcache, void *d_vcache,
+                                             const int32_t *d_pos, float *d_out, uint32_t *d_err,
+                                             cudaStream_t stream) {
+    if (!sh) return TRX_ERR_ARG;
+    const uint32_t H = sh->n_head, Hkv = sh->n_kv, hd = sh->head_dim;
+    if (H == 0 || Hkv == 0 || H % Hkv || hd == 0 || hd % 8 || hd > 512) return TRX_ERR_ARG;
+    if (sh->rope_dims % 2 || sh->rope_dims > hd || sh->max_pos == 0 || sh->max_pos > (1u << 24)) return TRX_ERR_ARG;
+    if (!(sh->eps >= 0.f)) return TRX_ERR_ARG;
+    if (!d_q || !d_k || !d_v || !d_qnorm_w || !d_knorm_w || !d_kcache || !d_vcache || !d_pos || !d_out || !d_err)
+        return TRX_ERR_ARG;
+    if ((sh->rope_dims && !d_rope_freq) || (reinterpret_cast<uintptr_t>(d_kcache) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_vcache) & 15))
+        return TRX_ERR_ARG;
+    trx::AttnArgs A{};
+    A.H = (int)H;
+    A.Hkv = (int)Hkv;
+    A.hd = (int)hd;
+    A.rope_half = (int)sh->rope_dims / 2;
+    A.gated = sh->gated ? 1 : 0;
+    A.qstride = (int)hd * (A.gated ? 2 : 1);
+    A.max_pos = (int)sh->max_pos;
+    A.chunk = sh->max_pos <= 2048 ? 64 : 128;
+    A.nsplit = (A.max_pos + A.chunk - 1) / A.chunk;
+    A.eps = sh->eps;
+    A.scale = 1.0f / sqrtf((float)hd);
+    const uint32_t rep = H / Hkv;
+    // The fixed limits of the static scratch: n_kv <= 64 and the partials within 4 MiB.
+    if (Hkv > trx::kStaticMaxKv || (uint64_t)Hkv * A.nsplit * rep * (hd + 2) > trx::kStaticPartFloats)
+        return TRX_ERR_UNSUPPORTED;
+    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u ||
+        (uint64_t)rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))
+        return TRX_ERR_UNSUPPORTED;
+    trx::StaticScratch sc;
+    const trx_status st = trx::static_scratch(sc);
+    if (st != TRX_OK) return st;
+    A.q = d_q;
+    A.k = d_k;
+    A.v = d_v;
+    A.qn = d_qnorm_w;
+    A.kn = d_knorm_w;
+    A.freq = d_rope_freq;
+    A.pos = d_pos;
+    A.kc = static_cast<__half *>(d_kcache);
+    A.vc = static_cast<__half *>(d_vcache);
+    A.out = d_out;
+    A.part = sc.part;
+    A.cnt = sc.cnt;
+    return trx::launch_attn_decode(A, d_err, stream);
+}

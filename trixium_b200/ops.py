@@ -195,6 +195,24 @@ def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, 
     return out
 
 
+def attn_decode_static(shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, err, out=None):
+    """trx_attn_decode without a context (the library's static scratch; nothing allocated by the
+    library).  err: a caller-owned int32 device word receiving the device error bits."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (q_norm, "q_norm"), (k_norm, "k_norm")):
+        _need(t, torch.float32, n)
+    _need(kcache, torch.float16, "kcache")
+    _need(vcache, torch.float16, "vcache")
+    _need(pos, torch.int32, "pos")
+    _need(err, torch.int32, "err")
+    if out is None:
+        out = torch.empty(shape.n_head * shape.head_dim, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().trx_attn_decode_static(ctypes.byref(shape), _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
+                                                 _ptr(k_norm), _ptr(rope_freq), _ptr(kcache), _ptr(vcache),
+                                                 _ptr(pos), _ptr(out), _ptr(err), _stream()),
+               "trx_attn_decode_static")
+    return out
+
+
 def attn_shape(n_head, n_kv, head_dim, max_pos, rope_dims=None, gated=False, eps=1e-6):
     return _lib.AttnShape(n_head, n_kv, head_dim, head_dim if rope_dims is None else rope_dims, max_pos,
                           1 if gated else 0, eps)
@@ -272,6 +290,6 @@ def row_bytes(cols, kind):
 
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
-           "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_shape",
+           "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_decode_static", "attn_shape",
            "deltanet_shape", "deltanet_step", "lmhead_argmax", "matvec_f_multi", "embed_lookup",
            "advance_position", "row_bytes", "L"]
