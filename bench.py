@@ -187,6 +187,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the per-launch graph and e2e legs")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decoder tok/s legs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -358,6 +359,10 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if world == 1 and not args.no_decode:
+        # The metric's second half: 8B-shape batch-1 decode tok/s (config 2), and config 1.
+        out["decode"] = {"qwen3-8b": decode_leg(ctx, "qwen3-8b", 1024, 128, 8),
+                         "qwen3-1.7b": decode_leg(ctx, "qwen3-1.7b", 512, 128, 8)}
     if rank == 0 and world == 1 and not args.no_cpu:
         out["cpu_baseline"] = cpu_baseline(kind, args.cpu_seconds)
     if rank == 0:
@@ -366,6 +371,47 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_leg(ctx, name, ctx_len, n_tokens, warmup):
+    """Batch-1 greedy decode tok/s of a BASELINE decoder config on synthetic random-init weights:
+    one CUDA graph per token (trixium_b200.decoder), `ctx_len` positions of synthetic context in
+    the caches, the token fed back on the device.  `e2e_tok_s` runs the public generate() API
+    (prompt from the host, token ids back to the host)."""
+    import torch
+    from trixium_b200 import decoder as D
+    cfg = D.CONFIGS[name]
+    w = D.SyntheticWeights(cfg, seed=0)
+    dec = D.Decoder(w, ctx=ctx, max_pos=ctx_len + 2 * n_tokens + warmup + 8)
+    dec.set_states(1)
+    dec.fill_context(ctx_len)
+    dec.tok.fill_(7)
+    dec.capture()
+    for _ in range(warmup):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    dec.fill_context(ctx_len)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n_tokens):
+        dec.graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / n_tokens
+    ctx.raise_on_error()
+    dec.fill_context(ctx_len)
+    t0 = time.perf_counter()
+    toks = dec.generate([7], n_tokens)
+    e2e_s = time.perf_counter() - t0
+    wb = cfg.weight_bytes_per_token()
+    out = {"config": name, "kind": "trit5" if cfg.kind == 5 else "2-bit", "context": ctx_len, "batch": 1,
+           "tokens_timed": n_tokens, "ms_per_token": round(ms, 4), "tok_s": round(1000.0 / ms, 1),
+           "e2e_tok_s": round(n_tokens / e2e_s, 1), "weight_bytes_per_token": wb,
+           "weight_GBps": round(wb / (ms * 1e-3) / 1e9, 1), "launches_per_token": dec.launches_per_step(),
+           "distinct_tokens": len(set(toks))}
+    del dec, w
+    torch.cuda.empty_cache()
+    return out
 
 
 _pc_cache = {}

@@ -137,15 +137,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
             const float *qv = qs + r * hd;
             const uint4 *kr = reinterpret_cast<const uint4 *>(kt + t * rowh);
             float acc = 0.f;
+            const float4 *q4 = reinterpret_cast<const float4 *>(qv);
             for (int j = 0; j < pieces; ++j) {
                 const uint4 w = kr[j];
-                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = h2_to_f2(u[e]);
-                    acc = fmaf(qv[8 * j + 2 * e], f.x, acc);
-                    acc = fmaf(qv[8 * j + 2 * e + 1], f.y, acc);
-                }
+                const float4 qa = q4[2 * j], qb = q4[2 * j + 1];
+                const float2 f0 = h2_to_f2(w.x), f1 = h2_to_f2(w.y), f2 = h2_to_f2(w.z), f3 = h2_to_f2(w.w);
+                acc = fmaf(qa.x, f0.x, acc);
+                acc = fmaf(qa.y, f0.y, acc);
+                acc = fmaf(qa.z, f1.x, acc);
+                acc = fmaf(qa.w, f1.y, acc);
+                acc = fmaf(qb.x, f2.x, acc);
+                acc = fmaf(qb.y, f2.y, acc);
+                acc = fmaf(qb.z, f3.x, acc);
+                acc = fmaf(qb.w, f3.y, acc);
             }
             sc[r * chunk + t] = __fmul_rn(acc, A.scale);
         }

@@ -11,21 +11,24 @@
 //    per row 16 bytes of scales and the chunk's codes (104 bytes of trit5, 128 of 2-bit), laid
 //    out in shared memory at a 144-byte row stride (9 x 16 B, odd: the 32 lanes' 16-byte loads
 //    of their own rows never conflict).
-//  * A task is a row block and a range of its chunks.  The CTA (up to 16 warps, one per SM)
-//    takes a contiguous range of (job, task) space; warp w takes every warps-th task of it and
-//    streams the blocks of its tasks global -> shared through a private ring of D slots with
-//    16-byte cp.async copies (consecutive lanes copy consecutive 16 bytes of a row, so every
-//    copy instruction reads whole 128-byte lines), tracked with cp.async.wait_group: no producer
-//    warp and no CTA-wide barrier inside a job.  Measured on B200, 1-D bulk (TMA) copies complete
-//    one after another per SM (~0.8 us exposed each), and a 227 KB ring cannot keep enough of
-//    them in flight while blocks are decoded; per-warp cp.async rings keep 70-150 KB in flight.
-//  * The quantised activation of the job is built once per CTA in shared memory, permuted per
-//    group into the words the decoders multiply with (read as broadcast 16-byte loads).
+//  * Row blocks are dealt to CTAs (up to 16 warps, one CTA per SM) in contiguous ranges of
+//    (job, row block) space.  A warp streams its blocks global -> shared through a private ring of
+//    D slots with 16-byte cp.async copies (each copy instruction reads 4 rows x 128 contiguous
+//    bytes), tracked with cp.async.wait_group: no producer warp.  Measured on B200, 1-D bulk (TMA)
+//    copies complete one after another per SM (~0.8 us exposed each) and a 227 KB ring cannot keep
+//    enough of them in flight while blocks are decoded; per-warp cp.async rings keep 70-150 KB in
+//    flight.
+//  * When a CTA holds fewer row blocks than warps (a single decode matvec), S warps share a row
+//    block, each taking a range of its chunks; after every round the S partial int64 sums per row
+//    are added in a fixed order through shared memory behind a named barrier (exact, no atomics).
+//  * The quantised activation of the job is built once per CTA in shared memory (x staged once,
+//    then quantised straight into the per-group permuted words the decoders multiply with, read as
+//    broadcast 16-byte loads).
 //  * Group sums are exact int32 (dp4a / dp2a).  The scale contribution (gs*m11) << (e16+B) is
-//    one int32 x int32 -> int64 multiply in the common case.  A task that covers a whole row
-//    finishes it in the lane (>> R, overflow checks, float scaling, epilogue); a row split over
-//    tasks (a single matvec too small to fill the GPU) is summed with 64-bit atomics in a
-//    self-cleaning global accumulator and finished by the last task to arrive.
+//    one int32 x int32 -> int64 multiply in the common case.  The warp that finishes a row applies
+//    >> R, the overflow checks, the float scaling and the epilogue.
+//  * Every launch is a programmatic dependent of its predecessor: the LUT is built and the first
+//    weight blocks are requested before griddepcontrol.wait; the activation is read after it.
 //  * trit5 decode: a 256-entry byte LUT (digits d0, d1, d2 and d3+3*d4 as bytes), replicated 32x
 //    (one copy per lane, so lookups never bank-conflict), addressed with one PRMT per byte.
 //    dp4a adds d0*x0+d1*x1+d2*x2+(d3+3d4)*x3; the d4 correction d4*(x4-3*x3) is a dp2a on
@@ -117,6 +120,50 @@ __device__ float block_sumsq64(const float *x, int n, float *red64) {
     return ss;
 }
 
+// Quantise x (fp32 in shared memory) straight into the permuted activation words, one warp per
+// group: each lane quantises the values of the words it writes; the group sum by a warp reduction.
+template <int KIND>
+__device__ __forceinline__ void permute_groups(const float *xs, float inv, int G, uint32_t *xp) {
+    const int lane = threadIdx.x & 31;
+    for (int g = threadIdx.x >> 5; g < G; g += blockDim.x >> 5) {
+        const float *xg = xs + g * 128;
+        if (KIND == TRX_KIND_TERNARY5) {
+            uint32_t *w = xp + g * kXwT5;
+            // Lane i < 26: byte i's activations x[5i .. 5i+4] (weights 128/129 see 0): word i, and
+            // y_i = x[5i+4] - 3*x[5i+3] for the 16-bit pairs (y[2m], y[2m+1]) of words 26 + m.
+            int q[5] = {0, 0, 0, 0, 0};
+            if (lane < 26) {
+#pragma unroll
+                for (int k = 0; k < 5; ++k) {
+                    const int l = 5 * lane + k;
+                    q[k] = l < 128 ? (int)quant_one(xg[l], inv) : 0;
+                }
+                w[lane] = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
+                          ((uint32_t)(q[3] & 0xff) << 24);
+            }
+            const int y = q[4] - 3 * q[3];
+            const int yn = __shfl_down_sync(0xffffffffu, y, 1);
+            if (lane < 28 && !(lane & 1)) w[26 + (lane >> 1)] = ((uint32_t)y & 0xffffu) | ((uint32_t)yn << 16);
+            const int sum = __reduce_add_sync(0xffffffffu, q[0] + q[1] + q[2] + q[3] + q[4]);
+            if (lane == 0) w[40] = (uint32_t)sum;
+            if (lane >= 1 && lane < 4) w[40 + lane] = 0u;
+        } else {
+            uint32_t *w = xp + g * kXw2b;
+            // Lane j = 4*wq + p: bytes x[16wq + 4b + p], b = 0..3 (the activations that meet bit
+            // pair p of code bytes 4wq .. 4wq+3).
+            const int wq = lane >> 2, p = lane & 3;
+            int q[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) q[b] = (int)quant_one(xg[16 * wq + 4 * b + p], inv);
+            w[lane] = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
+                      ((uint32_t)(q[3] & 0xff) << 24);
+            const int sum = __reduce_add_sync(0xffffffffu, q[0] + q[1] + q[2] + q[3]);
+            if (lane == 0) w[32] = (uint32_t)sum;
+            if (lane >= 1 && lane < 4) w[32 + lane] = 0u;
+        }
+    }
+}
+
 // Build the permuted int8 activation of one job in shared memory (all threads of the CTA).
 // q8: K bytes of staging, xp: G * xw words.  xs (or NULL): 4K bytes of shared staging for x, so x
 // and the norm weight are read from global memory once.  Returns e8.
@@ -137,14 +184,30 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
         __syncthreads();
         float r = 0.f;
         if (nw) {
-            if (ct < 64) {  // partial j: x[j]^2 + x[j+64]^2 + ... in index order (model/mirror.py:576-591)
-                float p = 0.f;
-                for (int i = ct; i < K; i += 64) p = __fadd_rn(p, __fmul_rn(xs[i], xs[i]));
-                red64[ct] = p;
-            }
-            __syncthreads();
-            if (ct < 32) {  // the halving tree: red[j] + red[j+32], then 16, 8, ... in one warp
-                float a = __fadd_rn(red64[ct], red64[ct + 32]);
+            if (ct < 32) {
+                // Lane j runs partials j and j+32 (x[j]^2 + x[j+64]^2 + ... in index order,
+                // model/mirror.py:576-591) side by side, loads ahead of the ordered adds, then the
+                // halving tree red[j] + red[j+32], 16, 8, ... in the same warp.
+                float p0 = 0.f, p1 = 0.f;
+                int i = ct;
+                for (; i + 3 * 64 + 32 < K; i += 4 * 64) {
+                    float v0[4], v1[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        v0[u] = xs[i + u * 64];
+                        v1[u] = xs[i + u * 64 + 32];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        p0 = __fadd_rn(p0, __fmul_rn(v0[u], v0[u]));
+                        p1 = __fadd_rn(p1, __fmul_rn(v1[u], v1[u]));
+                    }
+                }
+                for (; i < K; i += 64) {
+                    p0 = __fadd_rn(p0, __fmul_rn(xs[i], xs[i]));
+                    if (i + 32 < K) p1 = __fadd_rn(p1, __fmul_rn(xs[i + 32], xs[i + 32]));
+                }
+                float a = __fadd_rn(p0, p1);
                 for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
                 if (ct == 0) red64[0] = a;
             }
@@ -167,16 +230,16 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
             m = a > m ? a : m;
         }
         m = __reduce_max_sync(0xffffffffu, m);
-        if ((ct & 31) == 0) atomicMax(amax_s, m);
+        uint32_t *const wmax = reinterpret_cast<uint32_t *>(red64) + 32;  // per-warp maxima
+        if ((ct & 31) == 0) wmax[ct >> 5] = m;
         __syncthreads();
-        const uint32_t amax = *amax_s;
-        if (amax == 0u) {
-            for (int k = ct; k < K; k += nt) q8[k] = 0;
-        } else {
-            e8 = frexp_exp(__uint_as_float(amax)) - 7;
-            const float inv = pow2f(-e8);
-            for (int k = ct; k < K; k += nt) q8[k] = quant_one(xs[k], inv);
-        }
+        uint32_t amax = 0u;
+        for (int w = 0; w < (nt >> 5); ++w) amax = max(amax, wmax[w]);
+        e8 = amax ? frexp_exp(__uint_as_float(amax)) - 7 : 0;
+        const float inv = amax ? pow2f(-e8) : 0.f;  // all-zero x: every q is 0
+        permute_groups<KIND>(xs, inv, K / 128, xp);
+        __syncthreads();
+        return e8;
     } else {
         float r = 0.f;
         if (nw) {
@@ -593,8 +656,13 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
 
     if (KIND == TRX_KIND_TERNARY5) {  // the trit5 LUT: entry b at b*256, one replica per lane
         (void)lut_g;
-        for (int b = warp; b < 256; b += blockDim.x >> 5)
-            reinterpret_cast<uint32_t *>(lut + b * 256)[lane] = trit5_lut_entry((uint32_t)b);
+        // The 256 entries once (in lane 0's replica words), then every lane copies them into its
+        // own replica: each store instruction writes 32 distinct banks.
+        uint32_t *lw = reinterpret_cast<uint32_t *>(lut);
+        for (int b = tid; b < 256; b += blockDim.x) lw[b * 64] = trit5_lut_entry((uint32_t)b);
+        __syncthreads();
+        if (lane)
+            for (int b = warp; b < 256; b += blockDim.x >> 5) lw[b * 64 + lane] = lw[b * 64];
     }
     const uint32_t lane4x = 0x10000u | ((uint32_t)lane * 4u);
     const ScaleFast F2 = scale_fast(J.B2);
