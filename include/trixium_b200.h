@@ -203,10 +203,12 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const floa
  * belongs to another framework).  No counterpart in the reference.  Same computation and
  * arguments as trx_attn_decode; the partials and arrival counts live in the library's static
  * device arrays (limits: n_kv <= 64 and n_kv * splits * (H/n_kv) * (head_dim + 2) floats <= 2^20,
- * splits = ceil(max_pos / (max_pos <= 2048 ? 64 : 128)); larger shapes return
- * TRX_ERR_UNSUPPORTED), so the library allocates nothing.  Device error bits are OR'd into *d_err
- * (a caller-owned device word).  The first call on a device sets the arrays up and should come
- * before any other work on that device's streams; calls that overlap in time race on the arrays.
+ * splits = ceil(max_pos / chunk) with chunk the smallest of 64, 128, 256 (128 when head_dim >
+ * 128) giving at most 16 splits; larger shapes return TRX_ERR_UNSUPPORTED), so the library
+ * allocates nothing.  Device error bits are OR'd into *d_err (a caller-owned device word).  The
+ * first call on a device sets the arrays up (and waits for the device), so it should come before
+ * any stream capture and before other work on that device's streams; calls that overlap on the
+ * GPU race on the arrays.
  */
 trx_status trx_attn_decode_static(const trx_attn_shape *shape, const float *d_q, const float *d_k,
                                   const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,

@@ -199,46 +199,61 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
     __threadfence();
     const int ns = pos / chunk + 1;
     const float *pk = A.part + (size_t)kh * A.nsplit * rep * (hd + 2);
-    // Chunk weights per head: w_j = e^(m_j - M) / sum_j e^(m_j - M) l_j, staged in shared memory
-    // (reusing the score area: rep * chunk >= rep * ns floats... ns may exceed chunk, so use kt).
-    float *wts = reinterpret_cast<float *>(smem);  // [rep][ns], the K tile is no longer needed
+    // Chunk maxima and sums of every head, staged in shared memory with all their loads in flight
+    // at once (the K and V tiles are no longer needed): wm[rep][ns], wl[rep][ns].
+    float *wm = reinterpret_cast<float *>(smem);
+    float *wl = wm + rep * ns;
     for (int i = tid; i < rep * ns; i += kAttnThreads) {
         const int r = i / ns, j = i - r * ns;
-        wts[i] = __ldcg(pk + (size_t)(j * rep + r) * (hd + 2));
+        const float *pj = pk + (size_t)(j * rep + r) * (hd + 2);
+        wm[i] = __ldcg(pj);
+        wl[i] = __ldcg(pj + 1);
     }
     __syncthreads();
+    // Weights per head: w_j = e^(m_j - M) / sum_j e^(m_j - M) l_j (one reciprocal per head).
     for (int r = warp; r < rep; r += kAttnWarps) {
         float M = -INFINITY;
-        for (int j = lane; j < ns; j += 32) M = fmaxf(M, wts[r * ns + j]);
+        for (int j = lane; j < ns; j += 32) M = fmaxf(M, wm[r * ns + j]);
         for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float L = 0.f;
         for (int j = lane; j < ns; j += 32) {
-            const float w = expf(__fsub_rn(wts[r * ns + j], M));
-            wts[r * ns + j] = w;
-            L = fmaf(w, __ldcg(pk + (size_t)(j * rep + r) * (hd + 2) + 1), L);
+            const float w = expf(__fsub_rn(wm[r * ns + j], M));
+            wm[r * ns + j] = w;
+            L = fmaf(w, wl[r * ns + j], L);
         }
         for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float inv = __fdiv_rn(1.0f, L);  // one reciprocal per head
+        const float inv = __fdiv_rn(1.0f, L);
         __syncwarp();
-        for (int j = lane; j < ns; j += 32) wts[r * ns + j] = __fmul_rn(wts[r * ns + j], inv);
+        for (int j = lane; j < ns; j += 32) wm[r * ns + j] = __fmul_rn(wm[r * ns + j], inv);
     }
     __syncthreads();
     for (int i = tid; i < rep * hd; i += kAttnThreads) {
         const int r = i / hd, d = i - r * hd;
-        const float *w = wts + r * ns;
+        const float *w = wm + r * ns;
         const float *pd = pk + (size_t)r * (hd + 2) + 2 + d;
         const size_t step = (size_t)rep * (hd + 2);
         float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
         int j = 0;
-        for (; j + 4 <= ns; j += 4) {  // four independent L2 loads in flight
-            const float a0 = __ldcg(pd + j * step), a1 = __ldcg(pd + (j + 1) * step);
-            const float a2 = __ldcg(pd + (j + 2) * step), a3 = __ldcg(pd + (j + 3) * step);
-            O0 = fmaf(w[j], a0, O0);
-            O1 = fmaf(w[j + 1], a1, O1);
-            O2 = fmaf(w[j + 2], a2, O2);
-            O3 = fmaf(w[j + 3], a3, O3);
+        for (; j + 16 <= ns; j += 16) {  // sixteen independent L2 loads in flight
+            float a[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) a[u] = __ldcg(pd + (j + u) * step);
+#pragma unroll
+            for (int u = 0; u < 16; u += 4) {
+                O0 = fmaf(w[j + u], a[u], O0);
+                O1 = fmaf(w[j + u + 1], a[u + 1], O1);
+                O2 = fmaf(w[j + u + 2], a[u + 2], O2);
+                O3 = fmaf(w[j + u + 3], a[u + 3], O3);
+            }
         }
-        for (; j < ns; ++j) O0 = fmaf(w[j], __ldcg(pd + j * step), O0);
+        {
+            float a[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) a[u] = j + u < ns ? __ldcg(pd + (j + u) * step) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (j + u < ns) O0 = fmaf(w[j + u], a[u], O0);
+        }
         float o = (O0 + O1) + (O2 + O3);
         const int h = kh * rep + r;
         if (A.gated) {
@@ -248,6 +263,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
         A.out[(size_t)h * hd + d] = o;
     }
     if (tid == 0) A.cnt[kh] = 0u;
+}
+
+// Positions per CTA: the smallest of 64, 128, 256 that keeps the splits per kv head at 16 or fewer
+// (fewer partials to merge), capped so two staged tiles fit in shared memory.
+int attn_chunk(int max_pos, int hd) {
+    const int cap = hd <= 128 ? 256 : 128;
+    int chunk = 64;
+    while (chunk < cap && (max_pos + chunk - 1) / chunk > 16) chunk *= 2;
+    return chunk;
 }
 
 size_t attn_smem_bytes(int hd, int rep, int chunk) {
@@ -342,7 +366,7 @@ extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const flo
     A.gated = sh->gated ? 1 : 0;
     A.qstride = (int)hd * (A.gated ? 2 : 1);
     A.max_pos = (int)sh->max_pos;
-    A.chunk = sh->max_pos <= 2048 ? 64 : 128;
+    A.chunk = trx::attn_chunk((int)sh->max_pos, (int)hd);
     A.nsplit = (A.max_pos + A.chunk - 1) / A.chunk;
     A.eps = sh->eps;
     A.scale = 1.0f / sqrtf((float)hd);
@@ -351,7 +375,7 @@ extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const flo
     if (Hkv > trx::kStaticMaxKv || (uint64_t)Hkv * A.nsplit * rep * (hd + 2) > trx::kStaticPartFloats)
         return TRX_ERR_UNSUPPORTED;
     if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u ||
-        (uint64_t)rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))
+        2ull * rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))
         return TRX_ERR_UNSUPPORTED;
     trx::StaticScratch sc;
     const trx_status st = trx::static_scratch(sc);

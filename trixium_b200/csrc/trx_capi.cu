@@ -331,13 +331,15 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *
     A.gated = sh->gated ? 1 : 0;
     A.qstride = (int)hd * (A.gated ? 2 : 1);
     A.max_pos = (int)sh->max_pos;
-    A.chunk = sh->max_pos <= 2048 ? 64 : 128;
+    A.chunk = trx::attn_chunk(A.max_pos, A.hd);
     A.nsplit = (A.max_pos + A.chunk - 1) / A.chunk;
     A.eps = sh->eps;
     A.scale = 1.0f / sqrtf((float)hd);
     const uint32_t rep = H / Hkv;
     if ((uint64_t)Hkv * A.nsplit * rep * (hd + 2) > kAttnPartFloats) return TRX_ERR_UNSUPPORTED;
-    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u) return TRX_ERR_UNSUPPORTED;
+    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u ||
+        2ull * rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))  // the merge stages 2 floats per partial
+        return TRX_ERR_UNSUPPORTED;
     A.q = d_q;
     A.k = d_k;
     A.v = d_v;

@@ -106,6 +106,7 @@ struct DnArgs {
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
 size_t attn_smem_bytes(int hd, int rep, int chunk);
+int attn_chunk(int max_pos, int hd);
 
 trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
                         cudaStream_t st);
