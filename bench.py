@@ -359,6 +359,8 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if world > 1 and not args.no_decode:
+        out["decode"] = {"qwen3-8b": tp_decode_leg(ctx, "qwen3-8b", 1024, 64, 5, rank, world, dev)}
     if world == 1 and not args.no_decode:
         # The metric's second half: 8B-shape batch-1 decode tok/s (config 2), and config 1.
         out["decode"] = {"qwen3-8b": decode_leg(ctx, "qwen3-8b", 1024, 128, 8),
@@ -410,6 +412,50 @@ def decode_leg(ctx, name, ctx_len, n_tokens, warmup):
            "weight_GBps": round(wb / (ms * 1e-3) / 1e9, 1), "launches_per_token": dec.launches_per_step(),
            "distinct_tokens": len(set(toks))}
     del dec, w
+    torch.cuda.empty_cache()
+    return out
+
+
+def tp_decode_leg(ctx, name, ctx_len, n_tokens, warmup, rank, world, dev):
+    """Tensor-parallel batch-1 decode tok/s over `world` GPUs (trixium_b200.tp): every rank draws the
+    same synthetic image and keeps its row shard; one CUDA graph per token holds the kernels and
+    the NCCL all-gathers; the time is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from trixium_b200 import decoder as D, tp
+    cfg = D.CONFIGS[name]
+    full = D.SyntheticWeights(cfg, seed=0)
+    dec = tp.TPDecoder(tp.TPWeights(full, rank, world), ctx=ctx, max_pos=ctx_len + n_tokens + warmup + 8)
+    del full
+    torch.cuda.empty_cache()
+    dec.set_states(1)
+    dec.fill_context(ctx_len)
+    dec.tok.fill_(7)
+    dec.capture()
+    for _ in range(warmup):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    dec.fill_context(ctx_len)
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n_tokens):
+        dec.graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / n_tokens], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ctx.raise_on_error()
+    dec.release()
+    wb = cfg.weight_bytes_per_token()
+    out = {"config": name, "kind": "trit5" if cfg.kind == 5 else "2-bit", "context": ctx_len, "batch": 1,
+           "tensor_parallel": world, "scaling": "strong", "tokens_timed": n_tokens, "ms_per_token": round(ms, 4),
+           "tok_s": round(1000.0 / ms, 1), "weight_bytes_per_token": wb,
+           "weight_GBps_all_gpus": round(wb / (ms * 1e-3) / 1e9, 1),
+           "collectives_per_token": dec.collectives_per_step()}
+    del dec
     torch.cuda.empty_cache()
     return out
 

@@ -168,6 +168,19 @@ trx_status trx_lmhead_argmax(trx_ctx *ctx, const trx_entry *e, const void *d_pac
                              const float *d_norm_w, float eps, float *d_logits, int32_t *d_token,
                              cudaStream_t stream);
 
+/*
+ * One shard of a row-sharded LM head (tensor parallelism): as trx_lmhead_argmax, but writes the
+ * shard's argmax key to *d_key (one uint64 on the device: the orderable float bits of the largest
+ * logit in the high word, ~(row + row_offset) in the low word, so the largest key over all shards
+ * is the global greedy token with ties to the smallest row).  row_offset: the shard's first row.
+ */
+trx_status trx_lmhead_argmax_key(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                                 const float *d_norm_w, float eps, uint32_t row_offset, float *d_logits,
+                                 uint64_t *d_key, cudaStream_t stream);
+
+/* *d_token = the row of the largest of the n keys at d_keys (gathered shard keys). */
+trx_status trx_argmax_token(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token, cudaStream_t stream);
+
 /* Shape of one attention layer (model/configs.py head counts; mirror.py:945-996). */
 typedef struct trx_attn_shape {
     uint32_t n_head;     /* query heads H                                              */

@@ -23,7 +23,7 @@ SYMBOLS = (
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
     "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
     "trx_deltanet_step", "trx_lmhead_argmax", "trx_matvec_f_multi", "trx_embed_lookup", "trx_advance_position",
-    "trx_attn_decode_static",
+    "trx_attn_decode_static", "trx_lmhead_argmax_key", "trx_argmax_token",
 )
 
 
@@ -97,6 +97,9 @@ def lib():
                                  ctypes.c_int),
             "trx_advance_position": ([_vp, _vp, ctypes.c_int32, _vp], ctypes.c_int),
             "trx_attn_decode_static": ([ctypes.POINTER(AttnShape)] + [_vp] * 12, ctypes.c_int),
+            "trx_lmhead_argmax_key": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, ctypes.c_uint32, _vp, _vp, _vp],
+                                      ctypes.c_int),
+            "trx_argmax_token": ([_vp, _vp, ctypes.c_int32, _vp, _vp], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

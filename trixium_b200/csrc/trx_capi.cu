@@ -311,6 +311,32 @@ trx_status trx_lmhead_argmax(trx_ctx *ctx, const trx_entry *e, const void *d_pac
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
 
+trx_status trx_lmhead_argmax_key(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                                 const float *d_norm_w, float eps, uint32_t row_offset, float *d_logits,
+                                 uint64_t *d_key, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_key || !aligned16(d_packed) || (uint64_t)row_offset + e->rows > 0xffffffffull)
+        return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
+    J.x = d_x;
+    J.norm_w = d_norm_w;
+    J.eps = eps;
+    J.seg[0].y = d_logits;
+    J.out = trx::OUT_F32;
+    J.argmax = ctx->amax_key;
+    J.key_out = reinterpret_cast<unsigned long long *>(d_key);
+    J.row_offset = (int)row_offset;
+    J.arg_cnt = ctx->amax_cnt;
+    return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_argmax_token(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token, cudaStream_t stream) {
+    if (!ctx || !d_keys || !d_token || n < 1) return TRX_ERR_ARG;
+    return trx::launch_argmax_keys(reinterpret_cast<const unsigned long long *>(d_keys), n, d_token, stream);
+}
+
 trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
                            const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
                            const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,

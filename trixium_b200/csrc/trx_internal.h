@@ -65,6 +65,8 @@ struct MvJobs {
     unsigned long long *argmax;  // if set: greedy argmax key of the float results (see below)
     int *token;                  // if set (with argmax): per job, the argmax row; the keys and
     unsigned *arg_cnt;           // the arrival count arg_cnt are left at zero again
+    unsigned long long *key_out; // if set (with argmax): per job, the argmax key itself (row + row_offset)
+    int row_offset;              // added to the row in the argmax key (a shard's first global row)
     const int *skip;             // if set and *skip != 0, the launch does nothing
 };
 
@@ -111,6 +113,7 @@ int attn_chunk(int max_pos, int hd);
 trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
                         cudaStream_t st);
 trx_status launch_advance(int *pos, int n, cudaStream_t st);
+trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, cudaStream_t st);
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);

@@ -495,7 +495,7 @@ __device__ __forceinline__ unsigned long long finish_row(const MvJobs &J, const 
         float v = __fmul_rn((float)(int)(a >> o.R), o.sc);
         if (o.resid) v = __fadd_rn(o.resid[srow], v);
         if (o.y) reinterpret_cast<float *>(o.y)[srow] = v;
-        if (J.argmax) key = argmax_key(v, (uint32_t)row);
+        if (J.argmax) key = argmax_key(v, (uint32_t)(row + J.row_offset));
     } else {  // OUT_SWIGLU
         bad = bad || acc_bad(a2, o.R2);
         const float gv = __fmul_rn((float)(int)(a >> o.R), o.sc);
@@ -798,7 +798,7 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         __syncwarp();
         if (J.argmax) argmax_commit(J, job, best, lane);
     }
-    if (J.token) {  // greedy tokens: the last CTA to arrive turns each job's key into its row
+    if (J.token || J.key_out) {  // greedy tokens: the last CTA to arrive hands out each job's key
         __syncthreads();
         if (tid == 0) {
             __threadfence();
@@ -809,7 +809,8 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
             __threadfence();
             for (int j = tid; j < J.njobs; j += blockDim.x) {
                 const unsigned long long k = atomicExch(J.argmax + j, 0ull);
-                J.token[j] = k ? (int)(0xffffffffu - (uint32_t)k) : -1;
+                if (J.token) J.token[j] = k ? (int)(0xffffffffu - (uint32_t)k) : -1;
+                if (J.key_out) J.key_out[j] = k;
             }
             if (tid == 0) *J.arg_cnt = 0u;
         }

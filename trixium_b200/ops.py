@@ -266,6 +266,26 @@ def lmhead_argmax(ctx, w: DeviceTensor, x, token=None, logits=None, norm_w=None,
     return token
 
 
+def lmhead_argmax_key(ctx, w: DeviceTensor, x, key, row_offset=0, logits=None, norm_w=None, eps=1e-6):
+    """One shard of a row-sharded LM head: key (int64 device tensor of one element) = the shard's
+    argmax key with global row = local row + row_offset (trx_lmhead_argmax_key)."""
+    _need(x, torch.float32, "x")
+    _need(key, torch.int64, "key")
+    _lib.check(_lib.lib().trx_lmhead_argmax_key(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(norm_w),
+                                                ctypes.c_float(eps), int(row_offset), _ptr(logits), _ptr(key),
+                                                _stream()), "trx_lmhead_argmax_key")
+    return key
+
+
+def argmax_token(ctx, keys, token):
+    """token = the row of the largest key in `keys` (int64 device tensor of gathered shard keys)."""
+    _need(keys, torch.int64, "keys")
+    _need(token, torch.int32, "token")
+    _lib.check(_lib.lib().trx_argmax_token(ctx.h, _ptr(keys), keys.numel(), _ptr(token), _stream()),
+               "trx_argmax_token")
+    return token
+
+
 def deltanet_shape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel=4, eps=1e-6):
     return _lib.DeltaNetShape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel, eps)
 
@@ -291,5 +311,5 @@ def row_bytes(cols, kind):
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
            "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_decode_static", "attn_shape",
-           "deltanet_shape", "deltanet_step", "lmhead_argmax", "matvec_f_multi", "embed_lookup",
+           "deltanet_shape", "deltanet_step", "lmhead_argmax", "lmhead_argmax_key", "argmax_token", "matvec_f_multi", "embed_lookup",
            "advance_position", "row_bytes", "L"]

@@ -1,0 +1,306 @@
+"""Tensor-parallel batch-1 decoding over N GPUs of one node (one process per GPU, NCCL).
+
+Every weight matrix is sharded by output rows (the reference's channel sharding,
+model/layout.py:219-223). After each projection the ranks all-gather the output vector, so
+every rank computes whole rows from the complete, identically quantised input, and the results
+are bit-identical to one GPU. Splitting K instead would quantise each slice with its own exponent.
+
+Per layer:
+- **Attention:** rank r owns kv heads [r*Hkv/N, (r+1)*Hkv/N) and their query heads: the rows of
+  q/k/v, the KV cache and the attention of those heads are local. The head outputs are
+  all-gathered in head order, then o-proj rows, residual and all-gather of x.
+- **DeltaNet:** rank r owns key heads [r*nk/N, (r+1)*nk/N) and the value heads h with h % nk among
+  them, renumbered locally so the kernel's tiled head map holds. Their grouped outputs
+  (mirror.py:941-942) form one contiguous block of the layer output, all-gathered in rank order.
+- **FFN:** gate/up rows, SwiGLU, all-gather of the activation, down rows, residual, all-gather x.
+- **LM head:** vocabulary rows. Each rank's argmax key carries the global row; the keys are
+  all-gathered and the largest one is the token (ties to the smallest row).
+
+The plan functions below are pure index arithmetic, shared by the GPU engine (`TPDecoder`) and
+the CPU tests that run the oracle sharded over gloo ranks.
+"""
+
+import numpy as np
+
+
+def span(total, rank, world):
+    """Rows [a, b) of `rank` in an even split of `total` (which `world` must divide)."""
+    if total % world:
+        raise ValueError(f"{total} rows do not split evenly over {world} ranks")
+    n = total // world
+    return rank * n, (rank + 1) * n
+
+
+class AttnShard:
+    """Rows of one rank's attention-layer shard (query rows per head: hd, or 2*hd when gated)."""
+
+    def __init__(self, cfg, rank, world):
+        H, Hkv, hd = cfg.n_head, cfg.n_kv, cfg.head_dim
+        if Hkv % world:
+            raise ValueError(f"{Hkv} kv heads do not split over {world} ranks")
+        rep = H // Hkv
+        self.kv0, self.kv1 = span(Hkv, rank, world)
+        self.n_kv = self.kv1 - self.kv0
+        self.n_head = self.n_kv * rep
+        qh = hd * (2 if cfg.attn_gated else 1)
+        self.q_rows = np.arange(self.kv0 * rep * qh, self.kv1 * rep * qh)
+        self.k_rows = np.arange(self.kv0 * hd, self.kv1 * hd)
+        self.v_rows = self.k_rows.copy()
+
+
+class DeltaNetShard:
+    """Channels and value heads of one rank's DeltaNet-layer shard.
+
+    Local value head h' = (kh - k0) + m * nk' holds global head h = kh + m * nk (kh a local key
+    head, m < nv/nk), so the kernel's map h' % nk' = kh - k0 is the global map h % nk = kh."""
+
+    def __init__(self, cfg, rank, world):
+        nk, hk, nv, hv = cfg.dn_nk, cfg.dn_hk, cfg.dn_nv, cfg.dn_hv
+        if nk % world:
+            raise ValueError(f"{nk} key heads do not split over {world} ranks")
+        rep = nv // nk
+        self.k0, self.k1 = span(nk, rank, world)
+        self.nk = self.k1 - self.k0
+        self.nv = self.nk * rep
+        nq = nk * hk
+        # Global value head of each local value head h' = (kh - k0) + m * nk'.
+        self.heads = np.array([self.k0 + (hl % self.nk) + (hl // self.nk) * nk for hl in range(self.nv)])
+        q = np.arange(self.k0 * hk, self.k1 * hk)
+        k = nq + q
+        v = np.concatenate([2 * nq + h * hv + np.arange(hv) for h in self.heads])
+        self.channels = np.concatenate([q, k, v])             # qkv rows, conv taps, ring channels
+        self.z_rows = np.concatenate([h * hv + np.arange(hv) for h in self.heads])
+        self.head_rows = self.heads.copy()                      # beta, alpha, dt_bias, a
+        # The local grouped output is the global block [k0*rep*hv, k1*rep*hv).
+        self.out0, self.out1 = self.k0 * rep * hv, self.k1 * rep * hv
+
+
+# Shards of a device image -------------------------------------------------------------------------
+
+def _slice_rows(dt, rows):
+    """A DeviceTensor of the given rows (an index array) of `dt`, with dt's B and R."""
+    import torch
+    from . import ops
+    from . import layout as L
+    rb = L.row_bytes(dt.cols, dt.kind)
+    idx = torch.as_tensor(np.asarray(rows), dtype=torch.long, device=dt.data.device)
+    data = dt.data.view(dt.rows, rb).index_select(0, idx).contiguous().view(-1)
+    return ops.DeviceTensor.from_packed(data, len(rows), dt.cols, dt.kind, dt.bias, dt.rshift)
+
+
+class ShardPacked:
+    """Row subsets of the segments of a decoder.Packed, back to back (one segmented launch)."""
+
+    def __init__(self, packed, seg_rows):
+        import torch
+        from . import _lib
+        parts, self.entries, self.rows = [], [], []
+        for i, rows in enumerate(seg_rows):
+            t = _slice_rows(packed.tensor(i), rows)
+            parts.append(t.data)
+            self.entries.append(_lib.Entry(len(rows), t.cols, t.kind, t.bias, t.rshift))
+            self.rows.append(len(rows))
+        self.data = torch.cat(parts)
+        self.cols, self.kind = packed.cols, packed.kind
+
+
+class TPWeights:
+    """One rank's shard of a decoder.SyntheticWeights (every rank draws the same seeded image and
+    keeps its rows; the B/R of each tensor are the full tensor's)."""
+
+    def __init__(self, full, rank, world):
+        import torch
+        cfg = self.cfg = full.cfg
+        self.rank, self.world = rank, world
+        E, F, V = cfg.hidden, cfg.ffn, cfg.vocab
+        self.e0, self.e1 = span(E, rank, world)
+        self.f0, self.f1 = span(F, rank, world)
+        self.v0, self.v1 = span(V, rank, world)
+        er = np.arange(self.e0, self.e1)
+        fr = np.arange(self.f0, self.f1)
+        self.emb, self.out_norm, self.rope_freq = full.emb, full.out_norm, full.rope_freq
+        self.lm_head = _slice_rows(full.lm_head, np.arange(self.v0, self.v1))
+        self.layers = []
+        for l, lw in enumerate(full.layers):
+            w = {"attn_norm": lw["attn_norm"], "ffn_norm": lw["ffn_norm"],
+                 "gate": _slice_rows(lw["gate"], fr), "up": _slice_rows(lw["up"], fr),
+                 "down": _slice_rows(lw["down"], er), "out": _slice_rows(lw["out"], er)}
+            if cfg.layer_type(l) == "d":
+                sh = w["shard"] = DeltaNetShard(cfg, rank, world)
+                w["in"] = ShardPacked(lw["in"], [sh.channels, sh.z_rows, sh.head_rows, sh.head_rows])
+                idx = lambda t, rows: t.index_select(0, torch.as_tensor(rows, device=t.device)).contiguous()
+                w["conv_w"] = idx(lw["conv_w"], sh.channels)
+                w["ssm_a"] = idx(lw["ssm_a"], sh.heads)
+                w["dt_bias"] = idx(lw["dt_bias"], sh.heads)
+                w["ssm_norm"] = lw["ssm_norm"]
+            else:
+                sh = w["shard"] = AttnShard(cfg, rank, world)
+                w["in"] = ShardPacked(lw["in"], [sh.q_rows, sh.k_rows, sh.v_rows])
+                w["q_norm"], w["k_norm"] = lw["q_norm"], lw["k_norm"]
+            self.layers.append(w)
+
+
+# The tensor-parallel decoder ----------------------------------------------------------------------
+
+class TPDecoder:
+    """Greedy batch-1 decoding of a TPWeights shard; every rank runs the same steps in the same order
+    (the all-gathers are NCCL collectives on `group`, captured with the kernels in one CUDA graph)."""
+
+    def __init__(self, weights: TPWeights, group=None, ctx=None, max_pos=4096):
+        import torch
+        from . import ops
+        cfg = self.cfg = weights.cfg
+        self.w, self.group = weights, group
+        self.ctx = ctx or ops.default_context()
+        self.rank, self.world = weights.rank, weights.world
+        dev = weights.emb.device
+        f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)
+        E, F, N = cfg.hidden, cfg.ffn, self.world
+        self.x, self.x_loc = f32(E), f32(E // N)
+        self.act, self.act_loc = f32(F), f32(F // N)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.key = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.keys = torch.zeros(N, dtype=torch.int64, device=dev)
+        self.max_pos = max_pos
+        self.kc, self.vc, self.ring, self.state = {}, {}, {}, {}
+        a_sh = d_sh = None
+        for l, lw in enumerate(weights.layers):
+            sh = lw["shard"]
+            if cfg.layer_type(l) == "d":
+                d_sh = sh
+                C = len(sh.channels)
+                self.ring[l] = torch.zeros(cfg.dn_conv, C, device=dev)
+                self.state[l] = torch.zeros(sh.nv, cfg.dn_hv, cfg.dn_hk, device=dev)
+            else:
+                a_sh = sh
+                self.kc[l] = torch.zeros(max_pos, sh.n_kv, cfg.head_dim, dtype=torch.float16, device=dev)
+                self.vc[l] = torch.zeros_like(self.kc[l])
+        if a_sh is not None:
+            self.attn_shape = ops.attn_shape(a_sh.n_head, a_sh.n_kv, cfg.head_dim, max_pos,
+                                             rope_dims=cfg.rope_dims or cfg.head_dim, gated=cfg.attn_gated,
+                                             eps=cfg.eps)
+            self.q, self.k, self.v = f32(len(a_sh.q_rows)), f32(len(a_sh.k_rows)), f32(len(a_sh.v_rows))
+            self.attn_loc = f32(a_sh.n_head * cfg.head_dim)
+            self.attn = f32(cfg.n_head * cfg.head_dim)
+        if d_sh is not None:
+            self.dn_shape = ops.deltanet_shape(d_sh.nk, cfg.dn_hk, d_sh.nv, cfg.dn_hv, cfg.dn_conv, cfg.eps)
+            self.qkv, self.z = f32(len(d_sh.channels)), f32(d_sh.nv * cfg.dn_hv)
+            self.beta, self.alpha = f32(d_sh.nv), f32(d_sh.nv)
+            self.og_loc, self.og = f32(d_sh.nv * cfg.dn_hv), f32(cfg.dn_nv * cfg.dn_hv)
+        self.graph = None
+
+    def _gather(self, out, inp):
+        import torch.distributed as dist
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_gather_into_tensor(out, inp, group=self.group)
+
+    def set_states(self, seed=0):
+        """The global DeltaNet states ~N(0,1)/sqrt(hk) of Decoder.set_states, this rank's heads."""
+        import math
+        import torch
+        g = torch.Generator(device=self.tok.device)
+        g.manual_seed(seed)
+        cfg = self.cfg
+        for l, t in sorted(self.state.items()):
+            full = torch.randn((cfg.dn_nv, cfg.dn_hv, cfg.dn_hk), generator=g, device=t.device) / math.sqrt(cfg.dn_hk)
+            heads = torch.as_tensor(self.w.layers[l]["shard"].heads, device=t.device)
+            t.copy_(full.index_select(0, heads))
+
+    def fill_context(self, n, seed=0):
+        """Synthetic context of n positions (random fp16 K/V rows of this rank's heads), position n."""
+        import torch
+        g = torch.Generator(device=self.tok.device)
+        g.manual_seed(seed + self.rank)
+        for l in self.kc:
+            self.kc[l][:n] = torch.randn(self.kc[l][:n].shape, generator=g, device=self.tok.device).half()
+            self.vc[l][:n] = torch.randn(self.vc[l][:n].shape, generator=g, device=self.tok.device).half()
+        self.pos.fill_(n)
+
+    def enqueue_step(self):
+        """One token on every rank: reads self.tok and self.pos, writes the next token (the same on
+        every rank) and advances the position."""
+        from . import ops
+        cfg, w, ctx = self.cfg, self.w, self.ctx
+        xr = self.x[w.e0:w.e1]  # this rank's rows of the residual stream
+        ops.embed_lookup(ctx, w.emb, self.tok, self.x)
+        for l, lw in enumerate(w.layers):
+            p = lw["in"]
+            if cfg.layer_type(l) == "d":
+                ops.matvec_f_multi(ctx, p.entries, p.data, self.x, [self.qkv, self.z, self.beta, self.alpha],
+                                   norm_w=lw["attn_norm"], eps=cfg.eps)
+                ops.deltanet_step(ctx, self.dn_shape, self.qkv, self.z, self.beta, self.alpha, lw["dt_bias"],
+                                  lw["ssm_a"], lw["conv_w"], lw["ssm_norm"], self.ring[l], self.state[l], self.pos,
+                                  self.og_loc)
+                self._gather(self.og, self.og_loc)
+                ops.matvec_f(ctx, lw["out"], self.og, y=self.x_loc, resid=xr)
+            else:
+                ops.matvec_f_multi(ctx, p.entries, p.data, self.x, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
+                                   eps=cfg.eps)
+                ops.attn_decode(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"], w.rope_freq,
+                                self.kc[l], self.vc[l], self.pos, self.attn_loc)
+                self._gather(self.attn, self.attn_loc)
+                ops.matvec_f(ctx, lw["out"], self.attn, y=self.x_loc, resid=xr)
+            self._gather(self.x, self.x_loc)
+            ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x, act=self.act_loc, norm_w=lw["ffn_norm"], eps=cfg.eps)
+            self._gather(self.act, self.act_loc)
+            ops.matvec_f(ctx, lw["down"], self.act, y=self.x_loc, resid=xr)
+            self._gather(self.x, self.x_loc)
+        ops.lmhead_argmax_key(ctx, w.lm_head, self.x, self.key, row_offset=w.v0, norm_w=w.out_norm, eps=cfg.eps)
+        self._gather(self.keys, self.key)
+        ops.argmax_token(ctx, self.keys, self.tok)
+        ops.advance_position(ctx, self.pos)
+
+    def collectives_per_step(self):
+        return 4 * self.cfg.n_layer + 1
+
+    def _mutable(self):
+        return [self.tok, self.pos] + list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + \
+            list(self.state.values())
+
+    def capture(self):
+        """One step as a CUDA graph on every rank (NCCL collectives captured with the kernels)."""
+        import torch
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        live = self._mutable()
+        saved = [t.clone() for t in live]
+        with torch.cuda.stream(s):
+            self.enqueue_step()          # warm-up outside the capture, then every buffer restored
+            torch.cuda.synchronize()
+        for t, c in zip(live, saved):
+            t.copy_(c)
+        del saved
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(self.graph, stream=s):
+                self.enqueue_step()
+        torch.cuda.synchronize()
+        return self.graph
+
+    def release(self):
+        """Drop the captured graph (it holds NCCL work: release it before destroying the group)."""
+        self.graph = None
+
+    def step(self, token=None):
+        if token is not None:
+            self.tok.fill_(int(token))
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.enqueue_step()
+
+    def generate(self, prompt, n_new):
+        """Greedy decode as decoder.Decoder.generate (mirror.py:1036-1044), the same on every rank."""
+        import torch
+        for t in prompt:
+            self.step(t)
+        out = torch.empty(n_new, dtype=torch.int32, device=self.tok.device)
+        for i in range(n_new):
+            out[i:i + 1].copy_(self.tok)
+            if i + 1 < n_new:
+                self.step()
+        self.ctx.raise_on_error()
+        return out.cpu().tolist()
