@@ -76,10 +76,29 @@ struct MvGeom {
     int fixed;    // bytes of activation words and reductions (128-byte rounded): rings A start here
     int na;       // warps whose ring lies in region A (the rest: region C, after the trit5 LUT)
     int q8c;      // the quantiser's staging lies in region C
+    int xfast;    // float x takes the cp.async-staged prologue (build_activation_cp)
     int stage;    // bytes of that staging region
     int base;     // shared-window address of the dynamic shared memory the plan assumes
     int smem;     // dynamic shared bytes
 };
+
+// cp.async (16-byte, L2 only) -----------------------------------------------------------------------
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Predicated 16-byte copy to shared address dst + OFF.
+template <int OFF>
+__device__ __forceinline__ void cp16p(uint32_t dst, const void *src, bool p) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q cp.async.cg.shared.global [%0+%3], [%1], 16;\n}" ::"r"(dst),
+        "l"(src), "r"((int)p), "n"(OFF)
+        : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Quantisation helpers ----------------------------------------------------------------------------
 // 2^k as an fp32, exact for k in [-149, 127] (the scale of the power-of-two quantiser).
@@ -118,6 +137,36 @@ __device__ float block_sumsq64(const float *x, int n, float *red64) {
     const float ss = red64[0];
     __syncthreads();
     return ss;
+}
+
+// Canonical sum of squares by one warp from shared memory: lane j runs partials j and j+32
+// (x[j]^2 + x[j+64]^2 + ... in index order, model/mirror.py:576-591) side by side, loads ahead of
+// the ordered adds, then the halving tree red[j] + red[j+32], 16, 8, ... in the same warp.  The
+// sum is returned in lane 0.
+__device__ __forceinline__ float warp_sumsq64(const float *xs, int K) {
+    const int j = threadIdx.x & 31;
+    float p0 = 0.f, p1 = 0.f;
+    int i = j;
+    for (; i + 3 * 64 + 32 < K; i += 4 * 64) {
+        float v0[4], v1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            v0[u] = xs[i + u * 64];
+            v1[u] = xs[i + u * 64 + 32];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            p0 = __fadd_rn(p0, __fmul_rn(v0[u], v0[u]));
+            p1 = __fadd_rn(p1, __fmul_rn(v1[u], v1[u]));
+        }
+    }
+    for (; i < K; i += 64) {
+        p0 = __fadd_rn(p0, __fmul_rn(xs[i], xs[i]));
+        if (i + 32 < K) p1 = __fadd_rn(p1, __fmul_rn(xs[i + 32], xs[i + 32]));
+    }
+    float a = __fadd_rn(p0, p1);
+    for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
+    return a;
 }
 
 // Quantise x (fp32 in shared memory) straight into the permuted activation words, one warp per
@@ -185,30 +234,7 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
         float r = 0.f;
         if (nw) {
             if (ct < 32) {
-                // Lane j runs partials j and j+32 (x[j]^2 + x[j+64]^2 + ... in index order,
-                // model/mirror.py:576-591) side by side, loads ahead of the ordered adds, then the
-                // halving tree red[j] + red[j+32], 16, 8, ... in the same warp.
-                float p0 = 0.f, p1 = 0.f;
-                int i = ct;
-                for (; i + 3 * 64 + 32 < K; i += 4 * 64) {
-                    float v0[4], v1[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        v0[u] = xs[i + u * 64];
-                        v1[u] = xs[i + u * 64 + 32];
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        p0 = __fadd_rn(p0, __fmul_rn(v0[u], v0[u]));
-                        p1 = __fadd_rn(p1, __fmul_rn(v1[u], v1[u]));
-                    }
-                }
-                for (; i < K; i += 64) {
-                    p0 = __fadd_rn(p0, __fmul_rn(xs[i], xs[i]));
-                    if (i + 32 < K) p1 = __fadd_rn(p1, __fmul_rn(xs[i + 32], xs[i + 32]));
-                }
-                float a = __fadd_rn(p0, p1);
-                for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
+                const float a = warp_sumsq64(xs, K);
                 if (ct == 0) red64[0] = a;
             }
             __syncthreads();
@@ -314,6 +340,107 @@ __device__ int build_activation(const float *x, const int8_t *x8g, const float *
         int s = (int)qg[0] + (int)qg[1] + (int)qg[2] + (int)qg[3];
         s = __reduce_add_sync(0xffffffffu, s);
         if (lane == 0) xp[g * XW + XS] = (uint32_t)s;
+    }
+    __syncthreads();
+    return e8;
+}
+
+// Staged prologue: x is copied into shared memory with cp.async (every copy in flight at once, no
+// registers held), the norm weight likewise (issued before the predecessor is waited for, when the
+// caller passes nw_ready).  The canonical sum-of-squares chains, the normalisation and the max run
+// over shared memory; the quantiser then reads one float4 per lane (group g = a warp's 32 float4)
+// and builds the decoders' activation words with warp shuffles.  Bit-identical to
+// build_activation (same values, same order of every rounded operation).  Needs x and nw 16-byte
+// aligned; xs: K floats of shared memory, nws: K more when nw is given.  Returns e8.
+__device__ __forceinline__ uint32_t absmax4(float4 v) {
+    return max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+               max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+}
+
+__device__ __forceinline__ void stage_f32(float *dst, const float *src, int K) {
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) cp16(reinterpret_cast<float4 *>(dst) + i, reinterpret_cast<const float4 *>(src) + i);
+}
+
+template <int KIND>
+__device__ int build_activation_cp(const float *x, const float *nw, bool nw_ready, float eps, int K, float *xs,
+                                   float *nws, uint32_t *xp, float *red64) {
+    const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5, nwarps = blockDim.x >> 5;
+    const int G = K / 128, n4 = K / 4;
+    float4 *const xs4 = reinterpret_cast<float4 *>(xs);
+    stage_f32(xs, x, K);
+    if (nw && !nw_ready) stage_f32(nws, nw, K);
+    cp_commit();
+    cp_wait<0>();
+    __syncthreads();
+    uint32_t m = 0;
+    if (nw) {
+        if (warp == 0) {
+            const float a = warp_sumsq64(xs, K);
+            if (lane == 0) red64[0] = a;
+        }
+        __syncthreads();
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red64[0], (float)K), eps)));
+        const float4 *const nw4 = reinterpret_cast<const float4 *>(nws);
+        for (int i = ct; i < n4; i += blockDim.x) {
+            float4 v = xs4[i];
+            const float4 w = nw4[i];
+            v.x = __fmul_rn(__fmul_rn(v.x, r), w.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, r), w.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, r), w.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, r), w.w);
+            xs4[i] = v;
+            const uint32_t a = absmax4(v);
+            m = a > m ? a : m;
+        }
+    } else {
+        for (int i = ct; i < n4; i += blockDim.x) {
+            const uint32_t a = absmax4(xs4[i]);
+            m = a > m ? a : m;
+        }
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    uint32_t *const wmax = reinterpret_cast<uint32_t *>(red64) + 32;  // per-warp maxima
+    if (lane == 0) wmax[warp] = m;
+    __syncthreads();
+    const uint32_t amax = __reduce_max_sync(0xffffffffu, lane < nwarps ? wmax[lane] : 0u);
+    const int e8 = amax ? frexp_exp(__uint_as_float(amax)) - 7 : 0;
+    const float inv = amax ? pow2f(-e8) : 0.f;  // all-zero x: every q is 0
+#pragma unroll 2
+    for (int g = warp; g < G; g += nwarps) {
+        const float4 v = xs4[g * 32 + lane];
+        const int q0 = quant_one(v.x, inv), q1 = quant_one(v.y, inv), q2 = quant_one(v.z, inv),
+                  q3 = quant_one(v.w, inv);
+        // This lane's bytes x8[4l .. 4l+3] of the group.
+        const uint32_t W = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+                           ((uint32_t)(q3 & 0xff) << 24);
+        const int sum = __reduce_add_sync(0xffffffffu, q0 + q1 + q2 + q3);
+        if (KIND == TRX_KIND_TERNARY5) {
+            uint32_t *w = xp + g * kXwT5;
+            // Lane i < 26: word i = bytes x8[5i .. 5i+3], y_i = x8[5i+4] - 3*x8[5i+3] (bytes 128 and
+            // 129 of the last code byte are 0); the bytes come from lanes 5i/4 and 5i/4+1.
+            const int a = (5 * lane) >> 2, off = (5 * lane) & 3;
+            const uint32_t lo = __shfl_sync(0xffffffffu, W, a & 31);
+            const uint32_t hi0 = __shfl_sync(0xffffffffu, W, (a + 1) & 31);
+            const uint32_t hi = a + 1 < 32 ? hi0 : 0u;
+            const uint32_t w1 = __funnelshift_rc(lo, hi, 8 * off);      // x8[5i .. 5i+3]
+            const uint32_t w2 = __funnelshift_rc(lo, hi, 8 * off + 8);  // x8[5i+1 .. 5i+4]
+            const int y = lane < 26 ? (int)(int8_t)(w2 >> 24) - 3 * (int)(int8_t)(w1 >> 24) : 0;
+            const int yn = __shfl_down_sync(0xffffffffu, y, 1);
+            if (lane < 26) w[lane] = w1;
+            if (lane < 28 && !(lane & 1)) w[26 + (lane >> 1)] = ((uint32_t)y & 0xffffu) | ((uint32_t)yn << 16);
+            if (lane == 0) w[40] = (uint32_t)sum;
+            if (lane >= 1 && lane < 4) w[40 + lane] = 0u;
+        } else {
+            uint32_t *w = xp + g * kXw2b;
+            // Word 4wq+p = bytes x8[16wq + 4b + p], b = 0..3: a 4x4 byte transpose across each quad
+            // of lanes (lane 4wq+b holds x8[16wq + 4b .. 16wq + 4b + 3]).
+            const uint32_t s1 = __shfl_xor_sync(0xffffffffu, W, 1);
+            const uint32_t A = (lane & 1) ? __byte_perm(W, s1, 0x3715u) : __byte_perm(W, s1, 0x6240u);
+            const uint32_t s2 = __shfl_xor_sync(0xffffffffu, A, 2);
+            w[lane] = (lane & 2) ? __byte_perm(A, s2, 0x3276u) : __byte_perm(A, s2, 0x5410u);
+            if (lane == 0) w[32] = (uint32_t)sum;
+            if (lane >= 1 && lane < 4) w[32 + lane] = 0u;
+        }
     }
     __syncthreads();
     return e8;
@@ -515,23 +642,6 @@ __device__ __forceinline__ void argmax_commit(const MvJobs &J, int job, unsigned
     if (lane == 0 && best) atomicMax(J.argmax + job, best);
 }
 
-// cp.async (16-byte, L2 only) -----------------------------------------------------------------------
-__device__ __forceinline__ void cp16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-// Predicated 16-byte copy to shared address dst + OFF.
-template <int OFF>
-__device__ __forceinline__ void cp16p(uint32_t dst, const void *src, bool p) {
-    asm volatile(
-        "{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q cp.async.cg.shared.global [%0+%3], [%1], 16;\n}" ::"r"(dst),
-        "l"(src), "r"((int)p), "n"(OFF)
-        : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // Issue the copies of block (row block rbk, chunk c) of `job` into ring slot `dst`.  Per row,
 // the 16 scale bytes holding the chunk's scales land at ring bytes [0, 16) and the chunk's codes
@@ -700,9 +810,19 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     };
     // The first piece's first blocks (weights: written by no kernel) are requested before waiting
     // for the predecessor, by the warps whose ring is not the quantiser's staging area.
+    // Shared bytes the prologue writes outside the fixed area: the staged prologue x and the norm
+    // weight after the q8 bytes, the others the q8 bytes and x.
+    const bool fast = M.xfast && J.x;
     const int stage_off = M.q8c ? c_off : M.fixed;
-    const int stage_end = stage_off + ((J.cols + 15) / 16) * 16 + (xs ? 4 * J.cols : 0);
-    const bool early = ring_off + RING <= stage_off || ring_off >= stage_end;
+    const int xs_off = stage_off + ((J.cols + 15) / 16) * 16;
+    float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * J.cols);
+    const int st_lo = fast ? xs_off : stage_off;
+    const int st_hi = xs_off + (xs ? 4 * J.cols : 0) + (fast && J.norm_w ? 4 * J.cols : 0);
+    const bool early = ring_off + RING <= st_lo || ring_off >= st_hi;
+    if (fast && J.norm_w) {  // the norm weight is written by no kernel: staged before the wait
+        stage_f32(nws, J.norm_w, J.cols);
+        cp_commit();
+    }
     piece_begin(t0);
     if (early) {
 #pragma unroll
@@ -721,7 +841,8 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         __syncthreads();  // the previous piece's activation and rings are no longer in use
         const float *xj = J.x ? J.x + (uint64_t)job * J.x_stride : nullptr;
         const int8_t *x8j = J.x8 ? J.x8 + (uint64_t)job * J.x_stride : nullptr;
-        const int e8 = build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
+        const int e8 = fast ? build_activation_cp<KIND>(xj, J.norm_w, first, J.eps, J.cols, xs, nws, xp, red64)
+                            : build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
         unsigned long long best = 0ull;
 
         const int rounds = (pb - pa + R - 1) / R;
@@ -1010,6 +1131,8 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     if (M.stage < J.cols) return false;
     if ((reinterpret_cast<uintptr_t>(J.x) & 15) || (reinterpret_cast<uintptr_t>(J.norm_w) & 15) || (J.x_stride & 3))
         M.stage = J.cols;  // float4 loads need 16-byte aligned rows: the global prologue path
+    // The staged prologue: 16-byte aligned rows, shared staging for x and the norm weight.
+    M.xfast = M.stage >= (J.cols + 15) / 16 * 16 + 4 * J.cols * (J.norm_w ? 2 : 1) ? 1 : 0;
     return M.smem <= kSmemMax;
 }
 
