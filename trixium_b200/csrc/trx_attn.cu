@@ -21,6 +21,8 @@
 #include <cstring>
 #include <mutex>
 #include <cuda_fp16.h>
+#include <cooperative_groups.h>
+#include <cstdlib>
 #include <cuda_runtime.h>
 
 #include "trx_common.cuh"
@@ -265,6 +267,369 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
     if (tid == 0) A.cnt[kh] = 0u;
 }
 
+// Cluster decode attention -------------------------------------------------------------------
+// The same step with the splits of a kv head in one thread-block cluster (at most 16 CTAs): the
+// partials are merged through distributed shared memory instead of global scratch and an arrival
+// count.  Per CTA (split s of kv head kh, 256 threads):
+//  * before the dependency wait: the q/k norm weights and the RoPE frequencies into shared memory;
+//  * after it: the position, then the K and V rows [t0, min(t0 + chunk, pos + 1)) staged with
+//    cp.async while warps 0..REP-1 normalise and rotate their query heads; the CTA whose chunk
+//    holds pos normalises and rotates the new key and writes the new K/V row (fp16) to the cache
+//    and into its own tiles;
+//  * scores: hd/DPL lanes per position, each holding DPL dims of every query head in registers,
+//    the dot products finished by shuffles; softmax per head (one warp each);
+//  * P.V: hd/4 threads per position group, each 4 dims of every head, the groups' partial sums
+//    added in a fixed order;
+//  * merge: after a cluster barrier, every CTA forms the per-head weights
+//    w_j = e^(m_j - M) * (1 / sum_j e^(m_j - M) l_j) from all splits' (m, l), and writes its share
+//    of the outputs sum_j w_j o_j (times sigmoid(gate) for gated heads); a second barrier keeps
+//    every CTA's shared memory alive until all reads are done.
+namespace {
+namespace cg = cooperative_groups;
+
+constexpr int kClThreads = 256;
+
+__device__ __forceinline__ void cp4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// head_rmsnorm / head_rope with the weights in shared memory.
+__device__ void head_rmsnorm_s(float *v, int hd, const float *w, float eps, int lane) {
+    float p0 = 0.f, p1 = 0.f;
+    for (int i = lane; i < hd; i += 64) p0 = __fadd_rn(p0, __fmul_rn(v[i], v[i]));
+    for (int i = lane + 32; i < hd; i += 64) p1 = __fadd_rn(p1, __fmul_rn(v[i], v[i]));
+    float a = __fadd_rn(p0, p1);
+    for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
+    const float ss = __shfl_sync(0xffffffffu, a, 0);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(__fmul_rn(v[i], r), w[i]);
+    __syncwarp();
+}
+
+__device__ void head_rope_s(float *v, int half, const float *freq, int pos, int lane) {
+    for (int d = lane; d < half; d += 32) {
+        const float ang = __fmul_rn((float)pos, freq[d]);
+        float sn, c;
+        sincosf(ang, &sn, &c);
+        const float x0 = v[d], x1 = v[d + half];
+        v[d] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        v[d + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+    __syncwarp();
+}
+
+struct ClLayout {  // float offsets after the K and V tiles
+    int qs, cq, ck, cf, knew, sc, et, pp, om, ml, wt, total;
+};
+
+__host__ __device__ inline ClLayout cl_layout(int hd, int rep, int repp, int chunk) {
+    ClLayout L;
+    int o = 0;
+    L.qs = o; o += rep * hd;
+    L.cq = o; o += hd;
+    L.ck = o; o += hd;
+    L.cf = o; o += hd / 2;
+    L.knew = o; o += hd;
+    L.sc = o; o += rep * chunk;
+    L.et = o; o += chunk * repp;
+    L.pp = o; o += 1024 * rep;  // (256 / (hd/4)) position groups x rep x hd
+    L.om = o; o += rep * hd;
+    L.ml = o; o += 2 * rep;
+    L.wt = o; o += 16 * rep;
+    L.total = o;
+    return L;
+}
+
+__host__ __device__ inline size_t cl_smem_bytes(int hd, int rep, int chunk) {
+    const int repp = rep <= 4 ? 4 : 8;
+    const size_t tiles = (size_t)chunk * (hd + 8) * 2 + (size_t)chunk * hd * 2;
+    return tiles + (size_t)cl_layout(hd, rep, repp, chunk).total * 4;
+}
+
+template <int REP, int DPL>
+__global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, uint32_t *err) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int REPP = REP <= 4 ? 4 : 8;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int s = blockIdx.x, kh = blockIdx.y, ns = A.nsplit;
+    const int hd = A.hd, chunk = A.chunk, rowk = hd + 8;
+    __half *const kt = reinterpret_cast<__half *>(smem);  // [chunk][hd + 8]
+    __half *const vt = kt + (size_t)chunk * rowk;         // [chunk][hd]
+    float *const fb = reinterpret_cast<float *>(vt + (size_t)chunk * hd);
+    const ClLayout Ly = cl_layout(hd, REP, REPP, chunk);
+    float *const qs = fb + Ly.qs, *const cq = fb + Ly.cq, *const ck = fb + Ly.ck, *const cf = fb + Ly.cf;
+    float *const knew = fb + Ly.knew, *const sc = fb + Ly.sc, *const et = fb + Ly.et, *const pp = fb + Ly.pp;
+    float *const om = fb + Ly.om, *const mrow = fb + Ly.ml, *const lrow = mrow + REP, *const wt = fb + Ly.wt;
+
+    pdl_trigger();
+    // Weights written by no kernel: requested before the wait.
+    for (int i = tid; i < hd; i += kClThreads) {
+        cp4(cq + i, A.qn + i);
+        cp4(ck + i, A.kn + i);
+    }
+    for (int i = tid; i < A.rope_half; i += kClThreads) cp4(cf + i, A.freq + i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_wait();
+    const int pos = *A.pos;
+    if (pos < 0 || pos >= A.max_pos) {  // every CTA reads the same position: all leave together
+        if (tid == 0 && s == 0 && kh == 0) atomicOr(err, TRX_DEV_RANGE);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        return;
+    }
+    const int t0 = s * chunk;
+    const int n = max(0, min(chunk, pos + 1 - t0));
+    const bool owner = pos >= t0 && pos < t0 + chunk;
+    const int stride_t = A.Hkv * hd;
+    {
+        const int pieces = hd / 8;
+        for (int i = tid; i < n * pieces; i += kClThreads) {
+            const int t = i / pieces, j = i - t * pieces;
+            if (t0 + t == pos) continue;  // written below by this CTA
+            const size_t g = (size_t)(t0 + t) * stride_t + (size_t)kh * hd + 8 * j;
+            cp16_attn(kt + t * rowk + 8 * j, A.kc + g);
+            cp16_attn(vt + t * hd + 8 * j, A.vc + g);
+        }
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
+    __syncthreads();  // the norm weights and frequencies are visible
+    if (n > 0) {
+        for (int r = warp; r < REP; r += kClThreads / 32) {
+            const float *qh = A.q + (size_t)(kh * REP + r) * A.qstride;
+            float *v = qs + r * hd;
+            for (int i = lane; i < hd; i += 32) v[i] = qh[i];
+            __syncwarp();
+            head_rmsnorm_s(v, hd, cq, A.eps, lane);
+            head_rope_s(v, A.rope_half, cf, pos, lane);
+        }
+        if (owner && warp == kClThreads / 32 - 1) {
+            const float *kg = A.k + (size_t)kh * hd;
+            for (int i = lane; i < hd; i += 32) knew[i] = kg[i];
+            __syncwarp();
+            head_rmsnorm_s(knew, hd, ck, A.eps, lane);
+            head_rope_s(knew, A.rope_half, cf, pos, lane);
+            const int tp = pos - t0;
+            __half *kc = A.kc + (size_t)pos * stride_t + (size_t)kh * hd;
+            __half *vc = A.vc + (size_t)pos * stride_t + (size_t)kh * hd;
+            const float *vg = A.v + (size_t)kh * hd;
+            for (int i = lane; i < hd; i += 32) {
+                const __half kh16 = __float2half_rn(knew[i]), vh16 = __float2half_rn(vg[i]);
+                kc[i] = kh16;
+                vc[i] = vh16;
+                kt[tp * rowk + i] = kh16;
+                vt[tp * hd + i] = vh16;
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // K/V tiles and queries ready
+
+    if (n > 0) {
+        // Scores: lpp lanes per position, DPL dims each.
+        const int lpp = hd / DPL, ppw = 32 / lpp;
+        const int sub = lane % lpp, pl = lane / lpp;
+        float qr[REP][DPL];
+#pragma unroll
+        for (int r = 0; r < REP; ++r)
+#pragma unroll
+            for (int i = 0; i < DPL; i += 4) {
+                const float4 q4 = *reinterpret_cast<const float4 *>(qs + r * hd + sub * DPL + i);
+                qr[r][i] = q4.x;
+                qr[r][i + 1] = q4.y;
+                qr[r][i + 2] = q4.z;
+                qr[r][i + 3] = q4.w;
+            }
+        for (int tb = warp * ppw; tb < n; tb += (kClThreads / 32) * ppw) {
+            const int t = tb + pl;
+            float kv[DPL];
+            if (t < n) {
+#pragma unroll
+                for (int i = 0; i < DPL; i += 8) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(kt + t * rowk + sub * DPL + i);
+                    const float2 f0 = h2_to_f2(w.x), f1 = h2_to_f2(w.y), f2 = h2_to_f2(w.z), f3 = h2_to_f2(w.w);
+                    kv[i] = f0.x; kv[i + 1] = f0.y; kv[i + 2] = f1.x; kv[i + 3] = f1.y;
+                    kv[i + 4] = f2.x; kv[i + 5] = f2.y; kv[i + 6] = f3.x; kv[i + 7] = f3.y;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) kv[i] = 0.f;
+            }
+            float acc[REP];
+#pragma unroll
+            for (int r = 0; r < REP; ++r) {
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < DPL; i += 2) {
+                    a0 = fmaf(qr[r][i], kv[i], a0);
+                    a1 = fmaf(qr[r][i + 1], kv[i + 1], a1);
+                }
+                acc[r] = a0 + a1;
+            }
+            for (int o = lpp >> 1; o; o >>= 1)
+#pragma unroll
+                for (int r = 0; r < REP; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            if (sub == 0 && t < n)
+#pragma unroll
+                for (int r = 0; r < REP; ++r) sc[r * chunk + t] = __fmul_rn(acc[r], A.scale);
+        }
+        __syncthreads();
+        // Softmax per head: e = exp(s - m) into et[t][REPP], chunk max and sum.
+        for (int r = warp; r < REP; r += kClThreads / 32) {
+            float m = -INFINITY;
+            for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[r * chunk + t]);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float l = 0.f;
+            for (int t = lane; t < n; t += 32) {
+                const float e = expf(__fsub_rn(sc[r * chunk + t], m));
+                et[t * REPP + r] = e;
+                l += e;
+            }
+            for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (lane == 0) {
+                mrow[r] = m;
+                lrow[r] = l;
+            }
+        }
+        __syncthreads();
+        // P.V: position group grp (positions grp, grp + ngrp, ...), 4 dims per thread.
+        const int tpg = hd / 4, ngrp = kClThreads / tpg;
+        const int grp = tid / tpg, dq = tid - grp * tpg;
+        float acc[REP][4];
+#pragma unroll
+        for (int r = 0; r < REP; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+        for (int t = grp; t < n; t += ngrp) {
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vt + t * hd + 4 * dq);
+            const float2 v01 = h2_to_f2(vv.x), v23 = h2_to_f2(vv.y);
+            float e[REPP];
+#pragma unroll
+            for (int i = 0; i < REPP; i += 4) {
+                const float4 e4 = *reinterpret_cast<const float4 *>(et + t * REPP + i);
+                e[i] = e4.x;
+                e[i + 1] = e4.y;
+                e[i + 2] = e4.z;
+                e[i + 3] = e4.w;
+            }
+#pragma unroll
+            for (int r = 0; r < REP; ++r) {
+                acc[r][0] = fmaf(e[r], v01.x, acc[r][0]);
+                acc[r][1] = fmaf(e[r], v01.y, acc[r][1]);
+                acc[r][2] = fmaf(e[r], v23.x, acc[r][2]);
+                acc[r][3] = fmaf(e[r], v23.y, acc[r][3]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < REP; ++r)
+            *reinterpret_cast<float4 *>(pp + ((size_t)grp * REP + r) * hd + 4 * dq) =
+                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        __syncthreads();
+        for (int i = tid; i < REP * hd; i += kClThreads) {
+            float o = 0.f;
+            for (int g = 0; g < ngrp; ++g) o += pp[(size_t)g * REP * hd + i];
+            om[i] = o;
+        }
+    } else {
+        for (int i = tid; i < REP * hd; i += kClThreads) om[i] = 0.f;
+        if (tid < REP) {
+            mrow[tid] = -INFINITY;
+            lrow[tid] = 0.f;
+        }
+    }
+    cluster.sync();  // every split's (m, l, o) is visible in the cluster
+    for (int r = warp; r < REP; r += kClThreads / 32) {
+        float mj = -INFINITY, lj = 0.f;
+        if (lane < ns) {
+            mj = *cluster.map_shared_rank(mrow + r, lane);
+            lj = *cluster.map_shared_rank(lrow + r, lane);
+        }
+        float M = mj;
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = lane < ns ? expf(__fsub_rn(mj, M)) : 0.f;
+        float L = w * lj;
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = __fdiv_rn(1.0f, L);
+        if (lane < ns) wt[r * 16 + lane] = __fmul_rn(w, inv);
+    }
+    __syncthreads();
+    const int total = REP * hd, per = (total + ns - 1) / ns;
+    const int i0 = s * per, i1 = min(total, i0 + per);
+    for (int i = i0 + tid; i < i1; i += kClThreads) {
+        const int r = i / hd, d = i - r * hd;
+        float o = 0.f;
+        for (int j = 0; j < ns; ++j) o = fmaf(wt[r * 16 + j], *cluster.map_shared_rank(om + i, j), o);
+        const int h = kh * REP + r;
+        if (A.gated) {
+            const float g = A.q[(size_t)h * A.qstride + hd + d];
+            o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+        }
+        A.out[(size_t)h * hd + d] = o;
+    }
+    cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
+template <int REP, int DPL>
+cudaError_t launch_cl(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_t st) {
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    auto k = attn_cluster_kernel<REP, DPL>;
+    if (!(configured & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        configured |= bit;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(A.nsplit, A.Hkv);
+    cfg.blockDim = dim3(kClThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = A.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // A cluster this wide must fit on one GPC at this shared-memory size (asked once per shape).
+    static struct {
+        int dev, ns;
+        size_t smem;
+        int ok;
+    } seen[32];
+    static int nseen = 0;
+    int ok = -1;
+    for (int i = 0; i < nseen; ++i)
+        if (seen[i].dev == dev && seen[i].ns == A.nsplit && seen[i].smem == smem) ok = seen[i].ok;
+    if (ok < 0) {
+        int nc = 0;
+        ok = cudaOccupancyMaxActiveClusters(&nc, k, &cfg) == cudaSuccess && nc > 0 ? 1 : 0;
+        cudaGetLastError();
+        if (nseen < 32) seen[nseen++] = {dev, A.nsplit, smem, ok};
+    }
+    if (!ok) return cudaErrorNotSupported;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, k, A, err);
+}
+
+// The cluster plan: chunk a multiple of 32 with at most 16 splits, in shared memory.  false: the
+// shape takes the scratch-merge kernel.
+bool cl_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem) {
+    const int rep = A.H / A.Hkv;
+    if (!(rep == 1 || rep == 2 || rep == 4 || rep == 6 || rep == 8)) return false;
+    if (!(A.hd == 64 || A.hd == 128 || A.hd == 256)) return false;
+    if (getenv("TRX_NO_CLUSTER_ATTN")) return false;
+    chunk = ((A.max_pos + 15) / 16 + 31) / 32 * 32;
+    nsplit = (A.max_pos + chunk - 1) / chunk;
+    smem = cl_smem_bytes(A.hd, rep, chunk);
+    return nsplit <= 16 && smem <= 227 * 1024;
+}
+
+}  // namespace
+
 // Positions per CTA: the smallest of 64, 128, 256 that keeps the splits per kv head at 16 or fewer
 // (fewer partials to merge), capped so two staged tiles fit in shared memory.
 int attn_chunk(int max_pos, int hd) {
@@ -278,7 +643,24 @@ size_t attn_smem_bytes(int hd, int rep, int chunk) {
     return (size_t)2 * chunk * (hd + 8) * 2 + ((size_t)rep * hd + hd + (size_t)rep * chunk + 2 * rep) * 4;
 }
 
-trx_status launch_attn_decode(const AttnArgs &A, uint32_t *err, cudaStream_t st) {
+trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st) {
+    {
+        AttnArgs C = A0;
+        size_t csmem = 0;
+        if (cl_plan(A0, C.chunk, C.nsplit, csmem)) {
+            // 16 dims per lane up to 4 heads, 8 beyond: rep * DPL query values in registers <= 64.
+            cudaError_t e;
+            switch (A0.H / A0.Hkv) {
+                case 1: e = launch_cl<1, 16>(C, err, csmem, st); break;
+                case 2: e = launch_cl<2, 16>(C, err, csmem, st); break;
+                case 4: e = launch_cl<4, 16>(C, err, csmem, st); break;
+                case 6: e = launch_cl<6, 8>(C, err, csmem, st); break;
+                default: e = launch_cl<8, 8>(C, err, csmem, st); break;
+            }
+            if (e != cudaErrorNotSupported) return note_cuda(e);  // not supported: no cluster that wide fits
+        }
+    }
+    const AttnArgs &A = A0;
     const size_t smem = attn_smem_bytes(A.hd, A.H / A.Hkv, A.chunk);
     static unsigned long long configured = 0;
     int dev = 0;

@@ -75,7 +75,9 @@ struct MvGeom {
     int xw;       // activation words per group
     int fixed;    // bytes of activation words and reductions (128-byte rounded): rings A start here
     int na;       // warps whose ring lies in region A (the rest: region C, after the trit5 LUT)
-    int q8c;      // the quantiser's staging lies in region C
+    int sreg;     // the staging area lies in region C (1) or A (0)
+    int stage_off;  // its shared offset: the last bands (slot D-1, D-2, ...) of that region
+    int ebl;      // slots of a staging-region warp below the staging area
     int xfast;    // float x takes the cp.async-staged prologue (build_activation_cp)
     int stage;    // bytes of that staging region
     int base;     // shared-window address of the dynamic shared memory the plan assumes
@@ -111,10 +113,16 @@ __device__ __forceinline__ float prologue_value(const float *x, const float *w, 
     return v;
 }
 
+// The quantiser's value: clamp(lround_mirror(v * inv), -127, 127), without conversion
+// instructions (a quarter of the ALU rate): a = fp32(|t| + 0.5) is the mirror's own rounded sum
+// (fp32 addition is symmetric, so fp32(t - 0.5) = -a for t < 0), and floor(a) for a < 2^23 is the
+// mantissa of fp32_round_down(a + 2^23).  a >= 128 (and inf) clamps to 127.
 __device__ __forceinline__ int8_t quant_one(float v, float inv) {
-    int q = lround_mirror(__fmul_rn(v, inv));
-    q = q > 127 ? 127 : (q < -127 ? -127 : q);
-    return (int8_t)q;
+    const float t = __fmul_rn(v, inv);
+    const float a = __fadd_rn(fabsf(t), 0.5f);
+    uint32_t m = __float_as_uint(__fadd_rd(a, 8388608.0f)) & 0x7fffffu;
+    m = a < 128.0f ? m : 127u;
+    return (int8_t)(t < 0.f ? -(int)m : (int)m);
 }
 
 // Canonical sum of squares (model/mirror.py:576-591; doc/units.md "Sum of squares"): 64
@@ -518,13 +526,13 @@ __device__ __forceinline__ int gsum_2b(const uint4 *cp, const uint32_t *xg) {
 }
 
 // (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Fast range: a normal fp16
-// scale (biased exponent E in [1, 30]) with 0 <= e16+B = E-25+B <= 19, where m11 << (e16+B) =
-// scale * 2^B is an integer below 2^30: the contribution is gs * F2I(fp32(scale) * 2^B) (both
-// steps exact, the sign carried by the float), one 32x32->64 multiply.  Other scales (tiny or
-// subnormal ones, far below the tensor's largest) take the general floor/left shift.
+// scale (biased exponent E in [1, 30]) with 0 <= e16+B = E-25+B <= 19, where m11 << (e16+B) is
+// below 2^30: the contribution is (+-gs) * (m11 << (E-25+B)), one 32x32->64 multiply.  Other
+// scales (tiny or subnormal ones, far below the tensor's largest) take the general floor/left
+// shift.
 struct ScaleFast {
     int lo, span;  // fast iff E - lo in [0, span]
-    float p2B;     // 2^B
+    int sh;        // B - 25: the left shift is E + sh
 };
 
 __device__ __forceinline__ ScaleFast scale_fast(int B) {
@@ -532,7 +540,7 @@ __device__ __forceinline__ ScaleFast scale_fast(int B) {
     const int lo = max(1, 25 - B), hi = min(30, 44 - B);
     f.lo = hi >= lo ? lo : 64;  // an empty range: E - 64 < 0 fails the unsigned test below
     f.span = hi >= lo ? hi - lo : 0;
-    f.p2B = pow2f(B);
+    f.sh = B - 25;
     return f;
 }
 
@@ -542,8 +550,9 @@ __device__ __forceinline__ uint32_t scale_bits(uint2 s, int g) {
 }
 
 __device__ __forceinline__ long long contrib(int gs, uint32_t sb, int B, const ScaleFast &F) {
-    if ((unsigned)((int)((sb >> 10) & 31u) - F.lo) <= (unsigned)F.span)
-        return (long long)gs * (long long)__float2int_rz(__fmul_rn(__half2float(__ushort_as_half((unsigned short)sb)), F.p2B));
+    const int E = (int)((sb >> 10) & 31u);
+    if ((unsigned)(E - F.lo) <= (unsigned)F.span)
+        return (long long)(sb & 0x8000u ? -gs : gs) * (long long)(int)(((sb & 0x3ffu) | 0x400u) << (E + F.sh));
     return group_contrib(gs, sb, B);
 }
 
@@ -732,7 +741,6 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
 
     // Carve shared memory (must match plan_matvec): [activation words, reductions][rings A]
     // [trit5 LUT at window address 0x10000][rings C]; 2-bit: one ring region, no LUT.
-    constexpr int RING = D * NW * kBlkBytes;  // one warp's ring
     constexpr int slot_bytes = NW * kBlkBytes;
     uint32_t *const xp = reinterpret_cast<uint32_t *>(smem);
     unsigned char *p = smem + M.G * M.xw * 4;
@@ -747,10 +755,14 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         return;
     }
     unsigned char *const lut = smem + lut_off;  // trit5 only
-    const int ring_off = warp < M.na ? M.fixed + warp * RING : c_off + (warp - M.na) * RING;
+    // Rings are slot-major within a region: slot d of the region's k-th warp lies at region +
+    // (d * n + k) * slot_bytes (n warps in the region), so the last slots of a region's warps form
+    // one band, where the prologue stages its inputs.
+    const int sstride = (warp < M.na ? M.na : M.warps - M.na) * slot_bytes;
+    const int ring_off = warp < M.na ? M.fixed + warp * slot_bytes : c_off + (warp - M.na) * slot_bytes;
     unsigned char *const ring = smem + ring_off;
     const uint32_t ring_s = smem_u32(ring);
-    int8_t *const q8 = reinterpret_cast<int8_t *>(smem + (M.q8c ? c_off : M.fixed));  // staging; rings idle then
+    int8_t *const q8 = reinterpret_cast<int8_t *>(smem + M.stage_off);  // staging; those slots idle then
 
     // Combine area of warps sharing a row block: [2 parities][warps][32 lanes][NW] int64.
     long long *const red = reinterpret_cast<long long *>(smem + M.fixed - (M.S > 1 ? 8192 : 0));
@@ -808,26 +820,21 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         }
         cp_commit();
     };
-    // The first piece's first blocks (weights: written by no kernel) are requested before waiting
-    // for the predecessor, by the warps whose ring is not the quantiser's staging area.
-    // Shared bytes the prologue writes outside the fixed area: the staged prologue x and the norm
-    // weight after the q8 bytes, the others the q8 bytes and x.
+    // The staging area [q8 bytes][x fp32][norm weight fp32] covers the last bands of the staging
+    // region; the first piece's blocks for the slots below it (weights: written by no kernel) are
+    // requested before waiting for the predecessor, all D-1 by the warps of the other region.
     const bool fast = M.xfast && J.x;
-    const int stage_off = M.q8c ? c_off : M.fixed;
-    const int xs_off = stage_off + ((J.cols + 15) / 16) * 16;
+    const int xs_off = M.stage_off + ((J.cols + 15) / 16) * 16;
     float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * J.cols);
-    const int st_lo = fast ? xs_off : stage_off;
-    const int st_hi = xs_off + (xs ? 4 * J.cols : 0) + (fast && J.norm_w ? 4 * J.cols : 0);
-    const bool early = ring_off + RING <= st_lo || ring_off >= st_hi;
+    const int ne = (warp < M.na) == (M.sreg == 0) ? min(D - 1, M.ebl) : D - 1;
     if (fast && J.norm_w) {  // the norm weight is written by no kernel: staged before the wait
         stage_f32(nws, J.norm_w, J.cols);
         cp_commit();
     }
     piece_begin(t0);
-    if (early) {
 #pragma unroll
-        for (int d = 0; d < D - 1; ++d) issue_next(ring_s + d * slot_bytes);
-    }
+    for (int d = 0; d < D - 1; ++d)
+        if (d < ne) issue_next(ring_s + d * sstride);
     pdl_wait();
     if (J.skip && *J.skip) {
         cp_wait<0>();
@@ -846,10 +853,9 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         unsigned long long best = 0ull;
 
         const int rounds = (pb - pa + R - 1) / R;
-        if (!(first && early)) {
 #pragma unroll
-            for (int d = 0; d < D - 1; ++d) issue_next(ring_s + d * slot_bytes);
-        }
+        for (int d = 0; d < D - 1; ++d)
+            if (d >= (first ? ne : 0)) issue_next(ring_s + d * sstride);
         int rs = D - 1, slot = 0;
         LaneRow L, one;
         one.o = row_out(J, job, 0, e8);
@@ -861,13 +867,13 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
             long long acc0 = 0, acc1 = 0;
             if (valid) lane_row(J, job, rbk * 32 + lane, e8, one, L);
             for (int c = cA; valid && c < cB; ++c) {
-                issue_next(ring_s + rs * slot_bytes);
+                issue_next(ring_s + rs * sstride);
                 rs = rs + 1 == D ? 0 : rs + 1;
                 cp_wait<D - 1>();
                 __syncwarp();
                 const int ng = min(kCG, M.G - c * kCG);
                 const uint32_t *xg = xp + c * kCG * M.xw;
-                const unsigned char *rp = ring + (size_t)slot * slot_bytes + lane * kRowStride;
+                const unsigned char *rp = ring + (size_t)slot * sstride + lane * kRowStride;
 #pragma unroll
                 for (int w = 0; w < NW; ++w) {
                     const unsigned char *rw = rp + w * kBlkBytes;
@@ -1115,10 +1121,19 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
         int w = 1;
         while (w * 2 <= M.warps) w *= 2;  // sharing groups need a power-of-two warp count
         M.warps = w;
-        int R = 1;
-        while (R * 2 <= M.warps && R * 2 <= rbc) R *= 2;
-        M.S = M.warps / R;
-        while (M.S > 1 && M.S > M.nch) M.S /= 2;  // more sharers than chunks would only idle
+        // R row blocks at a time, S = warps/R warps per row block: the fewest chunk steps per warp,
+        // ceil(rbc/R) rounds of ceil(nch/S) chunks; ties go to the larger R (fewer sharers).
+        int bestR = 1;
+        long long best = -1;
+        for (int R = 1; R <= M.warps; R *= 2) {
+            const int S = M.warps / R;
+            const long long cost = ((rbc + R - 1) / R) * (long long)((M.nch + S - 1) / S);
+            if (best < 0 || cost <= best) {
+                best = cost;
+                bestR = R;
+            }
+        }
+        M.S = M.warps / bestR;
     }
     M.cpt = (M.nch + M.S - 1) / M.S;
     M.na = std::min(na_max, M.warps);
@@ -1126,13 +1141,22 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     M.base = kind == TRX_KIND_TERNARY5 ? reserved : 0;
     M.smem = kind == TRX_KIND_TERNARY5 ? c_off + nc * ring : M.fixed + M.warps * ring;
     // The quantiser's staging (q8, then x as fp32) lives in the larger ring region, idle then.
-    M.q8c = nc > M.na ? 1 : 0;
-    M.stage = (M.q8c ? nc : M.na) * ring;
+    // The staging area: the last bands of the region with the wider band (a band is the slot d of
+    // every warp of the region), as few as hold [q8 bytes][x fp32][norm weight fp32]; float4 loads
+    // need 16-byte aligned rows, else only the q8 bytes (the global prologue path).
+    const int slot = nw * kBlkBytes;
+    M.sreg = nc > M.na ? 1 : 0;
+    const int band = (M.sreg ? nc : M.na) * slot;
+    const bool aligned = !(reinterpret_cast<uintptr_t>(J.x) & 15) && !(reinterpret_cast<uintptr_t>(J.norm_w) & 15) &&
+                         !(J.x_stride & 3);
+    const int need = aligned ? (J.cols + 15) / 16 * 16 + 4 * J.cols * (J.norm_w ? 2 : 1) : J.cols;
+    const int nb = std::min(M.D, (need + band - 1) / band);
+    M.stage = nb * band;
     if (M.stage < J.cols) return false;
-    if ((reinterpret_cast<uintptr_t>(J.x) & 15) || (reinterpret_cast<uintptr_t>(J.norm_w) & 15) || (J.x_stride & 3))
-        M.stage = J.cols;  // float4 loads need 16-byte aligned rows: the global prologue path
-    // The staged prologue: 16-byte aligned rows, shared staging for x and the norm weight.
-    M.xfast = M.stage >= (J.cols + 15) / 16 * 16 + 4 * J.cols * (J.norm_w ? 2 : 1) ? 1 : 0;
+    M.stage_off = (M.sreg ? c_off : M.fixed) + (M.D - nb) * band;
+    M.ebl = M.D - nb;
+    if (!aligned) M.stage = J.cols;  // no x staging in shared memory: the global prologue path
+    M.xfast = aligned && M.stage >= need ? 1 : 0;
     return M.smem <= kSmemMax;
 }
 
