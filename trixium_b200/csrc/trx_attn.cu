@@ -301,7 +301,7 @@ __device__ void head_rmsnorm_s(float *v, int hd, const float *w, float eps, int 
     float a = __fadd_rn(p0, p1);
     for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
     const float ss = __shfl_sync(0xffffffffu, a, 0);
-    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)hd), eps));
     __syncwarp();
     for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(__fmul_rn(v[i], r), w[i]);
     __syncwarp();
@@ -320,7 +320,7 @@ __device__ void head_rope_s(float *v, int half, const float *freq, int pos, int 
 }
 
 struct ClLayout {  // float offsets after the K and V tiles
-    int qs, cq, ck, cf, knew, sc, et, pp, om, ml, wt, total;
+    int qs, cq, ck, cf, knew, sc, et, pp, om, ml, wt, mg, total;
 };
 
 __host__ __device__ inline ClLayout cl_layout(int hd, int rep, int repp, int chunk) {
@@ -333,18 +333,19 @@ __host__ __device__ inline ClLayout cl_layout(int hd, int rep, int repp, int chu
     L.knew = o; o += hd;
     L.sc = o; o += rep * chunk;
     L.et = o; o += chunk * repp;
-    L.pp = o; o += 1024 * rep;  // (256 / (hd/4)) position groups x rep x hd
+    L.pp = o; o += 4 * kClThreads * rep;  // (threads / (hd/4)) position groups x rep x hd
     L.om = o; o += rep * hd;
     L.ml = o; o += 2 * rep;
     L.wt = o; o += 16 * rep;
+    L.mg = o;  // the merge area (16 slots), when it gets its own region
     L.total = o;
     return L;
 }
 
-__host__ __device__ inline size_t cl_smem_bytes(int hd, int rep, int chunk) {
+__host__ __device__ inline size_t cl_smem_bytes(int hd, int rep, int chunk, int merge_slots) {
     const int repp = rep <= 4 ? 4 : 8;
     const size_t tiles = (size_t)chunk * (hd + 8) * 2 + (size_t)chunk * hd * 2;
-    return tiles + (size_t)cl_layout(hd, rep, repp, chunk).total * 4;
+    return tiles + ((size_t)cl_layout(hd, rep, repp, chunk).total + (size_t)merge_slots * rep * (hd + 2)) * 4;
 }
 
 template <int REP, int DPL>
@@ -364,6 +365,7 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
     float *const om = fb + Ly.om, *const mrow = fb + Ly.ml, *const lrow = mrow + REP, *const wt = fb + Ly.wt;
 
     pdl_trigger();
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");  // waited on before the merge
     // Weights written by no kernel: requested before the wait.
     for (int i = tid; i < hd; i += kClThreads) {
         cp4(cq + i, A.qn + i);
@@ -383,9 +385,9 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
     const bool owner = pos >= t0 && pos < t0 + chunk;
     const int stride_t = A.Hkv * hd;
     {
-        const int pieces = hd / 8;
-        for (int i = tid; i < n * pieces; i += kClThreads) {
-            const int t = i / pieces, j = i - t * pieces;
+        const int lp = __ffs(hd) - 4;  // log2(hd / 8): 16-byte pieces per row
+        for (int i = tid; i < (n << lp); i += kClThreads) {
+            const int t = i >> lp, j = i & ((1 << lp) - 1);
             if (t0 + t == pos) continue;  // written below by this CTA
             const size_t g = (size_t)(t0 + t) * stride_t + (size_t)kh * hd + 8 * j;
             cp16_attn(kt + t * rowk + 8 * j, A.kc + g);
@@ -426,52 +428,61 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
     __syncthreads();  // K/V tiles and queries ready
 
     if (n > 0) {
-        // Scores: lpp lanes per position, DPL dims each.
+        // Scores: lpp lanes per position, DPL dims each: pieces of 8 dims at 8*(sub + lpp*c), so
+        // the lanes of a quarter warp read 128 contiguous bytes of a K row.  Two positions per
+        // step (independent chains).
         const int lpp = hd / DPL, ppw = 32 / lpp;
         const int sub = lane % lpp, pl = lane / lpp;
+        constexpr int NP = DPL / 8;  // 8-dim pieces per lane
         float qr[REP][DPL];
 #pragma unroll
         for (int r = 0; r < REP; ++r)
 #pragma unroll
-            for (int i = 0; i < DPL; i += 4) {
-                const float4 q4 = *reinterpret_cast<const float4 *>(qs + r * hd + sub * DPL + i);
-                qr[r][i] = q4.x;
-                qr[r][i + 1] = q4.y;
-                qr[r][i + 2] = q4.z;
-                qr[r][i + 3] = q4.w;
+            for (int c = 0; c < NP; ++c) {
+                const float *qp = qs + r * hd + 8 * (sub + lpp * c);
+                const float4 a = *reinterpret_cast<const float4 *>(qp), b = *reinterpret_cast<const float4 *>(qp + 4);
+                qr[r][8 * c] = a.x; qr[r][8 * c + 1] = a.y; qr[r][8 * c + 2] = a.z; qr[r][8 * c + 3] = a.w;
+                qr[r][8 * c + 4] = b.x; qr[r][8 * c + 5] = b.y; qr[r][8 * c + 6] = b.z; qr[r][8 * c + 7] = b.w;
             }
-        for (int tb = warp * ppw; tb < n; tb += (kClThreads / 32) * ppw) {
-            const int t = tb + pl;
-            float kv[DPL];
-            if (t < n) {
+        const int step = (kClThreads / 32) * ppw;
+        for (int tb = warp * ppw; tb < n; tb += 2 * step) {
+            float acc[2][REP];
 #pragma unroll
-                for (int i = 0; i < DPL; i += 8) {
-                    const uint4 w = *reinterpret_cast<const uint4 *>(kt + t * rowk + sub * DPL + i);
+            for (int h = 0; h < 2; ++h) {
+                const int t = tb + h * step + pl;
+                float kv[DPL];
+#pragma unroll
+                for (int c = 0; c < NP; ++c) {
+                    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+                    if (t < n) w = *reinterpret_cast<const uint4 *>(kt + t * rowk + 8 * (sub + lpp * c));
                     const float2 f0 = h2_to_f2(w.x), f1 = h2_to_f2(w.y), f2 = h2_to_f2(w.z), f3 = h2_to_f2(w.w);
-                    kv[i] = f0.x; kv[i + 1] = f0.y; kv[i + 2] = f1.x; kv[i + 3] = f1.y;
-                    kv[i + 4] = f2.x; kv[i + 5] = f2.y; kv[i + 6] = f3.x; kv[i + 7] = f3.y;
+                    kv[8 * c] = f0.x; kv[8 * c + 1] = f0.y; kv[8 * c + 2] = f1.x; kv[8 * c + 3] = f1.y;
+                    kv[8 * c + 4] = f2.x; kv[8 * c + 5] = f2.y; kv[8 * c + 6] = f3.x; kv[8 * c + 7] = f3.y;
                 }
-            } else {
 #pragma unroll
-                for (int i = 0; i < DPL; ++i) kv[i] = 0.f;
-            }
-            float acc[REP];
+                for (int r = 0; r < REP; ++r) {
+                    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int r = 0; r < REP; ++r) {
-                float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                for (int i = 0; i < DPL; i += 2) {
-                    a0 = fmaf(qr[r][i], kv[i], a0);
-                    a1 = fmaf(qr[r][i + 1], kv[i + 1], a1);
+                    for (int i = 0; i < DPL; i += 2) {
+                        a0 = fmaf(qr[r][i], kv[i], a0);
+                        a1 = fmaf(qr[r][i + 1], kv[i + 1], a1);
+                    }
+                    acc[h][r] = a0 + a1;
                 }
-                acc[r] = a0 + a1;
             }
             for (int o = lpp >> 1; o; o >>= 1)
 #pragma unroll
-                for (int r = 0; r < REP; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-            if (sub == 0 && t < n)
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int r = 0; r < REP; ++r) sc[r * chunk + t] = __fmul_rn(acc[r], A.scale);
+                    for (int r = 0; r < REP; ++r) acc[h][r] += __shfl_xor_sync(0xffffffffu, acc[h][r], o);
+            if (sub == 0)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int t = tb + h * step + pl;
+                    if (t < n)
+#pragma unroll
+                        for (int r = 0; r < REP; ++r) sc[r * chunk + t] = __fmul_rn(acc[h][r], A.scale);
+                }
         }
         __syncthreads();
         // Softmax per head: e = exp(s - m) into et[t][REPP], chunk max and sum.
@@ -535,13 +546,30 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
             lrow[tid] = 0.f;
         }
     }
-    cluster.sync();  // every split's (m, l, o) is visible in the cluster
-    for (int r = warp; r < REP; r += kClThreads / 32) {
-        float mj = -INFINITY, lj = 0.f;
-        if (lane < ns) {
-            mj = *cluster.map_shared_rank(mrow + r, lane);
-            lj = *cluster.map_shared_rank(lrow + r, lane);
+    // Merge at rank 0: every CTA stores its (m, l, o) into slot s of rank 0's merge area (its own
+    // region when the plan found room, else rank 0's K/V tiles once every CTA is done with them),
+    // one cluster barrier, then rank 0 merges from its own shared memory.
+    const int slot = REP * (hd + 2);
+    float *mg = A.merge_own ? fb + Ly.mg : reinterpret_cast<float *>(smem);
+    // Every CTA of the cluster has started (arrival at entry) before any shared memory of another
+    // is written; this CTA's (m, l, o) are complete.
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (!A.merge_own)
+        cluster.sync();  // also: every CTA is done with its K/V tiles
+    else
+        __syncthreads();
+    {
+        float *dst = cluster.map_shared_rank(mg, 0) + (size_t)s * slot;
+        for (int i = tid; i < slot; i += kClThreads) {
+            const int r = i / (hd + 2), j = i - r * (hd + 2);
+            dst[i] = j == 0 ? mrow[r] : (j == 1 ? lrow[r] : om[r * hd + j - 2]);
         }
+    }
+    cluster.sync();  // every split's (m, l, o) is in rank 0's merge area
+    if (s != 0) return;
+    for (int r = warp; r < REP; r += kClThreads / 32) {
+        const float mj = lane < ns ? mg[lane * slot + r * (hd + 2)] : -INFINITY;
+        const float lj = lane < ns ? mg[lane * slot + r * (hd + 2) + 1] : 0.f;
         float M = mj;
         for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         const float w = lane < ns ? expf(__fsub_rn(mj, M)) : 0.f;
@@ -551,12 +579,11 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
         if (lane < ns) wt[r * 16 + lane] = __fmul_rn(w, inv);
     }
     __syncthreads();
-    const int total = REP * hd, per = (total + ns - 1) / ns;
-    const int i0 = s * per, i1 = min(total, i0 + per);
-    for (int i = i0 + tid; i < i1; i += kClThreads) {
+    for (int i = tid; i < REP * hd; i += kClThreads) {
         const int r = i / hd, d = i - r * hd;
+        const float *src = mg + r * (hd + 2) + 2 + d;
         float o = 0.f;
-        for (int j = 0; j < ns; ++j) o = fmaf(wt[r * 16 + j], *cluster.map_shared_rank(om + i, j), o);
+        for (int j = 0; j < ns; ++j) o = fmaf(wt[r * 16 + j], src[(size_t)j * slot], o);
         const int h = kh * REP + r;
         if (A.gated) {
             const float g = A.q[(size_t)h * A.qstride + hd + d];
@@ -564,7 +591,6 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
         }
         A.out[(size_t)h * hd + d] = o;
     }
-    cluster.sync();  // no CTA leaves while another still reads its shared memory
 }
 
 template <int REP, int DPL>
@@ -617,15 +643,21 @@ cudaError_t launch_cl(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_
 
 // The cluster plan: chunk a multiple of 32 with at most 16 splits, in shared memory.  false: the
 // shape takes the scratch-merge kernel.
-bool cl_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem) {
+bool cl_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem, int &merge_own) {
     const int rep = A.H / A.Hkv;
     if (!(rep == 1 || rep == 2 || rep == 4 || rep == 6 || rep == 8)) return false;
     if (!(A.hd == 64 || A.hd == 128 || A.hd == 256)) return false;
     if (getenv("TRX_NO_CLUSTER_ATTN")) return false;
     chunk = ((A.max_pos + 15) / 16 + 31) / 32 * 32;
     nsplit = (A.max_pos + chunk - 1) / chunk;
-    smem = cl_smem_bytes(A.hd, rep, chunk);
-    return nsplit <= 16 && smem <= 227 * 1024;
+    if (nsplit > 16) return false;
+    // The merge area in its own region when two CTAs still fit an SM with it, else in rank 0's
+    // K/V tiles (which must then hold it).
+    const size_t own = cl_smem_bytes(A.hd, rep, chunk, nsplit), tiles_only = cl_smem_bytes(A.hd, rep, chunk, 0);
+    merge_own = own <= 113 * 1024 ? 1 : 0;
+    smem = merge_own ? own : tiles_only;
+    if (!merge_own && (size_t)chunk * (2 * A.hd + 8) * 2 < (size_t)nsplit * rep * (A.hd + 2) * 4) return false;
+    return smem <= 227 * 1024;
 }
 
 }  // namespace
@@ -647,7 +679,7 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
     {
         AttnArgs C = A0;
         size_t csmem = 0;
-        if (cl_plan(A0, C.chunk, C.nsplit, csmem)) {
+        if (cl_plan(A0, C.chunk, C.nsplit, csmem, C.merge_own)) {
             // 16 dims per lane up to 4 heads, 8 beyond: rep * DPL query values in registers <= 64.
             cudaError_t e;
             switch (A0.H / A0.Hkv) {

@@ -127,12 +127,6 @@ __host__ __device__ __forceinline__ uint32_t trit5_lut_entry(uint32_t b) {
     return d0 | (d1 << 8) | (d2 << 16) | ((d3 + 3 * d4) << 24);
 }
 
-// Round-half-away in the mirror's form: floor(x + 0.5f) for x >= 0, ceil(x - 0.5f) otherwise,
-// the +-0.5 added in fp32 round-to-nearest (model/mirror.py:34-35).
-__device__ __forceinline__ int lround_mirror(float x) {
-    return x >= 0.f ? (int)floorf(__fadd_rn(x, 0.5f)) : (int)ceilf(__fsub_rn(x, 0.5f));
-}
-
 // frexp exponent of a positive finite float (the e in x = m * 2^e, m in [0.5, 1)).
 __device__ __forceinline__ int frexp_exp(float a) {
     int e;
@@ -146,8 +140,5 @@ __device__ __forceinline__ int frexp_exp(float a) {
 // for a launch without the programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-// Request the 128-byte line holding p into L2 (no register result, no ordering).
-__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 }  // namespace trx

@@ -88,6 +88,7 @@ struct AttnArgs {
     float *part;        // scratch partials: [Hkv][nsplit][H/Hkv][hd + 2]
     unsigned *cnt;      // [Hkv] arrival counts, zero between launches
     int H, Hkv, hd, rope_half, qstride, gated, max_pos, chunk, nsplit;
+    int merge_own;      // cluster kernel: the merge area has its own shared region
     float eps, scale;
 };
 

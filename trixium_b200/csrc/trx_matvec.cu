@@ -85,9 +85,6 @@ struct MvGeom {
 };
 
 // cp.async (16-byte, L2 only) -----------------------------------------------------------------------
-__device__ __forceinline__ void cp16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
 // Predicated 16-byte copy to shared address dst + OFF.
 template <int OFF>
 __device__ __forceinline__ void cp16p(uint32_t dst, const void *src, bool p) {
@@ -365,21 +362,31 @@ __device__ __forceinline__ uint32_t absmax4(float4 v) {
                max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
 }
 
-__device__ __forceinline__ void stage_f32(float *dst, const float *src, int K) {
-    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) cp16(reinterpret_cast<float4 *>(dst) + i, reinterpret_cast<const float4 *>(src) + i);
-}
-
 template <int KIND>
 __device__ int build_activation_cp(const float *x, const float *nw, bool nw_ready, float eps, int K, float *xs,
-                                   float *nws, uint32_t *xp, float *red64) {
+                                   float *nws, uint32_t *xp, float *red64, uint64_t *mb, uint32_t parity,
+                                   uint32_t *err, bool &ok) {
     const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5, nwarps = blockDim.x >> 5;
     const int G = K / 128, n4 = K / 4;
     float4 *const xs4 = reinterpret_cast<float4 *>(xs);
-    stage_f32(xs, x, K);
-    if (nw && !nw_ready) stage_f32(nws, nw, K);
-    cp_commit();
-    cp_wait<0>();
+    // One bulk copy each (tracked by its own barrier, not by the weight rings' cp.async groups);
+    // thread 0 waits, bounded, and the block learns the outcome at the barrier.
+    uint32_t *const flag = reinterpret_cast<uint32_t *>(red64) + 48;
+    if (ct == 0) {
+        fence_proxy_async();  // earlier generic accesses to these bytes come first
+        mbar_arrive_expect_tx(mb, 4u * K);
+        bulk_g2s(xs, x, 4u * K, mb);
+        if (nw && !nw_ready) {
+            mbar_arrive_expect_tx(mb + 1, 4u * K);
+            bulk_g2s(nws, nw, 4u * K, mb + 1);
+        }
+        bool w = mbar_wait_bounded(mb, parity, err);
+        if (nw) w = mbar_wait_bounded(mb + 1, parity, err) && w;
+        *flag = w ? 1u : 0u;
+    }
     __syncthreads();
+    ok = *flag != 0u;
+    if (!ok) return 0;
     uint32_t m = 0;
     if (nw) {
         if (warp == 0) {
@@ -747,6 +754,7 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     float *const red64 = reinterpret_cast<float *>(p);
     p += 64 * 4;
     uint32_t *const amax_s = reinterpret_cast<uint32_t *>(p);
+    uint64_t *const mb = reinterpret_cast<uint64_t *>(p + 16);  // bulk-copy barriers: x, norm weight
     // Offsets (not pointers chosen between regions) keep every access provably shared.
     const int lut_off = 0x10000 - M.base, c_off = lut_off + kLutBytes;
     if (KIND == TRX_KIND_TERNARY5 && smem_u32(smem) != (uint32_t)M.base) {
@@ -827,9 +835,14 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     const int xs_off = M.stage_off + ((J.cols + 15) / 16) * 16;
     float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * J.cols);
     const int ne = (warp < M.na) == (M.sreg == 0) ? min(D - 1, M.ebl) : D - 1;
-    if (fast && J.norm_w) {  // the norm weight is written by no kernel: staged before the wait
-        stage_f32(nws, J.norm_w, J.cols);
-        cp_commit();
+    if (tid == 0) {
+        mbar_init(mb, 1);
+        mbar_init(mb + 1, 1);
+        mbar_fence_init();
+        if (fast && J.norm_w) {  // the norm weight is written by no kernel: requested before the wait
+            mbar_arrive_expect_tx(mb + 1, 4u * J.cols);
+            bulk_g2s(nws, J.norm_w, 4u * J.cols, mb + 1);
+        }
     }
     piece_begin(t0);
 #pragma unroll
@@ -841,6 +854,7 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         return;
     }
 
+    int npiece = 0;
     for (long long t = t0; t < t1;) {
         const bool first = t == t0;
         if (!first) piece_begin(t);
@@ -848,8 +862,15 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         __syncthreads();  // the previous piece's activation and rings are no longer in use
         const float *xj = J.x ? J.x + (uint64_t)job * J.x_stride : nullptr;
         const int8_t *x8j = J.x8 ? J.x8 + (uint64_t)job * J.x_stride : nullptr;
-        const int e8 = fast ? build_activation_cp<KIND>(xj, J.norm_w, first, J.eps, J.cols, xs, nws, xp, red64)
+        bool ok = true;
+        const int e8 = fast ? build_activation_cp<KIND>(xj, J.norm_w, first, J.eps, J.cols, xs, nws, xp, red64, mb,
+                                                        (uint32_t)(npiece & 1), err, ok)
                             : build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
+        ++npiece;
+        if (!ok) {  // a staging copy timed out (recorded): leave with no copy of ours in flight
+            cp_wait<0>();
+            return;
+        }
         unsigned long long best = 0ull;
 
         const int rounds = (pb - pa + R - 1) / R;
@@ -1099,7 +1120,7 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     M.grid = (int)std::min<long long>(sms, rbt);
     const long long rbc = (rbt + M.grid - 1) / M.grid;
     const bool split = rbc < kMaxWarps && M.nch > 1;
-    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 127) / 128 * 128 + (split ? 8192 : 0);
+    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 16 + 127) / 128 * 128 + (split ? 8192 : 0);
     M.D = kind == TRX_KIND_TERNARY5 ? 2 : 3;
     const int ring = M.D * nw * kBlkBytes;  // one warp's ring
     // The trit5 LUT sits at shared-window address 0x10000 (its PRMT-built addresses need no add):
