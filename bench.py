@@ -327,7 +327,7 @@ def main():
         e2e_step()
     b.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max(a.elapsed_time(b), 1e-9) if e2e_steps else float("nan")
+    e2e_ms = max(a.elapsed_time(b), 1e-9) if e2e_steps else 0.0  # 0: leg skipped (--no-extra)
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, launch_ms], device=dev)
@@ -354,7 +354,8 @@ def main():
                      "kernel": "trx::tmv_kernel (trx_matvec_f_batch)"},
         "per_launch_single_matvec": None if single_ms is None else {
             "ms_per_matvec": single_ms / C, "gbs": round(alg_per_copy * C / (single_ms * 1e-3) / 1e9, 1)},
-        "e2e": {"value": round(alg_per_step * args.steps * world / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "e2e": {"value": round(alg_per_step * args.steps * world / (e2e_ms * 1e-3) / 1e9, 1) if e2e_ms > 0 else None,
+                "unit": "GB/s",
                 "h2d_bytes_per_step": C * K_COLS * 4, "d2h_bytes_per_step": C * N_ROWS * 4},
         "gpu_launches": args.steps,
         "clocks": clocks,

@@ -338,3 +338,42 @@ class Decoder:
                 self.step()
         self.ctx.raise_on_error()
         return out.cpu().tolist()
+
+
+def main(argv=None):
+    """Decode timing on synthetic weights: python -m trixium_b200.decoder --config qwen3-8b
+    --context 1024 --tokens 64 [--eager].  Prints one JSON line (ms and tok/s per token)."""
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--config", default="qwen3-8b", choices=sorted(CONFIGS))
+    ap.add_argument("--context", type=int, default=1024)
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--eager", action="store_true", help="launch the kernels directly (no CUDA graph)")
+    a = ap.parse_args(argv)
+    cfg = CONFIGS[a.config]
+    dec = Decoder(SyntheticWeights(cfg, seed=0), max_pos=a.context + a.tokens + a.warmup + 8)
+    dec.set_states(1)
+    dec.fill_context(a.context)
+    dec.tok.fill_(7)
+    if not a.eager:
+        dec.capture()
+    for _ in range(a.warmup):
+        dec.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.tokens):
+        dec.step()
+    e1.record()
+    torch.cuda.synchronize()
+    dec.ctx.raise_on_error()
+    ms = e0.elapsed_time(e1) / a.tokens
+    print(json.dumps({"config": a.config, "context": a.context, "tokens": a.tokens, "graph": not a.eager,
+                      "ms_per_token": round(ms, 4), "tok_s": round(1000.0 / ms, 1),
+                      "launches_per_token": dec.launches_per_step()}))
+
+
+if __name__ == "__main__":
+    main()
