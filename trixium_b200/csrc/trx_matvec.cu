@@ -101,7 +101,10 @@ __device__ __forceinline__ void cp_wait() {
 
 // Quantisation helpers ----------------------------------------------------------------------------
 // 2^k as an fp32, exact for k in [-149, 127] (the scale of the power-of-two quantiser).
-__device__ __forceinline__ float pow2f(int k) { return ldexpf(1.0f, k); }
+__device__ __forceinline__ float pow2f(int k) {
+    if (k >= -126) return __int_as_float((min(k, 128) + 127) << 23);  // k = 128 gives inf
+    return k >= -149 ? __int_as_float(1 << (k + 149)) : 0.f;           // subnormal powers
+}
 
 // The value the quantiser sees at position k: x[k], or the RMS-normalised x[k]*r*w[k].
 __device__ __forceinline__ float prologue_value(const float *x, const float *w, float r, int k) {
@@ -152,26 +155,26 @@ __device__ __forceinline__ float warp_sumsq64(const float *xs, int K) {
     const int j = threadIdx.x & 31;
     float p0 = 0.f, p1 = 0.f;
     int i = j;
-    for (; i + 3 * 64 + 32 < K; i += 4 * 64) {
-        float v0[4], v1[4];
+    for (; i + 7 * 64 + 32 < K; i += 8 * 64) {  // eight steps of both chains per round, loads first
+        float a[8], b[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            v0[u] = xs[i + u * 64];
-            v1[u] = xs[i + u * 64 + 32];
+        for (int u = 0; u < 8; ++u) {
+            a[u] = xs[i + u * 64];
+            b[u] = xs[i + u * 64 + 32];
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            p0 = __fadd_rn(p0, __fmul_rn(v0[u], v0[u]));
-            p1 = __fadd_rn(p1, __fmul_rn(v1[u], v1[u]));
+        for (int u = 0; u < 8; ++u) {
+            p0 = __fadd_rn(p0, __fmul_rn(a[u], a[u]));
+            p1 = __fadd_rn(p1, __fmul_rn(b[u], b[u]));
         }
     }
     for (; i < K; i += 64) {
         p0 = __fadd_rn(p0, __fmul_rn(xs[i], xs[i]));
         if (i + 32 < K) p1 = __fadd_rn(p1, __fmul_rn(xs[i + 32], xs[i + 32]));
     }
-    float a = __fadd_rn(p0, p1);
-    for (int o = 16; o; o >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o));
-    return a;
+    float a2 = __fadd_rn(p0, p1);
+    for (int o = 16; o; o >>= 1) a2 = __fadd_rn(a2, __shfl_down_sync(0xffffffffu, a2, o));
+    return a2;
 }
 
 // Quantise x (fp32 in shared memory) straight into the permuted activation words, one warp per
@@ -601,8 +604,11 @@ __device__ __forceinline__ float silu_f32(float g) {
 
 
 // Row output --------------------------------------------------------------------------------------
-// Segment s of a launch holds rows [seg_start(s), seg[s].row_end) of the packed tensor.
-__device__ __forceinline__ int seg_start(const MvJobs &J, int s) { return s ? J.seg[s - 1].row_end : 0; }
+// Segment s of a launch holds rows [seg_start(s), seg[s].row_end) of the packed tensor.  The
+// kernel reads the segment table from a shared copy made before the dependency wait (a lookup by
+// a row-dependent index into the parameter block would miss the constant cache on the critical
+// path).
+__device__ __forceinline__ int seg_start(const MvSeg *segs, int s) { return s ? segs[s - 1].row_end : 0; }
 
 // Per-block output context (uniform over a block: blocks never straddle segments).
 struct RowOut {
@@ -612,8 +618,8 @@ struct RowOut {
     const float *resid;    // residual of the segment's row 0, or nullptr
 };
 
-__device__ __forceinline__ RowOut row_out(const MvJobs &J, int job, int s, int e8) {
-    const MvSeg &S = J.seg[s];
+__device__ __forceinline__ RowOut row_out(const MvJobs &J, const MvSeg *segs, int job, int s, int e8) {
+    const MvSeg &S = segs[s];
     RowOut o;
     o.R = S.R;
     o.B = S.B;
@@ -716,7 +722,8 @@ struct LaneRow {
     RowOut o;
 };
 
-__device__ __forceinline__ void lane_row(const MvJobs &J, int job, int row, int e8, const LaneRow &one, LaneRow &L) {
+__device__ __forceinline__ void lane_row(const MvJobs &J, const MvSeg *segs, int job, int row, int e8,
+                                         const LaneRow &one, LaneRow &L) {
     if (J.nseg == 1) {  // one tensor: the context of segment 0, computed once per job
         L = one;
         L.row = row < J.rows ? row : -1;
@@ -726,11 +733,11 @@ __device__ __forceinline__ void lane_row(const MvJobs &J, int job, int row, int 
     L.row = row < J.rows ? row : -1;
     int sg = 0;
 #pragma unroll
-    for (int i = 0; i < kMaxSegs - 1; ++i) sg += (i < J.nseg - 1 && row >= J.seg[i].row_end) ? 1 : 0;
-    L.o = row_out(J, job, sg, e8);
+    for (int i = 0; i < kMaxSegs - 1; ++i) sg += (i < J.nseg - 1 && row >= segs[i].row_end) ? 1 : 0;
+    L.o = row_out(J, segs, job, sg, e8);
     L.B = L.o.B;
     L.F = scale_fast(L.B);
-    L.srow = row - seg_start(J, sg);
+    L.srow = row - seg_start(segs, sg);
 }
 
 // The matvec kernel ---------------------------------------------------------------------------------
@@ -755,6 +762,8 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     p += 64 * 4;
     uint32_t *const amax_s = reinterpret_cast<uint32_t *>(p);
     uint64_t *const mb = reinterpret_cast<uint64_t *>(p + 16);  // bulk-copy barriers: x, norm weight
+    MvSeg *const segs = reinterpret_cast<MvSeg *>(p + 32);      // the segment table
+    if (tid < J.nseg) segs[tid] = J.seg[tid];                    // visible after the piece barrier
     // Offsets (not pointers chosen between regions) keep every access provably shared.
     const int lut_off = 0x10000 - M.base, c_off = lut_off + kLutBytes;
     if (KIND == TRX_KIND_TERNARY5 && smem_u32(smem) != (uint32_t)M.base) {
@@ -879,14 +888,14 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
             if (d >= (first ? ne : 0)) issue_next(ring_s + d * sstride);
         int rs = D - 1, slot = 0;
         LaneRow L, one;
-        one.o = row_out(J, job, 0, e8);
+        one.o = row_out(J, segs, job, 0, e8);
         one.B = one.o.B;
         one.F = scale_fast(one.B);
         for (int k = 0; k < rounds; ++k) {
             const int rbk = pa + k * R + gi;
             const bool valid = k < kval;
             long long acc0 = 0, acc1 = 0;
-            if (valid) lane_row(J, job, rbk * 32 + lane, e8, one, L);
+            if (valid) lane_row(J, segs, job, rbk * 32 + lane, e8, one, L);
             for (int c = cA; valid && c < cB; ++c) {
                 issue_next(ring_s + rs * sstride);
                 rs = rs + 1 == D ? 0 : rs + 1;
@@ -1120,7 +1129,8 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     M.grid = (int)std::min<long long>(sms, rbt);
     const long long rbc = (rbt + M.grid - 1) / M.grid;
     const bool split = rbc < kMaxWarps && M.nch > 1;
-    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 16 + 127) / 128 * 128 + (split ? 8192 : 0);
+    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 16 + kMaxSegs * (int)sizeof(MvSeg) + 127) / 128 * 128 +
+              (split ? 8192 : 0);
     M.D = kind == TRX_KIND_TERNARY5 ? 2 : 3;
     const int ring = M.D * nw * kBlkBytes;  // one warp's ring
     // The trit5 LUT sits at shared-window address 0x10000 (its PRMT-built addresses need no add):
