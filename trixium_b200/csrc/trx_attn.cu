@@ -593,13 +593,330 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
     }
 }
 
-template <int REP, int DPL>
-cudaError_t launch_cl(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_t st) {
-    static unsigned long long configured = 0;
+// Tensor-core variant (head dim 64 or 128, at most 8 query heads per kv head): the same
+// prologue and merge, with scores and P.V on mma.sync m16n8k16 (f16 in, f32 accumulate).  Per
+// warp, 16-position blocks: S = Q K^T with the heads as the 16 rows (rows >= REP zero) and the
+// fp32 queries split into two fp16 parts (q = hi + lo, both products accumulated), then an online
+// softmax per head within the warp, then O^T += V^T P^T with V^T fragments from ldmatrix.trans and
+// P^T fragments taken straight from the score accumulators (p split the same way).  K and V are
+// fp16 already, so every product is exact up to the f32 accumulation.  The warps' (m, l, O) are
+// combined in shared memory in a fixed order.
+struct MmaLayout {  // float offsets after the K and V tiles
+    int qs, cq, ck, cf, knew, wp, om, ml, wt, mg, total;
+};
+
+__host__ __device__ inline MmaLayout mma_layout(int hd, int rep) {
+    MmaLayout L;
+    int o = 0;
+    L.qs = o; o += rep * hd;
+    L.cq = o; o += hd;
+    L.ck = o; o += hd;
+    L.cf = o; o += hd / 2;
+    L.knew = o; o += hd;
+    L.wp = o; o += (kClThreads / 32) * rep * (hd + 2);  // per-warp (m, l, o)
+    L.om = o; o += rep * hd;
+    L.ml = o; o += 2 * rep;
+    L.wt = o; o += 16 * rep;
+    L.mg = o;
+    L.total = o;
+    return L;
+}
+
+__host__ __device__ inline size_t mma_smem_bytes(int hd, int rep, int chunk, int merge_slots) {
+    return (size_t)2 * chunk * (hd + 8) * 2 + ((size_t)mma_layout(hd, rep).total + (size_t)merge_slots * rep * (hd + 2)) * 4;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    uint32_t u;
+    memcpy(&u, &h, 4);
+    return u;
+}
+
+// x = hi + lo with hi = fp16(x), lo = fp16(x - hi), for a pair: (hi word, lo word).
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+    const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+    const __half2 H = __halves2half2(h0, h1), Lo = __halves2half2(l0, l1);
+    memcpy(&hi, &H, 4);
+    memcpy(&lo, &Lo, 4);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uint32_t *err) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int KS = HD / 16;  // 16-dim steps
+    constexpr int NWARP = kClThreads / 32;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int s = blockIdx.x, kh = blockIdx.y, ns = A.nsplit;
+    const int chunk = A.chunk, rowk = HD + 8, rep = A.H / A.Hkv;
+    __half *const kt = reinterpret_cast<__half *>(smem);  // [chunk][HD + 8]
+    __half *const vt = kt + (size_t)chunk * rowk;         // [chunk][HD + 8]
+    float *const fb = reinterpret_cast<float *>(vt + (size_t)chunk * rowk);
+    const MmaLayout Ly = mma_layout(HD, rep);
+    float *const qs = fb + Ly.qs, *const cq = fb + Ly.cq, *const ck = fb + Ly.ck, *const cf = fb + Ly.cf;
+    float *const knew = fb + Ly.knew, *const wp = fb + Ly.wp, *const om = fb + Ly.om;
+    float *const mrow = fb + Ly.ml, *const lrow = mrow + rep, *const wt = fb + Ly.wt;
+
+    pdl_trigger();
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");  // waited on before the merge
+    for (int i = tid; i < HD; i += kClThreads) {
+        cp4(cq + i, A.qn + i);
+        cp4(ck + i, A.kn + i);
+    }
+    for (int i = tid; i < A.rope_half; i += kClThreads) cp4(cf + i, A.freq + i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_wait();
+    const int pos = *A.pos;
+    if (pos < 0 || pos >= A.max_pos) {  // every CTA reads the same position: all leave together
+        if (tid == 0 && s == 0 && kh == 0) atomicOr(err, TRX_DEV_RANGE);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        return;
+    }
+    const int t0 = s * chunk;
+    const int n = max(0, min(chunk, pos + 1 - t0));
+    const int nb16 = (n + 15) >> 4;  // 16-position blocks in use
+    const bool owner = pos >= t0 && pos < t0 + chunk;
+    const int stride_t = A.Hkv * HD;
+    {
+        constexpr int lp = HD == 64 ? 3 : 4;  // log2(HD / 8)
+        for (int i = tid; i < (n << lp); i += kClThreads) {
+            const int t = i >> lp, j = i & ((1 << lp) - 1);
+            if (t0 + t == pos) continue;  // written below by this CTA
+            const size_t gix = (size_t)(t0 + t) * stride_t + (size_t)kh * HD + 8 * j;
+            cp16_attn(kt + t * rowk + 8 * j, A.kc + gix);
+            cp16_attn(vt + t * rowk + 8 * j, A.vc + gix);
+        }
+        // Rows [n, 16*nb16) of the last block: zero (their scores are masked; P.V must see 0).
+        for (int i = tid; i < ((16 * nb16 - n) << lp); i += kClThreads) {
+            const int t = n + (i >> lp), j = i & ((1 << lp) - 1);
+            *reinterpret_cast<uint4 *>(kt + t * rowk + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4 *>(vt + t * rowk + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
+    __syncthreads();  // the norm weights and frequencies are visible
+    if (n > 0) {
+        for (int r = warp; r < rep; r += NWARP) {
+            const float *qh = A.q + (size_t)(kh * rep + r) * A.qstride;
+            float *v = qs + r * HD;
+            for (int i = lane; i < HD; i += 32) v[i] = qh[i];
+            __syncwarp();
+            head_rmsnorm_s(v, HD, cq, A.eps, lane);
+            head_rope_s(v, A.rope_half, cf, pos, lane);
+        }
+        if (owner && warp == NWARP - 1) {
+            const float *kg = A.k + (size_t)kh * HD;
+            for (int i = lane; i < HD; i += 32) knew[i] = kg[i];
+            __syncwarp();
+            head_rmsnorm_s(knew, HD, ck, A.eps, lane);
+            head_rope_s(knew, A.rope_half, cf, pos, lane);
+            const int tp = pos - t0;
+            __half *kc = A.kc + (size_t)pos * stride_t + (size_t)kh * HD;
+            __half *vc = A.vc + (size_t)pos * stride_t + (size_t)kh * HD;
+            const float *vg = A.v + (size_t)kh * HD;
+            for (int i = lane; i < HD; i += 32) {
+                const __half k16 = __float2half_rn(knew[i]), v16 = __float2half_rn(vg[i]);
+                kc[i] = k16;
+                vc[i] = v16;
+                kt[tp * rowk + i] = k16;
+                vt[tp * rowk + i] = v16;
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // K/V tiles and queries ready
+
+    // Per warp: blocks warp, warp + NWARP, ...  Lane (g, c): head row g; the running max and sum of
+    // head g; O^T columns 2c, 2c+1 (heads) of every 16-dim tile.
+    float m_run = -INFINITY, l_run = 0.f;
+    float ot[KS][4];
+#pragma unroll
+    for (int i = 0; i < KS; ++i) ot[i][0] = ot[i][1] = ot[i][2] = ot[i][3] = 0.f;
+    if (warp < nb16) {
+        const float *qg = qs + (g < rep ? g : 0) * HD + 2 * c;  // rows g >= rep use zeros below
+        const uint32_t vbase = smem_u32(vt);
+        for (int b = warp; b < nb16; b += NWARP) {
+            const int tb = 16 * b;
+            float sh[2][4], sl[2][4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sh[nt][0] = sh[nt][1] = sh[nt][2] = sh[nt][3] = 0.f;
+                sl[nt][0] = sl[nt][1] = sl[nt][2] = sl[nt][3] = 0.f;
+                const __half *kr = kt + (tb + 8 * nt + g) * rowk + 2 * c;
+#pragma unroll 2
+                for (int k = 0; k < KS; ++k) {
+                    // A fragments a0 (row g, dims 16k + 2c, +1) and a2 (dims + 8, + 9), split in two
+                    // fp16 parts; a1 = a3 = 0 (rows g + 8).
+                    const float2 xa = *reinterpret_cast<const float2 *>(qg + 16 * k);
+                    const float2 xb = *reinterpret_cast<const float2 *>(qg + 16 * k + 8);
+                    const bool on = g < rep;
+                    uint32_t qh0, ql0, qh2, ql2;
+                    split_h2(on ? xa.x : 0.f, on ? xa.y : 0.f, qh0, ql0);
+                    split_h2(on ? xb.x : 0.f, on ? xb.y : 0.f, qh2, ql2);
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kr + 16 * k);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kr + 16 * k + 8);
+                    mma16816(sh[nt], qh0, 0u, qh2, 0u, b0, b1);
+                    mma16816(sl[nt], ql0, 0u, ql2, 0u, b0, b1);
+                }
+            }
+            // Scores of head g at positions tb + 2c, +1 (tile 0) and tb + 8 + 2c, +1 (tile 1).
+            float sv[4];
+            sv[0] = (sh[0][0] + sl[0][0]) * A.scale;
+            sv[1] = (sh[0][1] + sl[0][1]) * A.scale;
+            sv[2] = (sh[1][0] + sl[1][0]) * A.scale;
+            sv[3] = (sh[1][1] + sl[1][1]) * A.scale;
+            const int tq[4] = {tb + 2 * c, tb + 2 * c + 1, tb + 8 + 2 * c, tb + 9 + 2 * c};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (tq[i] >= n) sv[i] = -INFINITY;
+            float bm = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+            const float m_new = fmaxf(m_run, bm);  // finite: every block holds a position < n
+            const float alpha = expf(m_run - m_new);
+            float pv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pv[i] = g < rep ? expf(sv[i] - m_new) : 0.f;
+            l_run = l_run * alpha + ((pv[0] + pv[1]) + (pv[2] + pv[3]));
+            m_run = m_new;
+            // Rescale O^T columns (heads 2c, 2c+1) by their heads' alpha.
+            const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c), a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+#pragma unroll
+            for (int i = 0; i < KS; ++i) {
+                ot[i][0] *= a0;
+                ot[i][1] *= a1;
+                ot[i][2] *= a0;
+                ot[i][3] *= a1;
+            }
+            uint32_t ph0, pl0, ph1, pl1;
+            split_h2(pv[0], pv[1], ph0, pl0);
+            split_h2(pv[2], pv[3], ph1, pl1);
+            const uint32_t arow = (uint32_t)(tb + (lane & 7) + ((lane >> 4) & 1) * 8);
+            const uint32_t acol = (uint32_t)(((lane >> 3) & 1) * 8);
+#pragma unroll
+            for (int i = 0; i < KS; ++i) {
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_trans(vbase + (arow * rowk + 16 * i + acol) * 2, v0, v1, v2, v3);
+                mma16816(ot[i], v0, v1, v2, v3, ph0, ph1);
+                mma16816(ot[i], v0, v1, v2, v3, pl0, pl1);
+            }
+        }
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    }
+    // This warp's partial: (m, l) of head g (lanes 4g), O of heads 2c, 2c+1 at dims 16i + g, + 8.
+    {
+        float *w = wp + (size_t)warp * rep * (HD + 2);
+        if (c == 0 && g < rep) {
+            w[g * (HD + 2)] = m_run;
+            w[g * (HD + 2) + 1] = l_run;
+        }
+#pragma unroll
+        for (int i = 0; i < KS; ++i) {
+            const int d = 16 * i + g;
+            if (2 * c < rep) {
+                w[(2 * c) * (HD + 2) + 2 + d] = ot[i][0];
+                w[(2 * c) * (HD + 2) + 2 + d + 8] = ot[i][2];
+            }
+            if (2 * c + 1 < rep) {
+                w[(2 * c + 1) * (HD + 2) + 2 + d] = ot[i][1];
+                w[(2 * c + 1) * (HD + 2) + 2 + d + 8] = ot[i][3];
+            }
+        }
+    }
+    __syncthreads();
+    // Combine the warps in order: M = max m_w, o = sum e^(m_w - M) o_w, l = sum e^(m_w - M) l_w.
+    const int nwu = min(NWARP, max(nb16, 1));  // warps that held a block (warp 0 at least, possibly empty)
+    for (int i = tid; i < rep * HD; i += kClThreads) {
+        const int r = i / HD, d = i - r * HD;
+        float M = -INFINITY;
+        for (int w = 0; w < nwu; ++w) M = fmaxf(M, wp[(w * rep + r) * (HD + 2)]);
+        float o = 0.f;
+        if (M != -INFINITY)
+            for (int w = 0; w < nwu; ++w) {
+                const float *pw = wp + (w * rep + r) * (HD + 2);
+                o = fmaf(expf(pw[0] - M), pw[2 + d], o);
+            }
+        om[i] = o;
+        if (d == 0) {
+            float L = 0.f;
+            if (M != -INFINITY)
+                for (int w = 0; w < nwu; ++w) {
+                    const float *pw = wp + (w * rep + r) * (HD + 2);
+                    L = fmaf(expf(pw[0] - M), pw[1], L);
+                }
+            mrow[r] = M;
+            lrow[r] = L;
+        }
+    }
+    // Merge at rank 0, as in attn_cluster_kernel.
+    const int slot = rep * (HD + 2);
+    float *mg = A.merge_own ? fb + Ly.mg : reinterpret_cast<float *>(smem);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (!A.merge_own)
+        cluster.sync();
+    else
+        __syncthreads();
+    {
+        float *dst = cluster.map_shared_rank(mg, 0) + (size_t)s * slot;
+        for (int i = tid; i < slot; i += kClThreads) {
+            const int r = i / (HD + 2), j = i - r * (HD + 2);
+            dst[i] = j == 0 ? mrow[r] : (j == 1 ? lrow[r] : om[r * HD + j - 2]);
+        }
+    }
+    cluster.sync();  // every split's (m, l, o) is in rank 0's merge area
+    if (s != 0) return;
+    for (int r = warp; r < rep; r += NWARP) {
+        const float mj = lane < ns ? mg[lane * slot + r * (HD + 2)] : -INFINITY;
+        const float lj = lane < ns ? mg[lane * slot + r * (HD + 2) + 1] : 0.f;
+        float M = mj;
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = lane < ns ? expf(__fsub_rn(mj, M)) : 0.f;
+        float L = w * lj;
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = __fdiv_rn(1.0f, L);
+        if (lane < ns) wt[r * 16 + lane] = __fmul_rn(w, inv);
+    }
+    __syncthreads();
+    for (int i = tid; i < rep * HD; i += kClThreads) {
+        const int r = i / HD, d = i - r * HD;
+        const float *src = mg + r * (HD + 2) + 2 + d;
+        float o = 0.f;
+        for (int j = 0; j < ns; ++j) o = fmaf(wt[r * 16 + j], src[(size_t)j * slot], o);
+        const int h = kh * rep + r;
+        if (A.gated) {
+            const float gg = A.q[(size_t)h * A.qstride + HD + d];
+            o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg))));
+        }
+        A.out[(size_t)h * HD + d] = o;
+    }
+}
+
+// Launch a cluster attention kernel: one cluster of nsplit CTAs per kv head.
+template <typename K>
+cudaError_t launch_cluster(K k, unsigned long long &configured, const AttnArgs &A, uint32_t *err, size_t smem,
+                           cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     const unsigned long long bit = 1ull << (dev & 63);
-    auto k = attn_cluster_kernel<REP, DPL>;
     if (!(configured & bit)) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -622,23 +939,53 @@ cudaError_t launch_cl(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_
     cfg.numAttrs = 1;
     // A cluster this wide must fit on one GPC at this shared-memory size (asked once per shape).
     static struct {
+        const void *k;
         int dev, ns;
         size_t smem;
         int ok;
-    } seen[32];
+    } seen[64];
     static int nseen = 0;
     int ok = -1;
     for (int i = 0; i < nseen; ++i)
-        if (seen[i].dev == dev && seen[i].ns == A.nsplit && seen[i].smem == smem) ok = seen[i].ok;
+        if (seen[i].k == (const void *)k && seen[i].dev == dev && seen[i].ns == A.nsplit && seen[i].smem == smem)
+            ok = seen[i].ok;
     if (ok < 0) {
         int nc = 0;
         ok = cudaOccupancyMaxActiveClusters(&nc, k, &cfg) == cudaSuccess && nc > 0 ? 1 : 0;
         cudaGetLastError();
-        if (nseen < 32) seen[nseen++] = {dev, A.nsplit, smem, ok};
+        if (nseen < 64) seen[nseen++] = {(const void *)k, dev, A.nsplit, smem, ok};
     }
     if (!ok) return cudaErrorNotSupported;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, k, A, err);
+}
+
+template <int REP, int DPL>
+cudaError_t launch_cl(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_t st) {
+    static unsigned long long configured = 0;
+    return launch_cluster(attn_cluster_kernel<REP, DPL>, configured, A, err, smem, st);
+}
+
+template <int HD>
+cudaError_t launch_mma(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_t st) {
+    static unsigned long long configured = 0;
+    return launch_cluster(attn_mma_kernel<HD>, configured, A, err, smem, st);
+}
+
+// The tensor-core plan: the cluster chunking, head dim 64 or 128, at most 8 query heads per kv
+// head.
+bool mma_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem, int &merge_own) {
+    const int rep = A.H / A.Hkv;
+    if (rep < 1 || rep > 8 || !(A.hd == 64 || A.hd == 128)) return false;
+    if (getenv("TRX_NO_CLUSTER_ATTN") || getenv("TRX_NO_MMA_ATTN")) return false;
+    chunk = ((A.max_pos + 15) / 16 + 31) / 32 * 32;
+    nsplit = (A.max_pos + chunk - 1) / chunk;
+    if (nsplit > 16) return false;
+    const size_t own = mma_smem_bytes(A.hd, rep, chunk, nsplit), tiles_only = mma_smem_bytes(A.hd, rep, chunk, 0);
+    merge_own = own <= 113 * 1024 ? 1 : 0;
+    smem = merge_own ? own : tiles_only;
+    if (!merge_own && (size_t)chunk * (2 * A.hd + 16) * 2 < (size_t)nsplit * rep * (A.hd + 2) * 4) return false;
+    return smem <= 227 * 1024;
 }
 
 // The cluster plan: chunk a multiple of 32 with at most 16 splits, in shared memory.  false: the
@@ -679,6 +1026,10 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
     {
         AttnArgs C = A0;
         size_t csmem = 0;
+        if (mma_plan(A0, C.chunk, C.nsplit, csmem, C.merge_own)) {
+            const cudaError_t e = A0.hd == 64 ? launch_mma<64>(C, err, csmem, st) : launch_mma<128>(C, err, csmem, st);
+            if (e != cudaErrorNotSupported) return note_cuda(e);
+        }
         if (cl_plan(A0, C.chunk, C.nsplit, csmem, C.merge_own)) {
             // 16 dims per lane up to 4 heads, 8 beyond: rep * DPL query values in registers <= 64.
             cudaError_t e;
