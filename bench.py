@@ -31,6 +31,11 @@ import time
 
 import numpy as np
 
+# Symmetric (peer-mapped) buffers of the tensor-parallel leg without NVLink multicast objects.
+os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+# The tensor-parallel decode leg's exchange: the kernels over peer memory, or NCCL all-gathers.
+TP_PEER_EXCHANGE = False
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -419,14 +424,15 @@ def decode_leg(ctx, name, ctx_len, n_tokens, warmup):
 
 def tp_decode_leg(ctx, name, ctx_len, n_tokens, warmup, rank, world, dev):
     """Tensor-parallel batch-1 decode tok/s over `world` GPUs (trixium_b200.tp): every rank draws the
-    same synthetic image and keeps its row shard; one CUDA graph per token holds the kernels and
-    the NCCL all-gathers; the time is the max over ranks."""
+    same synthetic image and keeps its row shard; one CUDA graph per token holds the kernels, which
+    exchange the sharded vectors themselves over peer memory (NCCL all-gathers where a layer type
+    has no exchanging kernel); the time is the max over ranks."""
     import torch
     import torch.distributed as dist
     from trixium_b200 import decoder as D, tp
     cfg = D.CONFIGS[name]
     full = D.SyntheticWeights(cfg, seed=0)
-    dec = tp.TPDecoder(tp.TPWeights(full, rank, world), ctx=ctx, max_pos=ctx_len + n_tokens + warmup + 8)
+    dec = tp.TPDecoder(tp.TPWeights(full, rank, world), ctx=ctx, max_pos=ctx_len + n_tokens + warmup + 8, p2p=TP_PEER_EXCHANGE)
     del full
     torch.cuda.empty_cache()
     dec.set_states(1)
@@ -455,6 +461,7 @@ def tp_decode_leg(ctx, name, ctx_len, n_tokens, warmup, rank, world, dev):
            "tensor_parallel": world, "scaling": "strong", "tokens_timed": n_tokens, "ms_per_token": round(ms, 4),
            "tok_s": round(1000.0 / ms, 1), "weight_bytes_per_token": wb,
            "weight_GBps_all_gpus": round(wb / (ms * 1e-3) / 1e9, 1),
+           "exchange": "peer memory (kernels)" if dec.p2p else "nccl all-gather",
            "collectives_per_token": dec.collectives_per_step()}
     del dec
     torch.cuda.empty_cache()

@@ -258,6 +258,62 @@ trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *shape, cons
                              float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
                              cudaStream_t stream);
 
+/*
+ * Tensor-parallel exchange over peer memory (no counterpart in the reference, which runs on one
+ * device; the reference's multi-device plan shards output rows and all-gathers the hidden vector,
+ * which these calls do without a collective library).  Every rank holds the same buffers at
+ * addresses its peers can store to (peer-mapped device memory).  A producing launch stores each
+ * result into dst[r] + offset for every rank r other than its own (its own result goes to the
+ * launch's usual output) and, when every CTA is done, adds 1 to *signal[r] on every rank r
+ * (its own included).  A consuming launch first waits, bounded, until its own counter *wait
+ * holds (*step + 1) * world, the completions of this step's producers on every rank; on timeout
+ * it records TRX_DEV_TIMEOUT and goes on.  *step is this rank's step counter (advanced once per
+ * step, e.g. with trx_advance_position), *arrive a launch arrival count, zero between launches.
+ * Every rank must run the same sequence of exchanging launches.  NULL dst entries get no copy;
+ * signal[0] == NULL: the launch signals nothing; wait == NULL: it waits for nothing.
+ */
+#define TRX_TP_MAX 8
+typedef struct trx_tp_xfer {
+    uint32_t world, rank;            /* world <= TRX_TP_MAX, rank < world                  */
+    void *dst[TRX_TP_MAX];           /* each rank's destination base (device addresses)   */
+    uint32_t offset;                 /* elements: this rank's first element in dst[*]     */
+    uint32_t *signal[TRX_TP_MAX];    /* each rank's counter of the completed gather point */
+    const uint32_t *wait;            /* this rank's counter to wait on, or NULL           */
+    const int32_t *step;             /* this rank's step counter                          */
+    uint32_t *arrive;                /* arrival count of the signalling launch            */
+} trx_tp_xfer;
+
+/* trx_matvec_f with an exchange: float results copied to dst (offset + row), input waited on. */
+trx_status trx_matvec_f_tp(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                           const float *d_norm_w, float eps, const float *d_resid, float *d_y,
+                           const trx_tp_xfer *tp, cudaStream_t stream);
+
+/* trx_matvec_f_multi with an exchange (wait only: its outputs stay on this rank). */
+trx_status trx_matvec_f_multi_tp(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
+                                 const float *d_x, const float *d_norm_w, float eps, float *const *d_y,
+                                 const float *const *d_resid, const trx_tp_xfer *tp, cudaStream_t stream);
+
+/* trx_matvec_swiglu with an exchange: silu(g)*u copied to dst (offset + row), input waited on. */
+trx_status trx_matvec_swiglu_tp(trx_ctx *ctx, const trx_entry *gate, const void *d_gate, const trx_entry *up,
+                                const void *d_up, const float *d_x, const float *d_norm_w, float eps,
+                                float *d_act, const trx_tp_xfer *tp, cudaStream_t stream);
+
+/* trx_lmhead_argmax_key with an exchange: the key copied to dst (offset, uint64), input waited on. */
+trx_status trx_lmhead_argmax_key_tp(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                                    const float *d_norm_w, float eps, uint32_t row_offset, float *d_logits,
+                                    uint64_t *d_key, const trx_tp_xfer *tp, cudaStream_t stream);
+
+/* trx_argmax_token after waiting for the exchange of the keys. */
+trx_status trx_argmax_token_tp(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token,
+                               const trx_tp_xfer *tp, cudaStream_t stream);
+
+/* trx_attn_decode with an exchange: out[h][d] copied to dst (offset + h*hd + d).  Head dims 64 and
+ * 128 with at most 8 query heads per kv head only (TRX_ERR_UNSUPPORTED otherwise). */
+trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *shape, const float *d_q, const float *d_k,
+                              const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                              const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                              float *d_out, const trx_tp_xfer *tp, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,3 +37,17 @@ def test_row_bytes(cols, kind):
 def test_row_bytes_rejects_bad_layouts():
     assert _lib.lib().trx_row_bytes(100, 5) == 0
     assert _lib.lib().trx_row_bytes(128, 3) == 0
+
+
+def test_bindings_match_header_arity():
+    """Every ctypes binding takes as many arguments as its prototype in the header declares."""
+    import re
+    from trixium_b200 import _lib
+    h = open(os.path.join(ROOT, "include", "trixium_b200.h")).read()
+    L = _lib.lib()
+    protos = re.findall(r"trx_status\s+(trx_\w+)\s*\(([^;]*)\);", h)
+    assert protos
+    for name, args in protos:
+        fn = getattr(L, name)
+        assert fn.argtypes is not None, name
+        assert len(fn.argtypes) == len([a for a in args.split(",") if a.strip()]), name

@@ -25,11 +25,12 @@ def single_gpu_tokens(name, device=0):
     return d.generate(PROMPT, N_NEW)
 
 
-def tp_tokens(name, rank, world, group=None, graph=False):
+def tp_tokens(name, rank, world, group=None, graph=False, p2p=False):
     from trixium_b200 import decoder as D, ops, tp
     full = D.SyntheticWeights(D.CONFIGS[name], seed=5)
     dec = tp.TPDecoder(tp.TPWeights(full, rank, world), group=group, ctx=ops.Context(torch.cuda.current_device()),
-                       max_pos=64)
+                       max_pos=64, p2p=p2p)
+    assert dec.p2p == (p2p and world > 1)
     del full
     if dec.state:
         dec.set_states(seed=2)
@@ -47,14 +48,16 @@ def test_tp_world1_matches_decoder(name):
     assert tp_tokens(name, 0, 1, graph=True) == want
 
 
-def _rank(rank, world, port, name, out):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+def _rank(rank, world, port, name, out, p2p=False):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
     torch.cuda.set_device(rank)
     from datetime import timedelta
     torch.distributed.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                                          device_id=torch.device("cuda", rank))
     try:
-        out[rank] = (tp_tokens(name, rank, world, graph=False), tp_tokens(name, rank, world, graph=True))
+        out[rank] = (tp_tokens(name, rank, world, graph=False, p2p=p2p),
+                     tp_tokens(name, rank, world, graph=True, p2p=p2p))
     finally:
         torch.distributed.destroy_process_group()
 
@@ -69,6 +72,25 @@ def test_tp_world2_matches_decoder(name):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     procs = [ctx.Process(target=_rank, args=(r, 2, port, name, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert out[r][0] == want and out[r][1] == want
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp_world2_peer_exchange_matches_decoder():
+    """The all-gathers done by the kernels themselves over peer memory (no NCCL on the data path)."""
+    want = single_gpu_tokens("tiny")
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, "tiny", out, True)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

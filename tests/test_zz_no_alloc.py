@@ -1,7 +1,10 @@
-"""The context-free decode attention (trx_attn_decode_static: static scratch, no allocation by the
-library) against the context entry point (trx_attn_decode): two calls in a row on identical inputs
-and separate caches give bit-identical outputs and cache rows.  Collected last on purpose: it must
-pass alone and after every other test of the session.
+"""The context-free decode attention (trx_attn_decode_static) against the context entry point
+(trx_attn_decode), for callers that must not allocate device memory while they run: two calls in a
+row on identical inputs and separate caches.  The static entry runs the scratch-merge kernel on the
+library's static arrays, the context entry the tensor-core kernel for this shape, so the outputs
+agree within the attention tolerance (1e-3 of the output scale), the cache rows written before
+exactly and the new rows within one fp16 step.  Collected last on purpose: it must pass alone and
+after every other test of the session.
 """
 import numpy as np
 import pytest
@@ -40,8 +43,12 @@ def test_static_attention_matches_context_entry():
             want = ops.attn_decode(ctx, shape, q, k, v, qn, kn, freq, caches[0][0], caches[0][1], pos)
             got = ops.attn_decode_static(shape, q, k, v, qn, kn, freq, caches[1][0], caches[1][1], pos, err)
             torch.cuda.synchronize()
-            assert torch.equal(got, want)
-            assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
+            scale = max(1.0, float(want.abs().max()))
+            assert float((got - want).abs().max()) <= 1e-3 * scale
+            p = 300 + step
+            for a, b in zip(caches[0], caches[1]):
+                assert torch.equal(a[:p], b[:p]) and torch.equal(a[p + 1:], b[p + 1:])
+                assert torch.allclose(a[p].float(), b[p].float(), rtol=1e-3, atol=1e-3)
         assert int(err.item()) == 0
         assert ctx.errors() == 0
     finally:

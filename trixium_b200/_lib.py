@@ -23,8 +23,12 @@ SYMBOLS = (
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
     "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
     "trx_deltanet_step", "trx_lmhead_argmax", "trx_matvec_f_multi", "trx_embed_lookup", "trx_advance_position",
-    "trx_attn_decode_static", "trx_lmhead_argmax_key", "trx_argmax_token",
+    "trx_attn_decode_static", "trx_lmhead_argmax_key", "trx_argmax_token", "trx_matvec_f_tp",
+    "trx_matvec_f_multi_tp", "trx_matvec_swiglu_tp", "trx_lmhead_argmax_key_tp", "trx_argmax_token_tp",
+    "trx_attn_decode_tp",
 )
+
+TP_MAX = 8
 
 
 class TrxError(RuntimeError):
@@ -56,6 +60,13 @@ class DeltaNetShape(ctypes.Structure):
                 ("v_head_dim", ctypes.c_uint32), ("conv_kernel", ctypes.c_uint32), ("eps", ctypes.c_float)]
 
 
+class TpXfer(ctypes.Structure):
+    """trx_tp_xfer: a launch's tensor-parallel exchange over peer memory."""
+    _fields_ = [("world", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("dst", ctypes.c_void_p * TP_MAX),
+                ("offset", ctypes.c_uint32), ("signal", ctypes.c_void_p * TP_MAX), ("wait", ctypes.c_void_p),
+                ("step", ctypes.c_void_p), ("arrive", ctypes.c_void_p)]
+
+
 class Entry(ctypes.Structure):
     """trx_entry: the BONS entry fields a matvec needs."""
     _fields_ = [("rows", ctypes.c_uint32), ("cols", ctypes.c_uint32), ("kind", ctypes.c_int32),
@@ -73,6 +84,7 @@ def lib():
             raise ImportError(f"{LIB_PATH} is not built (python -m trixium_b200.build)")
         L = ctypes.CDLL(LIB_PATH)
         E = ctypes.POINTER(Entry)
+        T = ctypes.POINTER(TpXfer)
         sig = {
             "trx_create": ([ctypes.POINTER(_vp), ctypes.c_int], ctypes.c_int),
             "trx_destroy": ([_vp], ctypes.c_int),
@@ -100,6 +112,14 @@ def lib():
             "trx_lmhead_argmax_key": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, ctypes.c_uint32, _vp, _vp, _vp],
                                       ctypes.c_int),
             "trx_argmax_token": ([_vp, _vp, ctypes.c_int32, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f_tp": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, T, _vp], ctypes.c_int),
+            "trx_matvec_f_multi_tp": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, T, _vp],
+                                      ctypes.c_int),
+            "trx_matvec_swiglu_tp": ([_vp, E, _vp, E, _vp, _vp, _vp, ctypes.c_float, _vp, T, _vp], ctypes.c_int),
+            "trx_lmhead_argmax_key_tp": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, ctypes.c_uint32, _vp, _vp, T, _vp],
+                                         ctypes.c_int),
+            "trx_argmax_token_tp": ([_vp, _vp, ctypes.c_int32, _vp, T, _vp], ctypes.c_int),
+            "trx_attn_decode_tp": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 10 + [T, _vp], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -907,7 +907,11 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
             o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg))));
         }
         A.out[(size_t)h * HD + d] = o;
+        for (int rr = 0; rr < A.tp.world; ++rr)  // the other ranks' copies (tensor-parallel gather)
+            if (rr != A.tp.rank && A.tp.dst[rr])
+                reinterpret_cast<float *>(A.tp.dst[rr])[A.tp.offset + (size_t)h * HD + d] = o;
     }
+    tp_signal(A.tp, gridDim.y);  // the rank-0 CTAs of the clusters arrive
 }
 
 // Launch a cluster attention kernel: one cluster of nsplit CTAs per kv head.
@@ -1023,13 +1027,14 @@ size_t attn_smem_bytes(int hd, int rep, int chunk) {
 }
 
 trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st) {
-    {
+    if (!A0.scratch_merge) {
         AttnArgs C = A0;
         size_t csmem = 0;
         if (mma_plan(A0, C.chunk, C.nsplit, csmem, C.merge_own)) {
             const cudaError_t e = A0.hd == 64 ? launch_mma<64>(C, err, csmem, st) : launch_mma<128>(C, err, csmem, st);
             if (e != cudaErrorNotSupported) return note_cuda(e);
         }
+        if (A0.tp.world) return TRX_ERR_UNSUPPORTED;  // only the tensor-core kernel exchanges its output
         if (cl_plan(A0, C.chunk, C.nsplit, csmem, C.merge_own)) {
             // 16 dims per lane up to 4 heads, 8 beyond: rep * DPL query values in registers <= 64.
             cudaError_t e;
@@ -1157,5 +1162,6 @@ extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const flo
     A.out = d_out;
     A.part = sc.part;
     A.cnt = sc.cnt;
+    A.scratch_merge = 1;  // the kernel whose partials and counts are the static arrays above
     return trx::launch_attn_decode(A, d_err, stream);
 }

@@ -168,13 +168,48 @@ trx_status trx_quantize_pow2(trx_ctx *ctx, const float *d_x, uint32_t n, int8_t 
     return trx::launch_quantize(d_x, (int)n, d_x8, d_e8, stream);
 }
 
+// A C-ABI tensor-parallel exchange as the kernels' TpXfer (all zero when t is NULL).  what: which
+// parts apply to the call (copies to dst, a completion signal, a wait before the input is read).
+enum { TP_PUSH = 1, TP_SIGNAL = 2, TP_WAIT = 4 };
+static trx_status tp_resolve(const trx_tp_xfer *t, int what, trx::TpXfer &X) {
+    X = trx::TpXfer{};
+    if (!t) return TRX_OK;
+    if (t->world < 1 || t->world > TRX_TP_MAX || t->rank >= t->world) return TRX_ERR_ARG;
+    X.world = (int)t->world;
+    X.rank = (int)t->rank;
+    X.offset = (int)t->offset;
+    if (what & TP_PUSH)
+        for (uint32_t r = 0; r < t->world; ++r) X.dst[r] = t->dst[r];
+    if ((what & TP_SIGNAL) && t->signal[0]) {
+        for (uint32_t r = 0; r < t->world; ++r) {
+            if (!t->signal[r]) return TRX_ERR_ARG;
+            X.signal[r] = t->signal[r];
+        }
+        if (!t->arrive) return TRX_ERR_ARG;
+        X.arrive = t->arrive;
+    }
+    if ((what & TP_WAIT) && t->wait) {
+        if (!t->step) return TRX_ERR_ARG;
+        X.wait = t->wait;
+        X.step = t->step;
+    }
+    return TRX_OK;
+}
+
 trx_status trx_matvec_f(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
                         const float *d_norm_w, float eps, const float *d_resid, float *d_y, cudaStream_t stream) {
+    return trx_matvec_f_tp(ctx, e, d_packed, d_x, d_norm_w, eps, d_resid, d_y, nullptr, stream);
+}
+
+trx_status trx_matvec_f_tp(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                           const float *d_norm_w, float eps, const float *d_resid, float *d_y,
+                           const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx) return TRX_ERR_ARG;
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x || !d_y || !aligned16(d_packed)) return TRX_ERR_ARG;
     trx::MvJobs J = base_jobs(ctx, e, d_packed);
+    if ((s = tp_resolve(tp, TP_PUSH | TP_SIGNAL | TP_WAIT, J.tp))) return s;
     J.x = d_x;
     J.norm_w = d_norm_w;
     J.eps = eps;
@@ -200,6 +235,12 @@ trx_status trx_matvec_fp(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
 trx_status trx_matvec_swiglu(trx_ctx *ctx, const trx_entry *gate, const void *d_gate, const trx_entry *up,
                              const void *d_up, const float *d_x, const float *d_norm_w, float eps, float *d_act,
                              cudaStream_t stream) {
+    return trx_matvec_swiglu_tp(ctx, gate, d_gate, up, d_up, d_x, d_norm_w, eps, d_act, nullptr, stream);
+}
+
+trx_status trx_matvec_swiglu_tp(trx_ctx *ctx, const trx_entry *gate, const void *d_gate, const trx_entry *up,
+                                const void *d_up, const float *d_x, const float *d_norm_w, float eps,
+                                float *d_act, const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx) return TRX_ERR_ARG;
     trx_status s = check_entry(gate);
     if (s) return s;
@@ -208,6 +249,7 @@ trx_status trx_matvec_swiglu(trx_ctx *ctx, const trx_entry *gate, const void *d_
     if (gate->rows != up->rows || gate->cols != up->cols || gate->kind != up->kind) return TRX_ERR_ARG;
     if (!d_gate || !d_up || !d_x || !d_act || !aligned16(d_gate) || !aligned16(d_up)) return TRX_ERR_ARG;
     trx::MvJobs J = base_jobs(ctx, gate, d_gate);
+    if ((s = tp_resolve(tp, TP_PUSH | TP_SIGNAL | TP_WAIT, J.tp))) return s;
     J.w2 = static_cast<const uint8_t *>(d_up);
     J.B2 = up->bias;
     J.R2 = up->rshift;
@@ -251,6 +293,12 @@ trx_status trx_matvec_f_batch(trx_ctx *ctx, const trx_entry *e, const void *d_pa
 trx_status trx_matvec_f_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
                               const float *d_x, const float *d_norm_w, float eps, float *const *d_y,
                               const float *const *d_resid, cudaStream_t stream) {
+    return trx_matvec_f_multi_tp(ctx, entries, nseg, d_packed, d_x, d_norm_w, eps, d_y, d_resid, nullptr, stream);
+}
+
+trx_status trx_matvec_f_multi_tp(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
+                                 const float *d_x, const float *d_norm_w, float eps, float *const *d_y,
+                                 const float *const *d_resid, const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx || !entries || nseg < 1 || nseg > trx::kMaxSegs || !d_y) return TRX_ERR_ARG;
     uint64_t rows = 0;
     for (int i = 0; i < nseg; ++i) {
@@ -262,6 +310,7 @@ trx_status trx_matvec_f_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, 
     if (rows > (1u << 30)) return TRX_ERR_UNSUPPORTED;
     if (!d_packed || !d_x || !aligned16(d_packed)) return TRX_ERR_ARG;
     trx::MvJobs J = base_jobs(ctx, &entries[0], d_packed);
+    if (trx_status st = tp_resolve(tp, TP_WAIT, J.tp)) return st;
     J.rows = (int)rows;
     J.nseg = nseg;
     int end = 0;
@@ -314,6 +363,13 @@ trx_status trx_lmhead_argmax(trx_ctx *ctx, const trx_entry *e, const void *d_pac
 trx_status trx_lmhead_argmax_key(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
                                  const float *d_norm_w, float eps, uint32_t row_offset, float *d_logits,
                                  uint64_t *d_key, cudaStream_t stream) {
+    return trx_lmhead_argmax_key_tp(ctx, e, d_packed, d_x, d_norm_w, eps, row_offset, d_logits, d_key, nullptr,
+                                    stream);
+}
+
+trx_status trx_lmhead_argmax_key_tp(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                                    const float *d_norm_w, float eps, uint32_t row_offset, float *d_logits,
+                                    uint64_t *d_key, const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx) return TRX_ERR_ARG;
     trx_status s = check_entry(e);
     if (s) return s;
@@ -329,18 +385,36 @@ trx_status trx_lmhead_argmax_key(trx_ctx *ctx, const trx_entry *e, const void *d
     J.key_out = reinterpret_cast<unsigned long long *>(d_key);
     J.row_offset = (int)row_offset;
     J.arg_cnt = ctx->amax_cnt;
+    if ((s = tp_resolve(tp, TP_PUSH | TP_SIGNAL | TP_WAIT, J.tp))) return s;
+    J.tp.arrive = nullptr;  // the argmax tail's last CTA signals
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
 
 trx_status trx_argmax_token(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token, cudaStream_t stream) {
+    return trx_argmax_token_tp(ctx, d_keys, n, d_token, nullptr, stream);
+}
+
+trx_status trx_argmax_token_tp(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token,
+                               const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx || !d_keys || !d_token || n < 1) return TRX_ERR_ARG;
-    return trx::launch_argmax_keys(reinterpret_cast<const unsigned long long *>(d_keys), n, d_token, stream);
+    trx::TpXfer X;
+    if (trx_status s = tp_resolve(tp, TP_WAIT, X)) return s;
+    return trx::launch_argmax_keys(reinterpret_cast<const unsigned long long *>(d_keys), n, d_token, X, ctx->err,
+                                   stream);
 }
 
 trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
                            const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
                            const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
                            float *d_out, cudaStream_t stream) {
+    return trx_attn_decode_tp(ctx, sh, d_q, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope_freq, d_kcache, d_vcache, d_pos,
+                              d_out, nullptr, stream);
+}
+
+trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
+                              const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                              const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                              float *d_out, const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx || !sh) return TRX_ERR_ARG;
     const uint32_t H = sh->n_head, Hkv = sh->n_kv, hd = sh->head_dim;
     if (H == 0 || Hkv == 0 || H % Hkv || Hkv > kAttnMaxKv || hd == 0 || hd % 8 || hd > 512) return TRX_ERR_ARG;
@@ -378,6 +452,7 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *
     A.out = d_out;
     A.part = ctx->attn_part;
     A.cnt = ctx->attn_cnt;
+    if (trx_status s = tp_resolve(tp, TP_PUSH | TP_SIGNAL, A.tp)) return s;
     return trx::launch_attn_decode(A, ctx->err, stream);
 }
 

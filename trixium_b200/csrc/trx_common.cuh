@@ -78,6 +78,46 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return true;
 }
 
+// Tensor-parallel waits and signals (TpXfer, trx_internal.h) ---------------------------------------
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread: wait until *wait >= (*step + 1) * world (peers' completions of the gather point),
+// bounded by kWaitNs (then TRX_DEV_TIMEOUT is recorded and the caller goes on).  The fence orders
+// the peers' stores before later bulk (async-proxy) reads of the same bytes.
+template <typename T>
+__device__ __forceinline__ void tp_wait(const T &X, uint32_t *err) {
+    if (!X.wait) return;
+    const unsigned target = (unsigned)(*X.step + 1) * (unsigned)X.world;
+    if ((int)(ld_acquire_sys(X.wait) - target) < 0) {
+        const unsigned long long t0 = global_ns();
+        while ((int)(ld_acquire_sys(X.wait) - target) < 0) {
+            if (global_ns() - t0 > kWaitNs) {
+                atomicOr(err, TRX_DEV_TIMEOUT);
+                break;
+            }
+        }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Every thread of an arriving CTA (after its stores): the last of `arrivals` CTAs adds 1 to every
+// rank's counter.
+template <typename T>
+__device__ __forceinline__ void tp_signal(const T &X, unsigned arrivals) {
+    if (!X.signal[0]) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(X.arrive, 1u) == arrivals - 1) {
+        *X.arrive = 0u;
+        __threadfence_system();
+        for (int r = 0; r < X.world; ++r) atomicAdd_system(X.signal[r], 1u);
+    }
+}
+
 // Integer dot products ---------------------------------------------------------------------------
 // acc + sum_k a.byte[k] * b.byte[k], a's bytes unsigned, b's signed (PTX dp4a.u32.s32).
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int acc) {

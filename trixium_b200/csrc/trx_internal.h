@@ -32,6 +32,21 @@ inline cudaError_t launch_kernel(void (*k)(KArgs...), dim3 grid, dim3 block, siz
 
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_SWIGLU = 2 };
 
+// Tensor-parallel exchange of one launch over peer memory (trx_tp_xfer of the C ABI).  A producer
+// stores its results into every rank's destination too and, once all its CTAs are done, adds 1 to
+// every rank's counter of the gather point; a consumer waits (bounded) until its own counter holds
+// (step + 1) * world arrivals before it reads its input.
+constexpr int kTpMax = 8;
+struct TpXfer {
+    int world, rank;
+    void *dst[kTpMax];          // each rank's destination base (nullptr: no copy to that rank)
+    int offset;                 // elements: this rank's first element in every destination
+    unsigned *signal[kTpMax];   // each rank's counter of the completed gather point (signal[0] null: none)
+    const unsigned *wait;       // this rank's counter to wait on before reading the input (nullptr: none)
+    const int *step;            // this rank's step counter
+    unsigned *arrive;           // this launch's arrival count, zero between launches
+};
+
 constexpr int kMaxSegs = 4;
 
 // A row segment of a launch: rows [previous row_end, row_end) belong to one tensor with its
@@ -68,6 +83,7 @@ struct MvJobs {
     unsigned long long *key_out; // if set (with argmax): per job, the argmax key itself (row + row_offset)
     int row_offset;              // added to the row in the argmax key (a shard's first global row)
     const int *skip;             // if set and *skip != 0, the launch does nothing
+    TpXfer tp;                   // tensor-parallel exchange (tp.world == 0: none)
 };
 
 // Argmax key of (value, row): orderable float bits in the high word, ~row in the low word, so
@@ -89,6 +105,8 @@ struct AttnArgs {
     unsigned *cnt;      // [Hkv] arrival counts, zero between launches
     int H, Hkv, hd, rope_half, qstride, gated, max_pos, chunk, nsplit;
     int merge_own;      // cluster kernel: the merge area has its own shared region
+    int scratch_merge;  // run the scratch-merge kernel on part/cnt even where a cluster kernel applies
+    TpXfer tp;          // tensor-parallel exchange of the output (tp.world == 0: none)
     float eps, scale;
 };
 
@@ -114,7 +132,8 @@ int attn_chunk(int max_pos, int hd);
 trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
                         cudaStream_t st);
 trx_status launch_advance(int *pos, int n, cudaStream_t st);
-trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, cudaStream_t st);
+trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, const TpXfer &tp, uint32_t *err,
+                              cudaStream_t st);
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);

@@ -631,6 +631,13 @@ __device__ __forceinline__ RowOut row_out(const MvJobs &J, const MvSeg *segs, in
     return o;
 }
 
+// A result's copies into the other ranks' destinations (tensor-parallel all-gather by stores over
+// peer memory).
+__device__ __forceinline__ void tp_push(const TpXfer &T, int i, float v) {
+    for (int r = 0; r < T.world; ++r)
+        if (r != T.rank && T.dst[r]) reinterpret_cast<float *>(T.dst[r])[T.offset + i] = v;
+}
+
 // Finish one row (srow: index within its segment) from its int64 sum(s): >> R, the overflow
 // checks of model/bitexact.py:116,118, then the launch's output.  SwiGLU: a = gate, a2 = up.
 // Returns the row's argmax key (0 when the launch keeps no argmax).
@@ -645,11 +652,14 @@ __device__ __forceinline__ unsigned long long finish_row(const MvJobs &J, const 
         if (o.resid) v = __fadd_rn(o.resid[srow], v);
         if (o.y) reinterpret_cast<float *>(o.y)[srow] = v;
         if (J.argmax) key = argmax_key(v, (uint32_t)(row + J.row_offset));
+        tp_push(J.tp, srow, v);
     } else {  // OUT_SWIGLU
         bad = bad || acc_bad(a2, o.R2);
         const float gv = __fmul_rn((float)(int)(a >> o.R), o.sc);
         const float uv = __fmul_rn((float)(int)(a2 >> o.R2), o.sc2);
-        reinterpret_cast<float *>(o.y)[srow] = __fmul_rn(silu_f32(gv), uv);
+        const float v = __fmul_rn(silu_f32(gv), uv);
+        reinterpret_cast<float *>(o.y)[srow] = v;
+        tp_push(J.tp, srow, v);
     }
     if (bad) atomicOr(err, TRX_DEV_OVERFLOW);
     return key;
@@ -858,6 +868,10 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     for (int d = 0; d < D - 1; ++d)
         if (d < ne) issue_next(ring_s + d * sstride);
     pdl_wait();
+    if (J.tp.wait) {  // the input's other ranks' parts are stored here by their launches
+        if (tid == 0) tp_wait(J.tp, err);
+        __syncthreads();
+    }
     if (J.skip && *J.skip) {
         cp_wait<0>();
         return;
@@ -955,6 +969,7 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
         __syncwarp();
         if (J.argmax) argmax_commit(J, job, best, lane);
     }
+    if (!J.key_out) tp_signal(J.tp, gridDim.x);
     if (J.token || J.key_out) {  // greedy tokens: the last CTA to arrive hands out each job's key
         __syncthreads();
         if (tid == 0) {
@@ -967,9 +982,20 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
             for (int j = tid; j < J.njobs; j += blockDim.x) {
                 const unsigned long long k = atomicExch(J.argmax + j, 0ull);
                 if (J.token) J.token[j] = k ? (int)(0xffffffffu - (uint32_t)k) : -1;
-                if (J.key_out) J.key_out[j] = k;
+                if (J.key_out) {
+                    J.key_out[j] = k;
+                    for (int r = 0; r < J.tp.world; ++r)
+                        if (r != J.tp.rank && J.tp.dst[r])
+                            reinterpret_cast<unsigned long long *>(J.tp.dst[r])[J.tp.offset + j] = k;
+                }
             }
             if (tid == 0) *J.arg_cnt = 0u;
+            if (J.key_out && J.tp.signal[0]) {  // this launch is complete on this rank
+                __threadfence_system();
+                __syncthreads();
+                if (tid == 0)
+                    for (int r = 0; r < J.tp.world; ++r) atomicAdd_system(J.tp.signal[r], 1u);
+            }
         }
     }
 }

@@ -29,10 +29,11 @@ __global__ void embed_kernel(const void *table, int vocab, int dim, int f16, con
 }
 
 // The token of the largest of n argmax keys (one per shard of a row-sharded LM head).
-__global__ void argmax_keys_kernel(const unsigned long long *keys, int n, int *token) {
+__global__ void argmax_keys_kernel(const unsigned long long *keys, int n, int *token, TpXfer tp, uint32_t *err) {
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) {
+        tp_wait(tp, err);  // the other ranks' keys, stored here by their launches
         unsigned long long best = 0ull;
         for (int i = 0; i < n; ++i) best = keys[i] > best ? keys[i] : best;
         *token = best ? (int)(0xffffffffu - (uint32_t)best) : -1;
@@ -51,8 +52,9 @@ trx_status launch_embed(const void *table, int vocab, int dim, int f16, const in
     return note_cuda(launch_kernel(embed_kernel, dim3(blocks), dim3(256), 0, st, table, vocab, dim, f16, token, x, err));
 }
 
-trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, cudaStream_t st) {
-    return note_cuda(launch_kernel(argmax_keys_kernel, dim3(1), dim3(32), 0, st, keys, n, token));
+trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, const TpXfer &tp, uint32_t *err,
+                              cudaStream_t st) {
+    return note_cuda(launch_kernel(argmax_keys_kernel, dim3(1), dim3(32), 0, st, keys, n, token, tp, err));
 }
 
 trx_status launch_advance(int *pos, int n, cudaStream_t st) {

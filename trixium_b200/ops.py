@@ -131,7 +131,7 @@ def quantize_pow2(ctx, x, x8=None, e8=None):
     return x8, e8
 
 
-def matvec_f(ctx, w: DeviceTensor, x, y=None, norm_w=None, eps=1e-6, resid=None):
+def matvec_f(ctx, w: DeviceTensor, x, y=None, norm_w=None, eps=1e-6, resid=None, tp=None):
     _need(x, torch.float32, "x")
     if norm_w is not None:
         _need(norm_w, torch.float32, "norm_w")
@@ -139,6 +139,11 @@ def matvec_f(ctx, w: DeviceTensor, x, y=None, norm_w=None, eps=1e-6, resid=None)
         _need(resid, torch.float32, "resid")
     if y is None:
         y = torch.empty(w.rows, dtype=torch.float32, device=x.device)
+    if tp is not None:  # tensor-parallel exchange (a _lib.TpXfer)
+        _lib.check(_lib.lib().trx_matvec_f_tp(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(norm_w),
+                                              ctypes.c_float(eps), _ptr(resid), _ptr(y), ctypes.byref(tp),
+                                              _stream()), "trx_matvec_f_tp")
+        return y
     _lib.check(_lib.lib().trx_matvec_f(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(norm_w),
                                        ctypes.c_float(eps), _ptr(resid), _ptr(y), _stream()), "trx_matvec_f")
     return y
@@ -153,10 +158,16 @@ def matvec_fp(ctx, w: DeviceTensor, x, y=None):
     return y
 
 
-def matvec_swiglu(ctx, gate: DeviceTensor, up: DeviceTensor, x, act=None, norm_w=None, eps=1e-6):
+def matvec_swiglu(ctx, gate: DeviceTensor, up: DeviceTensor, x, act=None, norm_w=None, eps=1e-6, tp=None):
     _need(x, torch.float32, "x")
     if act is None:
         act = torch.empty(gate.rows, dtype=torch.float32, device=x.device)
+    if tp is not None:
+        _lib.check(_lib.lib().trx_matvec_swiglu_tp(ctx.h, ctypes.byref(gate.entry), _ptr(gate.data),
+                                                   ctypes.byref(up.entry), _ptr(up.data), _ptr(x), _ptr(norm_w),
+                                                   ctypes.c_float(eps), _ptr(act), ctypes.byref(tp), _stream()),
+                   "trx_matvec_swiglu_tp")
+        return act
     _lib.check(_lib.lib().trx_matvec_swiglu(ctx.h, ctypes.byref(gate.entry), _ptr(gate.data),
                                             ctypes.byref(up.entry), _ptr(up.data), _ptr(x), _ptr(norm_w),
                                             ctypes.c_float(eps), _ptr(act), _stream()), "trx_matvec_swiglu")
@@ -176,7 +187,7 @@ def matvec_f_batch(ctx, w: DeviceTensor, w_stride, x, x_stride, y, y_stride, njo
     return y
 
 
-def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, out=None):
+def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, out=None, tp=None):
     """One decode step of GQA attention (trx_attn_decode).  shape: _lib.AttnShape; q (H*(1+gated)*hd),
     k/v (n_kv*hd) float32; caches [max_pos, n_kv, hd] float16; pos: int32 device tensor of one
     element (the position written and attended up to)."""
@@ -189,6 +200,12 @@ def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, 
         _need(rope_freq, torch.float32, "rope_freq")
     if out is None:
         out = torch.empty(shape.n_head * shape.head_dim, dtype=torch.float32, device=q.device)
+    if tp is not None:
+        _lib.check(_lib.lib().trx_attn_decode_tp(ctx.h, ctypes.byref(shape), _ptr(q), _ptr(k), _ptr(v),
+                                                 _ptr(q_norm), _ptr(k_norm), _ptr(rope_freq), _ptr(kcache),
+                                                 _ptr(vcache), _ptr(pos), _ptr(out), ctypes.byref(tp), _stream()),
+                   "trx_attn_decode_tp")
+        return out
     _lib.check(_lib.lib().trx_attn_decode(ctx.h, ctypes.byref(shape), _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
                                           _ptr(k_norm), _ptr(rope_freq), _ptr(kcache), _ptr(vcache), _ptr(pos),
                                           _ptr(out), _stream()), "trx_attn_decode")
@@ -218,7 +235,7 @@ def attn_shape(n_head, n_kv, head_dim, max_pos, rope_dims=None, gated=False, eps
                           1 if gated else 0, eps)
 
 
-def matvec_f_multi(ctx, entries, packed, x, ys, norm_w=None, eps=1e-6, resids=None):
+def matvec_f_multi(ctx, entries, packed, x, ys, norm_w=None, eps=1e-6, resids=None, tp=None):
     """Segments sharing one input (trx_matvec_f_multi): entries (list of _lib.Entry), packed (their row
     packets back to back, uint8 CUDA tensor), ys (one float32 output per segment)."""
     n = len(entries)
@@ -228,6 +245,11 @@ def matvec_f_multi(ctx, entries, packed, x, ys, norm_w=None, eps=1e-6, resids=No
     rp = None
     if resids is not None:
         rp = (ctypes.c_void_p * n)(*[(r.data_ptr() if r is not None else None) for r in resids])
+    if tp is not None:
+        _lib.check(_lib.lib().trx_matvec_f_multi_tp(ctx.h, arr, n, _ptr(packed), _ptr(x), _ptr(norm_w),
+                                                    ctypes.c_float(eps), yp, rp, ctypes.byref(tp), _stream()),
+                   "trx_matvec_f_multi_tp")
+        return ys
     _lib.check(_lib.lib().trx_matvec_f_multi(ctx.h, arr, n, _ptr(packed), _ptr(x), _ptr(norm_w), ctypes.c_float(eps),
                                              yp, rp, _stream()), "trx_matvec_f_multi")
     return ys
@@ -266,21 +288,31 @@ def lmhead_argmax(ctx, w: DeviceTensor, x, token=None, logits=None, norm_w=None,
     return token
 
 
-def lmhead_argmax_key(ctx, w: DeviceTensor, x, key, row_offset=0, logits=None, norm_w=None, eps=1e-6):
+def lmhead_argmax_key(ctx, w: DeviceTensor, x, key, row_offset=0, logits=None, norm_w=None, eps=1e-6, tp=None):
     """One shard of a row-sharded LM head: key (int64 device tensor of one element) = the shard's
     argmax key with global row = local row + row_offset (trx_lmhead_argmax_key)."""
     _need(x, torch.float32, "x")
     _need(key, torch.int64, "key")
+    if tp is not None:
+        _lib.check(_lib.lib().trx_lmhead_argmax_key_tp(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x),
+                                                       _ptr(norm_w), ctypes.c_float(eps), int(row_offset),
+                                                       _ptr(logits), _ptr(key), ctypes.byref(tp), _stream()),
+                   "trx_lmhead_argmax_key_tp")
+        return key
     _lib.check(_lib.lib().trx_lmhead_argmax_key(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(norm_w),
                                                 ctypes.c_float(eps), int(row_offset), _ptr(logits), _ptr(key),
                                                 _stream()), "trx_lmhead_argmax_key")
     return key
 
 
-def argmax_token(ctx, keys, token):
+def argmax_token(ctx, keys, token, tp=None):
     """token = the row of the largest key in `keys` (int64 device tensor of gathered shard keys)."""
     _need(keys, torch.int64, "keys")
     _need(token, torch.int32, "token")
+    if tp is not None:
+        _lib.check(_lib.lib().trx_argmax_token_tp(ctx.h, _ptr(keys), keys.numel(), _ptr(token), ctypes.byref(tp),
+                                                  _stream()), "trx_argmax_token_tp")
+        return token
     _lib.check(_lib.lib().trx_argmax_token(ctx.h, _ptr(keys), keys.numel(), _ptr(token), _stream()),
                "trx_argmax_token")
     return token

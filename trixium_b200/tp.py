@@ -146,7 +146,7 @@ class TPDecoder:
     """Greedy batch-1 decoding of a TPWeights shard; every rank runs the same steps in the same order
     (the all-gathers are NCCL collectives on `group`, captured with the kernels in one CUDA graph)."""
 
-    def __init__(self, weights: TPWeights, group=None, ctx=None, max_pos=4096):
+    def __init__(self, weights: TPWeights, group=None, ctx=None, max_pos=4096, p2p=False):
         import torch
         from . import ops
         cfg = self.cfg = weights.cfg
@@ -189,6 +189,80 @@ class TPDecoder:
             self.beta, self.alpha = f32(d_sh.nv), f32(d_sh.nv)
             self.og_loc, self.og = f32(d_sh.nv * cfg.dn_hv), f32(cfg.dn_nv * cfg.dn_hv)
         self.graph = None
+        self.p2p = bool(p2p) and self.world > 1 and self._p2p_supported(a_sh)
+        if self.p2p:
+            self._setup_p2p(a_sh)
+
+    # Exchange over peer memory ------------------------------------------------------------------
+    # Instead of an NCCL all-gather after each sharded projection, the producing kernel stores its
+    # rows into every rank's copy of the vector (peer-mapped symmetric buffers) and signals each
+    # rank's counter of that gather point; the consuming kernel waits on its own counter.  Gather
+    # points per step: per layer attention output, x after o, act, x after down; then the LM-head
+    # keys.
+    def _p2p_supported(self, a_sh):
+        cfg = self.cfg
+        if any(cfg.layer_type(l) != "a" for l in range(cfg.n_layer)) or a_sh is None:
+            return False  # DeltaNet outputs are gathered with NCCL
+        rep = a_sh.n_head // a_sh.n_kv
+        return cfg.head_dim in (64, 128) and 1 <= rep <= 8  # the tensor-core attention exchanges
+
+    def _setup_p2p(self, a_sh):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        cfg, dev = self.cfg, self.tok.device
+        gname = (self.group or dist.group.WORLD).group_name
+        self._symm = []
+
+        def shared(n, dtype):
+            t = symm.empty(n, dtype=dtype, device=dev)
+            t.zero_()
+            h = symm.rendezvous(t, gname)
+            self._symm.append((t, h))
+            return t, [int(p) for p in h.buffer_ptrs]
+
+        E, F, N = cfg.hidden, cfg.ffn, self.world
+        self.n_points = 4 * cfg.n_layer + 1
+        self.x, px = shared(E, torch.float32)
+        self.attn, pa = shared(cfg.n_head * cfg.head_dim, torch.float32)
+        self.act, pf = shared(F, torch.float32)
+        self.keys, pk = shared(N, torch.int64)
+        self.cnt, pc = shared(self.n_points, torch.int32)
+        self.step_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.arrive = torch.zeros(self.n_points, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        w, r = self.w, self.rank
+        a0 = a_sh.kv0 * (a_sh.n_head // a_sh.n_kv) * cfg.head_dim
+
+        def xfer(dst_ptrs=None, offset=0, signal=None, wait=None):
+            t = _lib.TpXfer()
+            t.world, t.rank, t.offset = N, r, offset
+            if dst_ptrs is not None:
+                for q in range(N):
+                    t.dst[q] = dst_ptrs[q] if q != r else None
+            if signal is not None:
+                for q in range(N):
+                    t.signal[q] = pc[q] + 4 * signal
+                t.arrive = self.arrive.data_ptr() + 4 * signal
+            if wait is not None:
+                t.wait = self.cnt.data_ptr() + 4 * wait
+            t.step = self.step_ctr.data_ptr()
+            return t
+
+        # Gather points: layer l: 4l attention output, 4l+1 x after o, 4l+2 act, 4l+3 x after down.
+        self._tp = []
+        for l in range(cfg.n_layer):
+            self._tp.append({
+                "qkv": xfer(wait=4 * l - 1) if l else None,
+                "attn": xfer(pa, a0, signal=4 * l),
+                "o": xfer(px, w.e0, signal=4 * l + 1, wait=4 * l),
+                "swiglu": xfer(pf, w.f0, signal=4 * l + 2, wait=4 * l + 1),
+                "down": xfer(px, w.e0, signal=4 * l + 3, wait=4 * l + 2),
+            })
+        self._tp_lm = xfer(pk, r, signal=4 * cfg.n_layer, wait=4 * cfg.n_layer - 1)
+        self._tp_tok = xfer(wait=4 * cfg.n_layer)
 
     def _gather(self, out, inp):
         import torch.distributed as dist
@@ -222,6 +296,8 @@ class TPDecoder:
     def enqueue_step(self):
         """One token on every rank: reads self.tok and self.pos, writes the next token (the same on
         every rank) and advances the position."""
+        if self.p2p:
+            return self._enqueue_step_p2p()
         from . import ops
         cfg, w, ctx = self.cfg, self.w, self.ctx
         xr = self.x[w.e0:w.e1]  # this rank's rows of the residual stream
@@ -253,12 +329,44 @@ class TPDecoder:
         ops.argmax_token(ctx, self.keys, self.tok)
         ops.advance_position(ctx, self.pos)
 
+    def _enqueue_step_p2p(self):
+        from . import ops
+        cfg, w, ctx = self.cfg, self.w, self.ctx
+        xr = self.x[w.e0:w.e1]
+        hd = cfg.head_dim
+        a_loc = None
+        ops.embed_lookup(ctx, w.emb, self.tok, self.x)
+        for l, lw in enumerate(w.layers):
+            t = self._tp[l]
+            p = lw["in"]
+            sh = lw["shard"]
+            if a_loc is None:
+                a0 = sh.kv0 * (sh.n_head // sh.n_kv) * hd
+                a_loc = self.attn[a0:a0 + sh.n_head * hd]
+            ops.matvec_f_multi(ctx, p.entries, p.data, self.x, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
+                               eps=cfg.eps, tp=t["qkv"])
+            ops.attn_decode(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"], w.rope_freq,
+                            self.kc[l], self.vc[l], self.pos, a_loc, tp=t["attn"])
+            ops.matvec_f(ctx, lw["out"], self.attn, y=xr, resid=xr, tp=t["o"])
+            ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x, act=self.act[w.f0:w.f1], norm_w=lw["ffn_norm"],
+                              eps=cfg.eps, tp=t["swiglu"])
+            ops.matvec_f(ctx, lw["down"], self.act, y=xr, resid=xr, tp=t["down"])
+        ops.lmhead_argmax_key(ctx, w.lm_head, self.x, self.keys[self.rank:self.rank + 1], row_offset=w.v0,
+                              norm_w=w.out_norm, eps=cfg.eps, tp=self._tp_lm)
+        ops.argmax_token(ctx, self.keys, self.tok, tp=self._tp_tok)
+        ops.advance_position(ctx, self.pos)
+        ops.advance_position(ctx, self.step_ctr)
+
     def collectives_per_step(self):
+        """NCCL collectives per step (0 when the exchanges go over peer memory)."""
+        if self.p2p:
+            return 0
         return 4 * self.cfg.n_layer + 1
 
     def _mutable(self):
+        extra = [self.cnt, self.step_ctr, self.arrive] if self.p2p else []
         return [self.tok, self.pos] + list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + \
-            list(self.state.values())
+            list(self.state.values()) + extra
 
     def capture(self):
         """One step as a CUDA graph on every rank (NCCL collectives captured with the kernels)."""
@@ -273,6 +381,10 @@ class TPDecoder:
         for t, c in zip(live, saved):
             t.copy_(c)
         del saved
+        if self.p2p:  # every rank's counters are restored before any rank signals again
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
             with torch.cuda.graph(self.graph, stream=s):
