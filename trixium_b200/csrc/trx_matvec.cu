@@ -652,7 +652,7 @@ __device__ __forceinline__ unsigned long long finish_row(const MvJobs &J, const 
         if (o.resid) v = __fadd_rn(o.resid[srow], v);
         if (o.y) reinterpret_cast<float *>(o.y)[srow] = v;
         if (J.argmax) key = argmax_key(v, (uint32_t)(row + J.row_offset));
-        tp_push(J.tp, srow, v);
+        if (!J.key_out) tp_push(J.tp, srow, v);  // a key launch exchanges its key, not its rows
     } else {  // OUT_SWIGLU
         bad = bad || acc_bad(a2, o.R2);
         const float gv = __fmul_rn((float)(int)(a >> o.R), o.sc);

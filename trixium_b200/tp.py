@@ -220,7 +220,9 @@ class TPDecoder:
             t.zero_()
             h = symm.rendezvous(t, gname)
             self._symm.append((t, h))
-            return t, [int(p) for p in h.buffer_ptrs]
+            base = [int(p) for p in h.buffer_ptrs]
+            off = t.data_ptr() - base[self.rank]  # the tensor's place inside its symmetric block
+            return t, [b + off for b in base]
 
         E, F, N = cfg.hidden, cfg.ffn, self.world
         self.n_points = 4 * cfg.n_layer + 1
