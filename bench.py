@@ -35,7 +35,7 @@ import numpy as np
 os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
 # The tensor-parallel decode leg's exchange (TRX_TP_EXCHANGE): "peer", the kernels over peer
 # memory, or "nccl", NCCL all-gathers.
-TP_PEER_EXCHANGE = os.environ.get("TRX_TP_EXCHANGE", "nccl") == "peer"
+TP_PEER_EXCHANGE = os.environ.get("TRX_TP_EXCHANGE", "peer") == "peer"
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
