@@ -105,16 +105,19 @@ __device__ __forceinline__ void tp_wait(const T &X, uint32_t *err) {
 }
 
 // Every thread of an arriving CTA (after its stores): the last of `arrivals` CTAs adds 1 to every
-// rank's counter.
+// rank's counter.  One system-scope fence per CTA, by the thread that arrives, after the block
+// barrier that orders the other threads' stores before it.
 template <typename T>
 __device__ __forceinline__ void tp_signal(const T &X, unsigned arrivals) {
     if (!X.signal[0]) return;
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(X.arrive, 1u) == arrivals - 1) {
-        *X.arrive = 0u;
+    if (threadIdx.x == 0) {
         __threadfence_system();
-        for (int r = 0; r < X.world; ++r) atomicAdd_system(X.signal[r], 1u);
+        if (atomicAdd(X.arrive, 1u) == arrivals - 1) {
+            *X.arrive = 0u;
+            __threadfence_system();
+            for (int r = 0; r < X.world; ++r) atomicAdd_system(X.signal[r], 1u);
+        }
     }
 }
 

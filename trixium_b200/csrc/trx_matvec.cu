@@ -991,10 +991,11 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
             }
             if (tid == 0) *J.arg_cnt = 0u;
             if (J.key_out && J.tp.signal[0]) {  // this launch is complete on this rank
-                __threadfence_system();
                 __syncthreads();
-                if (tid == 0)
+                if (tid == 0) {
+                    __threadfence_system();
                     for (int r = 0; r < J.tp.world; ++r) atomicAdd_system(J.tp.signal[r], 1u);
+                }
             }
         }
     }
