@@ -78,3 +78,21 @@ def test_sharded_oracle_matches_unsharded(name):
         p.join(timeout=300)
         assert p.exitcode == 0
     assert out[0] == want and out[1] == want
+
+
+@pytest.mark.parametrize("n_layer", [1, 2, 36])
+def test_exchange_plan_signals_before_waits(n_layer):
+    """Every gather point is signalled exactly once per step, by a launch that comes before the
+    launch waiting on it, and every point is waited on (no rank can run ahead into a buffer that a
+    peer has not read yet)."""
+    plan = tp.exchange_plan(n_layer)
+    signalled, waited = {}, set()
+    for i, (op, l, sig, wt) in enumerate(plan):
+        if wt is not None:
+            assert wt in signalled and signalled[wt] < i, (op, l, wt)
+            waited.add(wt)
+        if sig is not None:
+            assert sig not in signalled, (op, l, sig)
+            signalled[sig] = i
+    assert sorted(signalled) == list(range(4 * n_layer + 1))
+    assert waited == set(signalled)

@@ -142,6 +142,18 @@ class TPWeights:
 
 # The tensor-parallel decoder ----------------------------------------------------------------------
 
+def exchange_plan(n_layer):
+    """The peer-memory exchanges of one step, in launch order: (op, layer, gather point signalled or
+    None, gather point waited on or None).  Gather points: layer l: 4l attention output, 4l+1 x
+    after o, 4l+2 act, 4l+3 x after down; 4*n_layer the LM-head keys."""
+    plan = []
+    for l in range(n_layer):
+        plan += [("qkv", l, None, 4 * l - 1 if l else None), ("attn", l, 4 * l, None),
+                 ("o", l, 4 * l + 1, 4 * l), ("swiglu", l, 4 * l + 2, 4 * l + 1), ("down", l, 4 * l + 3, 4 * l + 2)]
+    plan += [("lm", n_layer - 1, 4 * n_layer, 4 * n_layer - 1), ("token", n_layer - 1, None, 4 * n_layer)]
+    return plan
+
+
 class TPDecoder:
     """Greedy batch-1 decoding of a TPWeights shard; every rank runs the same steps in the same order
     (the all-gathers are NCCL collectives on `group`, captured with the kernels in one CUDA graph)."""
@@ -253,18 +265,17 @@ class TPDecoder:
             t.step = self.step_ctr.data_ptr()
             return t
 
-        # Gather points: layer l: 4l attention output, 4l+1 x after o, 4l+2 act, 4l+3 x after down.
-        self._tp = []
-        for l in range(cfg.n_layer):
-            self._tp.append({
-                "qkv": xfer(wait=4 * l - 1) if l else None,
-                "attn": xfer(pa, a0, signal=4 * l),
-                "o": xfer(px, w.e0, signal=4 * l + 1, wait=4 * l),
-                "swiglu": xfer(pf, w.f0, signal=4 * l + 2, wait=4 * l + 1),
-                "down": xfer(px, w.e0, signal=4 * l + 3, wait=4 * l + 2),
-            })
-        self._tp_lm = xfer(pk, r, signal=4 * cfg.n_layer, wait=4 * cfg.n_layer - 1)
-        self._tp_tok = xfer(wait=4 * cfg.n_layer)
+        dst = {"attn": (pa, a0), "o": (px, w.e0), "swiglu": (pf, w.f0), "down": (px, w.e0), "lm": (pk, r)}
+        self._tp = [dict() for _ in range(cfg.n_layer)]
+        for op, l, sig, wt in exchange_plan(cfg.n_layer):
+            ptrs, off = dst.get(op, (None, 0))
+            t = xfer(ptrs, off, signal=sig, wait=wt) if (sig is not None or wt is not None) else None
+            if op == "lm":
+                self._tp_lm = t
+            elif op == "token":
+                self._tp_tok = t
+            else:
+                self._tp[l][op] = t
 
     def _gather(self, out, inp):
         import torch.distributed as dist
