@@ -372,6 +372,8 @@ def main():
         # The metric's second half: 8B-shape batch-1 decode tok/s (config 2), and config 1.
         out["decode"] = {"qwen3-8b": decode_leg(ctx, "qwen3-8b", 1024, 128, 8),
                          "qwen3-1.7b": decode_leg(ctx, "qwen3-1.7b", 512, 128, 8)}
+    if world == 1 and not args.no_decode:
+        out["q8_matvec"] = q8_leg(ctx, peak)
     if rank == 0 and world == 1 and not args.no_cpu:
         out["cpu_baseline"] = cpu_baseline(kind, args.cpu_seconds)
     if rank == 0:
@@ -380,6 +382,51 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def q8_leg(ctx, peak, rows=16384, cols=8192, launches=20, warmup=3):
+    """The Q8 row-dot matvec (trx_matvec_q8, model/bitexact.py:127-144) on a KIND_Q8 tensor of
+    rows x cols int8 weights with fp16 group-32 scales, two copies used in turn (272 MB, above
+    L2).  Algorithmic bytes per launch: the weights, the scales, x8 and the int32 results."""
+    import numpy as np
+    import torch
+    from trixium_b200 import image, layout as L, ops
+    rng = np.random.default_rng(21)
+    G = cols // 32
+    s = rng.uniform(0.005, 0.02, (rows, G)).astype(np.float16)
+    B = image.scale_bias(s)
+    R = image.result_shift(s, B, image.GS_MAX_Q8)
+    sb = L.ceil_div(G, L.SCALES_PER_BEAT) * L.BEAT_BYTES
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    tensors = []
+    for _ in range(2):
+        packed = torch.zeros(rows, L.q8_row_bytes(cols), dtype=torch.uint8, device="cuda")
+        packed[:, :2 * G] = torch.from_numpy(s).cuda().view(torch.uint8)
+        packed[:, sb:] = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, device="cuda",
+                                       generator=gen).view(torch.uint8)
+        tensors.append(ops.DeviceTensor.from_packed(packed.reshape(-1), rows, cols, L.KIND_Q8, B, R))
+    x8 = torch.randint(-127, 128, (cols,), dtype=torch.int8, device="cuda", generator=gen)
+    y = torch.empty(rows, dtype=torch.int32, device="cuda")
+    for i in range(warmup):
+        ops.matvec_q8(ctx, tensors[i % 2], x8, y)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for i in range(launches):
+        ops.matvec_q8(ctx, tensors[i % 2], x8, y)
+    b.record(st)
+    torch.cuda.synchronize()
+    ctx.raise_on_error()
+    ms = a.elapsed_time(b) / launches
+    alg = rows * (cols + 2 * G) + cols + 4 * rows
+    gbs = alg / (ms * 1e-3) / 1e9
+    del tensors
+    torch.cuda.empty_cache()
+    return {"kernel": "trx::q8_matvec_kernel (trx_matvec_q8)", "rows": rows, "cols": cols,
+            "launches_timed": launches, "ms_per_launch": round(ms, 4),
+            "algorithmic_bytes_per_launch": alg, "achieved_GBps": round(gbs, 1),
+            "frac": round(gbs / peak, 4), "inputs": "two tensors in turn, 272 MB > L2"}
 
 
 def decode_leg(ctx, name, ctx_len, n_tokens, warmup):

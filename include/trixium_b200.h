@@ -43,6 +43,7 @@ typedef int trx_status;
 #define TRX_DEV_RANGE      0x10u  /* an index read from device memory (a position) was out of range */
 
 #define TRX_KIND_TERNARY   0    /* KIND_TERNARY,  model/layout.py:46 */
+#define TRX_KIND_Q8        1    /* KIND_Q8,       model/layout.py:47 (int8 weights, group 32) */
 #define TRX_KIND_TERNARY5  5    /* KIND_TERNARY5, model/layout.py:50 */
 
 /* The fields of a BONS tensor-table entry a matvec needs (model/layout.py:311-333). */
@@ -67,7 +68,8 @@ trx_status trx_get_error(trx_ctx *ctx, cudaStream_t stream, uint32_t *bits);
 /* The message of the CUDA error behind the last TRX_ERR_CUDA returned on this thread. */
 const char *trx_last_cuda_error(void);
 
-/* Bytes of one row packet and of a whole tensor (model/layout.py:215-217). */
+/* Bytes of one row packet (model/layout.py:215-217): ternary kinds (cols % 128 == 0) and
+ * TRX_KIND_Q8 (cols % 32 == 0); 0 for any other kind or width. */
 uint64_t trx_row_bytes(uint32_t cols, int32_t kind);
 
 /*
@@ -76,6 +78,17 @@ uint64_t trx_row_bytes(uint32_t cols, int32_t kind);
  * (matvec_ternary).  x8: K int8.
  */
 trx_status trx_matvec_i8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                         const int8_t *d_x8, int32_t *d_out, cudaStream_t stream);
+
+/*
+ * Q8 row-dot engine matvec over KIND_Q8 row packets (e->kind == TRX_KIND_Q8; cols a multiple of
+ * 32, at most 32768): out[n] = (sum_g (gs[n,g]*m11[n,g]) <<or>> (e16[n,g]+B)) >> R as int32, gs the
+ * exact sum over the 32-weight group of q8w*x8.  Bit-exact with model/bitexact.py:127-144
+ * (matvec_q8), the mode of Q8 tensors in the engine's matvec (model/mirror.py:672-675) and of the
+ * K-cache scores (model/mirror.py:243-253).  Where the reference asserts (int48 accumulator,
+ * int32 result; :141, :143) TRX_DEV_OVERFLOW is set in the error word.  x8: K int8.
+ */
+trx_status trx_matvec_q8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
                          const int8_t *d_x8, int32_t *d_out, cudaStream_t stream);
 
 /*

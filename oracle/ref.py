@@ -83,6 +83,49 @@ def matvec_int(scales, codes, x8, B, R):
     return res.astype(np.int32)
 
 
+def q8_row_bytes(cols):
+    """model/layout.py:189-217 for KIND_Q8: ceil(G/16) scale beats + G code beats, G = cols/32."""
+    g = cols // 32
+    return -(-g // 16) * 32 + 32 * g
+
+
+def q8_decode_packed(packed, rows, cols):
+    """model/bons.py:177-200 (decode_rows) for KIND_Q8 -> (scales fp16 (rows,G), q8w int8)."""
+    g = cols // 32
+    d = np.asarray(packed, dtype=np.uint8).reshape(rows, q8_row_bytes(cols))
+    return d[:, :2 * g].copy().view(np.float16), d[:, -(-g // 16) * 32:].copy().view(np.int8)
+
+
+def q8_pack(scales, q8w):
+    """model/bons.py:132-160 (encode_rows) for KIND_Q8: scales then the int8 weights per row."""
+    rows, cols = q8w.shape
+    g = cols // 32
+    out = np.zeros((rows, q8_row_bytes(cols)), dtype=np.uint8)
+    out[:, :2 * g] = np.ascontiguousarray(np.asarray(scales, np.float16)).view(np.uint8).reshape(rows, 2 * g)
+    out[:, -(-g // 16) * 32:] = np.asarray(q8w, np.int8).view(np.uint8)
+    return out.reshape(-1)
+
+
+def matvec_q8(scales, q8w, x8, B, R):
+    """model/bitexact.py:127-144 (matvec_q8): exact sums of q8w*x8 over groups of 32, each times
+    m11 and shifted by e16+B (floor shift when negative), summed in int64, then >> R.
+    Raises OverflowError48 where the reference asserts (:141, :143)."""
+    rows, cols = q8w.shape
+    g = cols // 32
+    gs = np.einsum("rgk,gk->rg", np.asarray(q8w, np.int64).reshape(rows, g, 32),
+                   np.asarray(x8, dtype=np.int64).reshape(g, 32))
+    m11, e16 = fp16_parts(scales)
+    sh = e16 + B
+    prod = gs * m11
+    acc = np.where(sh >= 0, prod << np.clip(sh, 0, 63), prod >> np.clip(-sh, 0, 63)).sum(axis=1)
+    if np.any(np.abs(acc) >= 2 ** 47):
+        raise OverflowError48("int48 accumulator overflow")
+    res = acc >> R
+    if np.any(np.abs(res) >= 2 ** 31):
+        raise OverflowError48("int32 result overflow")
+    return res.astype(np.int32)
+
+
 def group_sums(codes, x8):
     """The exact per-(row, group) sums gs (model/bitexact.py:108)."""
     rows, cols = codes.shape

@@ -8,6 +8,8 @@ import re
 
 import pytest
 
+from oracle import ref
+
 from trixium_b200 import _lib, layout as L
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -34,7 +36,13 @@ def test_row_bytes(cols, kind):
     assert _lib.lib().trx_row_bytes(cols, kind) == L.row_bytes(cols, kind)
 
 
+@pytest.mark.parametrize("cols", [32, 96, 512, 544, 4160, 32768])
+def test_row_bytes_q8(cols):
+    assert _lib.lib().trx_row_bytes(cols, L.KIND_Q8) == L.q8_row_bytes(cols) == ref.q8_row_bytes(cols)
+
+
 def test_row_bytes_rejects_bad_layouts():
+    assert _lib.lib().trx_row_bytes(48, L.KIND_Q8) == 0
     assert _lib.lib().trx_row_bytes(100, 5) == 0
     assert _lib.lib().trx_row_bytes(128, 3) == 0
 

@@ -4,6 +4,7 @@ Fixtures: tests/golden/*.npz, made by tests/golden/make_golden.py from the refer
 model/bons.py (encode_rows, TensorSpec B/R), model/bitexact.py (matvec_ternary) and
 model/mirror.py (_quantize_f_pow2, _sumsq64).
 """
+import glob
 import os
 
 import numpy as np
@@ -102,3 +103,31 @@ def test_synthetic_distribution():
     frac = np.bincount(codes.reshape(-1), minlength=3) / codes.size
     assert abs(frac[1] - 0.4) < 0.01 and abs(frac[0] - 0.3) < 0.01 and abs(frac[2] - 0.3) < 0.01
     assert scales.dtype == np.float16 and np.all(scales >= 0)
+
+
+Q8_FILES = sorted(glob.glob(os.path.join(GOLDEN, "q8_*.npz")))
+
+
+@pytest.mark.parametrize("path", Q8_FILES, ids=[os.path.basename(f)[3:-4] for f in Q8_FILES])
+def test_q8_packer_and_oracle(path):
+    """KIND_Q8: the packer's bytes and B/R equal the converter's (the K-score case carries the
+    firmware's own B/R), and the oracle's Q8 row dot equals model/bitexact.py:matvec_q8."""
+    d = load(path)
+    rows, cols, B, R = int(d["rows"]), int(d["cols"]), int(d["B"]), int(d["R"])
+    kscores = "kscores" in path
+    t = image.Q8Tensor(d["scales"], d["q8w"], bias=B if kscores else None, rshift=R if kscores else None)
+    assert np.array_equal(t.packed, d["packed"])
+    assert (t.bias, t.rshift) == (B, R)
+    assert t.packed.size == rows * L.q8_row_bytes(cols) == rows * ref.q8_row_bytes(cols)
+    assert np.array_equal(ref.q8_pack(d["scales"], d["q8w"]), d["packed"])
+    s, w = ref.q8_decode_packed(d["packed"], rows, cols)
+    assert np.array_equal(w, d["q8w"]) and np.array_equal(s.view(np.uint16), d["scales"].view(np.uint16))
+    assert np.array_equal(ref.matvec_q8(s, w, d["x8"], B, R), d["y_int"])
+
+
+def test_q8_oracle_raises_where_reference_asserts():
+    d = load(os.path.join(GOLDEN, "q8_bound_16x512.npz"))
+    with pytest.raises(ref.OverflowError48):
+        ref.matvec_q8(d["scales"], d["q8w"], d["x8"], int(d["B"]), 0)        # int32 result
+    with pytest.raises(ref.OverflowError48):
+        ref.matvec_q8(d["scales"], d["q8w"], d["x8"], int(d["B"]) + 6, 0)    # int48 accumulator

@@ -6,6 +6,8 @@ Same names, arguments and results as the reference:
         model/bitexact.py:101-119
     matvec_ternary_rows(scales, codes, x8_rows (nr+1,K), B, R) -> int32 (nr+1, M)
         model/bitexact.py:121-125
+    matvec_q8(scales_f16 (M,K/32), q8w (M,K) int8, x8 (K,) int8, B, R) -> int32 (M,)
+        model/bitexact.py:127-144
 
 The codes are packed once into the converter's row packets (2-bit by default, or trit5 with
 kind=5) and cached on the device by the identity of the arrays; the matvec runs in
@@ -18,7 +20,7 @@ import torch
 
 from . import _lib
 from . import ops
-from .image import TernaryTensor
+from .image import Q8Tensor, TernaryTensor
 
 _cache = {}
 
@@ -63,3 +65,19 @@ def matvec_ternary_rows(scales_f16, codes, x8_rows, B, R, kind=0):
         outs.append(ops.matvec_i8_rows(ctx, dt, xt))
     _raise_device(ctx)
     return torch.cat(outs).cpu().numpy()
+
+
+def matvec_q8(scales_f16, q8w, x8, B, R):
+    ctx = ops.default_context()
+    q8w = np.asarray(q8w)
+    key = (id(scales_f16), id(q8w), np.shape(scales_f16), q8w.shape, int(B), int(R), "q8")
+    hit = _cache.get(key)
+    if hit is not None and hit[0] is scales_f16 and hit[1] is q8w:
+        dt = hit[2]
+    else:
+        dt = ops.DeviceTensor(Q8Tensor(scales_f16, q8w, bias=B, rshift=R))
+        _cache[key] = (scales_f16, q8w, dt)
+    x8_t = torch.from_numpy(np.ascontiguousarray(np.asarray(x8, dtype=np.int8))).to(ctx.device)
+    out = ops.matvec_q8(ctx, dt, x8_t)
+    _raise_device(ctx)
+    return out.cpu().numpy()

@@ -125,6 +125,11 @@ trx_status trx_get_error(trx_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
 const char *trx_last_cuda_error(void) { return trx::last_cuda_error(); }
 
 uint64_t trx_row_bytes(uint32_t cols, int32_t kind) {
+    if (kind == TRX_KIND_Q8) {
+        if (cols == 0 || cols % 32) return 0;
+        const uint64_t G = cols / 32;
+        return (G + 15) / 16 * 32 + 32 * G;
+    }
     if (!ternary_kind(kind) || cols == 0 || cols % 128) return 0;
     const uint64_t G = cols / 128;
     const uint64_t sb = (G + 15) / 16 * 32;
@@ -143,6 +148,17 @@ trx_status trx_matvec_i8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
     J.seg[0].y = d_out;
     J.out = trx::OUT_I32;
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+}
+
+trx_status trx_matvec_q8(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int32_t *d_out,
+                         cudaStream_t stream) {
+    if (!ctx || !e) return TRX_ERR_ARG;
+    if (e->kind != TRX_KIND_Q8 || e->rows == 0 || e->cols == 0 || (e->cols % 32) != 0) return TRX_ERR_LAYOUT;
+    if (e->cols > 32768u || e->rows > (1u << 30)) return TRX_ERR_UNSUPPORTED;
+    if (e->rshift < 0 || e->rshift > 47 || e->bias < -64 || e->bias > 64) return TRX_ERR_ARG;
+    if (!d_packed || !d_x8 || !d_out || !aligned16(d_packed)) return TRX_ERR_ARG;
+    return trx::launch_matvec_q8(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->bias,
+                                 e->rshift, d_x8, d_out, ctx->err, stream);
 }
 
 trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int nb,

@@ -184,4 +184,37 @@ __device__ __forceinline__ int frexp_exp(float a) {
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Fast range: a normal fp16
+// scale (biased exponent E in [1, 30]) with 0 <= e16+B = E-25+B <= 19, where m11 << (e16+B) is
+// below 2^30: the contribution is (+-gs) * (m11 << (E-25+B)), one 32x32->64 multiply.  Other
+// scales (tiny or subnormal ones, far below the tensor's largest) take the general floor/left
+// shift.
+struct ScaleFast {
+    int lo, span;  // fast iff E - lo in [0, span]
+    int sh;        // B - 25: the left shift is E + sh
+};
+
+__device__ __forceinline__ ScaleFast scale_fast(int B) {
+    ScaleFast f;
+    const int lo = max(1, 25 - B), hi = min(30, 44 - B);
+    f.lo = hi >= lo ? lo : 64;  // an empty range: E - 64 < 0 fails the unsigned test below
+    f.span = hi >= lo ? hi - lo : 0;
+    f.sh = B - 25;
+    return f;
+}
+
+__device__ __forceinline__ long long contrib(int gs, uint32_t sb, int B, const ScaleFast &F) {
+    const int E = (int)((sb >> 10) & 31u);
+    if ((unsigned)(E - F.lo) <= (unsigned)F.span)
+        return (long long)(sb & 0x8000u ? -gs : gs) * (long long)(int)(((sb & 0x3ffu) | 0x400u) << (E + F.sh));
+    return group_contrib(gs, sb, B);
+}
+
+// The checks of model/bitexact.py:116,118 (and :141,:143): the int48 accumulator and the int32
+// result after >> R.
+__device__ __forceinline__ bool acc_bad(long long a, int R) {
+    const long long r = a >> R;
+    return a >= (1ll << 47) || a <= -(1ll << 47) || r >= (1ll << 31) || r <= -(1ll << 31);
+}
+
 }  // namespace trx

@@ -535,35 +535,9 @@ __device__ __forceinline__ int gsum_2b(const uint4 *cp, const uint32_t *xg) {
     return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - (int)xw[32];
 }
 
-// (gs*m11) shifted by e16+B as int64 (model/bitexact.py:111-115).  Fast range: a normal fp16
-// scale (biased exponent E in [1, 30]) with 0 <= e16+B = E-25+B <= 19, where m11 << (e16+B) is
-// below 2^30: the contribution is (+-gs) * (m11 << (E-25+B)), one 32x32->64 multiply.  Other
-// scales (tiny or subnormal ones, far below the tensor's largest) take the general floor/left
-// shift.
-struct ScaleFast {
-    int lo, span;  // fast iff E - lo in [0, span]
-    int sh;        // B - 25: the left shift is E + sh
-};
-
-__device__ __forceinline__ ScaleFast scale_fast(int B) {
-    ScaleFast f;
-    const int lo = max(1, 25 - B), hi = min(30, 44 - B);
-    f.lo = hi >= lo ? lo : 64;  // an empty range: E - 64 < 0 fails the unsigned test below
-    f.span = hi >= lo ? hi - lo : 0;
-    f.sh = B - 25;
-    return f;
-}
-
 __device__ __forceinline__ uint32_t scale_bits(uint2 s, int g) {
     const uint32_t w = g < 2 ? s.x : s.y;
     return g & 1 ? w >> 16 : w & 0xffffu;
-}
-
-__device__ __forceinline__ long long contrib(int gs, uint32_t sb, int B, const ScaleFast &F) {
-    const int E = (int)((sb >> 10) & 31u);
-    if ((unsigned)(E - F.lo) <= (unsigned)F.span)
-        return (long long)(sb & 0x8000u ? -gs : gs) * (long long)(int)(((sb & 0x3ffu) | 0x400u) << (E + F.sh));
-    return group_contrib(gs, sb, B);
 }
 
 // The int64 sum of one chunk (ng <= 4 groups) of this lane's row.
@@ -590,11 +564,6 @@ __device__ __forceinline__ long long chunk_2b(const uint4 *cp, uint2 sc, int ng,
 __device__ __forceinline__ float row_float(long long acc, int R, int e8, int B) {
     const int res = (int)(acc >> R);
     return __fmul_rn((float)res, pow2f(e8 + R - B));
-}
-
-__device__ __forceinline__ bool acc_bad(long long a, int R) {
-    const long long r = a >> R;
-    return a >= (1ll << 47) || a <= -(1ll << 47) || r >= (1ll << 31) || r <= -(1ll << 31);
 }
 
 __device__ __forceinline__ float silu_f32(float g) {

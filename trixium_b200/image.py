@@ -126,6 +126,42 @@ class TernaryTensor:
         return TernaryTensor(self.scales, self.codes, kind, self.bias, self.rshift)
 
 
+GS_MAX_Q8 = 32 * 127 * 127   # max |group sum| of a Q8 row dot (model/bitexact.py:73)
+
+
+def pack_q8_rows(scales, q8w):
+    """scales (rows, cols/32) fp16, q8w (rows, cols) int8 -> KIND_Q8 row packets (uint8), byte for
+    byte model/bons.py:encode_rows (:150-154, :167-169)."""
+    q8w = np.asarray(q8w, dtype=np.int8)
+    rows, cols = q8w.shape
+    g = L.q8_groups(cols)
+    sb = L.ceil_div(g, L.SCALES_PER_BEAT) * L.BEAT_BYTES
+    out = np.zeros((rows, L.q8_row_bytes(cols)), dtype=np.uint8)
+    sc = np.ascontiguousarray(np.asarray(scales, dtype=np.float16).reshape(rows, g))
+    out[:, :2 * g] = sc.view(np.uint8).reshape(rows, 2 * g)
+    out[:, sb:] = np.ascontiguousarray(q8w).view(np.uint8)
+    return out.reshape(-1)
+
+
+class Q8Tensor:
+    """One packed KIND_Q8 tensor (group 32, w = q * scale): its bytes and entry fields.  B and R
+    follow the converter (model/bons.py:56-65 with GS_MAX_Q8) unless given."""
+
+    def __init__(self, scales, q8w, bias=None, rshift=None):
+        q8w = np.asarray(q8w, dtype=np.int8)
+        self.rows, self.cols = q8w.shape
+        self.kind = L.KIND_Q8
+        self.scales = np.asarray(scales, dtype=np.float16).reshape(self.rows, -1)
+        self.q8w = q8w
+        self.bias = scale_bias(self.scales) if bias is None else int(bias)
+        self.rshift = result_shift(self.scales, self.bias, GS_MAX_Q8) if rshift is None else int(rshift)
+        self.packed = pack_q8_rows(self.scales, q8w)
+
+    @property
+    def row_bytes(self):
+        return L.q8_row_bytes(self.cols)
+
+
 def synthetic_codes_scales(rng, rows, cols, p_zero=0.4, scale_sigma=0.02):
     """Codes {0,1,2} with P(code 1, w=0)=p_zero and P(code 0)=P(code 2)=(1-p_zero)/2, then
     fp16 scales |N(0,1)|*scale_sigma per 128-group."""

@@ -18,6 +18,7 @@ code_beats, mem_code_beats, row_beats) and model/layout.py:219-223 (shard_rows).
 
 BEAT_BYTES = 32
 GROUP = 128
+GROUP_Q8 = 32
 SCALES_PER_BEAT = 16
 TRIT5_GROUP_BYTES = 26
 
@@ -59,6 +60,20 @@ def code_bytes(cols, kind):
 def row_bytes(cols, kind):
     """Bytes of one row packet in memory (model/layout.py:215-217 times BEAT_BYTES)."""
     return scale_bytes(cols) + ceil_div(code_bytes(cols, kind), BEAT_BYTES) * BEAT_BYTES
+
+
+def q8_groups(cols):
+    """Groups of a KIND_Q8 row: 32 int8 weights (one beat) per fp16 scale (model/layout.py:41,47)."""
+    if cols % GROUP_Q8:
+        raise ValueError(f"cols {cols} is not a multiple of the {GROUP_Q8}-weight Q8 group")
+    return cols // GROUP_Q8
+
+
+def q8_row_bytes(cols):
+    """Bytes of one KIND_Q8 row packet: ceil(G/16) scale beats, then G beats of int8 weights
+    (model/layout.py:189-217 with code_beats = cols/32)."""
+    g = q8_groups(cols)
+    return (ceil_div(g, SCALES_PER_BEAT) + g) * BEAT_BYTES
 
 
 def tensor_bytes(rows, cols, kind):

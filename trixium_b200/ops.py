@@ -75,7 +75,8 @@ def default_context(device=None):
 
 
 class DeviceTensor:
-    """A packed ternary tensor resident on the device, with its BONS entry fields."""
+    """A packed tensor (ternary, or KIND_Q8 from image.Q8Tensor) resident on the device, with its
+    BONS entry fields."""
 
     def __init__(self, t: TernaryTensor, device=None):
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -107,6 +108,18 @@ def matvec_i8(ctx, w: DeviceTensor, x8, out=None):
         out = torch.empty(w.rows, dtype=torch.int32, device=x8.device)
     _lib.check(_lib.lib().trx_matvec_i8(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x8), _ptr(out),
                                         _stream()), "trx_matvec_i8")
+    return out
+
+
+def matvec_q8(ctx, w: DeviceTensor, x8, out=None):
+    """Q8 row dot of a KIND_Q8 tensor (model/bitexact.py:127-144): int32 (rows,)."""
+    if w.kind != L.KIND_Q8:
+        raise ValueError(f"matvec_q8 needs a KIND_Q8 tensor, got kind {w.kind}")
+    _need(x8, torch.int8, "x8")
+    if out is None:
+        out = torch.empty(w.rows, dtype=torch.int32, device=x8.device)
+    _lib.check(_lib.lib().trx_matvec_q8(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x8), _ptr(out),
+                                        _stream()), "trx_matvec_q8")
     return out
 
 
@@ -341,7 +354,7 @@ def row_bytes(cols, kind):
     return int(_lib.lib().trx_row_bytes(cols, kind))
 
 
-__all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_i8_rows", "quantize_pow2",
+__all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_q8", "matvec_i8_rows", "quantize_pow2",
            "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_decode_static", "attn_shape",
            "deltanet_shape", "deltanet_step", "lmhead_argmax", "lmhead_argmax_key", "argmax_token", "matvec_f_multi", "embed_lookup",
            "advance_position", "row_bytes", "L"]
