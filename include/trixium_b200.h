@@ -92,6 +92,16 @@ trx_status trx_matvec_q8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
                          const int8_t *d_x8, int32_t *d_out, cudaStream_t stream);
 
 /*
+ * Float projection of a KIND_Q8 tensor in the engine's arithmetic (model/mirror.py:664-678 with
+ * its Q8 branch :672-675, one K-segment): x8, e8 = the power-of-two quantisation of x (as
+ * trx_quantize_pow2), then y = float(trx_matvec_q8 result) * 2^(e8 + R - B).  Two launches on
+ * `stream`; the quantised x lives in the context's scratch, so calls on one context are
+ * serialised by the caller (one stream at a time).  x: K floats, y: rows floats.
+ */
+trx_status trx_matvec_q8_f(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
+                           const float *d_x, float *d_y, cudaStream_t stream);
+
+/*
  * Multi-row engine matvec: nb independent rows of x8 ([nb, K] int8) against one weight pass,
  * out [nb, rows] int32 (model/bitexact.py:121-125, matvec_ternary_rows).  nb <= 8.
  */

@@ -167,6 +167,14 @@ def matvec_f(scales, codes, x, B, R):
     return (res.astype(f32) * sc).astype(f32)
 
 
+def matvec_q8_f(scales, q8w, x, B, R):
+    """model/mirror.py:664-678 for a KIND_Q8 tensor (the :672-675 branch, one K-segment): quantise
+    x, the engine's Q8 int32 result, scaled by fp32 2**(e8+R-B)."""
+    x8, e8 = quantize_pow2(x)
+    res = matvec_q8(scales, q8w, x8, B, R)
+    return (res.astype(f32) * f32(np.exp2(f32(e8 + R - B)))).astype(f32)
+
+
 def matvec_f64(scales, codes, x):
     """fp64 reference of the fp projection: sum over groups of scale * sum((code-1)*x)
     (the float reference of test/model/test_bitexact.py:49-56, and model/fastref.py:119-125

@@ -112,3 +112,17 @@ def test_q8_full_size_rows_are_independent(ctx):
     pick[-1] = rows - 1
     wp = w[torch.from_numpy(pick).cuda()].cpu().numpy()
     assert np.array_equal(y[pick], ref.matvec_q8(s[pick], wp, x8, B, R))
+
+
+@pytest.mark.parametrize("rows,cols,xscale", [(96, 1024, 1.0), (257, 4160, 30.0), (33, 32, 1e-3), (16, 512, 0.0)])
+def test_q8_float_projection(ctx, rows, cols, xscale):
+    """trx_matvec_q8_f: quantise x (power of two), the Q8 row dot, scale by 2^(e8+R-B); equal in
+    every fp32 bit to the oracle's restatement of model/mirror.py:664-678."""
+    rng = np.random.default_rng(rows + cols)
+    s, w = random_q8(rng, rows, cols)
+    t = image.Q8Tensor(s, w)
+    x = (rng.standard_normal(cols) * xscale).astype(np.float32)
+    y = ops.matvec_q8_f(ctx, ops.DeviceTensor(t), torch.from_numpy(x).cuda()).cpu().numpy()
+    ctx.raise_on_error()
+    want = ref.matvec_q8_f(s, w, x, t.bias, t.rshift)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))

@@ -19,7 +19,7 @@ DEV_OVERFLOW, DEV_BADBYTE, DEV_TIMEOUT, DEV_INTERNAL, DEV_RANGE = 0x1, 0x2, 0x4,
 
 # Every symbol the header declares (tests check the library exports all of them).
 SYMBOLS = (
-    "trx_create", "trx_destroy", "trx_get_error", "trx_last_cuda_error", "trx_row_bytes", "trx_matvec_i8", "trx_matvec_q8",
+    "trx_create", "trx_destroy", "trx_get_error", "trx_last_cuda_error", "trx_row_bytes", "trx_matvec_i8", "trx_matvec_q8", "trx_matvec_q8_f",
     "trx_matvec_i8_rows", "trx_quantize_pow2", "trx_matvec_f", "trx_matvec_fp",
     "trx_matvec_swiglu", "trx_validate_packed", "trx_matvec_f_batch", "trx_attn_decode",
     "trx_deltanet_step", "trx_lmhead_argmax", "trx_matvec_f_multi", "trx_embed_lookup", "trx_advance_position",
@@ -93,6 +93,7 @@ def lib():
             "trx_last_cuda_error": ([], ctypes.c_char_p),
             "trx_matvec_i8": ([_vp, E, _vp, _vp, _vp, _vp], ctypes.c_int),
             "trx_matvec_q8": ([_vp, E, _vp, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_q8_f": ([_vp, E, _vp, _vp, _vp, _vp], ctypes.c_int),
             "trx_matvec_i8_rows": ([_vp, E, _vp, _vp, ctypes.c_int, _vp, _vp], ctypes.c_int),
             "trx_quantize_pow2": ([_vp, _vp, ctypes.c_uint32, _vp, _vp, _vp], ctypes.c_int),
             "trx_matvec_f": ([_vp, E, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp], ctypes.c_int),

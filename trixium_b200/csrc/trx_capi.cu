@@ -17,11 +17,14 @@ struct trx_ctx {
     // Greedy-argmax keys (one per job) and the matvec's arrival count (zero between launches).
     unsigned long long *amax_key;
     unsigned *amax_cnt;
+    // The quantised activation of trx_matvec_q8_f: 32 KiB of x8, then its exponent e8.
+    int8_t *q8x;
 };
 
 static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
 static const uint32_t kAttnMaxKv = 1024;
 static const int kMaxArgmaxJobs = 64;
+static const uint32_t kQ8MaxCols = 32768;
 
 namespace trx {
 bool pdl_enabled() {
@@ -85,6 +88,7 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaMalloc(&c->amax_key, kMaxArgmaxJobs * 8) != cudaSuccess ||
         cudaMemset(c->amax_key, 0, kMaxArgmaxJobs * 8) != cudaSuccess ||
         cudaMalloc(&c->amax_cnt, 16) != cudaSuccess || cudaMemset(c->amax_cnt, 0, 16) != cudaSuccess ||
+        cudaMalloc(&c->q8x, kQ8MaxCols + 16) != cudaSuccess ||
         trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
@@ -93,6 +97,7 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaFree(c->attn_cnt);
         cudaFree(c->amax_key);
         cudaFree(c->amax_cnt);
+        cudaFree(c->q8x);
         delete c;
         return TRX_ERR_CUDA;
     }
@@ -108,6 +113,7 @@ trx_status trx_destroy(trx_ctx *ctx) {
     cudaFree(ctx->attn_cnt);
     cudaFree(ctx->amax_key);
     cudaFree(ctx->amax_cnt);
+    cudaFree(ctx->q8x);
     delete ctx;
     return TRX_OK;
 }
@@ -150,15 +156,34 @@ trx_status trx_matvec_i8(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
     return trx::launch_matvec(J, ctx->lut, ctx->err, stream);
 }
 
-trx_status trx_matvec_q8(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int32_t *d_out,
-                         cudaStream_t stream) {
+static trx_status check_q8(const trx_ctx *ctx, const trx_entry *e, const void *packed) {
     if (!ctx || !e) return TRX_ERR_ARG;
     if (e->kind != TRX_KIND_Q8 || e->rows == 0 || e->cols == 0 || (e->cols % 32) != 0) return TRX_ERR_LAYOUT;
-    if (e->cols > 32768u || e->rows > (1u << 30)) return TRX_ERR_UNSUPPORTED;
+    if (e->cols > kQ8MaxCols || e->rows > (1u << 30)) return TRX_ERR_UNSUPPORTED;
     if (e->rshift < 0 || e->rshift > 47 || e->bias < -64 || e->bias > 64) return TRX_ERR_ARG;
-    if (!d_packed || !d_x8 || !d_out || !aligned16(d_packed)) return TRX_ERR_ARG;
+    if (!packed || !aligned16(packed)) return TRX_ERR_ARG;
+    return TRX_OK;
+}
+
+trx_status trx_matvec_q8(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int32_t *d_out,
+                         cudaStream_t stream) {
+    trx_status s = check_q8(ctx, e, d_packed);
+    if (s) return s;
+    if (!d_x8 || !d_out) return TRX_ERR_ARG;
     return trx::launch_matvec_q8(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->bias,
-                                 e->rshift, d_x8, d_out, ctx->err, stream);
+                                 e->rshift, d_x8, nullptr, d_out, ctx->err, stream);
+}
+
+trx_status trx_matvec_q8_f(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, float *d_y,
+                           cudaStream_t stream) {
+    trx_status s = check_q8(ctx, e, d_packed);
+    if (s) return s;
+    if (!d_x || !d_y) return TRX_ERR_ARG;
+    int *e8 = reinterpret_cast<int *>(ctx->q8x + kQ8MaxCols);
+    s = trx::launch_quantize(d_x, (int)e->cols, ctx->q8x, e8, stream);
+    if (s) return s;
+    return trx::launch_matvec_q8(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->bias,
+                                 e->rshift, ctx->q8x, e8, d_y, ctx->err, stream);
 }
 
 trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int nb,

@@ -217,4 +217,10 @@ __device__ __forceinline__ bool acc_bad(long long a, int R) {
     return a >= (1ll << 47) || a <= -(1ll << 47) || r >= (1ll << 31) || r <= -(1ll << 31);
 }
 
+// 2^k as an fp32, exact for k in [-149, 127] (the scale of the power-of-two quantiser).
+__device__ __forceinline__ float pow2f(int k) {
+    if (k >= -126) return __int_as_float((min(k, 128) + 127) << 23);  // k = 128 gives inf
+    return k >= -149 ? __int_as_float(1 << (k + 149)) : 0.f;           // subnormal powers
+}
+
 }  // namespace trx

@@ -136,8 +136,9 @@ trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token,
                               cudaStream_t st);
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
-trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, const int8_t *x8, int32_t *out,
-                            uint32_t *err, cudaStream_t st);
+// The Q8 row dot (trx_q8.cu): int32 results, or with e8 the float projection (fp32 out).
+trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, const int8_t *x8, const int *e8,
+                            void *out, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);
 trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStream_t st);
 trx_status launch_validate_t5(const uint8_t *w, int rows, int cols, uint32_t *err, cudaStream_t st);

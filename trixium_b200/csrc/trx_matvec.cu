@@ -100,12 +100,6 @@ __device__ __forceinline__ void cp_wait() {
 }
 
 // Quantisation helpers ----------------------------------------------------------------------------
-// 2^k as an fp32, exact for k in [-149, 127] (the scale of the power-of-two quantiser).
-__device__ __forceinline__ float pow2f(int k) {
-    if (k >= -126) return __int_as_float((min(k, 128) + 127) << 23);  // k = 128 gives inf
-    return k >= -149 ? __int_as_float(1 << (k + 149)) : 0.f;           // subnormal powers
-}
-
 // The value the quantiser sees at position k: x[k], or the RMS-normalised x[k]*r*w[k].
 __device__ __forceinline__ float prologue_value(const float *x, const float *w, float r, int k) {
     float v = __ldg(x + k);

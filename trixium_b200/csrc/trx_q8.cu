@@ -26,8 +26,12 @@ namespace {
 constexpr int kQ8Warps = 8;   // rows in flight per CTA, one per warp
 constexpr int kQ8Unroll = 4;  // 16-byte weight words in flight per lane
 
+// F32: the float projection of a Q8 tensor (model/mirror.py:664-678 with matvec_q8): x8 and its
+// exponent e8 come from the quantiser launched just before, y = fp32(result) * 2^(e8 + R - B).
+template <bool F32>
 __global__ void __launch_bounds__(kQ8Warps * 32) q8_matvec_kernel(const uint8_t *w, int rows, int cols, int B, int R,
-                                                                   const int8_t *x8, int32_t *out, uint32_t *err) {
+                                                                   const int8_t *x8, const int *e8, void *out,
+                                                                   uint32_t *err) {
     extern __shared__ uint4 xs[];  // x8 as cols/16 words
     pdl_trigger();
     pdl_wait();
@@ -43,6 +47,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_matvec_kernel(const uint8_t 
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const ScaleFast F = scale_fast(B);
+    const float ysc = F32 ? pow2f(*e8 + R - B) : 0.f;
     for (int row = blockIdx.x * kQ8Warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kQ8Warps) {
         const uint8_t *rp = w + (size_t)row * rb;
         const uint16_t *sc = reinterpret_cast<const uint16_t *>(rp);
@@ -78,17 +83,21 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_matvec_kernel(const uint8_t 
         for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) {
             if (acc_bad(acc, R)) atomicOr(err, TRX_DEV_OVERFLOW);
-            out[row] = (int)(acc >> R);
+            if (F32)
+                reinterpret_cast<float *>(out)[row] = __fmul_rn((float)(int)(acc >> R), ysc);
+            else
+                reinterpret_cast<int32_t *>(out)[row] = (int)(acc >> R);
         }
     }
 }
 
 // Resident CTAs of the kernel on the whole GPU (SMs x CTAs per SM at the given shared memory).
+template <bool F32>
 int q8_resident(size_t smem) {
     int dev = 0, sms = 0, per = 0;
     cudaGetDevice(&dev);
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, q8_matvec_kernel, kQ8Warps * 32, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, q8_matvec_kernel<F32>, kQ8Warps * 32, smem) != cudaSuccess ||
         per <= 0)
         per = 4;
     return sms * per;
@@ -96,14 +105,16 @@ int q8_resident(size_t smem) {
 
 }  // namespace
 
-trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, const int8_t *x8, int32_t *out,
-                            uint32_t *err, cudaStream_t st) {
+trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, const int8_t *x8, const int *e8,
+                            void *out, uint32_t *err, cudaStream_t st) {
     const size_t smem = (size_t)cols;  // <= 32 KiB: within the default dynamic shared memory limit
     long long grid = ((long long)rows + kQ8Warps - 1) / kQ8Warps;
-    const int resident = q8_resident(smem);
+    const int resident = e8 ? q8_resident<true>(smem) : q8_resident<false>(smem);
     if (grid > resident) grid = resident;  // one wave; the warps stride over the remaining rows
-    return note_cuda(launch_kernel(q8_matvec_kernel, dim3((unsigned)grid), dim3(kQ8Warps * 32), smem, st, w, rows,
-                                   cols, B, R, x8, out, err));
+    const dim3 g((unsigned)grid), b(kQ8Warps * 32);
+    if (e8)
+        return note_cuda(launch_kernel(q8_matvec_kernel<true>, g, b, smem, st, w, rows, cols, B, R, x8, e8, out, err));
+    return note_cuda(launch_kernel(q8_matvec_kernel<false>, g, b, smem, st, w, rows, cols, B, R, x8, e8, out, err));
 }
 
 }  // namespace trx

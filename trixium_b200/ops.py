@@ -123,6 +123,18 @@ def matvec_q8(ctx, w: DeviceTensor, x8, out=None):
     return out
 
 
+def matvec_q8_f(ctx, w: DeviceTensor, x, out=None):
+    """Float projection of a KIND_Q8 tensor (model/mirror.py:664-678, Q8 branch): fp32 (rows,)."""
+    if w.kind != L.KIND_Q8:
+        raise ValueError(f"matvec_q8_f needs a KIND_Q8 tensor, got kind {w.kind}")
+    _need(x, torch.float32, "x")
+    if out is None:
+        out = torch.empty(w.rows, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().trx_matvec_q8_f(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x), _ptr(out),
+                                          _stream()), "trx_matvec_q8_f")
+    return out
+
+
 def matvec_i8_rows(ctx, w: DeviceTensor, x8rows, out=None):
     _need(x8rows, torch.int8, "x8rows")
     nb = x8rows.shape[0]
@@ -354,7 +366,7 @@ def row_bytes(cols, kind):
     return int(_lib.lib().trx_row_bytes(cols, kind))
 
 
-__all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_q8", "matvec_i8_rows", "quantize_pow2",
+__all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_q8", "matvec_q8_f", "matvec_i8_rows", "quantize_pow2",
            "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_decode_static", "attn_shape",
            "deltanet_shape", "deltanet_step", "lmhead_argmax", "lmhead_argmax_key", "argmax_token", "matvec_f_multi", "embed_lookup",
            "advance_position", "row_bytes", "L"]
