@@ -626,13 +626,6 @@ __host__ __device__ inline size_t mma_smem_bytes(int hd, int rep, int chunk, int
     return (size_t)2 * chunk * (hd + 8) * 2 + ((size_t)mma_layout(hd, rep).total + (size_t)merge_slots * rep * (hd + 2)) * 4;
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    const __half2 h = __floats2half2_rn(lo, hi);
-    uint32_t u;
-    memcpy(&u, &h, 4);
-    return u;
-}
-
 // x = hi + lo with hi = fp16(x), lo = fp16(x - hi), for a pair: (hi word, lo word).
 __device__ __forceinline__ void split_h2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
     const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
