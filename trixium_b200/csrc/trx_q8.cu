@@ -6,13 +6,15 @@
 //   acc    = sum_g (gs * m11(g)) shifted by e16(g) + B             int64 (floor on right shifts)
 //   result = acc >> R                                              int32
 //
-// One warp per row, rows strided over one wave of resident CTAs.  The row's 16-byte words are
-// dealt round-robin to the lanes (word i to lane i % 32), so a warp's loads cover 512 contiguous
-// bytes and lane pair (2j, 2j+1) holds one whole group: each lane takes its half-group sum with
-// four dp4a against the matching x8 word (x8 staged once per CTA in shared memory), the pair adds
-// the halves by one shuffle and the even lane applies the group's scale.  Integer addition is
-// exact, so the order of the warp reduction does not change the result.  The weights are read
-// once with an evict-first hint; the launch is bound by HBM bandwidth.
+// A group of lpr lanes per row (lpr = 32 for rows of 2048 weights and more; 16, 8, ... for shorter
+// rows, so that every lane keeps kQ8Unroll 16-byte words in flight), rows strided over one wave of
+// resident CTAs.  The row's 16-byte words are dealt round-robin to its group (word i to lane
+// i % lpr), so a group's loads cover 16*lpr contiguous bytes and lane pair (2j, 2j+1) holds one
+// whole group of 32 weights: each lane takes its half-group sum with four dp4a against the
+// matching x8 word (x8 staged once per CTA in shared memory), the pair adds the halves by one
+// shuffle and the even lane applies the group's scale.  Integer addition is exact, so the order
+// of the reduction does not change the result.  The weights are read once with an evict-first
+// hint; the launch is bound by HBM bandwidth.
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -23,15 +25,21 @@ namespace trx {
 
 namespace {
 
-constexpr int kQ8Warps = 8;   // rows in flight per CTA, one per warp
-constexpr int kQ8Unroll = 4;  // 16-byte weight words in flight per lane
+#ifndef TRX_Q8_UNROLL
+#define TRX_Q8_UNROLL 4
+#endif
+#ifndef TRX_Q8_MINB
+#define TRX_Q8_MINB 1
+#endif
+constexpr int kQ8Warps = 8;                 // rows in flight per CTA, one per warp
+constexpr int kQ8Unroll = TRX_Q8_UNROLL;    // 16-byte weight words in flight per lane
 
 // F32: the float projection of a Q8 tensor (model/mirror.py:664-678 with matvec_q8): x8 and its
 // exponent e8 come from the quantiser launched just before, y = fp32(result) * 2^(e8 + R - B).
 template <bool F32>
-__global__ void __launch_bounds__(kQ8Warps * 32) q8_matvec_kernel(const uint8_t *w, int rows, int cols, int B, int R,
-                                                                   const int8_t *x8, const int *e8, void *out,
-                                                                   uint32_t *err) {
+__global__ void __launch_bounds__(kQ8Warps * 32, TRX_Q8_MINB)
+    q8_matvec_kernel(const uint8_t *w, int rows, int cols, int B, int R, int lpr_log2, const int8_t *x8, const int *e8,
+                     void *out, uint32_t *err) {
     extern __shared__ uint4 xs[];  // x8 as cols/16 words
     pdl_trigger();
     pdl_wait();
@@ -45,21 +53,29 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_matvec_kernel(const uint8_t 
         for (int i = threadIdx.x; i < cols; i += blockDim.x) reinterpret_cast<int8_t *>(xs)[i] = x8[i];
     }
     __syncthreads();
+    // A row is read by a group of lpr = 2^lpr_log2 lanes (2 <= lpr <= 32, chosen so that a short
+    // row still gives every lane kQ8Unroll words in flight); a warp reads 32/lpr rows at a time.
     const int lane = threadIdx.x & 31;
+    const int lpr = 1 << lpr_log2;
+    const int sl = lane & (lpr - 1);          // lane within the row's group
+    const int sub = lane >> lpr_log2;         // the group's row within the warp's set
+    const int rpw = 32 >> lpr_log2;           // rows per warp per pass
     const ScaleFast F = scale_fast(B);
     const float ysc = F32 ? pow2f(*e8 + R - B) : 0.f;
-    for (int row = blockIdx.x * kQ8Warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kQ8Warps) {
-        const uint8_t *rp = w + (size_t)row * rb;
+    for (int r0 = (blockIdx.x * kQ8Warps + (threadIdx.x >> 5)) * rpw; r0 < rows; r0 += gridDim.x * kQ8Warps * rpw) {
+        const int row = r0 + sub;
+        const int wend = row < rows ? nw : 0;  // a group past the last row loads nothing
+        const uint8_t *rp = w + (size_t)(row < rows ? row : 0) * rb;
         const uint16_t *sc = reinterpret_cast<const uint16_t *>(rp);
         const uint4 *cw = reinterpret_cast<const uint4 *>(rp + sb);
         long long acc = 0;
-        for (int w0 = 0; w0 < nw; w0 += 32 * kQ8Unroll) {
+        for (int w0 = 0; w0 < nw; w0 += lpr * kQ8Unroll) {  // the same trip count in every lane
             uint4 c[kQ8Unroll];
             uint32_t s[kQ8Unroll];
 #pragma unroll
             for (int u = 0; u < kQ8Unroll; ++u) {
-                const int i = w0 + u * 32 + lane;
-                if (i < nw) {
+                const int i = w0 + u * lpr + sl;
+                if (i < wend) {
                     c[u] = __ldcs(cw + i);
                     s[u] = __ldg(sc + (i >> 1));
                 } else {
@@ -69,19 +85,18 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_matvec_kernel(const uint8_t 
             }
 #pragma unroll
             for (int u = 0; u < kQ8Unroll; ++u) {
-                const int i = w0 + u * 32 + lane;
+                const int i = w0 + u * lpr + sl;
                 const uint4 xv = xs[i < nw ? i : 0];
                 int gs = __dp4a((int)c[u].x, (int)xv.x, 0);
                 gs = __dp4a((int)c[u].y, (int)xv.y, gs);
                 gs = __dp4a((int)c[u].z, (int)xv.z, gs);
                 gs = __dp4a((int)c[u].w, (int)xv.w, gs);
                 gs += __shfl_xor_sync(0xffffffffu, gs, 1);  // the partner lane's half of the group
-                if (!(lane & 1) && i < nw) acc += contrib(gs, s[u], B, F);
+                if (!(lane & 1) && i < wend) acc += contrib(gs, s[u], B, F);
             }
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) {
+        for (int o = lpr >> 1; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (sl == 0 && row < rows) {
             if (acc_bad(acc, R)) atomicOr(err, TRX_DEV_OVERFLOW);
             if (F32)
                 reinterpret_cast<float *>(out)[row] = __fmul_rn((float)(int)(acc >> R), ysc);
@@ -108,13 +123,17 @@ int q8_resident(size_t smem) {
 trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, const int8_t *x8, const int *e8,
                             void *out, uint32_t *err, cudaStream_t st) {
     const size_t smem = (size_t)cols;  // <= 32 KiB: within the default dynamic shared memory limit
-    long long grid = ((long long)rows + kQ8Warps - 1) / kQ8Warps;
+    const int nw = cols / 16;
+    int lg = 5;  // lanes per row: the largest power of two <= 32 giving each lane kQ8Unroll words
+    while (lg > 1 && (1 << lg) * kQ8Unroll > nw) --lg;
+    const long long rows_per_cta = (long long)kQ8Warps * (32 >> lg);
+    long long grid = ((long long)rows + rows_per_cta - 1) / rows_per_cta;
     const int resident = e8 ? q8_resident<true>(smem) : q8_resident<false>(smem);
     if (grid > resident) grid = resident;  // one wave; the warps stride over the remaining rows
     const dim3 g((unsigned)grid), b(kQ8Warps * 32);
     if (e8)
-        return note_cuda(launch_kernel(q8_matvec_kernel<true>, g, b, smem, st, w, rows, cols, B, R, x8, e8, out, err));
-    return note_cuda(launch_kernel(q8_matvec_kernel<false>, g, b, smem, st, w, rows, cols, B, R, x8, e8, out, err));
+        return note_cuda(launch_kernel(q8_matvec_kernel<true>, g, b, smem, st, w, rows, cols, B, R, lg, x8, e8, out, err));
+    return note_cuda(launch_kernel(q8_matvec_kernel<false>, g, b, smem, st, w, rows, cols, B, R, lg, x8, e8, out, err));
 }
 
 }  // namespace trx
