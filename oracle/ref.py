@@ -175,6 +175,32 @@ def matvec_q8_f(scales, q8w, x, B, R):
     return (res.astype(f32) * f32(np.exp2(f32(e8 + R - B)))).astype(f32)
 
 
+def hadamard_codes(signs, block):
+    """model/convert.py:99-118 with model/golden.py:256-263: block tensor b of the rotation has
+    codes H[i, j] * s[b*block + j] + 1, H[i, j] = (-1)^popcount(i & j); its scales are all
+    2^-floor(log2(block)/2) (model/golden.py:271-278).  Returns (scales, codes) of all blocks
+    stacked: (width, block/128) fp16 and (width, block) uint8."""
+    i = np.arange(block)
+    par = i[:, None] & i[None, :]
+    bits = np.zeros_like(par)
+    while par.any():
+        bits ^= par & 1
+        par >>= 1
+    H = np.where(bits & 1, -1, 1).astype(np.int64)
+    s = np.asarray(signs).astype(np.int64).reshape(-1, block)
+    codes = (H[None, :, :] * s[:, None, :] + 1).reshape(-1, block).astype(np.uint8)
+    k = block.bit_length() - 1
+    scales = np.full((codes.shape[0], block // 128), 2.0 ** -(k // 2), np.float16)
+    return scales, codes
+
+
+def hadamard_rotate(x, scales, codes, B, R):
+    """model/mirror.py:680-690 (rotate): block b of x' = matvec_f(block tensor b, x[b-th block])."""
+    block = codes.shape[1]
+    return np.concatenate([matvec_f(scales[b:b + block], codes[b:b + block], x[b:b + block], B, R)
+                           for b in range(0, len(x), block)])
+
+
 def matvec_f64(scales, codes, x):
     """fp64 reference of the fp projection: sum over groups of scale * sum((code-1)*x)
     (the float reference of test/model/test_bitexact.py:49-56, and model/fastref.py:119-125

@@ -137,8 +137,38 @@ def q8_cases():
     q8_case("kscores_77x128", q8w, scales, x8, B=B, R=R)
 
 
+def hadamard_case(width, block, seed):
+    """The rotation x' = R(s*x) per block as the engine computes it (model/mirror.py:680-690): the
+    converter's block tensors (model/convert.py:99-118, called here) and one quantised float
+    projection per block (model/mirror.py:664-678 inline: _quantize_f_pow2, matvec_ternary,
+    the 2^(e8+R-B) scale)."""
+    import types
+    from model import convert, golden
+    rng = np.random.default_rng(seed)
+    signs = np.where(rng.random(width) < 0.5, -1.0, 1.0).astype(f32)
+    x = (rng.standard_normal(width) * 2).astype(f32)
+    specs = convert._hadamard_specs(types.SimpleNamespace(hadamard_block=block, hadamard_signs={width: signs}))
+    y = np.empty(width, f32)
+    packed = []
+    for b, spec in enumerate(specs):
+        codes = spec.get_values()
+        packed.append(bons.encode_rows(spec, 0, block))
+        x8, e8 = mirror._quantize_f_pow2(x[b * block:(b + 1) * block])
+        r = bx.matvec_ternary(spec.scales, codes, x8, spec.bias, spec.rshift)
+        y[b * block:(b + 1) * block] = (r.astype(np.int32).astype(f32) *
+                                        f32(np.exp2(f32(e8 + spec.rshift - spec.bias)))).astype(f32)
+    # The float transform the rotation approximates, times the image's gain (golden.py:265-283).
+    y_ref = golden.hadamard_rotate(x, signs, block) * f32(golden.hadamard_image_gain(block))
+    np.savez_compressed(os.path.join(HERE, f"hadamard_{width}_{block}.npz"), x=x, signs=signs, block=block,
+                        packed=np.concatenate(packed), B=specs[0].bias, R=specs[0].rshift,
+                        scale=specs[0].scales[0, 0], y=y, y_ref=y_ref.astype(f32))
+
+
 def main():
     q8_cases()
+    hadamard_case(1024, 512, 30)
+    hadamard_case(2048, 1024, 31)
+    hadamard_case(512, 128, 32)
     # 1. The reference's own matvec accuracy case (test_bitexact.py:36-47).
     rng = np.random.default_rng(42)
     M, K = 64, 512

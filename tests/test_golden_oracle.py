@@ -131,3 +131,22 @@ def test_q8_oracle_raises_where_reference_asserts():
         ref.matvec_q8(d["scales"], d["q8w"], d["x8"], int(d["B"]), 0)        # int32 result
     with pytest.raises(ref.OverflowError48):
         ref.matvec_q8(d["scales"], d["q8w"], d["x8"], int(d["B"]) + 6, 0)    # int48 accumulator
+
+
+HAD_FILES = sorted(glob.glob(os.path.join(GOLDEN, "hadamard_*.npz")))
+
+
+@pytest.mark.parametrize("path", HAD_FILES, ids=[os.path.basename(f)[9:-4] for f in HAD_FILES])
+def test_hadamard_tensor_and_oracle_rotation(path):
+    """The rotation's block tensors equal the converter's bytes and B/R (model/convert.py:99-118),
+    and the oracle's blockwise engine rotation equals the reference's (model/mirror.py:680-690)."""
+    d = load(path)
+    block, B, R = int(d["block"]), int(d["B"]), int(d["R"])
+    t = image.hadamard_tensor(d["signs"], block)
+    assert np.array_equal(t.packed, d["packed"]) and (t.bias, t.rshift) == (B, R)
+    s, c = ref.hadamard_codes(d["signs"], block)
+    assert np.array_equal(c, t.codes) and np.array_equal(s.view(np.uint16), t.scales.view(np.uint16))
+    y = ref.hadamard_rotate(d["x"], s, c, B, R)
+    assert np.array_equal(y.view(np.uint32), d["y"].view(np.uint32))
+    # The engine's rotation approximates the float transform (int8 activations): within 2 %.
+    assert np.abs(y - d["y_ref"]).max() <= 0.02 * np.abs(d["y_ref"]).max()

@@ -162,6 +162,31 @@ class Q8Tensor:
         return L.q8_row_bytes(self.cols)
 
 
+def hadamard_tensor(signs, block, kind=L.KIND_TERNARY):
+    """The rotation x' = R(s*x) per block (PrismML's basis) as the converter stores it
+    (model/convert.py:99-118): per block b a block x block ternary tensor with codes
+    H[i, j]*s[b*block + j] + 1, H the +-1 Sylvester-Hadamard matrix ((-1)^popcount(i & j),
+    model/golden.py:256-263) and every scale 2^-floor(log2(block)/2) (model/golden.py:271-278).
+    The blocks are stacked into one TernaryTensor of width rows (every block has the same scales,
+    so the converter's B and R are the same for all of them)."""
+    signs = np.asarray(signs)
+    width = signs.size
+    if block & (block - 1) or block < L.GROUP or width % block:
+        raise ValueError(f"block {block} must be a power of two >= {L.GROUP} dividing width {width}")
+    i = np.arange(block)
+    par = np.bitwise_and(i[:, None], i[None, :])
+    odd = np.zeros_like(par)
+    while par.any():
+        odd ^= par & 1
+        par >>= 1
+    H = (1 - 2 * odd).astype(np.int16)
+    s = np.where(signs.reshape(-1, block) < 0, -1, 1).astype(np.int16)
+    codes = (H[None, :, :] * s[:, None, :] + 1).reshape(width, block).astype(np.uint8)
+    k = block.bit_length() - 1
+    scales = np.full((width, block // L.GROUP), 2.0 ** -(k // 2), dtype=np.float16)
+    return TernaryTensor(scales, codes, kind=kind)
+
+
 def synthetic_codes_scales(rng, rows, cols, p_zero=0.4, scale_sigma=0.02):
     """Codes {0,1,2} with P(code 1, w=0)=p_zero and P(code 0)=P(code 2)=(1-p_zero)/2, then
     fp16 scales |N(0,1)|*scale_sigma per 128-group."""

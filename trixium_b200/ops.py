@@ -212,6 +212,21 @@ def matvec_f_batch(ctx, w: DeviceTensor, w_stride, x, x_stride, y, y_stride, njo
     return y
 
 
+def hadamard_rotate(ctx, had: DeviceTensor, x, out=None):
+    """The engine's blockwise rotation (model/mirror.py:680-690): block b of the output is the
+    quantised float projection of block tensor b against x[b*block:(b+1)*block], all blocks in one
+    trx_matvec_f_batch launch.  had: the stacked block tensors (image.hadamard_tensor), width rows of
+    block columns; x, out: width floats."""
+    block, width = had.cols, had.rows
+    _need(x, torch.float32, "x")
+    if x.numel() != width:
+        raise ValueError(f"x has {x.numel()} elements, the rotation is {width} wide")
+    if out is None:
+        out = torch.empty(width, dtype=torch.float32, device=x.device)
+    one = DeviceTensor.from_packed(had.data, block, block, had.kind, had.bias, had.rshift)
+    return matvec_f_batch(ctx, one, block * L.row_bytes(block, had.kind), x, block, out, block, width // block)
+
+
 def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, out=None, tp=None):
     """One decode step of GQA attention (trx_attn_decode).  shape: _lib.AttnShape; q (H*(1+gated)*hd),
     k/v (n_kv*hd) float32; caches [max_pos, n_kv, hd] float16; pos: int32 device tensor of one
@@ -367,6 +382,6 @@ def row_bytes(cols, kind):
 
 
 __all__ = ["Context", "default_context", "DeviceTensor", "matvec_i8", "matvec_q8", "matvec_q8_f", "matvec_i8_rows", "quantize_pow2",
-           "matvec_f", "matvec_fp", "matvec_swiglu", "validate_packed", "matvec_f_batch", "attn_decode", "attn_decode_static", "attn_shape",
+           "matvec_f", "matvec_fp", "matvec_swiglu", "hadamard_rotate", "validate_packed", "matvec_f_batch", "attn_decode", "attn_decode_static", "attn_shape",
            "deltanet_shape", "deltanet_step", "lmhead_argmax", "lmhead_argmax_key", "argmax_token", "matvec_f_multi", "embed_lookup",
            "advance_position", "row_bytes", "L"]
