@@ -164,8 +164,47 @@ def hadamard_case(width, block, seed):
                         scale=specs[0].scales[0, 0], y=y, y_ref=y_ref.astype(f32))
 
 
+def bons_case():
+    """A one-layer tiny image from the reference's own generator and writer (model/tinygen.py
+    generate -> model/bons.py write_image; 2 channels, trit5, no int16 embedding), stored gzipped,
+    with what the reference's reader (model/bons.py:476-525) makes of it: the header fields, the
+    entry names, and per matvec tensor the sha256 of its decoded scales and codes and its engine
+    matvec on a seeded x8."""
+    import dataclasses
+    import gzip
+    import hashlib
+    import shutil
+    import tempfile
+    from model import tinygen
+    cfg = dataclasses.replace(tinygen.BONSAI_TINY, n_layer=1, name="bonsai-tiny-l1")
+    with tempfile.TemporaryDirectory() as tmp:
+        img, _, _ = tinygen.generate(tmp, n_channels=2, seed=1234, cfg=cfg, trit5=True, emb16=False)
+        with open(img, "rb") as src, gzip.GzipFile(os.path.join(HERE, "bons_tiny_l1_t5_n2.img.gz"), "wb",
+                                                    compresslevel=9, mtime=0) as dst:
+            shutil.copyfileobj(src, dst)
+        r = bons.BONSReader(img)
+        out = {k: r.header[k] for k in ("n_layer", "n_embd", "n_head", "n_kv_head", "head_dim", "ffn_dim",
+                                        "vocab", "n_channels", "n_tensors", "payload_beats")}
+        out["names"] = np.array([e["name"] for e in r.entries])
+        rng = np.random.default_rng(40)
+        for i, e in enumerate(r.entries):
+            if e["kind"] not in (layout.KIND_TERNARY, layout.KIND_TERNARY5, layout.KIND_Q8):
+                continue
+            scales, values = r.tensor(e["name"])
+            h = hashlib.sha256(np.ascontiguousarray(scales).tobytes() +
+                               np.ascontiguousarray(values).astype(np.int16).tobytes()).hexdigest()
+            x8 = rng.integers(-127, 128, e["cols"], dtype=np.int8)
+            if e["kind"] == layout.KIND_Q8:
+                y = bx.matvec_q8(scales, values, x8, e["bias"], e["rshift"])
+            else:
+                y = bx.matvec_ternary(scales, values, x8, e["bias"], e["rshift"])
+            out[f"e{i}_sha"], out[f"e{i}_x8"], out[f"e{i}_y"] = h, x8, y
+    np.savez_compressed(os.path.join(HERE, "bons_tiny_l1_t5_n2.npz"), **out)
+
+
 def main():
     q8_cases()
+    bons_case()
     hadamard_case(1024, 512, 30)
     hadamard_case(2048, 1024, 31)
     hadamard_case(512, 128, 32)
