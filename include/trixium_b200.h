@@ -242,9 +242,9 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const floa
  * splits = ceil(max_pos / chunk) with chunk the smallest of 64, 128, 256 (128 when head_dim >
  * 128) giving at most 16 splits; larger shapes return TRX_ERR_UNSUPPORTED), so the library
  * allocates nothing.  Device error bits are OR'd into *d_err (a caller-owned device word).  The
- * first call on a device sets the arrays up (and waits for the device), so it should come before
- * any stream capture and before other work on that device's streams; calls that overlap on the
- * GPU race on the arrays.
+ * arrays are zero when the library's module loads on a device and every launch leaves the arrival
+ * counts at zero again; each call looks the arrays' device addresses up on the host (no device
+ * work, no allocation).  Calls that overlap on the GPU race on the arrays.
  */
 trx_status trx_attn_decode_static(const trx_attn_shape *shape, const float *d_q, const float *d_k,
                                   const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,

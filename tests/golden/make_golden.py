@@ -1,9 +1,9 @@
 """Generate the golden fixtures for the ternary decode path from the reference's own Python.
 
-Run in a container that has the TriXium reference tree (read-only) at TRIXIUM_REF
-(default /root/reference):
+Run where the TriXium reference tree (read-only) is importable, with TRIXIUM_REF naming its
+root directory:
 
-    python tests/golden/make_golden.py
+    TRIXIUM_REF=<reference tree> python tests/golden/make_golden.py
 
 It imports the reference's `model.bons` (TensorSpec + encode_rows: the converter's row-packet
 bytes, with its per-tensor B/R), `model.bitexact` (matvec_ternary and matvec_q8, the engine's integer specs),
@@ -24,7 +24,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("TRIXIUM_REF", "/root/reference")
+REF = os.environ.get("TRIXIUM_REF")
+if not REF:
+    sys.exit("set TRIXIUM_REF to the root of the TriXium reference tree")
 sys.path.insert(0, REF)
 
 from model import bitexact as bx          # noqa: E402

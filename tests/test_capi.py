@@ -59,3 +59,18 @@ def test_bindings_match_header_arity():
         fn = getattr(L, name)
         assert fn.argtypes is not None, name
         assert len(fn.argtypes) == len([a for a in args.split(",") if a.strip()]), name
+
+
+def test_static_attention_rejects_shapes_beyond_its_arrays():
+    """trx_attn_decode_static checks its fixed limits on the host before any CUDA call: more than
+    64 kv heads, or partials beyond 2^20 floats, return TRX_ERR_UNSUPPORTED (the pointers here are
+    never dereferenced)."""
+    import ctypes
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(0x1000)  # 16-byte aligned, never touched
+    args = [fake] * 11 + [ctypes.c_void_p(0)]
+    too_many_kv = _lib.AttnShape(128, 128, 64, 64, 512, 0, 1e-6)
+    assert lib.trx_attn_decode_static(ctypes.byref(too_many_kv), *args) == -6
+    # 64 kv heads x 16 splits x 8 heads per kv head x (128 + 2) floats > 2^20.
+    too_many_partials = _lib.AttnShape(512, 64, 128, 128, 4096, 0, 1e-6)
+    assert lib.trx_attn_decode_static(ctypes.byref(too_many_partials), *args) == -6

@@ -909,17 +909,16 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
 
 // Launch a cluster attention kernel: one cluster of nsplit CTAs per kv head.
 template <typename K>
-cudaError_t launch_cluster(K k, unsigned long long &configured, const AttnArgs &A, uint32_t *err, size_t smem,
+cudaError_t launch_cluster(K k, DevBits &configured, const AttnArgs &A, uint32_t *err, size_t smem,
                            cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (!(configured & bit)) {
+    cudaError_t e0 = once_per_device(configured, [&] {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-        configured |= bit;
-    }
+        return e;
+    });
+    if (e0 != cudaSuccess) return e0;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(A.nsplit, A.Hkv);
     cfg.blockDim = dim3(kClThreads);
@@ -942,14 +941,19 @@ cudaError_t launch_cluster(K k, unsigned long long &configured, const AttnArgs &
         int ok;
     } seen[64];
     static int nseen = 0;
+    static std::mutex seen_mu;
     int ok = -1;
-    for (int i = 0; i < nseen; ++i)
-        if (seen[i].k == (const void *)k && seen[i].dev == dev && seen[i].ns == A.nsplit && seen[i].smem == smem)
-            ok = seen[i].ok;
+    {
+        std::lock_guard<std::mutex> lock(seen_mu);
+        for (int i = 0; i < nseen; ++i)
+            if (seen[i].k == (const void *)k && seen[i].dev == dev && seen[i].ns == A.nsplit && seen[i].smem == smem)
+                ok = seen[i].ok;
+    }
     if (ok < 0) {
         int nc = 0;
         ok = cudaOccupancyMaxActiveClusters(&nc, k, &cfg) == cudaSuccess && nc > 0 ? 1 : 0;
         cudaGetLastError();
+        std::lock_guard<std::mutex> lock(seen_mu);
         if (nseen < 64) seen[nseen++] = {(const void *)k, dev, A.nsplit, smem, ok};
     }
     if (!ok) return cudaErrorNotSupported;
@@ -959,13 +963,13 @@ cudaError_t launch_cluster(K k, unsigned long long &configured, const AttnArgs &
 
 template <int REP, int DPL>
 cudaError_t launch_cl(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_t st) {
-    static unsigned long long configured = 0;
+    static DevBits configured{0};
     return launch_cluster(attn_cluster_kernel<REP, DPL>, configured, A, err, smem, st);
 }
 
 template <int HD>
 cudaError_t launch_mma(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream_t st) {
-    static unsigned long long configured = 0;
+    static DevBits configured{0};
     return launch_cluster(attn_mma_kernel<HD>, configured, A, err, smem, st);
 }
 
@@ -974,7 +978,6 @@ cudaError_t launch_mma(const AttnArgs &A, uint32_t *err, size_t smem, cudaStream
 bool mma_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem, int &merge_own) {
     const int rep = A.H / A.Hkv;
     if (rep < 1 || rep > 8 || !(A.hd == 64 || A.hd == 128)) return false;
-    if (getenv("TRX_NO_CLUSTER_ATTN") || getenv("TRX_NO_MMA_ATTN")) return false;
     chunk = ((A.max_pos + 15) / 16 + 31) / 32 * 32;
     nsplit = (A.max_pos + chunk - 1) / chunk;
     if (nsplit > 16) return false;
@@ -991,7 +994,6 @@ bool cl_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem, int &merg
     const int rep = A.H / A.Hkv;
     if (!(rep == 1 || rep == 2 || rep == 4 || rep == 6 || rep == 8)) return false;
     if (!(A.hd == 64 || A.hd == 128 || A.hd == 256)) return false;
-    if (getenv("TRX_NO_CLUSTER_ATTN")) return false;
     chunk = ((A.max_pos + 15) / 16 + 31) / 32 * 32;
     nsplit = (A.max_pos + chunk - 1) / chunk;
     if (nsplit > 16) return false;
@@ -1043,16 +1045,11 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
     }
     const AttnArgs &A = A0;
     const size_t smem = attn_smem_bytes(A.hd, A.H / A.Hkv, A.chunk);
-    static unsigned long long configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (!(configured & bit)) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
-        if (e != cudaSuccess) return note_cuda(e);
-        configured |= bit;
-    }
+    static DevBits configured{0};
+    const cudaError_t e = once_per_device(configured, [] {
+        return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
+    });
+    if (e != cudaSuccess) return note_cuda(e);
     return note_cuda(launch_kernel(attn_decode_kernel, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
 }
 
@@ -1062,44 +1059,34 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
 // For callers that cannot allocate device memory while they run: a serving loop that reserved
 // all of the device's memory before it started, or a host runtime whose device allocator belongs
 // to another framework.  The partials and arrival counts live in this file's static device arrays
-// instead of a trx_ctx's scratch; the library allocates nothing.  The first call on a device sets
-// up (symbol addresses, counts zeroed) and should come before any other work on that device's
-// streams; calls that overlap in time race on the one array per device.
+// instead of a trx_ctx's scratch; the library allocates nothing.  The arrays are zero when the
+// module loads on a device (the counts must start at zero; every launch leaves them at zero
+// again).  Their device addresses are looked up on every call (host-side, allocation-free), so a
+// context torn down and recreated on the device (cudaDeviceReset) gets the new module's arrays.
+// Calls that overlap in time race on the one array per device.
 namespace trx {
 namespace {
 
 constexpr size_t kStaticPartFloats = size_t(1) << 20;  // 4 MiB: [n_kv][splits][H/n_kv][hd + 2]
 constexpr uint32_t kStaticMaxKv = 64;
 __device__ __align__(256) float g_static_part[kStaticPartFloats];
-__device__ __align__(256) unsigned g_static_cnt[kStaticMaxKv];  // must start at zero
+__device__ __align__(256) unsigned g_static_cnt[kStaticMaxKv];  // zero at module load and between launches
 
 struct StaticScratch {
-    bool ready;
     float *part;
     unsigned *cnt;
 };
-StaticScratch g_static[64];
-std::mutex g_static_mu;
 
+// The static arrays' device addresses in the current device's context (host code cannot use the
+// arrays' names as device addresses).
 trx_status static_scratch(StaticScratch &out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TRX_ERR_CUDA;
-    std::lock_guard<std::mutex> lock(g_static_mu);
-    StaticScratch &s = g_static[dev];
-    if (!s.ready) {
-        void *p = nullptr, *c = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_static_part);
-        if (e != cudaSuccess) return note_cuda(e);
-        e = cudaGetSymbolAddress(&c, g_static_cnt);
-        if (e != cudaSuccess) return note_cuda(e);
-        e = cudaMemset(c, 0, sizeof(g_static_cnt));
-        if (e == cudaSuccess) e = cudaDeviceSynchronize();
-        if (e != cudaSuccess) return note_cuda(e);
-        s.part = static_cast<float *>(p);
-        s.cnt = static_cast<unsigned *>(c);
-        s.ready = true;
-    }
-    out = s;
+    void *p = nullptr, *c = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_part);
+    if (e != cudaSuccess) return note_cuda(e);
+    e = cudaGetSymbolAddress(&c, g_static_cnt);
+    if (e != cudaSuccess) return note_cuda(e);
+    out.part = static_cast<float *>(p);
+    out.cnt = static_cast<unsigned *>(c);
     return TRX_OK;
 }
 
@@ -1140,7 +1127,7 @@ extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const flo
     if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u ||
         2ull * rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))
         return TRX_ERR_UNSUPPORTED;
-    trx::StaticScratch sc;
+    trx::StaticScratch sc{};
     const trx_status st = trx::static_scratch(sc);
     if (st != TRX_OK) return st;
     A.q = d_q;

@@ -27,10 +27,7 @@ static const int kMaxArgmaxJobs = 64;
 static const uint32_t kQ8MaxCols = 32768;
 
 namespace trx {
-bool pdl_enabled() {
-    static const bool on = std::getenv("TRX_NO_PDL") == nullptr;
-    return on;
-}
+bool pdl_enabled() { return true; }
 }  // namespace trx
 
 namespace {

@@ -1,5 +1,6 @@
 // Internal launch interface between the C ABI (trx_capi.cu) and the kernels.
 #pragma once
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <cuda_fp16.h>
@@ -9,8 +10,8 @@
 
 namespace trx {
 
-// Whether launches carry the programmatic-stream-serialization attribute (set TRX_NO_PDL in the
-// environment to launch plainly).
+// Whether launches carry the programmatic-stream-serialization attribute (always: every kernel of
+// the library waits for its predecessor with griddepcontrol.wait before reading its inputs).
 bool pdl_enabled();
 
 // Launch `k` on `st`, as a programmatic dependent of the stream's previous kernel when enabled.
@@ -28,6 +29,24 @@ inline cudaError_t launch_kernel(void (*k)(KArgs...), dim3 grid, dim3 block, siz
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+// Host set-up that a kernel needs once per device (its function attributes): bit d of `done` is
+// set once it has run on device d.  Several host threads may launch at once, so the bit is set
+// with an atomic OR (two threads may both run the set-up, which is idempotent).  A context torn
+// down and recreated on a device (cudaDeviceReset) forgets the attributes while the bit stays set;
+// such a program must not reuse the library's launches after the reset.
+using DevBits = std::atomic<unsigned long long>;
+template <typename F>
+inline cudaError_t once_per_device(DevBits &done, F &&setup) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = setup();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
 }
 
 enum { OUT_I32 = 0, OUT_F32 = 1, OUT_SWIGLU = 2 };

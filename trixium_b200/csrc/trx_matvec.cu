@@ -1184,16 +1184,11 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
 template <int KIND, int NW>
 static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, int grid, const uint32_t *lut, uint32_t *err,
                              cudaStream_t st) {
-    static unsigned long long configured = 0;  // devices whose attribute is set
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (!(configured & bit)) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(tmv_kernel<KIND, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-        if (e != cudaSuccess) return note_cuda(e);
-        configured |= bit;
-    }
+    static DevBits configured{0};  // devices whose attribute is set
+    const cudaError_t e = once_per_device(configured, [] {
+        return cudaFuncSetAttribute(tmv_kernel<KIND, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+    });
+    if (e != cudaSuccess) return note_cuda(e);
     return note_cuda(launch_kernel(tmv_kernel<KIND, NW>, dim3(grid), dim3(M.warps * 32), M.smem, st, J, M, lut, err));
 }
 
