@@ -52,18 +52,26 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(kind):
-    """dram bytes per launch of the timed kernel, from the committed ncu summary (or None)."""
-    path = os.path.join(ROOT, "profiles", f"matvec_k{kind}_config0_ncu.md")
-    if not os.path.exists(path):
-        return None
-    for line in open(path):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
-    return None
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one 96-copy batch launch of the
+# matvec kernel, per kind, from the ncu capture summarised in profiles/matvec_k{kind}_config0_ncu.md,
+# with the sha256 of the kernel sources it was captured from.  When the sources have changed since,
+# the figure no longer describes the kernel and the line reports null.
+KERNEL_TRAFFIC = {}
+KERNEL_SOURCES = ("trixium_b200/csrc/trx_matvec.cu", "trixium_b200/csrc/trx_common.cuh")
+
+
+def kernel_sources_sha():
+    import hashlib
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES:
+        with open(os.path.join(ROOT, f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()
+
+
+def measured_traffic(kind):
+    t = KERNEL_TRAFFIC.get(kind)
+    return float(t[0]) if t and t[1] == kernel_sources_sha() else None
 
 
 class ClockSampler:
@@ -119,13 +127,21 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def host_cores():
+    """The host threads this process may run on (its CPU affinity, else the machine's count)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(kind, seconds=10.0, threads=None):
-    """The C oracle (oracle/trx_oracle.c) on this host: repeated config-0 float projections."""
+    """The C oracle (oracle/trx_oracle.c) on this host: repeated config-0 float projections, on
+    every host core (the OpenMP thread count set explicitly: under torchrun OMP_NUM_THREADS is 1)."""
     from oracle import build as cor
     from trixium_b200 import image, layout as L
     lib = cor.lib()
-    if threads:
-        lib.trxo_set_threads(int(threads))
+    lib.trxo_set_threads(int(threads or host_cores()))
     t, x = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=kind)
     alg = L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * (K_COLS + N_ROWS)
     cor.matvec_f(t.packed, N_ROWS, K_COLS, kind, t.bias, t.rshift, x)   # warm-up
@@ -149,6 +165,7 @@ def run_reference(args, rank, world):
     from oracle import build as cor
     from trixium_b200 import image, layout as L
     lib = cor.lib()
+    lib.trxo_set_threads(host_cores())  # every host core, also under torchrun (OMP_NUM_THREADS=1)
     t, x = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=args.kind)
     alg = L.algorithmic_bytes(N_ROWS, K_COLS, args.kind) + 4 * (K_COLS + N_ROWS)
     for _ in range(args.warmup):
@@ -169,6 +186,74 @@ def run_reference(args, rank, world):
                          "sample": "one config-0 float projection per step (C oracle, OpenMP)"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def make_batch(ctx, kind, C, dev, rank):
+    """The benchmark's weights and inputs on the device: C copies of the config-0 tensor (copy 0 the
+    reference generator's seed-0 draw, copies 1..C-1 device draws of the same distribution) with one
+    (B, R) for all, C activations; copy 0's float projection checked bit-exact against the C oracle.
+    Returns (tensor, job stride, weights, x, y, parity)."""
+    import torch
+    from trixium_b200 import image, layout as L, ops
+    from oracle import build as cor
+    t0, x0 = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=kind)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    scales_all = [torch.from_numpy(t0.scales).to(dev)]
+    codes_all = [torch.from_numpy(t0.codes).to(dev)]
+    for _ in range(1, C):
+        c, s = image.synthetic_codes_scales_torch(gen, N_ROWS, K_COLS, dev)
+        codes_all.append(c)
+        scales_all.append(s)
+    # One (B, R) for every copy so a single entry describes them (max over the copies).
+    smax = max(float(s.float().abs().max()) for s in scales_all)
+    B = image.scale_bias(np.array([smax], dtype=np.float16))
+    R = max(image.result_shift(s.cpu().numpy(), B) for s in scales_all)
+    rb = L.row_bytes(K_COLS, kind)
+    wstride = N_ROWS * rb
+    W = torch.empty(C * wstride, dtype=torch.uint8, device=dev)
+    for j in range(C):
+        W[j * wstride:(j + 1) * wstride] = image.pack_rows_torch(scales_all[j], codes_all[j], kind)
+    del codes_all, scales_all
+    X = torch.randn(C, K_COLS, generator=gen, device=dev)
+    X[0] = torch.from_numpy(x0).to(dev)
+    Y = torch.empty(C, N_ROWS, dtype=torch.float32, device=dev)
+    wt = ops.DeviceTensor.from_packed(W, N_ROWS, K_COLS, kind, B, R)
+    ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
+    ctx.raise_on_error()
+    y_or, bad = cor.matvec_f(t0.packed if (t0.bias, t0.rshift) == (B, R) else
+                             image.pack_rows(t0.scales, t0.codes, kind), N_ROWS, K_COLS, kind, B, R, x0)
+    parity = bool(bad == 0 and np.array_equal(Y[0].cpu().numpy().view(np.uint32), y_or.view(np.uint32)))
+    return wt, wstride, W, X, Y, parity
+
+
+def other_kind_leg(ctx, kind, C, steps, warmup, dev, rank, peak):
+    """The config-0 batch in the other code image (2-bit beside trit5, or trit5 beside 2-bit): the
+    same timing, inputs resident, its own roofline figures."""
+    import torch
+    from trixium_b200 import layout as L, ops
+    wt, wstride, W, X, Y, parity = make_batch(ctx, kind, C, dev, rank)
+    for _ in range(warmup):
+        ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        a.record(st)
+        ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
+        b.record(st)
+    torch.cuda.synchronize()
+    ctx.raise_on_error()
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    alg = (L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * (K_COLS + N_ROWS)) * C
+    achieved = alg / (launch_ms * 1e-3) / 1e9
+    del wt, W, X, Y
+    torch.cuda.empty_cache()
+    return {"metric": metric_name(kind), "value": round(achieved, 1), "unit": "GB/s", "ms_per_launch": launch_ms,
+            "parity_copy0_bitexact": parity,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": measured_traffic(kind),
+                         "algorithmic_bytes_per_launch": alg}}
 
 
 def metric_name(kind):
@@ -217,39 +302,8 @@ def main():
     ctx = ops.Context(local)
 
     kind, C = args.kind, args.copies
-    # Copy 0: the reference generator's seed-0 draw; copies 1..C-1 drawn on the device.
-    t0, x0 = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=kind)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1000 + rank)
-    scales_all = [torch.from_numpy(t0.scales).to(dev)]
-    codes_all = [torch.from_numpy(t0.codes).to(dev)]
-    for _ in range(1, C):
-        c, s = image.synthetic_codes_scales_torch(gen, N_ROWS, K_COLS, dev)
-        codes_all.append(c)
-        scales_all.append(s)
-    # One (B, R) for every copy so a single entry describes them (max over the copies).
-    smax = max(float(s.float().abs().max()) for s in scales_all)
-    B = image.scale_bias(np.array([smax], dtype=np.float16))
-    R = max(image.result_shift(s.cpu().numpy(), B) for s in scales_all)
-    rb = L.row_bytes(K_COLS, kind)
-    wstride = N_ROWS * rb
-    W = torch.empty(C * wstride, dtype=torch.uint8, device=dev)
-    for j in range(C):
-        W[j * wstride:(j + 1) * wstride] = image.pack_rows_torch(scales_all[j], codes_all[j], kind)
-    del codes_all, scales_all
-    X = torch.randn(C, K_COLS, generator=gen, device=dev)
-    X[0] = torch.from_numpy(x0).to(dev)
-    Y = torch.empty(C, N_ROWS, dtype=torch.float32, device=dev)
-    wt = ops.DeviceTensor.from_packed(W, N_ROWS, K_COLS, kind, B, R)
-
-    # Parity of copy 0 with the C oracle before timing (bit-exact float results).
-    from oracle import build as cor
-    ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
-    ctx.raise_on_error()
-    y_or, bad = cor.matvec_f(t0.packed if (t0.bias, t0.rshift) == (B, R) else
-                             image.pack_rows(t0.scales, t0.codes, kind), N_ROWS, K_COLS, kind, B, R, x0)
-    parity = bool(bad == 0 and np.array_equal(Y[0].cpu().numpy().view(np.uint32), y_or.view(np.uint32)))
-
+    wt, wstride, W, X, Y, parity = make_batch(ctx, kind, C, dev, rank)
+    B, R = wt.bias, wt.rshift
     alg_per_copy = L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * (K_COLS + N_ROWS)
     alg_per_step = alg_per_copy * C
 
@@ -355,7 +409,7 @@ def main():
         "frac_of_8tbs_nominal": round(value / world / NOMINAL_HBM_GBS, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                     "traffic": profile_traffic(kind),
+                     "traffic": measured_traffic(kind), "kernel_sources_sha256": kernel_sources_sha(),
                      "algorithmic_bytes_per_launch": alg_per_step,
                      "kernel": "trx::tmv_kernel (trx_matvec_f_batch)"},
         "per_launch_single_matvec": None if single_ms is None else {
@@ -366,12 +420,18 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if world == 1 and not args.no_extra:
+        out["other_kind"] = other_kind_leg(ctx, 0 if kind == 5 else 5, C, args.steps, args.warmup, dev, rank, peak)
     if world > 1 and not args.no_decode:
         out["decode"] = {"qwen3-8b": tp_decode_leg(ctx, "qwen3-8b", 1024, 64, 5, rank, world, dev)}
     if world == 1 and not args.no_decode:
         # The metric's second half: 8B-shape batch-1 decode tok/s (config 2), and config 1.
         out["decode"] = {"qwen3-8b": decode_leg(ctx, "qwen3-8b", 1024, 128, 8),
-                         "qwen3-1.7b": decode_leg(ctx, "qwen3-1.7b", 512, 128, 8)}
+                         "qwen3-1.7b": decode_leg(ctx, "qwen3-1.7b", 512, 128, 8),
+                         # BASELINE configs 3 and 4 at batch 1: 256 tokens after 2048 of context;
+                         # 128 tokens at 4096 of context (the down projection K-segmented).
+                         "hybrid-2b": decode_leg(ctx, "hybrid-2b", 2048, 256, 8),
+                         "hybrid-27b": decode_leg(ctx, "hybrid-27b", 4096, 128, 8)}
     if world == 1 and not args.no_decode:
         out["q8_matvec"] = q8_leg(ctx, peak)
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -178,6 +178,30 @@ trx_status trx_matvec_f_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, 
 trx_status trx_embed_lookup(trx_ctx *ctx, const void *d_table, uint32_t vocab, uint32_t dim, int32_t f16,
                             const int32_t *d_token, float *d_x, cudaStream_t stream);
 
+/* x = mant[*d_token] * 2^exp[*d_token] as fp32: the int16 embedding table of a BONS image
+ * (ROLE_TOK_EMB16 rows [vocab][dim] and ROLE_TOK_EMB16_EXP exponents; model/mirror.py:777-783,
+ * firmware embed_row_bfp).  A token outside [0, vocab) sets TRX_DEV_RANGE and writes zeros. */
+trx_status trx_embed_lookup_bfp16(trx_ctx *ctx, const int16_t *d_mant, const int32_t *d_exp, uint32_t vocab,
+                                  uint32_t dim, const int32_t *d_token, float *d_x, cudaStream_t stream);
+
+/* y = (x * r) * w with r = 1/sqrt(ss/n + eps), ss the canonical 64-partial sum of squares
+ * (model/mirror.py:576-591, :697-700 rmsnorm).  One launch; y may not alias x. */
+trx_status trx_rmsnorm(trx_ctx *ctx, const float *d_x, const float *d_w, uint32_t n, float eps, float *d_y,
+                       cudaStream_t stream);
+
+/*
+ * Float projection of a K-segmented tensor (FLAG_KSEG: a matvec wider than one engine op stored as
+ * nseg tensors over consecutive column ranges, model/bons.py:83-113 split_wide), in the engine's
+ * arithmetic (model/mirror.py:664-678, firmware/infer_float.c:183-186): x quantised once (one
+ * exponent for the whole input), each segment's int32 engine result (>> R per segment), their
+ * int64 sum wrapped to int32, times 2^(e8 + R - B), plus d_resid when not NULL.  segs: the
+ * segments' entries in order (same rows, the tensor's B and R in every one; ternary kinds or
+ * TRX_KIND_Q8); d_packed: a host array of their device pointers.  x: the sum of the segments' cols
+ * floats (at most 32768).  Uses the context's scratch: calls on one context must not overlap.
+ */
+trx_status trx_matvec_f_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
+                             const float *d_x, const float *d_resid, float *d_y, cudaStream_t stream);
+
 /* *d_pos += n on the device (the decode loop's position, read by the attention and DeltaNet steps). */
 trx_status trx_advance_position(trx_ctx *ctx, int32_t *d_pos, int32_t n, cudaStream_t stream);
 
@@ -232,6 +256,19 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const floa
                            const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
                            const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
                            float *d_out, cudaStream_t stream);
+
+/*
+ * trx_attn_decode over an fp32 KV cache (caches [max_pos][n_kv][head_dim] float, 16-byte aligned):
+ * the reference mirror keeps its cache in fp32 (model/mirror.py:966, kc[l].append(k)), so a run
+ * that must follow the mirror's values to fp32 rounding (token parity in the engine's int8
+ * arithmetic, where an fp16-rounded cache moves activations across int8 rounding boundaries)
+ * takes this form.  Same arguments and computation otherwise; one launch of the scratch-merge
+ * kernel on the context's scratch (calls on one context must not overlap).
+ */
+trx_status trx_attn_decode_f32cache(trx_ctx *ctx, const trx_attn_shape *shape, const float *d_q, const float *d_k,
+                                    const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                                    const float *d_rope_freq, float *d_kcache, float *d_vcache,
+                                    const int32_t *d_pos, float *d_out, cudaStream_t stream);
 
 /*
  * trx_attn_decode without a context, for callers that cannot allocate device memory while they

@@ -175,6 +175,22 @@ def matvec_q8_f(scales, q8w, x, B, R):
     return (res.astype(f32) * f32(np.exp2(f32(e8 + R - B)))).astype(f32)
 
 
+def matvec_f_kseg(segments, x, B, R):
+    """model/mirror.py:664-678 over K-segments (FLAG_KSEG, model/bons.py:83-113): quantise the whole
+    x once, per segment the engine's int32 result on its column range (segments: (kind, scales,
+    values) in order; ternary codes or Q8 weights), the int64 sum wrapped to int32, times
+    fp32 2**(e8+R-B)."""
+    x8, e8 = quantize_pow2(x)
+    res, c0 = np.zeros(segments[0][2].shape[0], dtype=np.int64), 0
+    for kind, scales, values in segments:
+        cols = values.shape[1]
+        xs = x8[c0:c0 + cols]
+        r = matvec_q8(scales, values, xs, B, R) if kind == 1 else matvec_int(scales, values, xs, B, R)
+        res += r.astype(np.int64)
+        c0 += cols
+    return (res.astype(np.int32).astype(f32) * f32(np.exp2(f32(e8 + R - B)))).astype(f32)
+
+
 def hadamard_codes(signs, block):
     """model/convert.py:99-118 with model/golden.py:256-263: block tensor b of the rotation has
     codes H[i, j] * s[b*block + j] + 1, H[i, j] = (-1)^popcount(i & j); its scales are all

@@ -204,7 +204,185 @@ def bons_case():
     np.savez_compressed(os.path.join(HERE, "bons_tiny_l1_t5_n2.npz"), **out)
 
 
+def _hybrid_cfg(base, **kw):
+    import dataclasses
+    return dataclasses.replace(base, **kw)
+
+
+def _exact_weights(img, e):
+    """A matvec tensor as the mirror's exact mode dequantises it (model/mirror.py:648-662)."""
+    scales, codes = img.tensor(e["name"])
+    if e["kind"] == layout.KIND_F32:
+        return np.asarray(codes, dtype=f32).reshape(e["rows"], e["cols"])
+    g = 128 if layout.is_ternary(e["kind"]) else 32
+    off = 1.0 if layout.is_ternary(e["kind"]) else 0.0
+    w = (codes.astype(f32).reshape(e["rows"], -1, g) - f32(off)) * scales.astype(f32)[:, :, None]
+    return w.reshape(e["rows"], e["cols"])
+
+
+def hybrid_kernel_case(name, cfg, n_prompt=8, n_new=4, seed=1234):
+    """Kernel-level fixtures for decode attention and the gated-DeltaNet step from the reference's
+    firmware mirror (model/mirror.py:594-1044, hybrid27_generate with exact=True: fp32 weights, no
+    activation quantisation, the mathematical profile).  The image comes from the reference's own
+    tensor inventory and writer (model/tinygen.py make_tiny_hybrid_tensors, model/bons.py
+    write_image) with no rotation and the layers' output projections (attn_output, ssm_out)
+    replaced by identity matrices (code 2 on the diagonal, 1 elsewhere, scale 1.0), so the traced
+    layer outputs ("attn_out", "dn_out", mirror.py:1008-1011) are the attention and DeltaNet
+    results themselves.  Stored per (position, layer): the layer's normed input's projections
+    (q with its gate; qkv, z, beta and alpha before their activations), computed as the mirror's
+    exact mode does (dequantised fp32 weights times the traced "attn_norm" vector), and the
+    traced output; per layer the norm weights, conv taps, A and dt bias; the rope frequencies."""
+    import tempfile
+    from model import tinygen
+    import dataclasses
+    # The inventory as tinygen makes it (its rotation tensors need a block), then without them.
+    tensors = tinygen.make_tiny_hybrid_tensors(dataclasses.replace(cfg, hadamard_block=128), seed)
+    tensors = [t for t in tensors if t.role != layout.ROLE_HADAMARD]
+    cfg = dataclasses.replace(cfg, hadamard_block=0, hadamard_signs=None)
+    E = cfg.n_embd
+    for t in tensors:
+        if t.role in (layout.ROLE_ATTN_OUT, layout.ROLE_SSM_OUT):
+            assert t.rows == E and t.cols == E, (t.name, t.rows, t.cols)
+            t.values = (np.eye(E, dtype=np.uint8) + 1).astype(np.uint8)
+            t.scales = np.ones((E, E // 128), np.float16)
+            t.bias = bx.choose_scale_bias(bx.fp16_decompose(t.scales)[1])
+            t.rshift = bx.choose_result_shift(t.scales, t.bias)
+    trace = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "k.img")
+        bons.write_image(cfg, tensors, 1, path, emb16=True)
+        img = bons.BONSReader(path)
+        h = img.header
+        rng = np.random.default_rng(seed + 1)
+        prompt = [int(t) for t in rng.integers(0, cfg.vocab, n_prompt)]
+
+        def cb(pos, layer, tag, dtype, values):
+            trace[(pos, layer, tag)] = np.asarray(values)
+        mirror.hybrid27_generate(img, prompt, n_new, exact=True, trace=cb)
+        ent = lambda role, l: next(e for e in img.entries if e["role"] == role and e["layer"] == l)
+        f32row = lambda role, l: np.asarray(img.tensor(ent(role, l)["name"])[1], dtype=f32).reshape(-1)
+        out = {"n_embd": E, "n_head": h["n_head"], "n_kv": h["n_kv_head"], "head_dim": h["head_dim"],
+               "rope_dims": h["rope_dims"] or h["head_dim"], "gated": h["attn_gated"], "eps": f32(h["rms_eps"]),
+               "nk": h["dn_num_k_heads"], "hk": h["dn_k_head_dim"], "nv": h["dn_num_v_heads"],
+               "hv": h["dn_v_head_dim"], "conv": h["dn_conv_kernel"],
+               "layer_types": np.array([1 if t == "deltanet" else 0 for t in h["layer_types"]])}
+        rope_n = out["rope_dims"]
+        out["rope_freq"] = np.array([f32(np.float32(h["rope_theta"]) ** f32(-2.0 * i / rope_n))
+                                     for i in range(rope_n // 2)], dtype=f32)
+        npos = n_prompt + n_new - 1
+        out["npos"] = npos
+        for l, lt in enumerate(h["layer_types"]):
+            W = lambda role: _exact_weights(img, ent(role, l))
+            hn = np.stack([trace[(p, l, "attn_norm")] for p in range(npos)]).astype(f32)
+            if lt == "deltanet":
+                for key, role in (("qkv", layout.ROLE_ATTN_QKV), ("z", layout.ROLE_ATTN_ZGATE),
+                                  ("beta", layout.ROLE_SSM_BETA), ("alpha", layout.ROLE_SSM_ALPHA)):
+                    w = W(role)
+                    out[f"l{l}_{key}"] = np.stack([(w @ v).astype(f32) for v in hn])
+                out[f"l{l}_out"] = np.stack([trace[(p, l, "dn_out")] for p in range(npos)]).astype(f32)
+                out[f"l{l}_conv_w"] = f32row(layout.ROLE_SSM_CONV, l)
+                out[f"l{l}_ssm_a"] = f32row(layout.ROLE_SSM_A, l)
+                out[f"l{l}_dt_bias"] = f32row(layout.ROLE_SSM_DT, l)
+                out[f"l{l}_ssm_norm"] = f32row(layout.ROLE_SSM_NORM, l)
+            else:
+                for key, role in (("q", layout.ROLE_ATTN_Q), ("k", layout.ROLE_ATTN_K), ("v", layout.ROLE_ATTN_V)):
+                    w = W(role)
+                    out[f"l{l}_{key}"] = np.stack([(w @ v).astype(f32) for v in hn])
+                out[f"l{l}_out"] = np.stack([trace[(p, l, "attn_out")] for p in range(npos)]).astype(f32)
+                out[f"l{l}_q_norm"] = f32row(layout.ROLE_ATTN_Q_NORM, l)
+                out[f"l{l}_k_norm"] = f32row(layout.ROLE_ATTN_K_NORM, l)
+    np.savez_compressed(os.path.join(HERE, f"mirror_layers_{name}.npz"), **out)
+
+
+def hybrid_tokens_case(name, cfg, trit5, kseg_max, n_prompt=6, n_new=128, seed=1234):
+    """End-to-end fixture: a tiny hybrid image from the reference's own generator and writer
+    (model/tinygen.py generate: DeltaNet and gated attention layers, the Hadamard-rotated basis,
+    Q8 beta/alpha, the int16 embedding table; K-segmented where wider than kseg_max), stored
+    gzipped, and the reference mirror's greedy tokens for a seeded prompt in its engine arithmetic
+    (model/mirror.py:594-1044, hybrid27_generate with exact=False and the mathematical profile):
+    int8 power-of-two activations, the engine's integer matvec.  Per generated step the logits'
+    top-two margin is kept too (where it is tiny, fp32 rounding order may flip the argmax)."""
+    import gzip
+    import shutil
+    import tempfile
+    from model import tinygen
+    with tempfile.TemporaryDirectory() as tmp:
+        img_path, _, _ = tinygen.generate(tmp, n_channels=2, seed=seed, cfg=cfg, kseg_max=kseg_max, trit5=trit5)
+        with open(img_path, "rb") as src, gzip.GzipFile(os.path.join(HERE, f"tokens_{name}.img.gz"), "wb",
+                                                         compresslevel=9, mtime=0) as dst:
+            shutil.copyfileobj(src, dst)
+        img = bons.BONSReader(img_path)
+        rng = np.random.default_rng(seed + 2)
+        prompt = [int(t) for t in rng.integers(0, cfg.vocab, n_prompt)]
+        margins, ckpt = {}, {}
+
+        def cb(pos, layer, tag, dtype, values):
+            if tag == "logits":
+                v = np.sort(np.asarray(values, dtype=np.float64))
+                margins[pos] = v[-1] - v[-2]
+            if pos < 3 and tag in ("emb", "attn_res", "ffn_res", "out_norm", "logits"):
+                ckpt[f"p{pos}_l{layer}_{tag}"] = np.asarray(values, dtype=f32)
+        toks = mirror.hybrid27_generate(img, prompt, n_new, exact=False, silu_mode="mathematical", trace=cb)
+    npos = n_prompt + n_new - 1
+    np.savez_compressed(os.path.join(HERE, f"tokens_{name}.npz"), prompt=np.array(prompt), tokens=np.array(toks),
+                        margins=np.array([margins[p] for p in range(n_prompt - 1, npos)]), **ckpt)
+
+
+def kseg_case(name, rows, cols, kind, seed):
+    """A K-segmented projection (model/bons.py:83-113 split_wide: equal column ranges, the whole
+    tensor's B/R in each segment) through the converter's row packets and the mirror's float
+    projection (model/mirror.py:664-678: one exponent for the whole input, per segment the
+    engine's int32 result, their int64 sum wrapped to int32, scaled once)."""
+    rng = np.random.default_rng(seed)
+    if kind == layout.KIND_Q8:
+        values = rng.integers(-127, 128, (rows, cols), dtype=np.int8)
+        scales = rng.uniform(0.005, 0.02, (rows, cols // 32)).astype(np.float16)
+        spec = bons.TensorSpec(name, layout.ROLE_FFN_DOWN, 0, layout.KIND_Q8, rows, cols, scales=scales,
+                               values=values)
+        segs = bons.split_wide(spec)
+    else:
+        values, scales = bench_dist(rng, rows, cols)
+        spec = bons.TensorSpec(name, layout.ROLE_FFN_DOWN, 0, layout.KIND_TERNARY, rows, cols, scales=scales,
+                               values=values)
+        segs = bons.split_wide(spec)
+        for t in segs:
+            t.kind = kind          # write_image(trit5=True) switches the kind the same way.
+    assert len(segs) > 1 and all(t.flags & layout.FLAG_KSEG for t in segs)
+    x = rng.standard_normal(cols).astype(f32)
+    x8, e8 = mirror._quantize_f_pow2(x)
+    res, c0, out = None, 0, {}
+    for k, t in enumerate(segs):
+        assert (t.bias, t.rshift) == (spec.bias, spec.rshift) and t.kseg == k
+        out[f"packed{k}"] = bons.encode_rows(t, 0, rows)
+        out[f"cols{k}"] = t.cols
+        xs = x8[c0:c0 + t.cols]
+        if kind == layout.KIND_Q8:
+            r = bx.matvec_q8(t.scales, t.get_values(), xs, t.bias, t.rshift)
+        else:
+            r = bx.matvec_ternary(t.scales, t.get_values(), xs, t.bias, t.rshift)
+        res = r.astype(np.int64) if res is None else res + r.astype(np.int64)
+        c0 += t.cols
+    y = (res.astype(np.int32).astype(f32) * f32(np.exp2(f32(e8 + spec.rshift - spec.bias)))).astype(f32)
+    np.savez_compressed(os.path.join(HERE, f"kseg_{name}.npz"), nseg=len(segs), rows=rows, cols=cols, kind=kind,
+                        B=spec.bias, R=spec.rshift, x=x, y=y, **out)
+
+
 def main():
+    from model import tinygen
+    # Decode attention and the DeltaNet step, pinned to the mirror (identity output projections).
+    hybrid_kernel_case("hd64", _hybrid_cfg(tinygen.BONSAI_TINY_HYBRID, hadamard_block=0, dn_num_v_heads=4,
+                                           name="kernels-hd64"))
+    hybrid_kernel_case("hd256", _hybrid_cfg(tinygen.BONSAI_TINY_HYBRID, hadamard_block=0, n_embd=512, n_head=2,
+                                            n_kv_head=1, head_dim=256, rope_dims=64, dn_num_k_heads=2,
+                                            dn_k_head_dim=128, dn_num_v_heads=4, dn_v_head_dim=128,
+                                            ffn_dim=512, name="kernels-hd256"))
+    # Greedy tokens of the mirror's engine arithmetic on reference-made images.
+    hybrid_tokens_case("hybrid_t5_kseg", tinygen.BONSAI_TINY_HYBRID, trit5=True, kseg_max=256)
+    hybrid_tokens_case("hybrid_2b", tinygen.BONSAI_TINY_HYBRID, trit5=False, kseg_max=None)
+    # K-segmented projections at the hybrid-27b down projection's width and a wide Q8 tensor.
+    kseg_case("t5_24x17408", 24, 17408, layout.KIND_TERNARY5, 50)
+    kseg_case("2b_40x17408", 40, 17408, layout.KIND_TERNARY, 51)
+    kseg_case("q8_20x9216", 20, 9216, layout.KIND_Q8, 52)
     q8_cases()
     bons_case()
     hadamard_case(1024, 512, 30)

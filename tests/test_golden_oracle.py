@@ -150,3 +150,109 @@ def test_hadamard_tensor_and_oracle_rotation(path):
     assert np.array_equal(y.view(np.uint32), d["y"].view(np.uint32))
     # The engine's rotation approximates the float transform (int8 activations): within 2 %.
     assert np.abs(y - d["y_ref"]).max() <= 0.02 * np.abs(d["y_ref"]).max()
+
+
+# Decode attention and the gated-DeltaNet step against the reference's firmware mirror -------------
+# Fixtures mirror_layers_*.npz: model/mirror.py hybrid27_generate (exact=True, mathematical profile)
+# on a reference-written hybrid image whose output projections are identities, so its traced layer
+# outputs are the attention and DeltaNet results (tests/golden/make_golden.py hybrid_kernel_case).
+
+MIRROR_LAYERS = ["hd64", "hd256"]
+
+
+def mirror_layers(name):
+    return load(os.path.join(GOLDEN, f"mirror_layers_{name}.npz"))
+
+
+def _scale_err(got, want):
+    return float(np.abs(np.asarray(got, np.float64) - want).max() / max(1.0, float(np.abs(want).max())))
+
+
+@pytest.mark.parametrize("name", MIRROR_LAYERS)
+def test_attention_oracle_matches_the_mirror(name):
+    """oracle/ref.attn_decode step by step against the mirror's attention (model/mirror.py:945-996):
+    with fp32 cache rows the oracle follows the mirror to 1e-5 of the output scale; with the build's
+    fp16 cache to 1e-3."""
+    d = mirror_layers(name)
+    H, Hkv, hd, eps = int(d["n_head"]), int(d["n_kv"]), int(d["head_dim"]), float(d["eps"])
+    gated, freq, npos = bool(d["gated"]), d["rope_freq"], int(d["npos"])
+    n = 0
+    for l, dn in enumerate(d["layer_types"]):
+        if dn:
+            continue
+        qn, kn = d[f"l{l}_q_norm"], d[f"l{l}_k_norm"]
+        k32 = np.zeros((npos, Hkv, hd), np.float32)
+        v32 = np.zeros_like(k32)
+        k16 = np.zeros((npos, Hkv, hd), np.float16)
+        v16 = np.zeros_like(k16)
+        for p in range(npos):
+            qm = d[f"l{l}_q"][p].reshape(H, -1)
+            q, gate = qm[:, :hd].copy(), (qm[:, hd:].copy() if gated else None)
+            k, v = d[f"l{l}_k"][p].reshape(Hkv, hd), d[f"l{l}_v"][p].reshape(Hkv, hd)
+            rows32 = (np.stack([ref.rope_neox(ref.rmsnorm(k[h], kn, eps), p, freq) for h in range(Hkv)]),
+                      v.astype(np.float32))
+            o32 = ref.attn_decode(q, k, v, k32, v32, p, qn, kn, eps, freq, gate=gate, rows=rows32)
+            o16 = ref.attn_decode(q, k, v, k16, v16, p, qn, kn, eps, freq, gate=gate)
+            want = d[f"l{l}_out"][p]
+            assert _scale_err(o32.reshape(-1), want) <= 1e-5, (l, p)
+            assert _scale_err(o16.reshape(-1), want) <= 1e-3, (l, p)
+            n += 1
+    assert n > 0
+
+
+@pytest.mark.parametrize("name", MIRROR_LAYERS)
+def test_deltanet_oracle_matches_the_mirror(name):
+    """oracle/ref.deltanet_step from a zero state, step by step, against the mirror's DeltaNet
+    (model/mirror.py:892-943): the grouped-order gated-norm output to 1e-4 of its scale (the mirror
+    sums in sequence, the oracle with numpy's matmul)."""
+    d = mirror_layers(name)
+    nk, hk, nv, hv, K = (int(d[k]) for k in ("nk", "hk", "nv", "hv", "conv"))
+    eps = float(d["eps"])
+    C = 2 * nk * hk + nv * hv
+    n = 0
+    for l, dn in enumerate(d["layer_types"]):
+        if not dn:
+            continue
+        win = np.zeros((K - 1, C), np.float32)
+        S = np.zeros((nv, hv, hk), np.float32)
+        for p in range(int(d["npos"])):
+            og = ref.deltanet_step(d[f"l{l}_qkv"][p], d[f"l{l}_z"][p], d[f"l{l}_beta"][p], d[f"l{l}_alpha"][p],
+                                   d[f"l{l}_dt_bias"], d[f"l{l}_ssm_a"], d[f"l{l}_conv_w"].reshape(C, K), win, S,
+                                   d[f"l{l}_ssm_norm"], eps, nk, hk, nv, hv)
+            assert _scale_err(og, d[f"l{l}_out"][p]) <= 1e-4, (l, p)
+            n += 1
+    assert n > 0
+
+
+# K-segmented projections (model/bons.py:83-113 split_wide; model/mirror.py:664-678) --------------
+
+KSEG = ["t5_24x17408", "2b_40x17408", "q8_20x9216"]
+
+
+def kseg_segments(d):
+    out = []
+    kind, rows = int(d["kind"]), int(d["rows"])
+    for k in range(int(d["nseg"])):
+        cols = int(d[f"cols{k}"])
+        if kind == L.KIND_Q8:
+            s, v = ref.q8_decode_packed(d[f"packed{k}"], rows, cols)
+        else:
+            s, v = ref.decode_packed(d[f"packed{k}"], rows, cols, kind)
+        out.append((kind, s, v))
+    return out
+
+
+@pytest.mark.parametrize("name", KSEG)
+def test_kseg_oracle_bit_exact(name):
+    """The oracle's K-segmented float projection against the mirror's, fp32 bits."""
+    d = load(os.path.join(GOLDEN, f"kseg_{name}.npz"))
+    y = ref.matvec_f_kseg(kseg_segments(d), d["x"], int(d["B"]), int(d["R"]))
+    assert np.array_equal(y.view(np.uint32), d["y"].view(np.uint32))
+    # One segment-wide shift per segment is not one shift of the whole sum: the unsegmented
+    # projection of the same weights differs in the low bits somewhere.
+    if int(d["kind"]) != L.KIND_Q8:
+        segs = kseg_segments(d)
+        s = np.concatenate([a[1] for a in segs], axis=1)
+        c = np.concatenate([a[2] for a in segs], axis=1)
+        whole = ref.matvec_f(s, c, d["x"], int(d["B"]), int(d["R"]))
+        assert not np.array_equal(whole.view(np.uint32), d["y"].view(np.uint32))

@@ -1,0 +1,145 @@
+"""Greedy decoding straight from a BONS image against the reference's own engine mirror.
+
+Fixtures (tests/golden/tokens_*.npz + .img.gz, made by tests/golden/make_golden.py
+hybrid_tokens_case): tiny hybrid images from the reference's generator and writer
+(model/tinygen.py: DeltaNet and gated attention layers, the Hadamard-rotated basis, Q8 beta/alpha,
+the int16 embedding table; one image trit5 with every matvec wider than 256 K-segmented, one 2-bit)
+and the greedy tokens of model/mirror.py hybrid27_generate (exact=False, mathematical profile: int8
+activations, the engine's integer matvec) for a seeded prompt, 128 steps, with each step's top-two
+logit margin and the traced values of the first positions.
+
+The decoder here (trixium_b200.decoder.ImageDecoder) runs the mirror's arithmetic with its fp32 KV
+cache (trx_attn_decode_f32cache); its attention and DeltaNet kernels sum in parallel where the
+mirror sums in sequence, so values agree to fp32 rounding, and an int8 activation can round the
+other way where a value sits within that rounding of a .5 boundary.  The tests require:
+* the traced hidden states of the first positions within 1e-3 of their scale;
+* teacher-forced (fed the mirror's tokens), the greedy token of every step whose top-two margin is
+  at least 1e-3 equal to the mirror's;
+* free-running, the mirror's tokens until the first step whose margin is below 1e-3;
+* with the build's fp16 KV cache (the bench's configuration; the rounding of every cached value
+  moves activations across int8 boundaries), teacher-forced agreement on every step whose margin is
+  at least 5e-2.
+"""
+import gzip
+import os
+import shutil
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, load
+
+NAMES = ["hybrid_t5_kseg", "hybrid_2b"]
+MARGIN = 1e-3
+MARGIN_FP16 = 5e-2
+
+
+def _image(tmp_path_factory, name):
+    from trixium_b200 import bons
+    p = tmp_path_factory.mktemp("img") / f"{name}.img"
+    with gzip.open(os.path.join(GOLDEN, f"tokens_{name}.img.gz"), "rb") as src, open(p, "wb") as dst:
+        shutil.copyfileobj(src, dst)
+    return bons.BONSImage(str(p))
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_image_tables_read_like_the_mirror(tmp_path_factory, name):
+    """CPU: the int16 embedding row of the first prompt token times its exponent is the mirror's
+    traced embedding; K-segments come back in order and cover the tensor's width."""
+    from trixium_b200 import bons, layout as L
+    img = _image(tmp_path_factory, name)
+    d = load(os.path.join(GOLDEN, f"tokens_{name}.npz"))
+    mant, exps = img.embedding_bfp16()
+    t = int(d["prompt"][0])
+    x = (mant[t].astype(np.float32) * np.float32(2.0 ** int(exps[t]))).astype(np.float32)
+    assert np.array_equal(x.view(np.uint32), d["p0_l-1_emb"].view(np.uint32))
+    h = img.header
+    down = img.matvec_entries(bons.ROLE_FFN_DOWN, 0)
+    assert sum(e["cols"] for e in down) == h["ffn_dim"]
+    if "kseg" in name:
+        assert len(down) > 1 and [e["kseg"] for e in down] == list(range(len(down)))
+        assert all(e["flags"] & bons.FLAG_KSEG for e in down)
+        assert {e["kind"] for e in down} == {L.KIND_TERNARY5}
+    else:
+        assert len(down) == 1
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from trixium_b200 import ops
+    c = ops.Context(0)
+    yield c
+    c.close()
+
+
+def _decoder(tmp_path_factory, ctx, name, kv_dtype=torch.float32):
+    from trixium_b200 import decoder as D
+    img = _image(tmp_path_factory, name)
+    return D.ImageDecoder(D.ImageWeights(img), ctx=ctx, max_pos=160, kv_dtype=kv_dtype)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", NAMES)
+def test_first_positions_follow_the_mirror(tmp_path_factory, ctx, name):
+    d = load(os.path.join(GOLDEN, f"tokens_{name}.npz"))
+    dec = _decoder(tmp_path_factory, ctx, name)
+    got = {}
+    dec.trace = lambda l, tag, t: got.__setitem__((l, tag), t.cpu().numpy())
+    for p in range(3):
+        got.clear()
+        dec.step(int(d["prompt"][p]))
+        torch.cuda.synchronize()
+        for key, want in d.items():
+            if not key.startswith(f"p{p}_"):
+                continue
+            _, ls, tag = key.split("_", 2)
+            l = int(ls[1:])
+            if (l, tag) not in got:
+                continue
+            g = got[(l, tag)].astype(np.float64)
+            err = np.abs(g - want).max() / max(1.0, float(np.abs(want).max()))
+            assert err <= 1e-3, (p, l, tag, err)
+    assert ctx.errors() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv", ["fp32", "fp16"])
+@pytest.mark.parametrize("name", NAMES)
+def test_teacher_forced_tokens_match_the_mirror(tmp_path_factory, ctx, name, kv):
+    d = load(os.path.join(GOLDEN, f"tokens_{name}.npz"))
+    prompt, toks, margins = list(d["prompt"]), list(d["tokens"]), d["margins"]
+    margin = MARGIN if kv == "fp32" else MARGIN_FP16
+    dec = _decoder(tmp_path_factory, ctx, name, torch.float32 if kv == "fp32" else torch.float16)
+    dec.capture()
+    seq = prompt + toks
+    agree, checked = 0, 0
+    for p in range(len(seq) - 1):
+        dec.step(int(seq[p]))
+        if p >= len(prompt) - 1:
+            i = p - (len(prompt) - 1)       # generated step i predicts toks[i]
+            got = int(dec.tok.item())
+            agree += got == toks[i]
+            if margins[i] >= margin:
+                checked += 1
+                assert got == toks[i], (i, got, toks[i], float(margins[i]))
+    assert checked >= 100
+    assert ctx.errors() == 0
+    print(f"{name} ({kv} KV cache): {agree}/{len(toks)} steps agree teacher-forced ({checked} with margin >= {margin})")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", NAMES)
+def test_free_running_tokens_match_the_mirror(tmp_path_factory, ctx, name):
+    d = load(os.path.join(GOLDEN, f"tokens_{name}.npz"))
+    prompt, toks, margins = [int(t) for t in d["prompt"]], [int(t) for t in d["tokens"]], d["margins"]
+    dec = _decoder(tmp_path_factory, ctx, name)
+    dec.capture()
+    out = dec.generate(prompt, len(toks))
+    first_small = next((i for i, m in enumerate(margins) if m < MARGIN), len(toks))
+    assert out[:first_small] == toks[:first_small]
+    same = next((i for i, (a, b) in enumerate(zip(out, toks)) if a != b), len(toks))
+    print(f"{name}: free-running tokens identical for {same} of {len(toks)} steps "
+          f"(first margin below {MARGIN} at step {first_small})")

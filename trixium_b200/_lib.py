@@ -25,10 +25,13 @@ SYMBOLS = (
     "trx_deltanet_step", "trx_lmhead_argmax", "trx_matvec_f_multi", "trx_embed_lookup", "trx_advance_position",
     "trx_attn_decode_static", "trx_lmhead_argmax_key", "trx_argmax_token", "trx_matvec_f_tp",
     "trx_matvec_f_multi_tp", "trx_matvec_swiglu_tp", "trx_lmhead_argmax_key_tp", "trx_argmax_token_tp",
-    "trx_attn_decode_tp",
+    "trx_attn_decode_tp", "trx_embed_lookup_bfp16", "trx_rmsnorm", "trx_matvec_f_kseg",
+    "trx_attn_decode_f32cache",
 )
 
 TP_MAX = 8
+# Device error-word bits (trx_get_error).
+TRX_DEV_OVERFLOW, TRX_DEV_BADBYTE, TRX_DEV_TIMEOUT, TRX_DEV_INTERNAL, TRX_DEV_RANGE = 0x1, 0x2, 0x4, 0x8, 0x10
 
 
 class TrxError(RuntimeError):
@@ -122,6 +125,11 @@ def lib():
                                          ctypes.c_int),
             "trx_argmax_token_tp": ([_vp, _vp, ctypes.c_int32, _vp, T, _vp], ctypes.c_int),
             "trx_attn_decode_tp": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 10 + [T, _vp], ctypes.c_int),
+            "trx_embed_lookup_bfp16": ([_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, _vp, _vp, _vp],
+                                       ctypes.c_int),
+            "trx_rmsnorm": ([_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_float, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f_kseg": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+            "trx_attn_decode_f32cache": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -24,6 +24,18 @@ ENTRY_SIZE = 64
 FLAG_REPLICATED = 0x01
 FLAG_KSEG = 0x02
 
+# Tensor roles (model/layout.py:99-121).
+(ROLE_TOK_EMB, ROLE_OUT_NORM, ROLE_LM_HEAD, ROLE_ATTN_NORM, ROLE_ATTN_Q, ROLE_ATTN_K, ROLE_ATTN_V, ROLE_ATTN_OUT,
+ ROLE_ATTN_Q_NORM, ROLE_ATTN_K_NORM, ROLE_FFN_NORM, ROLE_FFN_GATE, ROLE_FFN_UP, ROLE_FFN_DOWN, ROLE_ROPE_TAB,
+ ROLE_TOK_EMB16, ROLE_TOK_EMB16_EXP) = range(17)
+(ROLE_ATTN_QKV, ROLE_ATTN_ZGATE, ROLE_SSM_OUT, ROLE_SSM_BETA, ROLE_SSM_ALPHA, ROLE_SSM_CONV, ROLE_SSM_A, ROLE_SSM_DT,
+ ROLE_SSM_NORM, ROLE_HADAMARD) = range(17, 27)
+
+
+def hadamard_layer(width_index, block_index):
+    """The entry `layer` of a rotation block tensor: width index * 256 + block (model/layout.py:124-128)."""
+    return width_index * 256 + block_index
+
 # Header (little-endian), model/layout.py:242-257: the fixed fields at 0..111 ...
 _HEADER = struct.Struct("<IIIIIIIIIIfIIIIIQII32s")
 _HEADER_KEYS = ("magic", "version", "n_layer", "n_embd", "n_head", "n_kv_head", "head_dim", "ffn_dim",
@@ -120,6 +132,46 @@ class BONSImage:
         if b.size < rows * rb:
             raise ValueError(f"{e['name']}: {b.size} bytes hold fewer than {rows} rows of {rb}")
         return b[:rows * rb]
+
+    def plain_rows(self, e):
+        """An unscaled tensor (KIND_F32, KIND_NORM16, KIND_F16) as a (rows, cols) numpy array: each
+        row's values from the start of its beat-padded row (model/bons.py:170-200)."""
+        dtype = {L.KIND_F32: np.float32, L.KIND_NORM16: np.int16, L.KIND_F16: np.float16}[e["kind"]]
+        rb = L.plain_row_bytes(e["cols"], e["kind"])
+        b = np.asarray(self.tensor_bytes(e))
+        if b.size < e["rows"] * rb:
+            raise ValueError(f"{e['name']}: {b.size} bytes hold fewer than {e['rows']} rows of {rb}")
+        width = np.dtype(dtype).itemsize * e["cols"]
+        rows = b[:e["rows"] * rb].reshape(e["rows"], rb)[:, :width]
+        return np.ascontiguousarray(rows).view(dtype).reshape(e["rows"], e["cols"])
+
+    def entries_of(self, role, layer=0, kind=None):
+        """The entries of (role, layer), optionally of one kind, in table order."""
+        return [e for e in self.entries if e["role"] == role and e["layer"] == layer and
+                (kind is None or e["kind"] == kind)]
+
+    def matvec_entries(self, role, layer=0):
+        """The matvec tensor of (role, layer) as its K-segments in order (FLAG_KSEG, the entries'
+        kseg field; model/mirror.py:635-643), or the one entry of an unsegmented tensor."""
+        es = [e for e in self.entries_of(role, layer)
+              if e["kind"] in L.TERNARY_KINDS or e["kind"] == L.KIND_Q8]
+        if not es:
+            raise KeyError((role, layer))
+        if es[0]["flags"] & FLAG_KSEG:
+            return sorted([e for e in es if e["flags"] & FLAG_KSEG], key=lambda e: e["kseg"])
+        return es[:1]
+
+    def embedding_bfp16(self):
+        """The int16 embedding table (ROLE_TOK_EMB16, [vocab][dim] mantissas) and its per-row
+        exponents (ROLE_TOK_EMB16_EXP, 16 per beat): row t is mant[t] * 2^exp[t]
+        (model/mirror.py:777-783).  None when the image has no table."""
+        m = self.entries_of(ROLE_TOK_EMB16, 0, L.KIND_NORM16)
+        x = self.entries_of(ROLE_TOK_EMB16_EXP, 0, L.KIND_NORM16)
+        if not m or not x:
+            return None
+        mant = self.plain_rows(m[0])
+        exps = self.plain_rows(x[0]).reshape(-1)[:mant.shape[0]].astype(np.int32)
+        return mant, exps
 
     def device_tensor(self, e, device=None):
         """The tensor on the device as an ops.DeviceTensor carrying the entry's B and R."""

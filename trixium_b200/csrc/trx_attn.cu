@@ -71,6 +71,9 @@ __device__ __forceinline__ void cp16_attn(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
+// CT: the cache element type, __half (the build's fp16 KV cache) or float (the fp32 cache of the
+// reference mirror, model/mirror.py:966, for parity runs).
+template <typename CT>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, uint32_t *err) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -83,9 +86,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
         if (tid == 0 && s == 0 && kh == 0) atomicOr(err, TRX_DEV_RANGE);
         return;
     }
-    const int rowh = hd + 8;  // halves per staged row (16 bytes of padding: conflict-free rows)
-    __half *kt = reinterpret_cast<__half *>(smem);
-    __half *vt = kt + chunk * rowh;
+    constexpr int EPP = 16 / (int)sizeof(CT);  // cache elements per 16-byte piece
+    const int rowh = hd + EPP;  // elements per staged row (16 bytes of padding: conflict-free rows)
+    CT *kt = reinterpret_cast<CT *>(smem);
+    CT *vt = kt + chunk * rowh;
     float *qs = reinterpret_cast<float *>(vt + chunk * rowh);  // [rep][hd]
     float *knew = qs + rep * hd;                                // [hd]
     float *sc = knew + hd;                                      // [rep][chunk]
@@ -95,7 +99,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
 
     const int t0 = s * chunk;
     const int n = min(chunk, pos + 1 - t0);  // positions of this chunk in use (<= 0: none)
-    const int stride_t = A.Hkv * hd;         // halves between positions in the cache
+    const int stride_t = A.Hkv * hd;         // elements between positions in the cache
+    CT *const kcache = reinterpret_cast<CT *>(A.kc);
+    CT *const vcache = reinterpret_cast<CT *>(A.vc);
     float *part = A.part + (size_t)(kh * A.nsplit + s) * rep * (hd + 2);
     if (n > 0) {
         // Query heads of this group: RMSNorm + RoPE, one warp per head.
@@ -107,29 +113,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
             head_rmsnorm(v, hd, A.qn, A.eps, lane);
             head_rope(v, A.rope_half, A.freq, pos, lane);
         }
-        // The new key and value: into the cache (fp16), by the CTA whose chunk holds pos.
+        // The new key and value: into the cache, by the CTA whose chunk holds pos.
         if (pos >= t0 && pos < t0 + chunk && warp == kAttnWarps - 1) {
             const float *kg = A.k + (size_t)kh * hd;
             for (int i = lane; i < hd; i += 32) knew[i] = __ldg(kg + i);
             __syncwarp();
             head_rmsnorm(knew, hd, A.kn, A.eps, lane);
             head_rope(knew, A.rope_half, A.freq, pos, lane);
-            __half *kc = A.kc + (size_t)pos * stride_t + (size_t)kh * hd;
-            __half *vc = A.vc + (size_t)pos * stride_t + (size_t)kh * hd;
+            CT *kc = kcache + (size_t)pos * stride_t + (size_t)kh * hd;
+            CT *vc = vcache + (size_t)pos * stride_t + (size_t)kh * hd;
             const float *vg = A.v + (size_t)kh * hd;
             for (int i = lane; i < hd; i += 32) {
-                kc[i] = __float2half_rn(knew[i]);
-                vc[i] = __float2half_rn(__ldg(vg + i));
+                if constexpr (sizeof(CT) == 2) {
+                    kc[i] = __float2half_rn(knew[i]);
+                    vc[i] = __float2half_rn(__ldg(vg + i));
+                } else {
+                    kc[i] = knew[i];
+                    vc[i] = __ldg(vg + i);
+                }
             }
         }
         __syncthreads();  // queries ready; the new cache row is visible to this CTA's copies
         // Stage K and V rows [t0, t0 + n).
-        const int pieces = hd / 8;  // 16-byte pieces per row
+        const int pieces = hd / EPP;  // 16-byte pieces per row
         for (int i = tid; i < n * pieces; i += kAttnThreads) {
             const int t = i / pieces, j = i - t * pieces;
-            const size_t g = (size_t)(t0 + t) * stride_t + (size_t)kh * hd + 8 * j;
-            cp16_attn(kt + t * rowh + 8 * j, A.kc + g);
-            cp16_attn(vt + t * rowh + 8 * j, A.vc + g);
+            const size_t g = (size_t)(t0 + t) * stride_t + (size_t)kh * hd + EPP * j;
+            cp16_attn(kt + t * rowh + EPP * j, kcache + g);
+            cp16_attn(vt + t * rowh + EPP * j, vcache + g);
         }
         asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
         __syncthreads();
@@ -137,21 +148,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
         for (int i = tid; i < rep * n; i += kAttnThreads) {
             const int r = i / n, t = i - r * n;
             const float *qv = qs + r * hd;
-            const uint4 *kr = reinterpret_cast<const uint4 *>(kt + t * rowh);
             float acc = 0.f;
             const float4 *q4 = reinterpret_cast<const float4 *>(qv);
-            for (int j = 0; j < pieces; ++j) {
-                const uint4 w = kr[j];
-                const float4 qa = q4[2 * j], qb = q4[2 * j + 1];
-                const float2 f0 = h2_to_f2(w.x), f1 = h2_to_f2(w.y), f2 = h2_to_f2(w.z), f3 = h2_to_f2(w.w);
-                acc = fmaf(qa.x, f0.x, acc);
-                acc = fmaf(qa.y, f0.y, acc);
-                acc = fmaf(qa.z, f1.x, acc);
-                acc = fmaf(qa.w, f1.y, acc);
-                acc = fmaf(qb.x, f2.x, acc);
-                acc = fmaf(qb.y, f2.y, acc);
-                acc = fmaf(qb.z, f3.x, acc);
-                acc = fmaf(qb.w, f3.y, acc);
+            if constexpr (sizeof(CT) == 2) {
+                const uint4 *kr = reinterpret_cast<const uint4 *>(kt + t * rowh);
+                for (int j = 0; j < pieces; ++j) {
+                    const uint4 w = kr[j];
+                    const float4 qa = q4[2 * j], qb = q4[2 * j + 1];
+                    const float2 f0 = h2_to_f2(w.x), f1 = h2_to_f2(w.y), f2 = h2_to_f2(w.z), f3 = h2_to_f2(w.w);
+                    acc = fmaf(qa.x, f0.x, acc);
+                    acc = fmaf(qa.y, f0.y, acc);
+                    acc = fmaf(qa.z, f1.x, acc);
+                    acc = fmaf(qa.w, f1.y, acc);
+                    acc = fmaf(qb.x, f2.x, acc);
+                    acc = fmaf(qb.y, f2.y, acc);
+                    acc = fmaf(qb.z, f3.x, acc);
+                    acc = fmaf(qb.w, f3.y, acc);
+                }
+            } else {
+                const float4 *kr = reinterpret_cast<const float4 *>(kt + t * rowh);
+                for (int j = 0; j < pieces; ++j) {
+                    const float4 w = kr[j], qa = q4[j];
+                    acc = fmaf(qa.x, w.x, acc);
+                    acc = fmaf(qa.y, w.y, acc);
+                    acc = fmaf(qa.z, w.z, acc);
+                    acc = fmaf(qa.w, w.w, acc);
+                }
             }
             sc[r * chunk + t] = __fmul_rn(acc, A.scale);
         }
@@ -181,7 +203,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
             const float *e = sc + r * chunk;
             float ax = 0.f, ay = 0.f;
             for (int t = 0; t < n; ++t) {
-                const float2 f = __half22float2(reinterpret_cast<const __half2 *>(vt + t * rowh)[dp]);
+                float2 f;
+                if constexpr (sizeof(CT) == 2)
+                    f = __half22float2(reinterpret_cast<const __half2 *>(vt + t * rowh)[dp]);
+                else
+                    f = reinterpret_cast<const float2 *>(vt + t * rowh)[dp];
                 ax = fmaf(e[t], f.x, ax);
                 ay = fmaf(e[t], f.y, ay);
             }
@@ -1009,16 +1035,18 @@ bool cl_plan(const AttnArgs &A, int &chunk, int &nsplit, size_t &smem, int &merg
 }  // namespace
 
 // Positions per CTA: the smallest of 64, 128, 256 that keeps the splits per kv head at 16 or fewer
-// (fewer partials to merge), capped so two staged tiles fit in shared memory.
-int attn_chunk(int max_pos, int hd) {
-    const int cap = hd <= 128 ? 256 : 128;
+// (fewer partials to merge), capped so two staged tiles of esize-byte cache elements fit in shared
+// memory.
+int attn_chunk(int max_pos, int hd, int esize) {
+    const int cap = (hd <= 128 ? 256 : 128) / (esize / 2);
     int chunk = 64;
     while (chunk < cap && (max_pos + chunk - 1) / chunk > 16) chunk *= 2;
     return chunk;
 }
 
-size_t attn_smem_bytes(int hd, int rep, int chunk) {
-    return (size_t)2 * chunk * (hd + 8) * 2 + ((size_t)rep * hd + hd + (size_t)rep * chunk + 2 * rep) * 4;
+size_t attn_smem_bytes(int hd, int rep, int chunk, int esize) {
+    return (size_t)2 * chunk * (hd + 16 / esize) * esize +
+           ((size_t)rep * hd + hd + (size_t)rep * chunk + 2 * rep) * 4;
 }
 
 trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st) {
@@ -1044,13 +1072,25 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
         }
     }
     const AttnArgs &A = A0;
-    const size_t smem = attn_smem_bytes(A.hd, A.H / A.Hkv, A.chunk);
+    const size_t smem = attn_smem_bytes(A.hd, A.H / A.Hkv, A.chunk, A.f32cache ? 4 : 2);
+    if (A.f32cache) {
+        static DevBits configured{0};
+        const cudaError_t e = once_per_device(configured, [] {
+            return cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        226 * 1024);
+        });
+        if (e != cudaSuccess) return note_cuda(e);
+        return note_cuda(
+            launch_kernel(attn_decode_kernel<float>, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
+    }
     static DevBits configured{0};
     const cudaError_t e = once_per_device(configured, [] {
-        return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
+        return cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    226 * 1024);
     });
     if (e != cudaSuccess) return note_cuda(e);
-    return note_cuda(launch_kernel(attn_decode_kernel, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
+    return note_cuda(
+        launch_kernel(attn_decode_kernel<__half>, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
 }
 
 }  // namespace trx
@@ -1116,7 +1156,7 @@ extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const flo
     A.gated = sh->gated ? 1 : 0;
     A.qstride = (int)hd * (A.gated ? 2 : 1);
     A.max_pos = (int)sh->max_pos;
-    A.chunk = trx::attn_chunk((int)sh->max_pos, (int)hd);
+    A.chunk = trx::attn_chunk((int)sh->max_pos, (int)hd, 2);
     A.nsplit = (A.max_pos + A.chunk - 1) / A.chunk;
     A.eps = sh->eps;
     A.scale = 1.0f / sqrtf((float)hd);
@@ -1124,7 +1164,7 @@ extern "C" trx_status trx_attn_decode_static(const trx_attn_shape *sh, const flo
     // The fixed limits of the static scratch: n_kv <= 64 and the partials within 4 MiB.
     if (Hkv > trx::kStaticMaxKv || (uint64_t)Hkv * A.nsplit * rep * (hd + 2) > trx::kStaticPartFloats)
         return TRX_ERR_UNSUPPORTED;
-    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u ||
+    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk, 2) > 226u * 1024u ||
         2ull * rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))
         return TRX_ERR_UNSUPPORTED;
     trx::StaticScratch sc{};

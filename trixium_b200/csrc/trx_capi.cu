@@ -17,14 +17,18 @@ struct trx_ctx {
     // Greedy-argmax keys (one per job) and the matvec's arrival count (zero between launches).
     unsigned long long *amax_key;
     unsigned *amax_cnt;
-    // The quantised activation of trx_matvec_q8_f: 32 KiB of x8, then its exponent e8.
+    // The quantised activation of trx_matvec_q8_f and trx_matvec_f_kseg: 32 KiB of x8, then its
+    // exponent e8.
     int8_t *q8x;
+    // trx_matvec_f_kseg: the segments' int32 engine results, [nseg][rows].
+    int32_t *kseg_part;
 };
 
 static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
 static const uint32_t kAttnMaxKv = 1024;
 static const int kMaxArgmaxJobs = 64;
 static const uint32_t kQ8MaxCols = 32768;
+static const uint64_t kKsegPartInts = 1ull << 20;  // 4 MiB of K-segment partial results
 
 namespace trx {
 bool pdl_enabled() { return true; }
@@ -86,6 +90,7 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaMemset(c->amax_key, 0, kMaxArgmaxJobs * 8) != cudaSuccess ||
         cudaMalloc(&c->amax_cnt, 16) != cudaSuccess || cudaMemset(c->amax_cnt, 0, 16) != cudaSuccess ||
         cudaMalloc(&c->q8x, kQ8MaxCols + 16) != cudaSuccess ||
+        cudaMalloc(&c->kseg_part, kKsegPartInts * 4) != cudaSuccess ||
         trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
@@ -95,6 +100,7 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaFree(c->amax_key);
         cudaFree(c->amax_cnt);
         cudaFree(c->q8x);
+        cudaFree(c->kseg_part);
         delete c;
         return TRX_ERR_CUDA;
     }
@@ -111,6 +117,7 @@ trx_status trx_destroy(trx_ctx *ctx) {
     cudaFree(ctx->amax_key);
     cudaFree(ctx->amax_cnt);
     cudaFree(ctx->q8x);
+    cudaFree(ctx->kseg_part);
     delete ctx;
     return TRX_OK;
 }
@@ -374,6 +381,57 @@ trx_status trx_embed_lookup(trx_ctx *ctx, const void *d_table, uint32_t vocab, u
     return trx::launch_embed(d_table, (int)vocab, (int)dim, f16 ? 1 : 0, d_token, d_x, ctx->err, stream);
 }
 
+trx_status trx_embed_lookup_bfp16(trx_ctx *ctx, const int16_t *d_mant, const int32_t *d_exp, uint32_t vocab,
+                                  uint32_t dim, const int32_t *d_token, float *d_x, cudaStream_t stream) {
+    if (!ctx || !d_mant || !d_exp || !d_token || !d_x || vocab == 0 || dim == 0) return TRX_ERR_ARG;
+    return trx::launch_embed_bfp16(d_mant, d_exp, (int)vocab, (int)dim, d_token, d_x, ctx->err, stream);
+}
+
+trx_status trx_rmsnorm(trx_ctx *ctx, const float *d_x, const float *d_w, uint32_t n, float eps, float *d_y,
+                       cudaStream_t stream) {
+    if (!ctx || !d_x || !d_w || !d_y || n == 0 || n > (1u << 24) || !(eps >= 0.f)) return TRX_ERR_ARG;
+    return trx::launch_rmsnorm(d_x, d_w, (int)n, eps, d_y, stream);
+}
+
+trx_status trx_matvec_f_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
+                             const float *d_x, const float *d_resid, float *d_y, cudaStream_t stream) {
+    if (!ctx || !segs || !d_packed || !d_x || !d_y || nseg < 1 || nseg > 64) return TRX_ERR_ARG;
+    const uint32_t rows = segs[0].rows;
+    uint64_t K = 0;
+    for (int i = 0; i < nseg; ++i) {
+        const trx_entry *e = segs + i;
+        const trx_status s = e->kind == TRX_KIND_Q8 ? check_q8(ctx, e, d_packed[i]) : check_entry(e);
+        if (s) return s;
+        if (!d_packed[i] || !aligned16(d_packed[i])) return TRX_ERR_ARG;
+        if (e->rows != rows || e->bias != segs[0].bias || e->rshift != segs[0].rshift) return TRX_ERR_ARG;
+        K += e->cols;
+    }
+    if (K > kQ8MaxCols) return TRX_ERR_UNSUPPORTED;
+    if ((uint64_t)nseg * rows > kKsegPartInts) return TRX_ERR_UNSUPPORTED;
+    int *e8 = reinterpret_cast<int *>(ctx->q8x + kQ8MaxCols);
+    trx_status s = trx::launch_quantize(d_x, (int)K, ctx->q8x, e8, stream);
+    if (s) return s;
+    uint64_t c0 = 0;
+    for (int i = 0; i < nseg; ++i) {
+        const trx_entry *e = segs + i;
+        int32_t *part = ctx->kseg_part + (size_t)i * rows;
+        if (e->kind == TRX_KIND_Q8) {
+            s = trx::launch_matvec_q8(static_cast<const uint8_t *>(d_packed[i]), (int)rows, (int)e->cols, e->bias,
+                                      e->rshift, ctx->q8x + c0, nullptr, part, ctx->err, stream);
+        } else {
+            trx::MvJobs J = base_jobs(ctx, e, d_packed[i]);
+            J.x8 = ctx->q8x + c0;
+            J.seg[0].y = part;
+            J.out = trx::OUT_I32;
+            s = trx::launch_matvec(J, ctx->lut, ctx->err, stream);
+        }
+        if (s) return s;
+        c0 += e->cols;
+    }
+    return trx::launch_kseg_combine(ctx->kseg_part, nseg, (int)rows, e8, segs[0].rshift, segs[0].bias, d_resid, d_y,
+                                    stream);
+}
+
 trx_status trx_advance_position(trx_ctx *ctx, int32_t *d_pos, int32_t n, cudaStream_t stream) {
     if (!ctx || !d_pos) return TRX_ERR_ARG;
     return trx::launch_advance(d_pos, n, stream);
@@ -449,10 +507,11 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *sh, const float *
                               d_out, nullptr, stream);
 }
 
-trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
-                              const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
-                              const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
-                              float *d_out, const trx_tp_xfer *tp, cudaStream_t stream) {
+// One decode-attention launch's arguments from the C ABI's (esize: bytes per cache element).
+static trx_status attn_args(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
+                            const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                            const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                            float *d_out, int esize, trx::AttnArgs &A) {
     if (!ctx || !sh) return TRX_ERR_ARG;
     const uint32_t H = sh->n_head, Hkv = sh->n_kv, hd = sh->head_dim;
     if (H == 0 || Hkv == 0 || H % Hkv || Hkv > kAttnMaxKv || hd == 0 || hd % 8 || hd > 512) return TRX_ERR_ARG;
@@ -461,7 +520,7 @@ trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const floa
     if (!d_q || !d_k || !d_v || !d_qnorm_w || !d_knorm_w || !d_kcache || !d_vcache || !d_pos || !d_out)
         return TRX_ERR_ARG;
     if ((sh->rope_dims && !d_rope_freq) || !aligned16(d_kcache) || !aligned16(d_vcache)) return TRX_ERR_ARG;
-    trx::AttnArgs A{};
+    A = trx::AttnArgs{};
     A.H = (int)H;
     A.Hkv = (int)Hkv;
     A.hd = (int)hd;
@@ -469,14 +528,15 @@ trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const floa
     A.gated = sh->gated ? 1 : 0;
     A.qstride = (int)hd * (A.gated ? 2 : 1);
     A.max_pos = (int)sh->max_pos;
-    A.chunk = trx::attn_chunk(A.max_pos, A.hd);
+    A.chunk = trx::attn_chunk(A.max_pos, A.hd, esize);
     A.nsplit = (A.max_pos + A.chunk - 1) / A.chunk;
     A.eps = sh->eps;
     A.scale = 1.0f / sqrtf((float)hd);
     const uint32_t rep = H / Hkv;
     if ((uint64_t)Hkv * A.nsplit * rep * (hd + 2) > kAttnPartFloats) return TRX_ERR_UNSUPPORTED;
-    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk) > 226u * 1024u ||
-        2ull * rep * A.nsplit > (uint64_t)A.chunk * (hd + 8))  // the merge stages 2 floats per partial
+    // The merge stages 2 floats per partial in the tiles' shared memory.
+    if (trx::attn_smem_bytes((int)hd, (int)rep, A.chunk, esize) > 226u * 1024u ||
+        2ull * rep * A.nsplit * 4 > 2ull * A.chunk * (hd + 16 / esize) * esize)
         return TRX_ERR_UNSUPPORTED;
     A.q = d_q;
     A.k = d_k;
@@ -490,7 +550,31 @@ trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const floa
     A.out = d_out;
     A.part = ctx->attn_part;
     A.cnt = ctx->attn_cnt;
+    A.f32cache = esize == 4 ? 1 : 0;
+    return TRX_OK;
+}
+
+trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
+                              const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                              const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                              float *d_out, const trx_tp_xfer *tp, cudaStream_t stream) {
+    trx::AttnArgs A;
+    if (trx_status s = attn_args(ctx, sh, d_q, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope_freq, d_kcache, d_vcache, d_pos,
+                                 d_out, 2, A))
+        return s;
     if (trx_status s = tp_resolve(tp, TP_PUSH | TP_SIGNAL, A.tp)) return s;
+    return trx::launch_attn_decode(A, ctx->err, stream);
+}
+
+trx_status trx_attn_decode_f32cache(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
+                                    const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                                    const float *d_rope_freq, float *d_kcache, float *d_vcache, const int32_t *d_pos,
+                                    float *d_out, cudaStream_t stream) {
+    trx::AttnArgs A;
+    if (trx_status s = attn_args(ctx, sh, d_q, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope_freq, d_kcache, d_vcache, d_pos,
+                                 d_out, 4, A))
+        return s;
+    A.scratch_merge = 1;  // the scratch-merge kernel is the one with an fp32-cache form
     return trx::launch_attn_decode(A, ctx->err, stream);
 }
 

@@ -54,6 +54,53 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Shared-window address forms of the above (barrier given by its shared address).
+__device__ __forceinline__ void mbar_init_s(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx_s(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// 3-D tiled TMA load (no multicast): the box of `map` at element coordinates (x, y, z) into shared
+// address dst, completing its bytes on barrier `bar`.  x * element size must be a multiple of 16.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *map, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_map(const void *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_s(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait by shared address: false (timeout bit set by lane 0 of the caller) if the phase did
+// not complete within kWaitNs.
+__device__ __forceinline__ bool mbar_wait_bounded_s(uint32_t bar, uint32_t parity, uint32_t *err) {
+    if (mbar_try_wait_s(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait_s(bar, parity)) {
+        if (global_ns() - t0 > kWaitNs) {
+            if (err && (threadIdx.x & 31) == 0) atomicOr(err, TRX_DEV_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

@@ -125,6 +125,7 @@ struct AttnArgs {
     int H, Hkv, hd, rope_half, qstride, gated, max_pos, chunk, nsplit;
     int merge_own;      // cluster kernel: the merge area has its own shared region
     int scratch_merge;  // run the scratch-merge kernel on part/cnt even where a cluster kernel applies
+    int f32cache;       // kc/vc hold fp32 elements (the scratch-merge kernel only)
     TpXfer tp;          // tensor-parallel exchange of the output (tp.world == 0: none)
     float eps, scale;
 };
@@ -145,12 +146,17 @@ struct DnArgs {
 };
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
-size_t attn_smem_bytes(int hd, int rep, int chunk);
-int attn_chunk(int max_pos, int hd);
+size_t attn_smem_bytes(int hd, int rep, int chunk, int esize);
+int attn_chunk(int max_pos, int hd, int esize);
 
 trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
                         cudaStream_t st);
 trx_status launch_advance(int *pos, int n, cudaStream_t st);
+trx_status launch_embed_bfp16(const int16_t *mant, const int *exps, int vocab, int dim, const int *token, float *x,
+                              uint32_t *err, cudaStream_t st);
+trx_status launch_rmsnorm(const float *x, const float *w, int n, float eps, float *y, cudaStream_t st);
+trx_status launch_kseg_combine(const int *parts, int nseg, int rows, const int *e8, int R, int B, const float *resid,
+                               float *y, cudaStream_t st);
 trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, const TpXfer &tp, uint32_t *err,
                               cudaStream_t st);
 

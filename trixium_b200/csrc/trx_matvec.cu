@@ -35,8 +35,11 @@
 //    16-bit activation pairs, d4 = (d3+3d4)/3 computed for four bytes at once.
 //  * 2-bit decode: four masks per word; dp4a on (code << 2p) bytes into four accumulators.
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "trx_common.cuh"
@@ -48,15 +51,27 @@ namespace trx {
 #ifndef TRX_MV_MAX_WARPS
 #define TRX_MV_MAX_WARPS 16
 #endif
+// Rows per lane of a full-size trit5 / 2-bit launch (a launch whose CTAs share row blocks between
+// warps, or a SwiGLU pair, always takes one).  Measured on B200 (config-0 batch): two rows per lane
+// (the activation words loaded once for both) ran slower for both kinds than one row per lane with
+// more warps (trit5 2.2 against 3.1-3.2 TB/s; 2-bit 4.3 against 4.7 TB/s), so one is the default.
+#ifndef TRX_MV_R_T5
+#define TRX_MV_R_T5 1
+#endif
+#ifndef TRX_MV_R_2B
+#define TRX_MV_R_2B 1
+#endif
 constexpr int kMaxWarps = TRX_MV_MAX_WARPS;
-constexpr int kMvThreads = 16 * 32;               // launch bound (a launch may use fewer warps)
+constexpr int kMvThreads = kMaxWarps * 32;       // launch bound (a launch may use fewer warps)
 constexpr int kLutWords = 256 * 64;              // 256 entries x 256-byte stride (32 replicas used)
 constexpr int kLutBytes = kLutWords * 4;         // 64 KiB
 constexpr int kXwT5 = 44;    // words per group: 26 dp4a words, 14 dp2a words, sum(x), 3 zero
 constexpr int kXw2b = 36;    // words per group: 32 dp4a words, sum(x), 3 zero
 constexpr int kCG = 4;                           // groups per chunk
-constexpr int kRowStride = 144;                  // ring bytes per row of a block
-constexpr int kBlkBytes = 32 * kRowStride;       // one tensor's block (32 rows x one chunk)
+constexpr int kCbT5 = 112;   // trit5 codes box per row: the chunk's 104 bytes from the 16-byte boundary at or below them
+constexpr int kCb2b = 144;   // 2-bit codes box per row: the chunk's 128 bytes and the next 16 (an odd 16-byte stride)
+constexpr int kScBox = 16;   // scales box per row: the 8 fp16 scales of chunks 2j, 2j+1
+constexpr int kMaxD = 3;     // ring slots per warp at most
 constexpr int kSmemMax = 227 * 1024;
 
 // Geometry of one launch, derived on the host (plan_matvec) and passed by value.
@@ -65,6 +80,7 @@ struct MvGeom {
     int nch;      // chunks per row (the last may hold fewer than kCG groups)
     int cpt;      // chunks per warp per row block
     int S;        // warps sharing a row block (a power of two; 1: a warp owns whole row blocks)
+    int R;        // rows per lane (a row block is 32 R rows)
     int nrb;      // row blocks per job
     int grid;     // CTAs
     int rb;       // row packet bytes in global memory
@@ -73,31 +89,30 @@ struct MvGeom {
     int warps;    // warps per CTA
     int D;        // ring depth (blocks)
     int xw;       // activation words per group
-    int fixed;    // bytes of activation words and reductions (128-byte rounded): rings A start here
+    int cb;       // codes box bytes per row (kCbT5 or kCb2b)
+    int cbytes;   // codes bytes of one tensor in a slot (32 R rows x cb)
+    int slot;     // bytes of one ring slot: NW codes boxes, then NW scales boxes
+    int wjob;     // the tensor maps have a job dimension (jobs read distinct weights)
+    int fixed;    // bytes of activation words, reductions and barriers (128-byte rounded): rings A start here
+    int red_off;  // shared offset of the combine area of warps sharing a row block
+    int bar_off;  // shared offset of the ring barriers ([kMaxWarps][kMaxD] uint64)
     int na;       // warps whose ring lies in region A (the rest: region C, after the trit5 LUT)
     int sreg;     // the staging area lies in region C (1) or A (0)
     int stage_off;  // its shared offset: the last bands (slot D-1, D-2, ...) of that region
     int ebl;      // slots of a staging-region warp below the staging area
-    int xfast;    // float x takes the cp.async-staged prologue (build_activation_cp)
+    int xfast;    // float x takes the bulk-copy-staged prologue (build_activation_cp)
     int stage;    // bytes of that staging region
     int base;     // shared-window address of the dynamic shared memory the plan assumes
     int smem;     // dynamic shared bytes
 };
 
-// cp.async (16-byte, L2 only) -----------------------------------------------------------------------
-// Predicated 16-byte copy to shared address dst + OFF.
-template <int OFF>
-__device__ __forceinline__ void cp16p(uint32_t dst, const void *src, bool p) {
-    asm volatile(
-        "{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q cp.async.cg.shared.global [%0+%3], [%1], 16;\n}" ::"r"(dst),
-        "l"(src), "r"((int)p), "n"(OFF)
-        : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+// TMA tensor maps of one launch: per tensor (NW), the codes box {cb bytes, 32 R rows, 1 job} and
+// the scales box {16 bytes, 32 R rows, 1 job} over the packed tensor viewed as [jobs][rows][row
+// packet bytes].  Boxes past the tensor's rows or a row's end are zero-filled by the copy engine.
+struct MvMaps {
+    CUtensorMap codes[2];
+    CUtensorMap scales[2];
+};
 
 // Quantisation helpers ----------------------------------------------------------------------------
 // The value the quantiser sees at position k: x[k], or the RMS-normalised x[k]*r*w[k].
@@ -459,19 +474,23 @@ __device__ int build_activation_cp(const float *x, const float *nw, bool nw_read
 }
 
 // Group sums -----------------------------------------------------------------------------------------
-// trit5, group g of a chunk whose 104 code bytes start at byte H (0 or 8) of the 28-word window
-// cw.  xg: the group's 44 activation words.  Returns sum((digit - 1) * x).
-template <int H, int g>
-__device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], uint32_t lane4x, const uint32_t *xg) {
-    uint32_t xa[kXwT5];
+// The activation words of one group, loaded once per group and shared by the R rows of a lane.
+template <int N>
+__device__ __forceinline__ void load_xwords(const uint32_t *xg, uint32_t (&xa)[N]) {
 #pragma unroll
-    for (int i = 0; i < kXwT5 / 4; ++i) {
+    for (int i = 0; i < N / 4; ++i) {
         const uint4 v = reinterpret_cast<const uint4 *>(xg)[i];
         xa[4 * i] = v.x;
         xa[4 * i + 1] = v.y;
         xa[4 * i + 2] = v.z;
         xa[4 * i + 3] = v.w;
     }
+}
+
+// trit5, group g of a chunk whose 104 code bytes start at byte H (0 or 8) of the 28-word window
+// cw.  xa: the group's 44 activation words.  Returns sum((digit - 1) * x).
+template <int H, int g>
+__device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], uint32_t lane4x, const uint32_t (&xa)[kXwT5]) {
     int acc[4] = {0, 0, 0, 0};  // independent chains (byte position within a quad)
 #pragma unroll
     for (int q = 0; q < 7; ++q) {
@@ -503,18 +522,9 @@ __device__ __forceinline__ int gsum_t5(const uint32_t (&cw)[28], uint32_t lane4x
     return (acc[0] + acc[1]) + (acc[2] + acc[3]) - (int)xa[40];
 }
 
-// 2-bit, group g of a chunk: the 32 code bytes at cp (shared, 16-byte aligned).  Returns
-// sum((code - 1) * x).
-__device__ __forceinline__ int gsum_2b(const uint4 *cp, const uint32_t *xg) {
-    uint32_t xw[kXw2b];
-#pragma unroll
-    for (int i = 0; i < kXw2b / 4; ++i) {
-        const uint4 v = reinterpret_cast<const uint4 *>(xg)[i];
-        xw[4 * i] = v.x;
-        xw[4 * i + 1] = v.y;
-        xw[4 * i + 2] = v.z;
-        xw[4 * i + 3] = v.w;
-    }
+// 2-bit, one group: the 32 code bytes at cp (shared, 16-byte aligned), xw its 36 activation words.
+// Returns sum((code - 1) * x).
+__device__ __forceinline__ int gsum_2b(const uint4 *cp, const uint32_t (&xw)[kXw2b]) {
     const uint4 c0 = cp[0], c1 = cp[1];
     const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
@@ -534,24 +544,67 @@ __device__ __forceinline__ uint32_t scale_bits(uint2 s, int g) {
     return g & 1 ? w >> 16 : w & 0xffffu;
 }
 
-// The int64 sum of one chunk (ng <= 4 groups) of this lane's row.
-template <int H>
-__device__ __forceinline__ long long chunk_t5(const uint32_t (&cw)[28], uint2 sc, int ng, const uint32_t *xg,
-                                              uint32_t lane4x, int B, const ScaleFast &F) {
-    long long a = contrib(gsum_t5<H, 0>(cw, lane4x, xg), scale_bits(sc, 0), B, F);
-    if (ng > 1) a += contrib(gsum_t5<H, 1>(cw, lane4x, xg + kXwT5), scale_bits(sc, 1), B, F);
-    if (ng > 2) a += contrib(gsum_t5<H, 2>(cw, lane4x, xg + 2 * kXwT5), scale_bits(sc, 2), B, F);
-    if (ng > 3) a += contrib(gsum_t5<H, 3>(cw, lane4x, xg + 3 * kXwT5), scale_bits(sc, 3), B, F);
-    return a;
-}
-
-__device__ __forceinline__ long long chunk_2b(const uint4 *cp, uint2 sc, int ng, const uint32_t *xg, int B,
-                                              const ScaleFast &F) {
-    long long a = contrib(gsum_2b(cp, xg), scale_bits(sc, 0), B, F);
-    if (ng > 1) a += contrib(gsum_2b(cp + 2, xg + kXw2b), scale_bits(sc, 1), B, F);
-    if (ng > 2) a += contrib(gsum_2b(cp + 4, xg + 2 * kXw2b), scale_bits(sc, 2), B, F);
-    if (ng > 3) a += contrib(gsum_2b(cp + 6, xg + 3 * kXw2b), scale_bits(sc, 3), B, F);
-    return a;
+// One chunk c (ng <= 4 groups) of the R rows of this lane held in a ring slot: codes at `codes`
+// (row r of the lane at (lane + 32 r) * cb; trit5: the chunk's bytes from byte H = 8 (c & 1) of
+// the row's window), scales at `scales` (16 bytes per row, this chunk's 4 at byte soff = 8 (c & 1)).
+// Group by group, the activation words are loaded once and used for every row.
+template <int KIND, int R, int H>
+__device__ __forceinline__ void chunk_rows(const unsigned char *codes, const unsigned char *scales, int soff, int lane,
+                                           int ng, const uint32_t *xg, uint32_t lane4x, const int (&Bv)[R],
+                                           const ScaleFast (&Fv)[R], long long (&acc)[R]) {
+    uint2 sc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) sc[r] = *reinterpret_cast<const uint2 *>(scales + (lane + 32 * r) * kScBox + soff);
+    if (KIND == TRX_KIND_TERNARY5) {
+        uint32_t cw[R][28];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const uint4 *rp = reinterpret_cast<const uint4 *>(codes + (lane + 32 * r) * kCbT5);
+#pragma unroll
+            for (int i = 0; i < 7; ++i) {
+                const uint4 v = rp[i];
+                cw[r][4 * i] = v.x;
+                cw[r][4 * i + 1] = v.y;
+                cw[r][4 * i + 2] = v.z;
+                cw[r][4 * i + 3] = v.w;
+            }
+        }
+        uint32_t xa[kXwT5];
+        load_xwords(xg, xa);
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] += contrib(gsum_t5<H, 0>(cw[r], lane4x, xa), scale_bits(sc[r], 0), Bv[r], Fv[r]);
+        if (ng > 1) {
+            load_xwords(xg + kXwT5, xa);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                acc[r] += contrib(gsum_t5<H, 1>(cw[r], lane4x, xa), scale_bits(sc[r], 1), Bv[r], Fv[r]);
+        }
+        if (ng > 2) {
+            load_xwords(xg + 2 * kXwT5, xa);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                acc[r] += contrib(gsum_t5<H, 2>(cw[r], lane4x, xa), scale_bits(sc[r], 2), Bv[r], Fv[r]);
+        }
+        if (ng > 3) {
+            load_xwords(xg + 3 * kXwT5, xa);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                acc[r] += contrib(gsum_t5<H, 3>(cw[r], lane4x, xa), scale_bits(sc[r], 3), Bv[r], Fv[r]);
+        }
+    } else {
+#pragma unroll
+        for (int g = 0; g < kCG; ++g) {
+            if (g < ng) {
+                uint32_t xw[kXw2b];
+                load_xwords(xg + g * kXw2b, xw);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const uint4 *cp = reinterpret_cast<const uint4 *>(codes + (lane + 32 * r) * kCb2b) + 2 * g;
+                    acc[r] += contrib(gsum_2b(cp, xw), scale_bits(sc[r], g), Bv[r], Fv[r]);
+                }
+            }
+        }
+    }
 }
 
 // The float epilogue value of one finished row (the firmware's int32 -> float scaling).
@@ -638,55 +691,7 @@ __device__ __forceinline__ void argmax_commit(const MvJobs &J, int job, unsigned
 }
 
 
-// Issue the copies of block (row block rbk, chunk c) of `job` into ring slot `dst`.  Per row,
-// the 16 scale bytes holding the chunk's scales land at ring bytes [0, 16) and the chunk's codes
-// at [16, ...) (trit5: from the 16-byte boundary at or below their start, so an odd chunk's codes
-// begin at byte 8 of the window).  Lane l copies 16-byte piece l%8 of rows l/8, l/8+4, ...: each
-// copy instruction reads 4 rows x 128 contiguous bytes.
-template <int KIND, int NW>
-__device__ __forceinline__ void issue_block(const MvJobs &J, const MvGeom &M, int job, int rbk, int c, uint32_t dst,
-                                            int lane) {
-    const int r0 = rbk * 32;
-    const int nrows = min(32, J.rows - r0);
-    const int ng = min(kCG, M.G - c * kCG);
-    const int sub = lane >> 3, k = lane & 7;
-    const int soff = 16 * (c >> 1);
-    int off, doff;
-    bool pv;
-    if (KIND == TRX_KIND_TERNARY5) {  // piece 0: scales; pieces 1..7: codes
-        const int head = (c & 1) * 8;
-        const int np = (head + 26 * ng + 15) >> 4;
-        off = k ? M.sbytes + 104 * c - head + 16 * (k - 1) : soff;
-        doff = 16 * k;
-        pv = k <= np;
-    } else {                          // pieces 0..7: codes; scales in a pass of their own
-        off = M.sbytes + 128 * c + 16 * k;
-        doff = 16 + 16 * k;
-        pv = k < 2 * ng;
-    }
-    const int nv = pv ? (nrows - sub + 3) >> 2 : 0;  // copies (of rows sub, sub+4, ...) this lane makes
-    const uint64_t jbase = (uint64_t)job * J.w_stride + (uint64_t)r0 * M.rb;
-    const uint64_t rstep = 4ull * M.rb;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-        const uint8_t *base = (w ? J.w2 : J.w) + jbase;
-        const uint8_t *src = base + (uint64_t)sub * M.rb + off;
-        const uint32_t d = dst + w * kBlkBytes + sub * kRowStride + doff;
-        cp16p<0 * 4 * kRowStride>(d, src, 0 < nv);
-        cp16p<1 * 4 * kRowStride>(d, src + rstep, 1 < nv);
-        cp16p<2 * 4 * kRowStride>(d, src + 2 * rstep, 2 < nv);
-        cp16p<3 * 4 * kRowStride>(d, src + 3 * rstep, 3 < nv);
-        src += 4 * rstep;
-        cp16p<4 * 4 * kRowStride>(d, src, 4 < nv);
-        cp16p<5 * 4 * kRowStride>(d, src + rstep, 5 < nv);
-        cp16p<6 * 4 * kRowStride>(d, src + 2 * rstep, 6 < nv);
-        cp16p<7 * 4 * kRowStride>(d, src + 3 * rstep, 7 < nv);
-        if (KIND != TRX_KIND_TERNARY5)
-            cp16p<0>(dst + w * kBlkBytes + lane * kRowStride, base + (uint64_t)lane * M.rb + soff, lane < nrows);
-    }
-}
-
-// This lane's output context for the row it owns in the current task.
+// This lane's output context for one of the rows it owns in the current task.
 struct LaneRow {
     int row;        // row of the packed tensor (or -1 past the end)
     int srow;       // row within its segment
@@ -714,21 +719,29 @@ __device__ __forceinline__ void lane_row(const MvJobs &J, const MvSeg *segs, int
 }
 
 // The matvec kernel ---------------------------------------------------------------------------------
-// Ring depth: trit5 shares shared memory with its 64 KiB LUT.
-template <int KIND>
-constexpr int ring_depth() { return KIND == TRX_KIND_TERNARY5 ? 2 : 3; }
-
+// Ring depth: trit5 shares shared memory with its 64 KiB LUT, a SwiGLU pair streams two tensors.
+#ifndef TRX_MV_D_T5
+#define TRX_MV_D_T5 2
+#endif
 template <int KIND, int NW>
-__global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_kernel(MvJobs J, MvGeom M, const uint32_t *lut_g, uint32_t *err) {
-    constexpr int D = ring_depth<KIND>();
+constexpr int ring_depth() { return KIND == TRX_KIND_TERNARY5 ? (NW == 2 ? 2 : TRX_MV_D_T5) : (NW == 2 ? 2 : 3); }
+
+// Work decomposition: a row block is 32 R rows (lane l owns rows l, l + 32, ...); a block is one
+// chunk (4 groups) of a row block.  Each warp streams its blocks through a private ring of D slots:
+// one elected lane issues the block's TMA boxes (codes and scales of each tensor) on the slot's
+// mbarrier; the lanes wait on it (bounded), decode, and the slot is refilled with the block D
+// ahead.  No producer warp, no CTA barrier inside a job.
+template <int KIND, int NW, int R>
+__global__ void __launch_bounds__(kMvThreads, 1)
+    tmv_kernel(const __grid_constant__ MvMaps maps, MvJobs J, MvGeom M, uint32_t *err) {
+    constexpr int D = ring_depth<KIND, NW>();
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     pdl_trigger();
 
-    // Carve shared memory (must match plan_matvec): [activation words, reductions][rings A]
+    // Carve shared memory (must match plan_matvec): [activation words, reductions, barriers][rings A]
     // [trit5 LUT at window address 0x10000][rings C]; 2-bit: one ring region, no LUT.
-    constexpr int slot_bytes = NW * kBlkBytes;
     uint32_t *const xp = reinterpret_cast<uint32_t *>(smem);
     unsigned char *p = smem + M.G * M.xw * 4;
     float *const red64 = reinterpret_cast<float *>(p);
@@ -737,6 +750,7 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     uint64_t *const mb = reinterpret_cast<uint64_t *>(p + 16);  // bulk-copy barriers: x, norm weight
     MvSeg *const segs = reinterpret_cast<MvSeg *>(p + 32);      // the segment table
     if (tid < J.nseg) segs[tid] = J.seg[tid];                    // visible after the piece barrier
+    const uint32_t bars = smem_u32(smem + M.bar_off) + (uint32_t)(warp * kMaxD * 8);  // this warp's slot barriers
     // Offsets (not pointers chosen between regions) keep every access provably shared.
     const int lut_off = 0x10000 - M.base, c_off = lut_off + kLutBytes;
     if (KIND == TRX_KIND_TERNARY5 && smem_u32(smem) != (uint32_t)M.base) {
@@ -746,16 +760,16 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     }
     unsigned char *const lut = smem + lut_off;  // trit5 only
     // Rings are slot-major within a region: slot d of the region's k-th warp lies at region +
-    // (d * n + k) * slot_bytes (n warps in the region), so the last slots of a region's warps form
-    // one band, where the prologue stages its inputs.
-    const int sstride = (warp < M.na ? M.na : M.warps - M.na) * slot_bytes;
-    const int ring_off = warp < M.na ? M.fixed + warp * slot_bytes : c_off + (warp - M.na) * slot_bytes;
+    // (d * n + k) * slot (n warps in the region), so the last slots of a region's warps form one
+    // band, where the prologue stages its inputs.
+    const int sstride = (warp < M.na ? M.na : M.warps - M.na) * M.slot;
+    const int ring_off = warp < M.na ? M.fixed + warp * M.slot : c_off + (warp - M.na) * M.slot;
     unsigned char *const ring = smem + ring_off;
     const uint32_t ring_s = smem_u32(ring);
     int8_t *const q8 = reinterpret_cast<int8_t *>(smem + M.stage_off);  // staging; those slots idle then
 
-    // Combine area of warps sharing a row block: [2 parities][warps][32 lanes][NW] int64.
-    long long *const red = reinterpret_cast<long long *>(smem + M.fixed - (M.S > 1 ? 8192 : 0));
+    // Combine area of warps sharing a row block: [2 parities][warps][32 lanes][NW * R] int64.
+    long long *const red = reinterpret_cast<long long *>(smem + M.red_off);
 
     // This CTA's share of the (job, row block) space.
     const long long total = (long long)J.njobs * M.nrb;
@@ -767,7 +781,6 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     }
 
     if (KIND == TRX_KIND_TERNARY5) {  // the trit5 LUT: entry b at b*256, one replica per lane
-        (void)lut_g;
         // The 256 entries once (in lane 0's replica words), then every lane copies them into its
         // own replica: each store instruction writes 32 distinct banks.
         uint32_t *lw = reinterpret_cast<uint32_t *>(lut);
@@ -778,9 +791,9 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     }
     const uint32_t lane4x = 0x10000u | ((uint32_t)lane * 4u);
     const ScaleFast F2 = scale_fast(J.B2);
-    // Warp w: group gi = w / S (row block gi of each round of R = warps/S row blocks), chunks
+    // Warp w: group gi = w / S (row block gi of each round of Rr = warps/S row blocks), chunks
     // [cA, cB) of that row block.
-    const int R = M.warps / M.S;
+    const int Rr = M.warps / M.S;
     const int gi = warp / M.S, sub = warp - gi * M.S;
     const int cA = sub * M.cpt, cB = min(M.nch, cA + M.cpt);
     const int nc = cB > cA ? cB - cA : 0;
@@ -789,26 +802,58 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
                           : nullptr;
 
     // Issue cursor of the current piece: (round, chunk) and blocks issued, of `nitems`.
-    int job = 0, pa = 0, pb = 0, kval = 0, nitems = 0, ik = 0, ic = 0, issued = 0;
+    // The CTA's row blocks go to the warp groups round-robin over its whole range (u = t - t0 is
+    // group u % Rr's), so the groups' totals differ by one at most even when the range spans jobs.
+    int job = 0, pa = 0, pb = 0, gsh = 0, kval = 0, nitems = 0, ik = 0, ic = 0, issued = 0;
+    uint32_t inflight = 0;  // bit d: slot d has copies in flight
     auto piece_begin = [&](long long t) {
         job = (int)(t / M.nrb);
         const long long jb = (long long)job * M.nrb;
         pa = (int)(t - jb);                          // this piece: row blocks [pa, pb) of `job`
         pb = (int)(min(t1, jb + M.nrb) - jb);
-        kval = pb - pa > gi ? (pb - pa - gi + R - 1) / R : 0;  // rounds with a row block for gi
-        nitems = kval * nc;                                     // blocks this warp streams
+        gsh = (int)(((long long)gi - (t - t0) % Rr + Rr) % Rr);  // this group's first row block: pa + gsh
+        kval = pb - pa > gsh ? (pb - pa - gsh + Rr - 1) / Rr : 0;  // rounds with a row block for gi
+        nitems = kval * nc;                                         // blocks this warp streams
         ik = ic = issued = 0;
     };
-    auto issue_next = [&](uint32_t dst) {
+    // Issue the next block of this warp's sequence into slot d: lane 0 arms the slot's barrier
+    // with the slot's bytes (full boxes: the copy engine counts zero-filled bytes too) and issues
+    // the boxes.  The caller has made every lane's reads of the slot complete (__syncwarp).
+    auto issue_next = [&](int d) {
         if (issued < nitems) {
-            issue_block<KIND, NW>(J, M, job, pa + ik * R + gi, cA + ic, dst, lane);
+            if (lane == 0) {
+                const int rbk = pa + gsh + ik * Rr, c = cA + ic;
+                const uint32_t dst = ring_s + (uint32_t)(d * sstride);
+                const uint32_t bar = bars + 8u * d;
+                const int y = rbk * 32 * R, z = M.wjob ? job : 0;
+                const int xc = KIND == TRX_KIND_TERNARY5 ? M.sbytes + 104 * c - 8 * (c & 1) : M.sbytes + 128 * c;
+                const int xsc = 16 * (c >> 1);
+                fence_proxy_async();  // this warp's reads of the slot come before the copy engine's writes
+                mbar_expect_tx_s(bar, (uint32_t)M.slot);
+#pragma unroll
+                for (int w = 0; w < NW; ++w) {
+                    tma_load_3d(dst + w * M.cbytes, &maps.codes[w], xc, y, z, bar);
+                    tma_load_3d(dst + NW * M.cbytes + w * 32 * R * kScBox, &maps.scales[w], xsc, y, z, bar);
+                }
+            }
             if (++ic == nc) {
                 ic = 0;
                 ++ik;
             }
             ++issued;
+            inflight |= 1u << d;
         }
-        cp_commit();
+    };
+    uint32_t phase = 0;  // bit d: the parity of slot d's next completion
+    // Before any early return: wait (bounded) for this warp's copies in flight into its slots.
+    auto drain = [&]() {
+#pragma unroll
+        for (int d = 0; d < D; ++d)
+            if (inflight & (1u << d)) {
+                mbar_wait_bounded_s(bars + 8u * d, (phase >> d) & 1u, err);
+                phase ^= 1u << d;
+            }
+        inflight = 0;
     };
     // The staging area [q8 bytes][x fp32][norm weight fp32] covers the last bands of the staging
     // region; the first piece's blocks for the slots below it (weights: written by no kernel) are
@@ -817,30 +862,41 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
     const int xs_off = M.stage_off + ((J.cols + 15) / 16) * 16;
     float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * J.cols);
     const int ne = (warp < M.na) == (M.sreg == 0) ? min(D - 1, M.ebl) : D - 1;
+    if (lane == 0) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) mbar_init_s(bars + 8u * d, 1);
+    }
     if (tid == 0) {
         mbar_init(mb, 1);
         mbar_init(mb + 1, 1);
-        mbar_fence_init();
-        if (fast && J.norm_w) {  // the norm weight is written by no kernel: requested before the wait
-            mbar_arrive_expect_tx(mb + 1, 4u * J.cols);
-            bulk_g2s(nws, J.norm_w, 4u * J.cols, mb + 1);
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            tma_prefetch_map(&maps.codes[w]);
+            tma_prefetch_map(&maps.scales[w]);
         }
+    }
+    if (lane == 0) mbar_fence_init();
+    __syncwarp();
+    if (tid == 0 && fast && J.norm_w) {  // the norm weight is written by no kernel: requested before the wait
+        mbar_arrive_expect_tx(mb + 1, 4u * J.cols);
+        bulk_g2s(nws, J.norm_w, 4u * J.cols, mb + 1);
     }
     piece_begin(t0);
 #pragma unroll
     for (int d = 0; d < D - 1; ++d)
-        if (d < ne) issue_next(ring_s + d * sstride);
+        if (d < ne) issue_next(d);
     pdl_wait();
     if (J.tp.wait) {  // the input's other ranks' parts are stored here by their launches
         if (tid == 0) tp_wait(J.tp, err);
         __syncthreads();
     }
     if (J.skip && *J.skip) {
-        cp_wait<0>();
+        drain();
         return;
     }
 
     int npiece = 0;
+    bool dead = false;  // a slot's wait ran out (recorded): no further waits or copies
     for (long long t = t0; t < t1;) {
         const bool first = t == t0;
         if (!first) piece_begin(t);
@@ -853,85 +909,112 @@ __global__ void __launch_bounds__(NW == 2 ? kMvThreads / 2 : kMvThreads, 1) tmv_
                                                         (uint32_t)(npiece & 1), err, ok)
                             : build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
         ++npiece;
-        if (!ok) {  // a staging copy timed out (recorded): leave with no copy of ours in flight
-            cp_wait<0>();
+        if (!ok) {  // a staging copy timed out (recorded)
+            drain();
             return;
         }
         unsigned long long best = 0ull;
 
-        const int rounds = (pb - pa + R - 1) / R;
+        const int rounds = (pb - pa + Rr - 1) / Rr;
+        __syncwarp();
 #pragma unroll
         for (int d = 0; d < D - 1; ++d)
-            if (d >= (first ? ne : 0)) issue_next(ring_s + d * sstride);
+            if (d >= (first ? ne : 0)) issue_next(d);
         int rs = D - 1, slot = 0;
-        LaneRow L, one;
+        LaneRow one;
         one.o = row_out(J, segs, job, 0, e8);
         one.B = one.o.B;
         one.F = scale_fast(one.B);
+        one.row = -1;
+        one.srow = 0;
+        LaneRow L[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) L[r] = one;
         for (int k = 0; k < rounds; ++k) {
-            const int rbk = pa + k * R + gi;
+            const int rbk = pa + gsh + k * Rr;
             const bool valid = k < kval;
-            long long acc0 = 0, acc1 = 0;
-            if (valid) lane_row(J, segs, job, rbk * 32 + lane, e8, one, L);
+            long long acc0[R], acc1[R];
+            int Bv[R];
+            ScaleFast Fv[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                acc0[r] = acc1[r] = 0;
+                if (valid) lane_row(J, segs, job, rbk * 32 * R + lane + 32 * r, e8, one, L[r]);
+                Bv[r] = L[r].B;
+                Fv[r] = L[r].F;
+            }
             for (int c = cA; valid && c < cB; ++c) {
-                issue_next(ring_s + rs * sstride);
+                if (!dead) issue_next(rs);
                 rs = rs + 1 == D ? 0 : rs + 1;
-                cp_wait<D - 1>();
-                __syncwarp();
+                if (!dead) dead = !mbar_wait_bounded_s(bars + 8u * slot, (phase >> slot) & 1u, err);
+                if (!dead) {
+                    phase ^= 1u << slot;
+                    inflight &= ~(1u << slot);
+                }
                 const int ng = min(kCG, M.G - c * kCG);
                 const uint32_t *xg = xp + c * kCG * M.xw;
-                const unsigned char *rp = ring + (size_t)slot * sstride + lane * kRowStride;
+                const unsigned char *sp = ring + (size_t)slot * sstride;
+                const int soff = (c & 1) * 8;
 #pragma unroll
                 for (int w = 0; w < NW; ++w) {
-                    const unsigned char *rw = rp + w * kBlkBytes;
-                    const uint2 sc = *reinterpret_cast<const uint2 *>(rw + (c & 1) * 8);
-                    const int Bw = w ? J.B2 : L.B;
-                    const ScaleFast &Fw = w ? F2 : L.F;
-                    long long a;
-                    if (KIND == TRX_KIND_TERNARY5) {
-                        uint32_t cw[28];
-#pragma unroll
-                        for (int i = 0; i < 7; ++i) {
-                            const uint4 v = reinterpret_cast<const uint4 *>(rw + 16)[i];
-                            cw[4 * i] = v.x;
-                            cw[4 * i + 1] = v.y;
-                            cw[4 * i + 2] = v.z;
-                            cw[4 * i + 3] = v.w;
-                        }
-                        a = (c & 1) ? chunk_t5<8>(cw, sc, ng, xg, lane4x, Bw, Fw)
-                                    : chunk_t5<0>(cw, sc, ng, xg, lane4x, Bw, Fw);
+                    const unsigned char *codes = sp + w * M.cbytes;
+                    const unsigned char *scales = sp + NW * M.cbytes + w * 32 * R * kScBox;
+                    if (w == 0) {
+                        if (KIND == TRX_KIND_TERNARY5 && (c & 1))
+                            chunk_rows<KIND, R, 8>(codes, scales, soff, lane, ng, xg, lane4x, Bv, Fv, acc0);
+                        else
+                            chunk_rows<KIND, R, 0>(codes, scales, soff, lane, ng, xg, lane4x, Bv, Fv, acc0);
                     } else {
-                        a = chunk_2b(reinterpret_cast<const uint4 *>(rw + 16), sc, ng, xg, Bw, Fw);
+                        int B2v[R];
+                        ScaleFast F2v[R];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) {
+                            B2v[r] = J.B2;
+                            F2v[r] = F2;
+                        }
+                        if (KIND == TRX_KIND_TERNARY5 && (c & 1))
+                            chunk_rows<KIND, R, 8>(codes, scales, soff, lane, ng, xg, lane4x, B2v, F2v, acc1);
+                        else
+                            chunk_rows<KIND, R, 0>(codes, scales, soff, lane, ng, xg, lane4x, B2v, F2v, acc1);
                     }
-                    if (w) acc1 += a;
-                    else acc0 += a;
                 }
                 __syncwarp();  // every lane is done with the slot before it is refilled
                 slot = slot + 1 == D ? 0 : slot + 1;
             }
             if (M.S > 1) {
                 // The S warps of the group add their partial sums in a fixed order (exact int64).
-                long long *rd = red + (size_t)(k & 1) * M.warps * 32 * NW;
-                rd[(warp * 32 + lane) * NW] = acc0;
-                if (NW == 2) rd[(warp * 32 + lane) * NW + 1] = acc1;
+                long long *rd = red + (size_t)(k & 1) * M.warps * 32 * NW * R;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    rd[((warp * 32 + lane) * R + r) * NW] = acc0[r];
+                    if (NW == 2) rd[((warp * 32 + lane) * R + r) * NW + 1] = acc1[r];
+                }
                 asm volatile("bar.sync %0, %1;" ::"r"(1 + gi), "r"(M.S * 32) : "memory");
                 if (sub == 0 && valid) {
-                    acc0 = acc1 = 0;
-                    for (int s2 = 0; s2 < M.S; ++s2) {
-                        acc0 += rd[((gi * M.S + s2) * 32 + lane) * NW];
-                        if (NW == 2) acc1 += rd[((gi * M.S + s2) * 32 + lane) * NW + 1];
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        acc0[r] = acc1[r] = 0;
+                        for (int s2 = 0; s2 < M.S; ++s2) {
+                            acc0[r] += rd[(((gi * M.S + s2) * 32 + lane) * R + r) * NW];
+                            if (NW == 2) acc1[r] += rd[(((gi * M.S + s2) * 32 + lane) * R + r) * NW + 1];
+                        }
                     }
                 }
             }
-            if (valid && sub == 0 && L.row >= 0) {
-                const unsigned long long key = finish_row(J, L.o, L.row, L.srow, acc0, acc1, err);
-                best = key > best ? key : best;
+            if (valid && sub == 0) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    if (L[r].row >= 0) {
+                        const unsigned long long key = finish_row(J, L[r].o, L[r].row, L[r].srow, acc0[r], acc1[r], err);
+                        best = key > best ? key : best;
+                    }
+                }
             }
         }
-        cp_wait<0>();
         __syncwarp();
         if (J.argmax) argmax_commit(J, job, best, lane);
     }
+    if (dead) drain();  // the slots whose copies never completed: one more bounded wait each
     if (!J.key_out) tp_signal(J.tp, gridDim.x);
     if (J.token || J.key_out) {  // greedy tokens: the last CTA to arrive hands out each job's key
         __syncthreads();
@@ -1102,32 +1185,50 @@ static DevInfo dev_info() {
 
 static int num_sms() { return dev_info().sms; }
 
-// Plan a launch: chunks, tasks (rows split over tasks only when the launch has too few row blocks
-// to give every warp slot of the GPU one), warps and ring depth that fit shared memory.
+// Plan a launch: chunks, rows per lane, tasks (rows split over tasks only when the launch has too
+// few row blocks to give every warp slot of the GPU one), warps and ring depth that fit shared
+// memory.
 bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     const int kind = J.kind;
+    const bool t5 = kind == TRX_KIND_TERNARY5;
     M.G = J.cols / 128;
     M.nch = (M.G + kCG - 1) / kCG;
     M.sbytes = (M.G + 15) / 16 * 32;
-    M.rb = M.sbytes + ((kind == TRX_KIND_TERNARY5 ? 26 : 32) * M.G + 31) / 32 * 32;
+    M.rb = M.sbytes + ((t5 ? 26 : 32) * M.G + 31) / 32 * 32;
     M.nw = nw;
-    M.xw = kind == TRX_KIND_TERNARY5 ? kXwT5 : kXw2b;
-    M.nrb = (J.rows + 31) / 32;
+    M.xw = t5 ? kXwT5 : kXw2b;
+    M.cb = t5 ? kCbT5 : kCb2b;
+    M.D = t5 ? (nw == 2 ? 2 : TRX_MV_D_T5) : (nw == 2 ? 2 : 3);
+    M.wjob = (J.njobs > 1 && J.w_stride != 0) ? 1 : 0;
     // Row blocks are dealt to CTAs; when a CTA gets fewer row blocks than it has warps, the warps
-    // share row blocks (S per row block, chunks split between them, sums combined in shared memory).
-    const long long rbt = (long long)J.njobs * M.nrb;
-    M.grid = (int)std::min<long long>(sms, rbt);
-    const long long rbc = (rbt + M.grid - 1) / M.grid;
-    const bool split = rbc < kMaxWarps && M.nch > 1;
-    M.fixed = (M.G * M.xw * 4 + 64 * 4 + 16 + 16 + kMaxSegs * (int)sizeof(MvSeg) + 127) / 128 * 128 +
-              (split ? 8192 : 0);
-    M.D = kind == TRX_KIND_TERNARY5 ? 2 : 3;
-    const int ring = M.D * nw * kBlkBytes;  // one warp's ring
+    // share row blocks (S per row block, chunks split between them, sums combined in shared memory)
+    // and a lane owns one row; otherwise R rows.
+    bool split = false;
+    long long rbc = 0;
+    for (int R = nw == 2 ? 1 : (t5 ? TRX_MV_R_T5 : TRX_MV_R_2B);; R = 1) {
+        M.R = R;
+        M.nrb = (J.rows + 32 * R - 1) / (32 * R);
+        const long long rbt = (long long)J.njobs * M.nrb;
+        M.grid = (int)std::min<long long>(sms, rbt);
+        rbc = (rbt + M.grid - 1) / M.grid;
+        split = rbc < kMaxWarps && M.nch > 1;
+        if (!split || R == 1) break;
+    }
+    M.cbytes = 32 * M.R * M.cb;
+    M.slot = nw * 32 * M.R * (M.cb + kScBox);
+    int fixed = M.G * M.xw * 4 + 64 * 4 + 16 + 16 + kMaxSegs * (int)sizeof(MvSeg);
+    fixed = (fixed + 7) / 8 * 8;
+    M.bar_off = fixed;
+    fixed = (fixed + kMaxWarps * kMaxD * 8 + 127) / 128 * 128;
+    M.red_off = fixed;
+    fixed += split ? 2 * kMaxWarps * 32 * nw * M.R * 8 : 0;
+    M.fixed = (fixed + 127) / 128 * 128;
+    const int ring = M.D * M.slot;  // one warp's ring
     // The trit5 LUT sits at shared-window address 0x10000 (its PRMT-built addresses need no add):
     // ring region A below it, region C above it.  2-bit: region A only.
     const int lut_off = 0x10000 - reserved, c_off = lut_off + kLutBytes;
     int na_max, nc_max;
-    if (kind == TRX_KIND_TERNARY5) {
+    if (t5) {
         if (M.fixed > lut_off) return false;
         na_max = (lut_off - M.fixed) / ring;
         nc_max = (kSmemMax - c_off) / ring;
@@ -1135,23 +1236,23 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
         na_max = (kSmemMax - M.fixed) / ring;
         nc_max = 0;
     }
-    M.warps = std::min(nw == 2 ? kMaxWarps / 2 : kMaxWarps, na_max + nc_max);
-    if (M.warps < 4) return false;
+    M.warps = std::min(kMaxWarps, na_max + nc_max);
+    if (M.warps < 2) return false;
     M.S = 1;
     if (split) {
         int w = 1;
         while (w * 2 <= M.warps) w *= 2;  // sharing groups need a power-of-two warp count
         M.warps = w;
-        // R row blocks at a time, S = warps/R warps per row block: the fewest chunk steps per warp,
-        // ceil(rbc/R) rounds of ceil(nch/S) chunks; ties go to the larger R (fewer sharers).
+        // Rr row blocks at a time, S = warps/Rr warps per row block: the fewest chunk steps per warp,
+        // ceil(rbc/Rr) rounds of ceil(nch/S) chunks; ties go to the larger Rr (fewer sharers).
         int bestR = 1;
         long long best = -1;
-        for (int R = 1; R <= M.warps; R *= 2) {
-            const int S = M.warps / R;
-            const long long cost = ((rbc + R - 1) / R) * (long long)((M.nch + S - 1) / S);
+        for (int Rr = 1; Rr <= M.warps; Rr *= 2) {
+            const int S = M.warps / Rr;
+            const long long cost = ((rbc + Rr - 1) / Rr) * (long long)((M.nch + S - 1) / S);
             if (best < 0 || cost <= best) {
                 best = cost;
-                bestR = R;
+                bestR = Rr;
             }
         }
         M.S = M.warps / bestR;
@@ -1159,15 +1260,14 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     M.cpt = (M.nch + M.S - 1) / M.S;
     M.na = std::min(na_max, M.warps);
     const int nc = M.warps - M.na;
-    M.base = kind == TRX_KIND_TERNARY5 ? reserved : 0;
-    M.smem = kind == TRX_KIND_TERNARY5 ? c_off + nc * ring : M.fixed + M.warps * ring;
+    M.base = t5 ? reserved : 0;
+    M.smem = t5 ? c_off + nc * ring : M.fixed + M.warps * ring;
     // The quantiser's staging (q8, then x as fp32) lives in the larger ring region, idle then.
     // The staging area: the last bands of the region with the wider band (a band is the slot d of
     // every warp of the region), as few as hold [q8 bytes][x fp32][norm weight fp32]; float4 loads
     // need 16-byte aligned rows, else only the q8 bytes (the global prologue path).
-    const int slot = nw * kBlkBytes;
     M.sreg = nc > M.na ? 1 : 0;
-    const int band = (M.sreg ? nc : M.na) * slot;
+    const int band = (M.sreg ? nc : M.na) * M.slot;
     const bool aligned = !(reinterpret_cast<uintptr_t>(J.x) & 15) && !(reinterpret_cast<uintptr_t>(J.norm_w) & 15) &&
                          !(J.x_stride & 3);
     const int need = aligned ? (J.cols + 15) / 16 * 16 + 4 * J.cols * (J.norm_w ? 2 : 1) : J.cols;
@@ -1181,29 +1281,86 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     return M.smem <= kSmemMax;
 }
 
-template <int KIND, int NW>
-static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, int grid, const uint32_t *lut, uint32_t *err,
-                             cudaStream_t st) {
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (the library links
+// only the CUDA runtime).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static std::atomic<EncodeTiledFn> fn{nullptr};
+    EncodeTiledFn f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            f = reinterpret_cast<EncodeTiledFn>(p);
+        fn.store(f, std::memory_order_release);
+    }
+    return f;
+}
+
+// A uint8 box map over [njobs][rows][rb] bytes (job stride s1 bytes), box {bx bytes, by rows, 1}.
+static bool encode_box(CUtensorMap *m, const void *base, uint64_t rb, uint64_t rows, uint64_t njobs, uint64_t s1,
+                       uint32_t bx, uint32_t by) {
+    const EncodeTiledFn f = encode_tiled();
+    if (!f) return false;
+    const cuuint64_t dims[3] = {rb, rows, njobs};
+    const cuuint64_t strides[2] = {rb, s1};
+    const cuuint32_t box[3] = {bx, by, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static trx_status encode_maps(const MvJobs &J, const MvGeom &M, MvMaps &maps) {
+    memset(&maps, 0, sizeof(maps));
+    const uint64_t njobs = M.wjob ? (uint64_t)J.njobs : 1;
+    const uint64_t s1 = M.wjob ? J.w_stride : (uint64_t)J.rows * M.rb;
+    if (s1 % 16) return TRX_ERR_UNSUPPORTED;
+    for (int w = 0; w < M.nw; ++w) {
+        const void *base = w ? J.w2 : J.w;
+        if (!encode_box(&maps.codes[w], base, M.rb, J.rows, njobs, s1, M.cb, 32 * M.R) ||
+            !encode_box(&maps.scales[w], base, M.rb, J.rows, njobs, s1, kScBox, 32 * M.R))
+            return TRX_ERR_CUDA;
+    }
+    return TRX_OK;
+}
+
+template <int KIND, int NW, int R>
+static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, const MvMaps &maps, uint32_t *err, cudaStream_t st) {
     static DevBits configured{0};  // devices whose attribute is set
     const cudaError_t e = once_per_device(configured, [] {
-        return cudaFuncSetAttribute(tmv_kernel<KIND, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        return cudaFuncSetAttribute(tmv_kernel<KIND, NW, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
     });
     if (e != cudaSuccess) return note_cuda(e);
-    return note_cuda(launch_kernel(tmv_kernel<KIND, NW>, dim3(grid), dim3(M.warps * 32), M.smem, st, J, M, lut, err));
+    return note_cuda(
+        launch_kernel(tmv_kernel<KIND, NW, R>, dim3(M.grid), dim3(M.warps * 32), M.smem, st, maps, J, M, err));
 }
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st) {
+    (void)lut;  // the trit5 LUT is built in each CTA's shared memory
     MvGeom M;
     const DevInfo di = dev_info();
-    const int sms = di.sms;
     const int nw = J.w2 ? 2 : 1;
-    if (!plan_matvec(J, nw, sms, di.reserved, M)) return TRX_ERR_UNSUPPORTED;
-    const int grid = M.grid;
-    if (J.kind == TRX_KIND_TERNARY5)
-        return nw == 2 ? launch_tmv<TRX_KIND_TERNARY5, 2>(J, M, grid, lut, err, st)
-                       : launch_tmv<TRX_KIND_TERNARY5, 1>(J, M, grid, lut, err, st);
-    return nw == 2 ? launch_tmv<TRX_KIND_TERNARY, 2>(J, M, grid, lut, err, st)
-                   : launch_tmv<TRX_KIND_TERNARY, 1>(J, M, grid, lut, err, st);
+    if (!plan_matvec(J, nw, di.sms, di.reserved, M)) return TRX_ERR_UNSUPPORTED;
+    MvMaps maps;
+    const trx_status s = encode_maps(J, M, maps);
+    if (s != TRX_OK) return s;
+    if (J.kind == TRX_KIND_TERNARY5) {
+        if (nw == 2) return launch_tmv<TRX_KIND_TERNARY5, 2, 1>(J, M, maps, err, st);
+#if TRX_MV_R_T5 > 1
+        if (M.R == 2) return launch_tmv<TRX_KIND_TERNARY5, 1, 2>(J, M, maps, err, st);
+#endif
+        return launch_tmv<TRX_KIND_TERNARY5, 1, 1>(J, M, maps, err, st);
+    }
+    if (nw == 2) return launch_tmv<TRX_KIND_TERNARY, 2, 1>(J, M, maps, err, st);
+#if TRX_MV_R_2B > 1
+    if (M.R == 2) return launch_tmv<TRX_KIND_TERNARY, 1, 2>(J, M, maps, err, st);
+#endif
+    return launch_tmv<TRX_KIND_TERNARY, 1, 1>(J, M, maps, err, st);
 }
 
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st) {

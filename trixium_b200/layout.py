@@ -76,6 +76,13 @@ def q8_row_bytes(cols):
     return (ceil_div(g, SCALES_PER_BEAT) + g) * BEAT_BYTES
 
 
+def plain_row_bytes(cols, kind):
+    """Bytes of one row of an unscaled tensor: fp32 (KIND_F32), int16 (KIND_NORM16) or fp16
+    (KIND_F16) values, the row padded to whole beats (model/layout.py:189-217, no scale beats)."""
+    width = {KIND_F32: 4, KIND_NORM16: 2, KIND_F16: 2}[kind]
+    return ceil_div(width * cols, BEAT_BYTES) * BEAT_BYTES
+
+
 def tensor_bytes(rows, cols, kind):
     return rows * row_bytes(cols, kind)
 

@@ -229,10 +229,23 @@ def hadamard_rotate(ctx, had: DeviceTensor, x, out=None):
 
 def attn_decode(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, out=None, tp=None):
     """One decode step of GQA attention (trx_attn_decode).  shape: _lib.AttnShape; q (H*(1+gated)*hd),
-    k/v (n_kv*hd) float32; caches [max_pos, n_kv, hd] float16; pos: int32 device tensor of one
-    element (the position written and attended up to)."""
+    k/v (n_kv*hd) float32; caches [max_pos, n_kv, hd] float16 (or float32: trx_attn_decode_f32cache,
+    the reference mirror's cache type); pos: int32 device tensor of one element (the position
+    written and attended up to)."""
     for t, n in ((q, "q"), (k, "k"), (v, "v"), (q_norm, "q_norm"), (k_norm, "k_norm")):
         _need(t, torch.float32, n)
+    if kcache.dtype == torch.float32:
+        _need(vcache, torch.float32, "vcache")
+        _need(pos, torch.int32, "pos")
+        if tp is not None:
+            raise ValueError("the fp32-cache attention has no tensor-parallel exchange")
+        if out is None:
+            out = torch.empty(shape.n_head * shape.head_dim, dtype=torch.float32, device=q.device)
+        _lib.check(_lib.lib().trx_attn_decode_f32cache(ctx.h, ctypes.byref(shape), _ptr(q), _ptr(k), _ptr(v),
+                                                       _ptr(q_norm), _ptr(k_norm), _ptr(rope_freq), _ptr(kcache),
+                                                       _ptr(vcache), _ptr(pos), _ptr(out), _stream()),
+                   "trx_attn_decode_f32cache")
+        return out
     _need(kcache, torch.float16, "kcache")
     _need(vcache, torch.float16, "vcache")
     _need(pos, torch.int32, "pos")
@@ -304,6 +317,43 @@ def embed_lookup(ctx, table, token, x):
     _lib.check(_lib.lib().trx_embed_lookup(ctx.h, _ptr(table), table.shape[0], table.shape[1], 1 if f16 else 0,
                                            _ptr(token), _ptr(x), _stream()), "trx_embed_lookup")
     return x
+
+
+def embed_lookup_bfp16(ctx, mant, exps, token, x):
+    """x = mant[token] * 2^exps[token] (an image's int16 embedding table: mant int16 [vocab, dim],
+    exps int32 [vocab]; token: int32 device tensor of one element)."""
+    _need(mant, torch.int16, "mant")
+    _need(exps, torch.int32, "exps")
+    _need(token, torch.int32, "token")
+    _need(x, torch.float32, "x")
+    _lib.check(_lib.lib().trx_embed_lookup_bfp16(ctx.h, _ptr(mant), _ptr(exps), mant.shape[0], mant.shape[1],
+                                                 _ptr(token), _ptr(x), _stream()), "trx_embed_lookup_bfp16")
+    return x
+
+
+def rmsnorm(ctx, x, w, eps=1e-6, y=None):
+    """y = RMSNorm(x) * w with the canonical 64-partial sum of squares (trx_rmsnorm)."""
+    _need(x, torch.float32, "x")
+    _need(w, torch.float32, "w")
+    if y is None:
+        y = torch.empty_like(x)
+    _lib.check(_lib.lib().trx_rmsnorm(ctx.h, _ptr(x), _ptr(w), x.numel(), ctypes.c_float(eps), _ptr(y), _stream()),
+               "trx_rmsnorm")
+    return y
+
+
+def matvec_f_kseg(ctx, segs, x, y=None, resid=None):
+    """Float projection of a K-segmented tensor (trx_matvec_f_kseg): segs, the segments' DeviceTensors
+    in column order (ternary or KIND_Q8, the tensor's B/R in each); x: the full input."""
+    _need(x, torch.float32, "x")
+    n = len(segs)
+    arr = (_lib.Entry * n)(*[t.entry for t in segs])
+    ptrs = (ctypes.c_void_p * n)(*[t.data.data_ptr() for t in segs])
+    if y is None:
+        y = torch.empty(segs[0].rows, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().trx_matvec_f_kseg(ctx.h, arr, n, ptrs, _ptr(x), _ptr(resid), _ptr(y), _stream()),
+               "trx_matvec_f_kseg")
+    return y
 
 
 def advance_position(ctx, pos, n=1):

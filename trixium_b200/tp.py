@@ -122,6 +122,8 @@ class TPWeights:
         self.lm_head = _slice_rows(full.lm_head, np.arange(self.v0, self.v1))
         self.layers = []
         for l, lw in enumerate(full.layers):
+            if isinstance(lw["down"], list):
+                raise ValueError("tensor-parallel decoding takes no K-segmented tensors (ffn wider than 16384)")
             w = {"attn_norm": lw["attn_norm"], "ffn_norm": lw["ffn_norm"],
                  "gate": _slice_rows(lw["gate"], fr), "up": _slice_rows(lw["up"], fr),
                  "down": _slice_rows(lw["down"], er), "out": _slice_rows(lw["out"], er)}
