@@ -237,14 +237,14 @@ def other_kind_leg(ctx, kind, C, steps, warmup, dev, rank, peak):
         ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    for a, b in ev:
-        a.record(st)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(steps):
         ops.matvec_f_batch(ctx, wt, wstride, X, K_COLS, Y, N_ROWS, C)
-        b.record(st)
+    b.record(st)
     torch.cuda.synchronize()
     ctx.raise_on_error()
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    launch_ms = a.elapsed_time(b) / steps
     alg = (L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * (K_COLS + N_ROWS)) * C
     achieved = alg / (launch_ms * 1e-3) / 1e9
     del wt, W, X, Y
@@ -318,14 +318,14 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # Back-to-back launches between two events: a launch's average duration is the timed region
+    # over K (events between launches would serialise each launch's start behind its predecessor's
+    # end, which programmatic dependent launch otherwise overlaps).
     stream = torch.cuda.current_stream()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        ev[i][0].record(stream)
         step()
-        ev[i][1].record(stream)
     e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -333,7 +333,7 @@ def main():
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    launch_ms = ms / args.steps
     ctx.raise_on_error()
 
     # Per-launch variant: one launch per copy (a single 2.75 MB matvec per kernel), in a CUDA graph.

@@ -300,8 +300,9 @@ def hybrid_tokens_case(name, cfg, trit5, kseg_max, n_prompt=6, n_new=128, seed=1
     Q8 beta/alpha, the int16 embedding table; K-segmented where wider than kseg_max), stored
     gzipped, and the reference mirror's greedy tokens for a seeded prompt in its engine arithmetic
     (model/mirror.py:594-1044, hybrid27_generate with exact=False and the mathematical profile):
-    int8 power-of-two activations, the engine's integer matvec.  Per generated step the logits'
-    top-two margin is kept too (where it is tiny, fp32 rounding order may flip the argmax)."""
+    int8 power-of-two activations, the engine's integer matvec.  Per generated step the logits and
+    their top-two margin are kept too (where the margin is tiny, fp32 rounding order may flip the
+    argmax)."""
     import gzip
     import shutil
     import tempfile
@@ -314,18 +315,21 @@ def hybrid_tokens_case(name, cfg, trit5, kseg_max, n_prompt=6, n_new=128, seed=1
         img = bons.BONSReader(img_path)
         rng = np.random.default_rng(seed + 2)
         prompt = [int(t) for t in rng.integers(0, cfg.vocab, n_prompt)]
-        margins, ckpt = {}, {}
+        margins, ckpt, logits = {}, {}, {}
 
         def cb(pos, layer, tag, dtype, values):
             if tag == "logits":
                 v = np.sort(np.asarray(values, dtype=np.float64))
                 margins[pos] = v[-1] - v[-2]
+                logits[pos] = np.asarray(values, dtype=f32)
             if pos < 3 and tag in ("emb", "attn_res", "ffn_res", "out_norm", "logits"):
                 ckpt[f"p{pos}_l{layer}_{tag}"] = np.asarray(values, dtype=f32)
         toks = mirror.hybrid27_generate(img, prompt, n_new, exact=False, silu_mode="mathematical", trace=cb)
     npos = n_prompt + n_new - 1
+    steps = range(n_prompt - 1, npos)
     np.savez_compressed(os.path.join(HERE, f"tokens_{name}.npz"), prompt=np.array(prompt), tokens=np.array(toks),
-                        margins=np.array([margins[p] for p in range(n_prompt - 1, npos)]), **ckpt)
+                        margins=np.array([margins[p] for p in steps]),
+                        logits=np.stack([logits[p] for p in steps]), **ckpt)
 
 
 def kseg_case(name, rows, cols, kind, seed):

@@ -109,25 +109,35 @@ def test_first_positions_follow_the_mirror(tmp_path_factory, ctx, name):
 @pytest.mark.parametrize("kv", ["fp32", "fp16"])
 @pytest.mark.parametrize("name", NAMES)
 def test_teacher_forced_tokens_match_the_mirror(tmp_path_factory, ctx, name, kv):
+    """Fed the mirror's tokens, every step's logits are compared with the mirror's: with eps the
+    step's largest logit difference, the greedy token must equal the mirror's wherever the mirror's
+    top-two margin is at least 2 eps (below that, the difference can explain a flip), and eps must
+    stay small: 5e-2 of the logit scale with the fp32 cache (rounding-order differences that move
+    an int8 activation accumulate in the DeltaNet state), 0.2 with the fp16 cache."""
     d = load(os.path.join(GOLDEN, f"tokens_{name}.npz"))
-    prompt, toks, margins = list(d["prompt"]), list(d["tokens"]), d["margins"]
-    margin = MARGIN if kv == "fp32" else MARGIN_FP16
+    prompt, toks, margins, ref_logits = list(d["prompt"]), list(d["tokens"]), d["margins"], d["logits"]
     dec = _decoder(tmp_path_factory, ctx, name, torch.float32 if kv == "fp32" else torch.float16)
     dec.capture()
     seq = prompt + toks
-    agree, checked = 0, 0
+    scale = float(np.abs(ref_logits).max())
+    agree, eps_max, explained = 0, 0.0, 0
     for p in range(len(seq) - 1):
         dec.step(int(seq[p]))
         if p >= len(prompt) - 1:
             i = p - (len(prompt) - 1)       # generated step i predicts toks[i]
             got = int(dec.tok.item())
-            agree += got == toks[i]
-            if margins[i] >= margin:
-                checked += 1
-                assert got == toks[i], (i, got, toks[i], float(margins[i]))
-    assert checked >= 100
+            eps = float(np.abs(dec.logits.cpu().numpy().astype(np.float64) - ref_logits[i]).max())
+            eps_max = max(eps_max, eps)
+            if got == toks[i]:
+                agree += 1
+            else:
+                assert margins[i] < 2 * eps, (i, got, toks[i], float(margins[i]), eps)
+                explained += 1
+    assert eps_max <= (5e-2 if kv == "fp32" else 0.2) * scale, (eps_max, scale)
+    assert agree >= 120, agree
     assert ctx.errors() == 0
-    print(f"{name} ({kv} KV cache): {agree}/{len(toks)} steps agree teacher-forced ({checked} with margin >= {margin})")
+    print(f"{name} ({kv} KV cache): {agree}/{len(toks)} steps agree teacher-forced; largest logit difference "
+          f"{eps_max:.3g} (scale {scale:.3g}); {explained} flips within twice that")
 
 
 @pytest.mark.gpu

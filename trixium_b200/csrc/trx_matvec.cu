@@ -855,13 +855,15 @@ __global__ void __launch_bounds__(kMvThreads, 1)
             }
         inflight = 0;
     };
-    // The staging area [q8 bytes][x fp32][norm weight fp32] covers the last bands of the staging
-    // region; the first piece's blocks for the slots below it (weights: written by no kernel) are
-    // requested before waiting for the predecessor, all D-1 by the warps of the other region.
+    // The staging area [q8 bytes][x fp32][norm weight fp32] has a region of its own when shared
+    // memory has room (decode-size launches), else it covers the last bands of the staging region.
+    // The first piece's blocks for every slot outside it (weights: written by no kernel) are
+    // requested before waiting for the predecessor: a decode-size launch streams its whole weight
+    // share while the previous kernel still runs.
     const bool fast = M.xfast && J.x;
     const int xs_off = M.stage_off + ((J.cols + 15) / 16) * 16;
     float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * J.cols);
-    const int ne = (warp < M.na) == (M.sreg == 0) ? min(D - 1, M.ebl) : D - 1;
+    const int ne = (warp < M.na) == (M.sreg == 0) ? min(D, M.ebl) : D;
     if (lane == 0) {
 #pragma unroll
         for (int d = 0; d < D; ++d) mbar_init_s(bars + 8u * d, 1);
@@ -883,7 +885,7 @@ __global__ void __launch_bounds__(kMvThreads, 1)
     }
     piece_begin(t0);
 #pragma unroll
-    for (int d = 0; d < D - 1; ++d)
+    for (int d = 0; d < D; ++d)
         if (d < ne) issue_next(d);
     pdl_wait();
     if (J.tp.wait) {  // the input's other ranks' parts are stored here by their launches
@@ -918,9 +920,9 @@ __global__ void __launch_bounds__(kMvThreads, 1)
         const int rounds = (pb - pa + Rr - 1) / Rr;
         __syncwarp();
 #pragma unroll
-        for (int d = 0; d < D - 1; ++d)
+        for (int d = 0; d < D; ++d)
             if (d >= (first ? ne : 0)) issue_next(d);
-        int rs = D - 1, slot = 0;
+        int slot = 0;
         LaneRow one;
         one.o = row_out(J, segs, job, 0, e8);
         one.B = one.o.B;
@@ -944,8 +946,6 @@ __global__ void __launch_bounds__(kMvThreads, 1)
                 Fv[r] = L[r].F;
             }
             for (int c = cA; valid && c < cB; ++c) {
-                if (!dead) issue_next(rs);
-                rs = rs + 1 == D ? 0 : rs + 1;
                 if (!dead) dead = !mbar_wait_bounded_s(bars + 8u * slot, (phase >> slot) & 1u, err);
                 if (!dead) {
                     phase ^= 1u << slot;
@@ -979,6 +979,7 @@ __global__ void __launch_bounds__(kMvThreads, 1)
                     }
                 }
                 __syncwarp();  // every lane is done with the slot before it is refilled
+                if (!dead) issue_next(slot);  // the block D ahead of the one just consumed
                 slot = slot + 1 == D ? 0 : slot + 1;
             }
             if (M.S > 1) {
@@ -1271,6 +1272,15 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     const bool aligned = !(reinterpret_cast<uintptr_t>(J.x) & 15) && !(reinterpret_cast<uintptr_t>(J.norm_w) & 15) &&
                          !(J.x_stride & 3);
     const int need = aligned ? (J.cols + 15) / 16 * 16 + 4 * J.cols * (J.norm_w ? 2 : 1) : J.cols;
+    const int own = (M.smem + 127) / 128 * 128;
+    if (own + need <= kSmemMax) {  // a region of its own after the rings: no slot waits for the prologue
+        M.stage_off = own;
+        M.stage = need;
+        M.ebl = M.D;
+        M.xfast = aligned ? 1 : 0;
+        M.smem = own + need;
+        return true;
+    }
     const int nb = std::min(M.D, (need + band - 1) / band);
     M.stage = nb * band;
     if (M.stage < J.cols) return false;

@@ -499,7 +499,7 @@ class ImageDecoder(Decoder):
         f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)
         self.hn = f32(cfg.hidden)
         self.rin = f32(max(cfg.hidden, cfg.ffn, cfg.n_head * cfg.head_dim, cfg.dn_nv * cfg.dn_hv))
-        self.gate_buf, self.up_buf = f32(cfg.ffn), f32(cfg.ffn)
+        self.logits = f32(cfg.vocab)
         self.trace = None
 
     def _rotate(self, x, width):
@@ -563,7 +563,7 @@ class ImageDecoder(Decoder):
             self._tr(l, "ffn_res", self.x)
         ops.rmsnorm(ctx, self.x, w.out_norm, cfg.eps, y=self.hn)
         self._tr(-1, "out_norm", self.hn)
-        ops.lmhead_argmax(ctx, w.lm_head, self._rotate(self.hn, E), token=self.tok)
+        ops.lmhead_argmax(ctx, w.lm_head, self._rotate(self.hn, E), token=self.tok, logits=self.logits)
         ops.advance_position(ctx, self.pos)
 
     def launches_per_step(self):
