@@ -103,10 +103,22 @@ trx_status trx_matvec_q8_f(trx_ctx *ctx, const trx_entry *e, const void *d_packe
 
 /*
  * Multi-row engine matvec: nb independent rows of x8 ([nb, K] int8) against one weight pass,
- * out [nb, rows] int32 (model/bitexact.py:121-125, matvec_ternary_rows).  nb <= 8.
+ * out [nb, rows] int32 (model/bitexact.py:121-125, matvec_ternary_rows).  nb <= 32: up to 8 rows
+ * on the integer dot-product path, 9..32 on the tensor cores (tcgen05 kind::i8, decoded codes times
+ * the rows, exact int32 group sums, the engine's int64 scale epilogue).  The tensor-core form uses
+ * the context's scratch: calls on one context must not overlap.
  */
 trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
                               const int8_t *d_x8, int nb, int32_t *d_out, cudaStream_t stream);
+
+/*
+ * Batched float projection: nb <= 32 independent fp32 rows x [nb, K] (a decode batch), each
+ * quantised with its own power-of-two exponent (model/mirror.py:45-51), against one weight pass on
+ * the tensor cores, y [nb, rows] = float(int32 result) * 2^(e8_row + R - B) (model/mirror.py:664-678
+ * per row).  Two launches (the rows' quantisation, the tensor-core matvec) on the context's scratch.
+ */
+trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                             int nb, float *d_y, cudaStream_t stream);
 
 /*
  * Power-of-two int8 activation quantisation: e8 = frexp(max|x|) - 7,

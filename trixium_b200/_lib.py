@@ -26,7 +26,7 @@ SYMBOLS = (
     "trx_attn_decode_static", "trx_lmhead_argmax_key", "trx_argmax_token", "trx_matvec_f_tp",
     "trx_matvec_f_multi_tp", "trx_matvec_swiglu_tp", "trx_lmhead_argmax_key_tp", "trx_argmax_token_tp",
     "trx_attn_decode_tp", "trx_embed_lookup_bfp16", "trx_rmsnorm", "trx_matvec_f_kseg",
-    "trx_attn_decode_f32cache",
+    "trx_attn_decode_f32cache", "trx_matvec_f_rows",
 )
 
 TP_MAX = 8
@@ -130,6 +130,7 @@ def lib():
             "trx_rmsnorm": ([_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_float, _vp, _vp], ctypes.c_int),
             "trx_matvec_f_kseg": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
             "trx_attn_decode_f32cache": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
+            "trx_matvec_f_rows": ([_vp, E, _vp, _vp, ctypes.c_int, _vp, _vp], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

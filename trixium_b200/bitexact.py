@@ -60,8 +60,8 @@ def matvec_ternary_rows(scales_f16, codes, x8_rows, B, R, kind=0):
     dt = _device_tensor(scales_f16, codes, B, R, kind)
     x = np.ascontiguousarray(np.asarray(x8_rows, dtype=np.int8))
     outs = []
-    for c0 in range(0, x.shape[0], 8):
-        xt = torch.from_numpy(x[c0:c0 + 8]).to(ctx.device)
+    for c0 in range(0, x.shape[0], 32):  # up to 32 rows per launch (9..32 on the tensor cores)
+        xt = torch.from_numpy(x[c0:c0 + 32]).to(ctx.device)
         outs.append(ops.matvec_i8_rows(ctx, dt, xt))
     _raise_device(ctx)
     return torch.cat(outs).cpu().numpy()

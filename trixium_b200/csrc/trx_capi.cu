@@ -22,6 +22,13 @@ struct trx_ctx {
     int8_t *q8x;
     // trx_matvec_f_kseg: the segments' int32 engine results, [nseg][rows].
     int32_t *kseg_part;
+    // Batched rows on the tensor cores: the permuted activation rows, their group sums and
+    // exponents; the K-split partial sums and tile arrival counts (zero between launches).
+    int8_t *rows_x8p;
+    int *rows_xsum;
+    int *rows_e8;
+    unsigned long long *rows_acc;
+    unsigned *rows_cnt;
 };
 
 static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
@@ -29,6 +36,9 @@ static const uint32_t kAttnMaxKv = 1024;
 static const int kMaxArgmaxJobs = 64;
 static const uint32_t kQ8MaxCols = 32768;
 static const uint64_t kKsegPartInts = 1ull << 20;  // 4 MiB of K-segment partial results
+static const int kRowsMax = 32;                      // batch rows of the tensor-core path
+static const uint64_t kRowsAcc = 1ull << 19;          // int64 partial sums (4 MiB): nb * N of a K-split launch
+static const int kRowsTiles = 4096;                   // arrival counts (128-row tiles)
 
 namespace trx {
 bool pdl_enabled() { return true; }
@@ -91,6 +101,13 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaMalloc(&c->amax_cnt, 16) != cudaSuccess || cudaMemset(c->amax_cnt, 0, 16) != cudaSuccess ||
         cudaMalloc(&c->q8x, kQ8MaxCols + 16) != cudaSuccess ||
         cudaMalloc(&c->kseg_part, kKsegPartInts * 4) != cudaSuccess ||
+        cudaMalloc(&c->rows_x8p, (size_t)kRowsMax * kQ8MaxCols) != cudaSuccess ||
+        cudaMalloc(&c->rows_xsum, (size_t)kRowsMax * (kQ8MaxCols / 128) * 4) != cudaSuccess ||
+        cudaMalloc(&c->rows_e8, kRowsMax * 4) != cudaSuccess ||
+        cudaMalloc(&c->rows_acc, kRowsAcc * 8) != cudaSuccess ||
+        cudaMemset(c->rows_acc, 0, kRowsAcc * 8) != cudaSuccess ||
+        cudaMalloc(&c->rows_cnt, kRowsTiles * 4) != cudaSuccess ||
+        cudaMemset(c->rows_cnt, 0, kRowsTiles * 4) != cudaSuccess ||
         trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
@@ -101,6 +118,11 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaFree(c->amax_cnt);
         cudaFree(c->q8x);
         cudaFree(c->kseg_part);
+        cudaFree(c->rows_x8p);
+        cudaFree(c->rows_xsum);
+        cudaFree(c->rows_e8);
+        cudaFree(c->rows_acc);
+        cudaFree(c->rows_cnt);
         delete c;
         return TRX_ERR_CUDA;
     }
@@ -118,6 +140,11 @@ trx_status trx_destroy(trx_ctx *ctx) {
     cudaFree(ctx->amax_cnt);
     cudaFree(ctx->q8x);
     cudaFree(ctx->kseg_part);
+    cudaFree(ctx->rows_x8p);
+    cudaFree(ctx->rows_xsum);
+    cudaFree(ctx->rows_e8);
+    cudaFree(ctx->rows_acc);
+    cudaFree(ctx->rows_cnt);
     delete ctx;
     return TRX_OK;
 }
@@ -190,12 +217,30 @@ trx_status trx_matvec_q8_f(trx_ctx *ctx, const trx_entry *e, const void *d_packe
                                  e->rshift, ctx->q8x, e8, d_y, ctx->err, stream);
 }
 
+static trx_status rows_tc(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, const int8_t *d_x8,
+                          int nb, int32_t *d_out_i, float *d_out_f, cudaStream_t stream) {
+    return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->kind,
+                                   e->bias, e->rshift, d_x, d_x8, nb, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8,
+                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsTiles, d_out_i, d_out_f, ctx->err,
+                                   trx::device_sms(), trx::device_reserved_smem(), stream);
+}
+
+trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, int nb,
+                             float *d_y, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_y || nb < 1 || nb > kRowsMax || !aligned16(d_packed)) return TRX_ERR_ARG;
+    return rows_tc(ctx, e, d_packed, d_x, nullptr, nb, nullptr, d_y, stream);
+}
+
 trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int nb,
                               int32_t *d_out, cudaStream_t stream) {
     if (!ctx) return TRX_ERR_ARG;
     trx_status s = check_entry(e);
     if (s) return s;
-    if (!d_packed || !d_x8 || !d_out || nb < 1 || nb > 8 || !aligned16(d_packed)) return TRX_ERR_ARG;
+    if (!d_packed || !d_x8 || !d_out || nb < 1 || nb > kRowsMax || !aligned16(d_packed)) return TRX_ERR_ARG;
+    if (nb > 8) return rows_tc(ctx, e, d_packed, nullptr, d_x8, nb, d_out, nullptr, stream);
     trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x8 = d_x8;
     J.x_stride = e->cols;

@@ -1185,6 +1185,8 @@ static DevInfo dev_info() {
 }
 
 static int num_sms() { return dev_info().sms; }
+int device_sms() { return dev_info().sms; }
+int device_reserved_smem() { return dev_info().reserved; }
 
 // Plan a launch: chunks, rows per lane, tasks (rows split over tasks only when the launch has too
 // few row blocks to give every warp slot of the GPU one), warps and ring depth that fit shared

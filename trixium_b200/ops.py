@@ -145,6 +145,18 @@ def matvec_i8_rows(ctx, w: DeviceTensor, x8rows, out=None):
     return out
 
 
+def matvec_f_rows(ctx, w: DeviceTensor, xrows, out=None):
+    """Batched float projection (trx_matvec_f_rows): xrows [nb, K] float32 (nb <= 32), each row
+    quantised with its own exponent, on the tensor cores; returns [nb, rows] float32."""
+    _need(xrows, torch.float32, "xrows")
+    nb = xrows.shape[0]
+    if out is None:
+        out = torch.empty(nb, w.rows, dtype=torch.float32, device=xrows.device)
+    _lib.check(_lib.lib().trx_matvec_f_rows(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(xrows), nb, _ptr(out),
+                                            _stream()), "trx_matvec_f_rows")
+    return out
+
+
 def quantize_pow2(ctx, x, x8=None, e8=None):
     _need(x, torch.float32, "x")
     if x8 is None:
