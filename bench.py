@@ -434,6 +434,7 @@ def main():
                          "hybrid-27b": decode_leg(ctx, "hybrid-27b", 4096, 128, 8)}
     if world == 1 and not args.no_decode:
         out["q8_matvec"] = q8_leg(ctx, peak)
+        out["batched_rows"] = [rows_leg(ctx, peak, k, nb) for k in (5, 0) for nb in (16, 32)]
     if rank == 0 and world == 1 and not args.no_cpu:
         out["cpu_baseline"] = cpu_baseline(kind, args.cpu_seconds)
     if rank == 0:
@@ -487,6 +488,47 @@ def q8_leg(ctx, peak, rows=16384, cols=8192, launches=20, warmup=3):
             "launches_timed": launches, "ms_per_launch": round(ms, 4),
             "algorithmic_bytes_per_launch": alg, "achieved_GBps": round(gbs, 1),
             "frac": round(gbs / peak, 4), "inputs": "two tensors in turn, 272 MB > L2"}
+
+
+def rows_leg(ctx, peak, kind, nb, launches=20, copies=48, warmup=3):
+    """The batched path (trx_matvec_f_rows, tcgen05 kind::i8): nb activation rows against one pass
+    over a config-0 tensor (K=2048, N=6144), `copies` distinct tensors used in turn (above L2).
+    Reports the weight stream (GB/s of algorithmic bytes, as the matvec) and rows x rows per second
+    (batched projections)."""
+    import torch
+    from trixium_b200 import image, layout as L, ops
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    rb = L.row_bytes(K_COLS, kind)
+    tensors = []
+    W = torch.empty(copies * N_ROWS * rb, dtype=torch.uint8, device="cuda")
+    t0, _ = image.synthetic_matvec_case(N_ROWS, K_COLS, seed=0, kind=kind)
+    for j in range(copies):
+        c, s = image.synthetic_codes_scales_torch(gen, N_ROWS, K_COLS, "cuda")
+        W[j * N_ROWS * rb:(j + 1) * N_ROWS * rb] = image.pack_rows_torch(s, c, kind)
+        tensors.append(ops.DeviceTensor.from_packed(W[j * N_ROWS * rb:(j + 1) * N_ROWS * rb], N_ROWS, K_COLS, kind,
+                                                    t0.bias, t0.rshift))
+    X = torch.randn(nb, K_COLS, generator=gen, device="cuda")
+    Y = torch.empty(nb, N_ROWS, device="cuda")
+    for i in range(warmup):
+        ops.matvec_f_rows(ctx, tensors[i % copies], X, Y)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(launches):
+        ops.matvec_f_rows(ctx, tensors[i % copies], X, Y)
+    b.record()
+    torch.cuda.synchronize()
+    ctx.raise_on_error()
+    ms = a.elapsed_time(b) / launches
+    alg = L.algorithmic_bytes(N_ROWS, K_COLS, kind) + 4 * nb * (K_COLS + N_ROWS)
+    del tensors, W
+    torch.cuda.empty_cache()
+    return {"kernel": "trx::rows_kernel (trx_matvec_f_rows: tcgen05.mma kind::i8, TMEM accumulators)",
+            "kind": "trit5" if kind == 5 else "2-bit", "rows": N_ROWS, "cols": K_COLS, "batch": nb,
+            "ms_per_launch": round(ms, 4), "weight_GBps": round(alg / (ms * 1e-3) / 1e9, 1),
+            "frac": round(alg / (ms * 1e-3) / 1e9 / peak, 4),
+            "row_projections_per_s": round(nb / (ms * 1e-3), 1),
+            "inputs": f"{copies} tensors in turn ({copies * N_ROWS * rb / 1e6:.0f} MB > L2), includes the rows' quantisation launch"}
 
 
 def decode_leg(ctx, name, ctx_len, n_tokens, warmup):

@@ -115,10 +115,28 @@ trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_pa
  * Batched float projection: nb <= 32 independent fp32 rows x [nb, K] (a decode batch), each
  * quantised with its own power-of-two exponent (model/mirror.py:45-51), against one weight pass on
  * the tensor cores, y [nb, rows] = float(int32 result) * 2^(e8_row + R - B) (model/mirror.py:664-678
- * per row).  Two launches (the rows' quantisation, the tensor-core matvec) on the context's scratch.
+ * per row), plus d_resid [nb, rows] when not NULL.  Two launches (the rows' quantisation, the
+ * tensor-core matvec) on the context's scratch.
  */
 trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
-                             int nb, float *d_y, cudaStream_t stream);
+                             int nb, const float *d_resid, float *d_y, cudaStream_t stream);
+
+/* The per-row steps around the batched projections of a decode batch (nrows independent sequences;
+ * model/mirror.py:1002-1034 per sequence):
+ *   trx_embed_lookup_rows: x[r] = table[tokens[r]] (as trx_embed_lookup, fp16 or fp32 table);
+ *   trx_rmsnorm_rows: y[r] = RMSNorm(x[r]) * w (as trx_rmsnorm), rows of n floats;
+ *   trx_silu_mul: act = silu(g) * u elementwise over n floats (model/mirror.py:713,1020);
+ *   trx_argmax_rows: tokens[r] = the largest of logits[r][0..V), ties to the smallest index;
+ *   trx_advance_positions: pos[i] += n for i < count. */
+trx_status trx_embed_lookup_rows(trx_ctx *ctx, const void *d_table, uint32_t vocab, uint32_t dim, int32_t f16,
+                                 const int32_t *d_tokens, int32_t nrows, float *d_x, cudaStream_t stream);
+trx_status trx_rmsnorm_rows(trx_ctx *ctx, const float *d_x, const float *d_w, uint32_t n, int32_t nrows, float eps,
+                            float *d_y, cudaStream_t stream);
+trx_status trx_silu_mul(trx_ctx *ctx, const float *d_g, const float *d_u, uint64_t n, float *d_act,
+                        cudaStream_t stream);
+trx_status trx_argmax_rows(trx_ctx *ctx, const float *d_logits, uint32_t V, int32_t nrows, int32_t *d_tokens,
+                           cudaStream_t stream);
+trx_status trx_advance_positions(trx_ctx *ctx, int32_t *d_pos, int32_t count, int32_t n, cudaStream_t stream);
 
 /*
  * Power-of-two int8 activation quantisation: e8 = frexp(max|x|) - 7,
@@ -270,6 +288,16 @@ trx_status trx_attn_decode(trx_ctx *ctx, const trx_attn_shape *shape, const floa
                            float *d_out, cudaStream_t stream);
 
 /*
+ * trx_attn_decode for a batch of nseq independent sequences in one launch: q [nseq][H*(1+gated)*hd],
+ * k/v [nseq][n_kv*hd], caches [nseq][max_pos][n_kv][hd] fp16, d_pos [nseq] (each sequence's own
+ * position), out [nseq][H*hd]; the scratch-merge kernel with a sequence grid dimension.
+ */
+trx_status trx_attn_decode_rows(trx_ctx *ctx, const trx_attn_shape *shape, int32_t nseq, const float *d_q,
+                                const float *d_k, const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                                const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                                float *d_out, cudaStream_t stream);
+
+/*
  * trx_attn_decode over an fp32 KV cache (caches [max_pos][n_kv][head_dim] float, 16-byte aligned):
  * the reference mirror keeps its cache in fp32 (model/mirror.py:966, kc[l].append(k)), so a run
  * that must follow the mirror's values to fp32 rounding (token parity in the engine's int8
@@ -329,6 +357,17 @@ trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *shape, cons
                              const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
                              float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
                              cudaStream_t stream);
+
+/*
+ * trx_deltanet_step for a batch of nseq independent sequences in one launch: every per-sequence
+ * argument (qkv, z, beta, alpha, conv ring, state, position, output) is nseq consecutive copies of
+ * the single-sequence layout; the weights (dt_bias, ssm_a, conv_w, norm_w) are shared.
+ */
+trx_status trx_deltanet_step_rows(trx_ctx *ctx, const trx_deltanet_shape *shape, int32_t nseq, const float *d_qkv,
+                                  const float *d_z, const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                                  const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                                  float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                                  cudaStream_t stream);
 
 /*
  * Tensor-parallel exchange over peer memory (no counterpart in the reference, which runs on one

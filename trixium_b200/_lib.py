@@ -26,7 +26,8 @@ SYMBOLS = (
     "trx_attn_decode_static", "trx_lmhead_argmax_key", "trx_argmax_token", "trx_matvec_f_tp",
     "trx_matvec_f_multi_tp", "trx_matvec_swiglu_tp", "trx_lmhead_argmax_key_tp", "trx_argmax_token_tp",
     "trx_attn_decode_tp", "trx_embed_lookup_bfp16", "trx_rmsnorm", "trx_matvec_f_kseg",
-    "trx_attn_decode_f32cache", "trx_matvec_f_rows",
+    "trx_attn_decode_f32cache", "trx_matvec_f_rows", "trx_embed_lookup_rows", "trx_rmsnorm_rows", "trx_silu_mul",
+    "trx_argmax_rows", "trx_advance_positions", "trx_attn_decode_rows", "trx_deltanet_step_rows",
 )
 
 TP_MAX = 8
@@ -130,7 +131,17 @@ def lib():
             "trx_rmsnorm": ([_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_float, _vp, _vp], ctypes.c_int),
             "trx_matvec_f_kseg": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
             "trx_attn_decode_f32cache": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
-            "trx_matvec_f_rows": ([_vp, E, _vp, _vp, ctypes.c_int, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f_rows": ([_vp, E, _vp, _vp, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
+            "trx_embed_lookup_rows": ([_vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32, _vp, ctypes.c_int32,
+                                       _vp, _vp], ctypes.c_int),
+            "trx_rmsnorm_rows": ([_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_float, _vp, _vp],
+                                 ctypes.c_int),
+            "trx_silu_mul": ([_vp, _vp, _vp, ctypes.c_uint64, _vp, _vp], ctypes.c_int),
+            "trx_argmax_rows": ([_vp, _vp, ctypes.c_uint32, ctypes.c_int32, _vp, _vp], ctypes.c_int),
+            "trx_advance_positions": ([_vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp], ctypes.c_int),
+            "trx_attn_decode_rows": ([_vp, ctypes.POINTER(AttnShape), ctypes.c_int32] + [_vp] * 11, ctypes.c_int),
+            "trx_deltanet_step_rows": ([_vp, ctypes.POINTER(DeltaNetShape), ctypes.c_int32] + [_vp] * 13,
+                                       ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

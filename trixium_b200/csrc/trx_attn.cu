@@ -78,6 +78,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x, kh = blockIdx.y;
+    if (blockIdx.z) {  // sequence z of a batch: its own inputs, cache, position, output and scratch
+        const long long z = blockIdx.z;
+        A.q += z * A.q_bs;
+        A.k += z * A.kv_bs;
+        A.v += z * A.kv_bs;
+        A.kc = reinterpret_cast<__half *>(reinterpret_cast<CT *>(A.kc) + z * A.cache_bs);
+        A.vc = reinterpret_cast<__half *>(reinterpret_cast<CT *>(A.vc) + z * A.cache_bs);
+        A.pos += z;
+        A.out += z * A.out_bs;
+        A.part += z * A.part_bs;
+        A.cnt += z * A.Hkv;
+    }
     const int hd = A.hd, rep = A.H / A.Hkv, chunk = A.chunk;
     pdl_trigger();
     pdl_wait();
@@ -1080,8 +1092,8 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
                                         226 * 1024);
         });
         if (e != cudaSuccess) return note_cuda(e);
-        return note_cuda(
-            launch_kernel(attn_decode_kernel<float>, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
+        return note_cuda(launch_kernel(attn_decode_kernel<float>, dim3(A.nsplit, A.Hkv, A.nseq > 0 ? A.nseq : 1),
+                                       dim3(kAttnThreads), smem, st, A, err));
     }
     static DevBits configured{0};
     const cudaError_t e = once_per_device(configured, [] {
@@ -1089,8 +1101,8 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
                                     226 * 1024);
     });
     if (e != cudaSuccess) return note_cuda(e);
-    return note_cuda(
-        launch_kernel(attn_decode_kernel<__half>, dim3(A.nsplit, A.Hkv), dim3(kAttnThreads), smem, st, A, err));
+    return note_cuda(launch_kernel(attn_decode_kernel<__half>, dim3(A.nsplit, A.Hkv, A.nseq > 0 ? A.nseq : 1),
+                                   dim3(kAttnThreads), smem, st, A, err));
 }
 
 }  // namespace trx

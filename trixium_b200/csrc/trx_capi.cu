@@ -31,8 +31,8 @@ struct trx_ctx {
     unsigned *rows_cnt;
 };
 
-static const uint64_t kAttnPartFloats = 1ull << 22;  // 16 MiB of attention partials
-static const uint32_t kAttnMaxKv = 1024;
+static const uint64_t kAttnPartFloats = 1ull << 24;  // 64 MiB of attention partials (batches of sequences)
+static const uint32_t kAttnMaxKv = 4096;  // arrival counts: kv heads (or value heads) x sequences
 static const int kMaxArgmaxJobs = 64;
 static const uint32_t kQ8MaxCols = 32768;
 static const uint64_t kKsegPartInts = 1ull << 20;  // 4 MiB of K-segment partial results
@@ -218,20 +218,50 @@ trx_status trx_matvec_q8_f(trx_ctx *ctx, const trx_entry *e, const void *d_packe
 }
 
 static trx_status rows_tc(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, const int8_t *d_x8,
-                          int nb, int32_t *d_out_i, float *d_out_f, cudaStream_t stream) {
+                          int nb, int32_t *d_out_i, float *d_out_f, const float *d_resid, cudaStream_t stream) {
     return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->kind,
                                    e->bias, e->rshift, d_x, d_x8, nb, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8,
-                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsTiles, d_out_i, d_out_f, ctx->err,
-                                   trx::device_sms(), trx::device_reserved_smem(), stream);
+                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsTiles, d_out_i, d_out_f, d_resid,
+                                   ctx->err, trx::device_sms(), trx::device_reserved_smem(), stream);
 }
 
 trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, int nb,
-                             float *d_y, cudaStream_t stream) {
+                             const float *d_resid, float *d_y, cudaStream_t stream) {
     if (!ctx) return TRX_ERR_ARG;
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x || !d_y || nb < 1 || nb > kRowsMax || !aligned16(d_packed)) return TRX_ERR_ARG;
-    return rows_tc(ctx, e, d_packed, d_x, nullptr, nb, nullptr, d_y, stream);
+    return rows_tc(ctx, e, d_packed, d_x, nullptr, nb, nullptr, d_y, d_resid, stream);
+}
+
+trx_status trx_embed_lookup_rows(trx_ctx *ctx, const void *d_table, uint32_t vocab, uint32_t dim, int32_t f16,
+                                 const int32_t *d_tokens, int32_t nrows, float *d_x, cudaStream_t stream) {
+    if (!ctx || !d_table || !d_tokens || !d_x || vocab == 0 || dim == 0 || nrows < 1 || nrows > 65535)
+        return TRX_ERR_ARG;
+    return trx::launch_embed_rows(d_table, (int)vocab, (int)dim, f16 ? 1 : 0, d_tokens, nrows, d_x, ctx->err, stream);
+}
+
+trx_status trx_rmsnorm_rows(trx_ctx *ctx, const float *d_x, const float *d_w, uint32_t n, int32_t nrows, float eps,
+                            float *d_y, cudaStream_t stream) {
+    if (!ctx || !d_x || !d_w || !d_y || n == 0 || n > (1u << 24) || nrows < 1 || !(eps >= 0.f)) return TRX_ERR_ARG;
+    return trx::launch_rmsnorm_rows(d_x, d_w, (int)n, nrows, eps, d_y, stream);
+}
+
+trx_status trx_silu_mul(trx_ctx *ctx, const float *d_g, const float *d_u, uint64_t n, float *d_act,
+                        cudaStream_t stream) {
+    if (!ctx || !d_g || !d_u || !d_act || n == 0) return TRX_ERR_ARG;
+    return trx::launch_silu_mul(d_g, d_u, (long long)n, d_act, stream);
+}
+
+trx_status trx_argmax_rows(trx_ctx *ctx, const float *d_logits, uint32_t V, int32_t nrows, int32_t *d_tokens,
+                           cudaStream_t stream) {
+    if (!ctx || !d_logits || !d_tokens || V == 0 || nrows < 1) return TRX_ERR_ARG;
+    return trx::launch_argmax_rows(d_logits, (int)V, nrows, d_tokens, stream);
+}
+
+trx_status trx_advance_positions(trx_ctx *ctx, int32_t *d_pos, int32_t count, int32_t n, cudaStream_t stream) {
+    if (!ctx || !d_pos || count < 1) return TRX_ERR_ARG;
+    return trx::launch_advance_rows(d_pos, count, n, stream);
 }
 
 trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const int8_t *d_x8, int nb,
@@ -240,7 +270,7 @@ trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_pa
     trx_status s = check_entry(e);
     if (s) return s;
     if (!d_packed || !d_x8 || !d_out || nb < 1 || nb > kRowsMax || !aligned16(d_packed)) return TRX_ERR_ARG;
-    if (nb > 8) return rows_tc(ctx, e, d_packed, nullptr, d_x8, nb, d_out, nullptr, stream);
+    if (nb > 8) return rows_tc(ctx, e, d_packed, nullptr, d_x8, nb, d_out, nullptr, nullptr, stream);
     trx::MvJobs J = base_jobs(ctx, e, d_packed);
     J.x8 = d_x8;
     J.x_stride = e->cols;
@@ -611,6 +641,26 @@ trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *sh, const floa
     return trx::launch_attn_decode(A, ctx->err, stream);
 }
 
+trx_status trx_attn_decode_rows(trx_ctx *ctx, const trx_attn_shape *sh, int32_t nseq, const float *d_q,
+                                const float *d_k, const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
+                                const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,
+                                float *d_out, cudaStream_t stream) {
+    trx::AttnArgs A;
+    if (trx_status s = attn_args(ctx, sh, d_q, d_k, d_v, d_qnorm_w, d_knorm_w, d_rope_freq, d_kcache, d_vcache, d_pos,
+                                 d_out, 2, A))
+        return s;
+    if (nseq < 1 || nseq > 65535) return TRX_ERR_ARG;
+    A.scratch_merge = 1;  // the kernel with a sequence dimension
+    A.nseq = nseq;
+    A.q_bs = (long long)A.H * A.qstride;
+    A.kv_bs = (long long)A.Hkv * A.hd;
+    A.cache_bs = (long long)A.max_pos * A.Hkv * A.hd;
+    A.out_bs = (long long)A.H * A.hd;
+    A.part_bs = (long long)A.Hkv * A.nsplit * (A.H / A.Hkv) * (A.hd + 2);
+    if ((uint64_t)nseq * A.part_bs > kAttnPartFloats || (uint64_t)nseq * A.Hkv > kAttnMaxKv) return TRX_ERR_UNSUPPORTED;
+    return trx::launch_attn_decode(A, ctx->err, stream);
+}
+
 trx_status trx_attn_decode_f32cache(trx_ctx *ctx, const trx_attn_shape *sh, const float *d_q, const float *d_k,
                                     const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
                                     const float *d_rope_freq, float *d_kcache, float *d_vcache, const int32_t *d_pos,
@@ -628,7 +678,16 @@ trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, const f
                              const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
                              float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
                              cudaStream_t stream) {
-    if (!ctx || !sh) return TRX_ERR_ARG;
+    return trx_deltanet_step_rows(ctx, sh, 1, d_qkv, d_z, d_beta, d_alpha, d_dt_bias, d_ssm_a, d_conv_w, d_norm_w,
+                                  d_conv_ring, d_state, d_pos, d_out, stream);
+}
+
+trx_status trx_deltanet_step_rows(trx_ctx *ctx, const trx_deltanet_shape *sh, int32_t nseq, const float *d_qkv,
+                                  const float *d_z, const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                                  const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                                  float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                                  cudaStream_t stream) {
+    if (!ctx || !sh || nseq < 1 || nseq > 65535) return TRX_ERR_ARG;
     const uint32_t nk = sh->n_k_heads, hk = sh->k_head_dim, nv = sh->n_v_heads, hv = sh->v_head_dim;
     const uint32_t K = sh->conv_kernel;
     if (nk == 0 || nv == 0 || nv % nk || nv > kAttnMaxKv) return TRX_ERR_ARG;
@@ -637,16 +696,17 @@ trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, const f
     if (!d_qkv || !d_z || !d_beta || !d_alpha || !d_dt_bias || !d_ssm_a || !d_conv_w || !d_norm_w || !d_conv_ring ||
         !d_state || !d_pos || !d_out)
         return TRX_ERR_ARG;
-    if ((uint64_t)nv * hv > kAttnPartFloats) return TRX_ERR_UNSUPPORTED;
+    if ((uint64_t)nseq * nv * hv > kAttnPartFloats || (uint64_t)nseq * nv > kAttnMaxKv) return TRX_ERR_UNSUPPORTED;
     trx::DnArgs A{};
+    A.nseq = nseq;
     A.nk = (int)nk;
     A.hk = (int)hk;
     A.nv = (int)nv;
     A.hv = (int)hv;
     A.K = (int)K;
     A.C = (int)(2 * nk * hk + nv * hv);
-    // Rows per CTA: about two CTAs per SM over all heads, at least 8 rows each.
-    int nsplit = (int)((2 * 148 + nv - 1) / nv);
+    // Rows per CTA: about two CTAs per SM over all heads and sequences, at least 8 rows each.
+    int nsplit = (int)((2 * 148 + (uint64_t)nv * nseq - 1) / ((uint64_t)nv * nseq));
     int rows = (int)((hv + nsplit - 1) / nsplit);
     if (rows < 8) rows = 8;
     A.rows = rows;

@@ -56,6 +56,19 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_kernel(DnArgs A, uint32_t
     extern __shared__ __align__(16) float dsm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x, h = blockIdx.y;
+    if (blockIdx.z) {  // sequence z of a batch
+        const long long z = blockIdx.z, vh = (long long)A.nv * A.hv;
+        A.qkv += z * A.C;
+        A.z += z * vh;
+        A.beta += z * A.nv;
+        A.alpha += z * A.nv;
+        A.pos += z;
+        A.win += z * (long long)A.K * A.C;
+        A.S += z * vh * A.hk;
+        A.out += z * vh;
+        A.part += z * vh;
+        A.cnt += z * A.nv;
+    }
     const int hk = A.hk, hv = A.hv, nk = A.nk, nq = A.nk * A.hk;
     pdl_trigger();
     pdl_wait();
@@ -168,7 +181,8 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_kernel(DnArgs A, uint32_t
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st) {
     const size_t smem = (size_t)(2 * A.hk + (A.rows > A.hv ? A.rows : A.hv)) * 4;
-    return note_cuda(launch_kernel(deltanet_kernel, dim3(A.nsplit, A.nv), dim3(kDnThreads), smem, st, A, err));
+    return note_cuda(launch_kernel(deltanet_kernel, dim3(A.nsplit, A.nv, A.nseq > 1 ? A.nseq : 1), dim3(kDnThreads),
+                                   smem, st, A, err));
 }
 
 }  // namespace trx

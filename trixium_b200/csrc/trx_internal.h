@@ -126,6 +126,11 @@ struct AttnArgs {
     int merge_own;      // cluster kernel: the merge area has its own shared region
     int scratch_merge;  // run the scratch-merge kernel on part/cnt even where a cluster kernel applies
     int f32cache;       // kc/vc hold fp32 elements (the scratch-merge kernel only)
+    // Independent sequences (the scratch-merge kernel: blockIdx.z = sequence; 0 for one): elements
+    // between sequences of q, k/v, the caches, the output and the partials; pos and the arrival
+    // counts are per sequence (pos + z, cnt + z * Hkv).
+    long long q_bs, kv_bs, cache_bs, out_bs, part_bs;
+    int nseq;
     TpXfer tp;          // tensor-parallel exchange of the output (tp.world == 0: none)
     float eps, scale;
 };
@@ -143,6 +148,8 @@ struct DnArgs {
     unsigned *cnt;      // [nv] arrival counts, zero between launches
     int nk, hk, nv, hv, K, C, rows, nsplit;
     float eps, scale;
+    int nseq;           // independent sequences (blockIdx.z; 0 or 1: one), each with its own
+                        // inputs, ring, state, position, output, partials and counts
 };
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
@@ -152,6 +159,12 @@ int attn_chunk(int max_pos, int hd, int esize);
 trx_status launch_embed(const void *table, int vocab, int dim, int f16, const int *token, float *x, uint32_t *err,
                         cudaStream_t st);
 trx_status launch_advance(int *pos, int n, cudaStream_t st);
+trx_status launch_embed_rows(const void *table, int vocab, int dim, int f16, const int *tokens, int nrows, float *x,
+                             uint32_t *err, cudaStream_t st);
+trx_status launch_rmsnorm_rows(const float *x, const float *w, int n, int nrows, float eps, float *y, cudaStream_t st);
+trx_status launch_silu_mul(const float *g, const float *u, long long n, float *act, cudaStream_t st);
+trx_status launch_argmax_rows(const float *logits, int V, int nrows, int *tokens, cudaStream_t st);
+trx_status launch_advance_rows(int *pos, int count, int n, cudaStream_t st);
 trx_status launch_embed_bfp16(const int16_t *mant, const int *exps, int vocab, int dim, const int *token, float *x,
                               uint32_t *err, cudaStream_t st);
 trx_status launch_rmsnorm(const float *x, const float *w, int n, float eps, float *y, cudaStream_t st);
@@ -166,8 +179,8 @@ trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cu
 // nb*K/128 ints, nb ints; acc_scratch (acc_cap int64) and cnt (cnt_cap) zero between launches.
 trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, int R, const float *x, const int8_t *x8,
                               int nb, int8_t *x8p, int *xsum, int *e8, unsigned long long *acc_scratch,
-                              size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f, uint32_t *err,
-                              int sms, int reserved, cudaStream_t st);
+                              size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f,
+                              const float *resid, uint32_t *err, int sms, int reserved, cudaStream_t st);
 int device_sms();
 int device_reserved_smem();
 // The Q8 row dot (trx_q8.cu): int32 results, or with e8 the float projection (fp32 out).

@@ -191,6 +191,7 @@ struct RowsArgs {
     const int *e8;            // [nb] (float outputs)
     int32_t *out_i;           // [nb][N] int32, or
     float *out_f;             // [nb][N] fp32
+    const float *resid;       // [nb][N] added to the fp32 results, or nullptr
     unsigned long long *acc;  // [nb][N] int64 partial sums (ks > 1), zero between launches
     unsigned *cnt;            // [tiles] arrival counts (ks > 1), zero between launches
     RowsPlan P;
@@ -503,9 +504,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     auto finish = [&](int b, long long a) {
         if (acc_bad(a, A.R)) atomicOr(err, TRX_DEV_OVERFLOW);
         const int res = (int)(a >> A.R);
-        if (A.out_f)
-            A.out_f[(size_t)b * A.N + n] = __fmul_rn((float)res, pow2f(A.e8[b] + A.R - A.B));
-        else
+        if (A.out_f) {
+            float v = __fmul_rn((float)res, pow2f(A.e8[b] + A.R - A.B));
+            if (A.resid) v = __fadd_rn(A.resid[(size_t)b * A.N + n], v);
+            A.out_f[(size_t)b * A.N + n] = v;
+        } else
             A.out_i[(size_t)b * A.N + n] = res;
     };
     if (A.ks == 1) {
@@ -595,8 +598,8 @@ static trx_status launch_rows_t(const RowsMaps &maps, const RowsArgs &A, int gri
 
 trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, int R, const float *x, const int8_t *x8,
                               int nb, int8_t *x8p, int *xsum, int *e8, unsigned long long *acc_scratch,
-                              size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f, uint32_t *err,
-                              int sms, int reserved, cudaStream_t st) {
+                              size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f,
+                              const float *resid, uint32_t *err, int sms, int reserved, cudaStream_t st) {
     const int BN = nb <= 16 ? 16 : 32;
     RowsArgs A{};
     A.N = N;
@@ -621,6 +624,7 @@ trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, i
     A.e8 = e8;
     A.out_i = out_i;
     A.out_f = out_f;
+    A.resid = resid;
     A.acc = acc_scratch;
     A.cnt = cnt;
     A.base = reserved;

@@ -16,6 +16,8 @@ __global__ void embed_kernel(const void *table, int vocab, int dim, int f16, con
                              uint32_t *err) {
     pdl_trigger();
     pdl_wait();
+    token += blockIdx.y;  // row y of a batch: its token and output row
+    x += (size_t)blockIdx.y * dim;
     const int t = *token;
     const bool ok = t >= 0 && t < vocab;
     if (!ok && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, TRX_DEV_RANGE);
@@ -49,6 +51,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
     __shared__ float part[64];
     pdl_trigger();
     pdl_wait();
+    x += (size_t)blockIdx.x * n;  // one CTA per row
+    y += (size_t)blockIdx.x * n;
     const int t = threadIdx.x;
     if (t < 64) {
         float p = 0.f;
@@ -62,6 +66,48 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
     }
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(part[0], (float)n), eps)));
     for (int i = t; i < n; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], r), w[i]);
+}
+
+// act = silu(g) * u elementwise (model/mirror.py:713,1020: x / (1 + exp(-x)) in fp32, mathematical
+// profile), as the SwiGLU epilogue of the matvec kernel computes it.
+__global__ void silu_mul_kernel(const float *g, const float *u, long long n, float *act) {
+    pdl_trigger();
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        act[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]);
+    }
+}
+
+// Per row of logits [nrows][V]: the index of the largest value, ties to the smallest index (the
+// greedy token, model/mirror.py:1031; doc/units.md:149).  One CTA per row.
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float *logits, int V, int *tokens) {
+    __shared__ unsigned long long best_s[8];
+    pdl_trigger();
+    pdl_wait();
+    const float *l = logits + (size_t)blockIdx.x * V;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long k = argmax_key(l[i], (uint32_t)i);
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+    }
+    if ((threadIdx.x & 31) == 0) best_s[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) best = best_s[w] > best ? best_s[w] : best;
+        tokens[blockIdx.x] = best ? (int)(0xffffffffu - (uint32_t)best) : -1;
+    }
+}
+
+__global__ void advance_rows_kernel(int *pos, int count, int n) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) pos[i] += n;
 }
 
 // The float result of a K-segmented projection (model/mirror.py:664-678): the segments' int32
@@ -102,6 +148,32 @@ trx_status launch_embed(const void *table, int vocab, int dim, int f16, const in
                         cudaStream_t st) {
     const int blocks = (dim + 255) / 256 < 16 ? (dim + 255) / 256 : 16;
     return note_cuda(launch_kernel(embed_kernel, dim3(blocks), dim3(256), 0, st, table, vocab, dim, f16, token, x, err));
+}
+
+trx_status launch_embed_rows(const void *table, int vocab, int dim, int f16, const int *tokens, int nrows, float *x,
+                             uint32_t *err, cudaStream_t st) {
+    const int blocks = (dim + 255) / 256 < 16 ? (dim + 255) / 256 : 16;
+    return note_cuda(
+        launch_kernel(embed_kernel, dim3(blocks, nrows), dim3(256), 0, st, table, vocab, dim, f16, tokens, x, err));
+}
+
+trx_status launch_rmsnorm_rows(const float *x, const float *w, int n, int nrows, float eps, float *y,
+                               cudaStream_t st) {
+    return note_cuda(launch_kernel(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, x, w, n, eps, y));
+}
+
+trx_status launch_silu_mul(const float *g, const float *u, long long n, float *act, cudaStream_t st) {
+    long long blocks = (n + 255) / 256;
+    if (blocks > 1184) blocks = 1184;
+    return note_cuda(launch_kernel(silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0, st, g, u, n, act));
+}
+
+trx_status launch_argmax_rows(const float *logits, int V, int nrows, int *tokens, cudaStream_t st) {
+    return note_cuda(launch_kernel(argmax_rows_kernel, dim3(nrows), dim3(256), 0, st, logits, V, tokens));
+}
+
+trx_status launch_advance_rows(int *pos, int count, int n, cudaStream_t st) {
+    return note_cuda(launch_kernel(advance_rows_kernel, dim3((count + 255) / 256), dim3(256), 0, st, pos, count, n));
 }
 
 trx_status launch_embed_bfp16(const int16_t *mant, const int *exps, int vocab, int dim, const int *token, float *x,

@@ -145,15 +145,70 @@ def matvec_i8_rows(ctx, w: DeviceTensor, x8rows, out=None):
     return out
 
 
-def matvec_f_rows(ctx, w: DeviceTensor, xrows, out=None):
+def matvec_f_rows(ctx, w: DeviceTensor, xrows, out=None, resid=None):
     """Batched float projection (trx_matvec_f_rows): xrows [nb, K] float32 (nb <= 32), each row
-    quantised with its own exponent, on the tensor cores; returns [nb, rows] float32."""
+    quantised with its own exponent, on the tensor cores; returns [nb, rows] float32 (plus resid)."""
     _need(xrows, torch.float32, "xrows")
     nb = xrows.shape[0]
     if out is None:
         out = torch.empty(nb, w.rows, dtype=torch.float32, device=xrows.device)
-    _lib.check(_lib.lib().trx_matvec_f_rows(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(xrows), nb, _ptr(out),
-                                            _stream()), "trx_matvec_f_rows")
+    if resid is not None:
+        _need(resid, torch.float32, "resid")
+    _lib.check(_lib.lib().trx_matvec_f_rows(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(xrows), nb, _ptr(resid),
+                                            _ptr(out), _stream()), "trx_matvec_f_rows")
+    return out
+
+
+def embed_lookup_rows(ctx, table, tokens, x):
+    """x[r] = table[tokens[r]] for every row r (fp16 or fp32 table [vocab, dim])."""
+    _need(tokens, torch.int32, "tokens")
+    _need(x, torch.float32, "x")
+    f16 = table.dtype == torch.float16
+    _lib.check(_lib.lib().trx_embed_lookup_rows(ctx.h, _ptr(table), table.shape[0], table.shape[1], 1 if f16 else 0,
+                                                _ptr(tokens), tokens.numel(), _ptr(x), _stream()),
+               "trx_embed_lookup_rows")
+    return x
+
+
+def rmsnorm_rows(ctx, x, w, eps=1e-6, y=None):
+    """Row-wise RMSNorm of x [nrows, n] (trx_rmsnorm_rows)."""
+    _need(x, torch.float32, "x")
+    if y is None:
+        y = torch.empty_like(x)
+    _lib.check(_lib.lib().trx_rmsnorm_rows(ctx.h, _ptr(x), _ptr(w), x.shape[-1], x.numel() // x.shape[-1],
+                                           ctypes.c_float(eps), _ptr(y), _stream()), "trx_rmsnorm_rows")
+    return y
+
+
+def silu_mul(ctx, g, u, act=None):
+    if act is None:
+        act = torch.empty_like(g)
+    _lib.check(_lib.lib().trx_silu_mul(ctx.h, _ptr(g), _ptr(u), g.numel(), _ptr(act), _stream()), "trx_silu_mul")
+    return act
+
+
+def argmax_rows(ctx, logits, tokens):
+    _need(logits, torch.float32, "logits")
+    _lib.check(_lib.lib().trx_argmax_rows(ctx.h, _ptr(logits), logits.shape[-1], logits.numel() // logits.shape[-1],
+                                          _ptr(tokens), _stream()), "trx_argmax_rows")
+    return tokens
+
+
+def advance_positions(ctx, pos, n=1):
+    _need(pos, torch.int32, "pos")
+    _lib.check(_lib.lib().trx_advance_positions(ctx.h, _ptr(pos), pos.numel(), n, _stream()), "trx_advance_positions")
+
+
+def attn_decode_rows(ctx, shape, q, k, v, q_norm, k_norm, rope_freq, kcache, vcache, pos, out=None):
+    """Decode attention for a batch of independent sequences (trx_attn_decode_rows): q [nseq, ...],
+    caches [nseq, max_pos, n_kv, hd] fp16, pos [nseq] int32."""
+    nseq = pos.numel()
+    _need(kcache, torch.float16, "kcache")
+    if out is None:
+        out = torch.empty(nseq, shape.n_head * shape.head_dim, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().trx_attn_decode_rows(ctx.h, ctypes.byref(shape), nseq, _ptr(q), _ptr(k), _ptr(v),
+                                               _ptr(q_norm), _ptr(k_norm), _ptr(rope_freq), _ptr(kcache),
+                                               _ptr(vcache), _ptr(pos), _ptr(out), _stream()), "trx_attn_decode_rows")
     return out
 
 
@@ -436,6 +491,20 @@ def deltanet_step(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, norm_
     _lib.check(_lib.lib().trx_deltanet_step(ctx.h, ctypes.byref(shape), _ptr(qkv), _ptr(z), _ptr(beta), _ptr(alpha),
                                             _ptr(dt_bias), _ptr(ssm_a), _ptr(conv_w), _ptr(norm_w), _ptr(conv_ring),
                                             _ptr(state), _ptr(pos), _ptr(out), _stream()), "trx_deltanet_step")
+    return out
+
+
+def deltanet_step_rows(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, norm_w, conv_ring, state, pos,
+                       out=None):
+    """The gated-DeltaNet step of a batch of sequences (trx_deltanet_step_rows): every per-sequence
+    tensor has a leading sequence dimension; pos [nseq] int32."""
+    nseq = pos.numel()
+    if out is None:
+        out = torch.empty(nseq, shape.n_v_heads * shape.v_head_dim, dtype=torch.float32, device=qkv.device)
+    _lib.check(_lib.lib().trx_deltanet_step_rows(ctx.h, ctypes.byref(shape), nseq, _ptr(qkv), _ptr(z), _ptr(beta),
+                                                 _ptr(alpha), _ptr(dt_bias), _ptr(ssm_a), _ptr(conv_w), _ptr(norm_w),
+                                                 _ptr(conv_ring), _ptr(state), _ptr(pos), _ptr(out), _stream()),
+               "trx_deltanet_step_rows")
     return out
 
 
