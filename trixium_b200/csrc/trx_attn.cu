@@ -714,6 +714,23 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
     }
     for (int i = tid; i < A.rope_half; i += kClThreads) cp4(cf + i, A.freq + i);
     asm volatile("cp.async.commit_group;" ::: "memory");
+    // The K/V rows of the whole chunk (within the cache) are staged before the dependency wait: the
+    // rows before the current position were written by earlier decode steps, which completed before
+    // any kernel of this step started; row pos (this step's) and the rows after it are replaced or
+    // masked below.  The copies overlap the predecessor's tail.
+    const int t0 = s * chunk;
+    const int stride_t = A.Hkv * HD;
+    constexpr int lp = HD == 64 ? 3 : 4;  // log2(HD / 8)
+    {
+        const int nmax = max(0, min(chunk, A.max_pos - t0));
+        for (int i = tid; i < (nmax << lp); i += kClThreads) {
+            const int t = i >> lp, j = i & ((1 << lp) - 1);
+            const size_t gix = (size_t)(t0 + t) * stride_t + (size_t)kh * HD + 8 * j;
+            cp16_attn(kt + t * rowk + 8 * j, A.kc + gix);
+            cp16_attn(vt + t * rowk + 8 * j, A.vc + gix);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     pdl_wait();
     const int pos = *A.pos;
     if (pos < 0 || pos >= A.max_pos) {  // every CTA reads the same position: all leave together
@@ -721,28 +738,10 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         return;
     }
-    const int t0 = s * chunk;
     const int n = max(0, min(chunk, pos + 1 - t0));
     const int nb16 = (n + 15) >> 4;  // 16-position blocks in use
     const bool owner = pos >= t0 && pos < t0 + chunk;
-    const int stride_t = A.Hkv * HD;
-    {
-        constexpr int lp = HD == 64 ? 3 : 4;  // log2(HD / 8)
-        for (int i = tid; i < (n << lp); i += kClThreads) {
-            const int t = i >> lp, j = i & ((1 << lp) - 1);
-            if (t0 + t == pos) continue;  // written below by this CTA
-            const size_t gix = (size_t)(t0 + t) * stride_t + (size_t)kh * HD + 8 * j;
-            cp16_attn(kt + t * rowk + 8 * j, A.kc + gix);
-            cp16_attn(vt + t * rowk + 8 * j, A.vc + gix);
-        }
-        // Rows [n, 16*nb16) of the last block: zero (their scores are masked; P.V must see 0).
-        for (int i = tid; i < ((16 * nb16 - n) << lp); i += kClThreads) {
-            const int t = n + (i >> lp), j = i & ((1 << lp) - 1);
-            *reinterpret_cast<uint4 *>(kt + t * rowk + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4 *>(vt + t * rowk + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
-        }
-    }
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncthreads();  // the norm weights and frequencies are visible
     if (n > 0) {
         for (int r = warp; r < rep; r += NWARP) {
@@ -759,20 +758,32 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
             __syncwarp();
             head_rmsnorm_s(knew, HD, ck, A.eps, lane);
             head_rope_s(knew, A.rope_half, cf, pos, lane);
-            const int tp = pos - t0;
             __half *kc = A.kc + (size_t)pos * stride_t + (size_t)kh * HD;
             __half *vc = A.vc + (size_t)pos * stride_t + (size_t)kh * HD;
             const float *vg = A.v + (size_t)kh * HD;
             for (int i = lane; i < HD; i += 32) {
-                const __half k16 = __float2half_rn(knew[i]), v16 = __float2half_rn(vg[i]);
-                kc[i] = k16;
-                vc[i] = v16;
-                kt[tp * rowk + i] = k16;
-                vt[tp * rowk + i] = v16;
+                kc[i] = __float2half_rn(knew[i]);
+                vc[i] = __float2half_rn(vg[i]);
             }
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // the staged rows have landed
+    // Rows [n, 16*nb16) of the last block: zero (their scores are masked; P.V must see 0).  The
+    // owner puts the new row into its tiles.
+    for (int i = tid; i < ((16 * nb16 - n) << lp); i += kClThreads) {
+        const int t = n + (i >> lp), j = i & ((1 << lp) - 1);
+        *reinterpret_cast<uint4 *>(kt + t * rowk + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4 *>(vt + t * rowk + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (n > 0 && owner && warp == NWARP - 1) {
+        const int tp = pos - t0;
+        const float *vg = A.v + (size_t)kh * HD;
+        for (int i = lane; i < HD; i += 32) {
+            kt[tp * rowk + i] = __float2half_rn(knew[i]);
+            vt[tp * rowk + i] = __float2half_rn(vg[i]);
+        }
+    }
     __syncthreads();  // K/V tiles and queries ready
 
     // Per warp: blocks warp, warp + NWARP, ...  Lane (g, c): head row g; the running max and sum of

@@ -381,8 +381,10 @@ __device__ int build_activation_cp(const float *x, const float *nw, bool nw_read
     const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5, nwarps = blockDim.x >> 5;
     const int G = K / 128, n4 = K / 4;
     float4 *const xs4 = reinterpret_cast<float4 *>(xs);
-    // One bulk copy each (tracked by its own barrier, not by the weight rings' cp.async groups);
-    // thread 0 waits, bounded, and the block learns the outcome at the barrier.
+    // One bulk copy each (tracked by its own barrier, not by the weight rings' barriers); thread 0
+    // waits, bounded, and the block learns the outcome at the barrier.  (Measured on B200 in decode
+    // launches: the bulk copy of x reaches the built activation sooner than coalesced loads by
+    // every thread.)
     uint32_t *const flag = reinterpret_cast<uint32_t *>(red64) + 48;
     if (ct == 0) {
         fence_proxy_async();  // earlier generic accesses to these bytes come first
