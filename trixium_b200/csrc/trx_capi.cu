@@ -23,7 +23,7 @@ struct trx_ctx {
     // trx_matvec_f_kseg: the segments' int32 engine results, [nseg][rows].
     int32_t *kseg_part;
     // Batched rows on the tensor cores: the permuted activation rows, their group sums and
-    // exponents; the K-split partial sums and tile arrival counts (zero between launches).
+    // exponents; the K-split partial sums and per-row arrival counts (zero between launches).
     int8_t *rows_x8p;
     int *rows_xsum;
     int *rows_e8;
@@ -38,7 +38,7 @@ static const uint32_t kQ8MaxCols = 32768;
 static const uint64_t kKsegPartInts = 1ull << 20;  // 4 MiB of K-segment partial results
 static const int kRowsMax = 32;                      // batch rows of the tensor-core path
 static const uint64_t kRowsAcc = 1ull << 19;          // int64 partial sums (4 MiB): nb * N of a K-split launch
-static const int kRowsTiles = 4096;                   // arrival counts (128-row tiles)
+static const int kRowsCnt = 1 << 19;                  // per-row arrival counts of a K-split launch (2 MiB)
 
 namespace trx {
 bool pdl_enabled() { return true; }
@@ -102,12 +102,12 @@ trx_status trx_create(trx_ctx **ctx, int device) {
         cudaMalloc(&c->q8x, kQ8MaxCols + 16) != cudaSuccess ||
         cudaMalloc(&c->kseg_part, kKsegPartInts * 4) != cudaSuccess ||
         cudaMalloc(&c->rows_x8p, (size_t)kRowsMax * kQ8MaxCols) != cudaSuccess ||
-        cudaMalloc(&c->rows_xsum, (size_t)kRowsMax * (kQ8MaxCols / 128) * 4) != cudaSuccess ||
+        cudaMalloc(&c->rows_xsum, (size_t)32 * (kQ8MaxCols / 128) * 4) != cudaSuccess ||
         cudaMalloc(&c->rows_e8, kRowsMax * 4) != cudaSuccess ||
         cudaMalloc(&c->rows_acc, kRowsAcc * 8) != cudaSuccess ||
         cudaMemset(c->rows_acc, 0, kRowsAcc * 8) != cudaSuccess ||
-        cudaMalloc(&c->rows_cnt, kRowsTiles * 4) != cudaSuccess ||
-        cudaMemset(c->rows_cnt, 0, kRowsTiles * 4) != cudaSuccess ||
+        cudaMalloc(&c->rows_cnt, kRowsCnt * 4) != cudaSuccess ||
+        cudaMemset(c->rows_cnt, 0, kRowsCnt * 4) != cudaSuccess ||
         trx::launch_build_lut(c->lut, 0) != TRX_OK ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(c->err);
@@ -221,7 +221,7 @@ static trx_status rows_tc(trx_ctx *ctx, const trx_entry *e, const void *d_packed
                           int nb, int32_t *d_out_i, float *d_out_f, const float *d_resid, cudaStream_t stream) {
     return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->kind,
                                    e->bias, e->rshift, d_x, d_x8, nb, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8,
-                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsTiles, d_out_i, d_out_f, d_resid,
+                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsCnt, d_out_i, d_out_f, d_resid,
                                    ctx->err, trx::device_sms(), trx::device_reserved_smem(), stream);
 }
 

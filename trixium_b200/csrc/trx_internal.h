@@ -176,7 +176,8 @@ trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token,
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 // Batched rows on the tensor cores (trx_rows.cu): nb <= 32 rows of x (fp32, each quantised with its
 // own exponent) or x8 (int8), int32 or fp32 outputs [nb][N].  x8p/xsum/e8: scratch of nb*K bytes,
-// nb*K/128 ints, nb ints; acc_scratch (acc_cap int64) and cnt (cnt_cap) zero between launches.
+// K/128*32 ints and nb ints; acc_scratch (acc_cap int64) and cnt (cnt_cap per-row counts) zero
+// between launches.
 trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, int R, const float *x, const int8_t *x8,
                               int nb, int8_t *x8p, int *xsum, int *e8, unsigned long long *acc_scratch,
                               size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f,

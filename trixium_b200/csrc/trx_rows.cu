@@ -1,31 +1,39 @@
 // Batched ternary matvec on the B200's 5th-generation tensor cores (sm_100a tcgen05, kind::i8):
-// nb independent int8 activation rows against one pass over a packed tensor, bit-exact with
+// nb <= 32 independent int8 activation rows against one pass over a packed tensor, bit-exact with
 // model/bitexact.py:121-125 (matvec_ternary_rows: every row is model/bitexact.py:101-119's
 // matvec_ternary), and the float form (each row quantised with its own exponent, model/mirror.py
 // :45-51 and :664-678).
 //
-// Per CTA: a tile of 128 output rows (the MMA's M) over a range of K chunks (4 groups of 128).
-//  * Codes and scales arrive by TMA boxes {chunk bytes, 128 rows} into a two-slot ring.
-//  * Each iteration handles a pair of groups: 256 threads, thread t decodes group (t >> 7) of the
-//    pair for row t & 127 into that group's A tile: 128 rows x 128 int8 codes in {0, 1, 2}, K-major
-//    with the 128-byte swizzle (a row's eight 16-byte pieces at piece ^ (row & 7)), written with
-//    16-byte stores.  trit5: a per-lane replicated 256-entry LUT of 8-byte entries (digits d0..d3 |
-//    d4), addressed with one PRMT per byte; 2-bit: the four bit planes of each code word.
-//  * The codes' K order is permuted within each group (all five digits of a trit5 byte are not four
-//    contiguous K slots); the activation is permuted the same way once per launch by the prep
-//    kernel (x8p), whose tiles arrive by TMA with the same swizzle: B = x8p rows, K-major.
-//  * One thread issues the pair's MMAs (M = 128, N = BN, K = 32; four per group) into the pair's
-//    TMEM buffer (int32, one BN-column block per group; two buffers) and commits them to an
-//    mbarrier; the MMAs of pair i overlap the epilogue of pair i - 1 and the decode of pair i + 1.
-//  * Epilogue: warps w and w + 4 read TMEM lanes 32 (w % 4) .. (the tile's rows), w / 4 picks the
-//    group; per (row, batch row) the exact group sum is the MMA's sum of codes * x8 minus sum(x8)
-//    (codes are 0, 1, 2 for w + 1), and the scale contribution (gs * m11) shifted by e16 + B is
-//    added in int64 (model/bitexact.py:111-115).
-//  * K split over ks CTAs per row tile when the tiles alone would leave SMs idle: partial int64
-//    sums added with 64-bit atomics (exact), the tile's last CTA applies >> R, the checks of
+// Work: a unit is (a tile of 128 output rows, a range of K chunks of 4 groups).  A persistent CTA
+// takes a contiguous range of units; its three decoder warpgroups take its units in turn, so each
+// warpgroup owns the 128 rows of its unit (one row per thread, the MMA's M = 128 TMEM lanes) and no
+// sums are exchanged between them.  Warp roles:
+//  * the last warp, one thread: the producer.  It streams each warpgroup's chunks, in one order all
+//    roles follow, through that warpgroup's ring of D / 3 shared-memory slots (TMA boxes: the chunk's
+//    codes and scales for the 128 rows, and the activation tiles of its groups, B = BN batch rows x
+//    128 int8, 128-byte swizzled), and refills a slot once the MMAs that read it are complete.
+//  * the decoder warpgroups.  Thread r decodes its row's group into the 128 int8 codes {0, 1, 2}
+//    (trit5: a per-lane replicated 256-entry LUT of 8-byte entries, digits d0..d3 | d4, addressed by
+//    one PRMT per byte; 2-bit: the four bit planes of each code word) and writes them straight into
+//    its warpgroup's A buffer in tensor memory (tcgen05.st, its own lane): the unpacked codes never
+//    touch shared memory.  Two A/D buffer pairs per warpgroup: the MMAs of a group run while the
+//    next one is decoded.  One warp of the warpgroup per chunk (in turn) issues, from one elected
+//    lane of the converged warp, the four MMAs of each of the chunk's groups (M = 128, N = BN,
+//    K = 32, A from tensor memory) once all four warps' rows are in, and commits them; a tcgen05.mma
+//    from a thread in a divergent branch issued at about 0.4x that rate (measured on B200).
+//  * The same threads read each group's result back (tcgen05.ld, BN int32 per row), subtract the
+//    group's activation sum (staged in shared memory; the codes are w + 1) and add the exact scale
+//    contribution (gs * m11) shifted by e16 + B in int64 (model/bitexact.py:111-115).
+//  * The codes' K order is permuted within each group (a trit5 byte's five digits are not four
+//    contiguous K slots); the prep kernel permutes the activation the same way (x8p) and writes the
+//    group sums.
+//  * A unit covering part of K adds its int64 partial sums with 64-bit atomics (exact in any order);
+//    each row's last unit (a per-row arrival count) applies >> R, the checks of
 //    model/bitexact.py:116,118 and the output, and leaves the scratch at zero.
-// Every wait (TMA, MMA completion) is bounded; on expiry TRX_DEV_TIMEOUT is recorded, the CTA
-// stops issuing, waits (bounded) for what it issued, frees its TMEM and returns.
+// Every wait (TMA, MMA completion, decoded buffer) is bounded; on expiry TRX_DEV_TIMEOUT is
+// recorded, every role stops, the producer waits (bounded) for what it armed, the tensor memory is
+// freed and the CTA returns.
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -38,20 +46,20 @@
 namespace trx {
 namespace {
 
-constexpr int kRowsM = 128;       // rows of a tile (the MMA's M)
-constexpr int kRowsThreads = 256;
-constexpr int kRowsCb5 = 112;     // trit5 codes box per row (the chunk's 104 bytes from the 16-byte boundary below)
-constexpr int kRowsCb2 = 144;     // 2-bit codes box per row (the chunk's 128 bytes and the next 16)
-constexpr int kRowsLut = 0x10000; // shared-window address of the LUT (64 KiB: 256 entries x 32 lanes x 8 bytes)
+constexpr int kRowsM = 128;                       // rows of a tile (the MMA's M, the TMEM lanes)
+constexpr int kRowsCb5 = 112;  // trit5 codes box per row (the chunk's 104 bytes from the 16-byte boundary below)
+constexpr int kRowsCb2 = 144;  // 2-bit codes box per row (the chunk's 128 bytes and the next 16)
+constexpr int kRowsLut = 0x10000;  // shared-window address of the LUT (64 KiB: 256 entries x 32 lanes x 8 bytes)
+constexpr int kRowsMaxD = 8;       // ring slots at most
+constexpr int kRowsTmemCols = 512; // per warpgroup A 2 x 32 and D 2 x BN columns
 
 // Shared-memory plan (offsets from the dynamic base, which sits at window address `reserved`).
 struct RowsPlan {
-    int slot;        // one code-ring slot: codes box, then scales box
-    int ring_off;    // 2 slots
-    int bt_off[3];   // the activation tiles of a pair (2 groups x BN rows x 128 bytes), 3 buffers
-    int misc_off;    // barriers, TMEM address, per-pair scales and activation sums
-    int lut_off;     // window 0x10000
-    int a_off;       // 2 buffers x 2 groups x 16 KiB, 1024-aligned
+    int D;                    // ring slots
+    int slot_off[kRowsMaxD];  // each slot: [activation tiles 4 x BN x 128][codes 128 x cb][scales 128 x 16]
+    int codes_off, scales_off;  // within a slot
+    int lut_off;              // trit5: window 0x10000
+    int xs_off;               // the activation's group sums [G][BN] int32
     int smem;
 };
 
@@ -66,23 +74,42 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
            ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
-// Instruction descriptor of kind::i8: D int32 (2), A unsigned 8-bit (0), B signed 8-bit (1), both
-// K-major, N >> 3, M >> 4.
+// Instruction descriptor of kind::i8: D int32 (2), A unsigned 8-bit (0: the codes 0, 1, 2), B signed
+// 8-bit (1), both K-major, N >> 3, M >> 4.
 template <int BN>
 __device__ __forceinline__ uint32_t umma_idesc_i8() {
     return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kRowsM >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+// D[tmem] (+)= A[tmem] * B[smem]^T: A in tensor memory (lane = row, 4 int8 K elements per column).
+__device__ __forceinline__ void umma_i8_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, int acc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// The same issued by one elected lane of a converged warp (all lanes execute it; warp-uniform
+// operands): measured on B200 about 2.5x the issue rate of a thread in a divergent branch.
+__device__ __forceinline__ void umma_i8_ta_elect(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                 int acc) {
+    asm volatile(
+        "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+        " @e tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_elect(uint32_t bar) {
+    asm volatile(
+        "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+        " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
+        : "memory");
 }
 
 // TMEM loads, one lane per thread: 16 consecutive 32-bit columns.
@@ -97,6 +124,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// TMEM store, one lane per thread: 32 consecutive 32-bit columns (a row's 128 int8 codes).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&o)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]), "r"(o[8]), "r"(o[9]),
+        "r"(o[10]), "r"(o[11]), "r"(o[12]), "r"(o[13]), "r"(o[14]), "r"(o[15]), "r"(o[16]), "r"(o[17]), "r"(o[18]),
+        "r"(o[19]), "r"(o[20]), "r"(o[21]), "r"(o[22]), "r"(o[23]), "r"(o[24]), "r"(o[25]), "r"(o[26]), "r"(o[27]),
+        "r"(o[28]), "r"(o[29]), "r"(o[30]), "r"(o[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // 2-D TMA load (no multicast) at element coordinates (x, y).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *map, int x, int y, uint32_t bar) {
     asm volatile(
@@ -104,6 +144,22 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *map, int x
         "[%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+
+// Non-blocking test of a phase (mbarrier.try_wait may suspend the thread for a while before it
+// reports an incomplete phase; a thread polling several barriers must not be held on one).
+__device__ __forceinline__ bool mbar_test_wait_s(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive_s(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // The 8-byte trit5 LUT entry of byte b: digits d0..d3 in the low word, d4 in byte 0 of the high
@@ -130,7 +186,8 @@ __host__ __device__ __forceinline__ int slot_lane(int kind, int s) {
 
 // Per batch row: the quantised activation (fp32 rows: the power-of-two quantiser with its own
 // exponent, model/mirror.py:45-51; int8 rows: as given), permuted per group to the decoders' K
-// order (x8p [nb][K]), and each group's activation sum (xsum [nb][G]).  One CTA per batch row.
+// order (x8p [nb][K]), and each group's activation sum (xsum [G][32], batch row minor).  One CTA per
+// batch row.
 __global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const int8_t *x8, int K, int kind,
                                                         int8_t *x8p, int *xsum, int *e8_out) {
     extern __shared__ int8_t q[];  // K bytes
@@ -166,17 +223,16 @@ __global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const in
         if (t == 0) e8_out[b] = 0;
     }
     __syncthreads();
-    const int G = K / 128;
     for (int i = t; i < K; i += blockDim.x) {
         const int g = i >> 7, s = i & 127;
         x8p[(size_t)b * K + i] = q[g * 128 + slot_lane(kind, s)];
     }
-    for (int g = t >> 5; g < G; g += blockDim.x >> 5) {
+    for (int g = t >> 5; g < K / 128; g += blockDim.x >> 5) {
         const int lane = t & 31;
         int s = 0;
         for (int j = lane; j < 128; j += 32) s += q[g * 128 + j];
         s = __reduce_add_sync(0xffffffffu, s);
-        if (lane == 0) xsum[(size_t)b * G + g] = s;
+        if (lane == 0) xsum[(size_t)g * 32 + b] = s;
     }
 }
 
@@ -186,8 +242,8 @@ __global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const in
 struct RowsArgs {
     int N, K, G, nch, sbytes, rb, kind, nb;
     int B, R;
-    int ks, cps;              // K splits per tile, chunks per split
-    const int *xsum;          // [nb][G]
+    int tiles, ks, cps;       // row tiles, K splits per tile, chunks per split (unit u: tile u / ks, split u % ks)
+    const int *xsum;          // [G][32]
     const int *e8;            // [nb] (float outputs)
     int32_t *out_i;           // [nb][N] int32, or
     float *out_f;             // [nb][N] fp32
@@ -204,10 +260,10 @@ struct RowsMaps {
 
 namespace {
 
-// Decode one trit5 group (its 26 bytes from byte OFF of the row's 112-byte window) into 32 words
-// of codes in the slot order above, and store them as the row's 128-byte A row (swizzled).
+// Decode one trit5 group (its 26 bytes from byte OFF of the row's 112-byte window) into 32 words of
+// codes in the slot order above.
 template <int OFF>
-__device__ __forceinline__ void decode_t5(const unsigned char *win, uint32_t lane8x, unsigned char *arow, int r) {
+__device__ __forceinline__ void decode_t5(const unsigned char *win, uint32_t lane8x, uint32_t (&o)[32]) {
     constexpr int p0 = OFF / 16, p1 = (OFF + 25) / 16;  // 16-byte pieces holding the group
     uint32_t w[12];
 #pragma unroll
@@ -218,37 +274,82 @@ __device__ __forceinline__ void decode_t5(const unsigned char *win, uint32_t lan
         w[4 * (p - p0) + 2] = v.z;
         w[4 * (p - p0) + 3] = v.w;
     }
-    uint32_t E[26], F[26];
+    uint32_t F[26];
 #pragma unroll
     for (int i = 0; i < 26; ++i) {
         const int pb = OFF - 16 * p0 + i;  // byte of w (compile time)
         // 0x10000 + byte * 256 + lane * 8: this lane's replica of the 8-byte entry.
         const uint32_t a = __byte_perm(w[pb >> 2], lane8x, 0x7604u | ((pb & 3) << 4));
-        asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(E[i]), "=r"(F[i]) : "r"(a));
+        uint32_t e;
+        asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(e), "=r"(F[i]) : "r"(a));
+        if (i < 25)
+            o[i] = e;
+        else
+            o[25] = __byte_perm(e, F[24], 0x4210u);  // digits 0..2 of byte 25, digit 4 of byte 24
     }
-    uint32_t o[32];
-#pragma unroll
-    for (int i = 0; i < 25; ++i) o[i] = E[i];
-    o[25] = __byte_perm(E[25], F[24], 0x4210u);  // digits 0..2 of byte 25, digit 4 of byte 24
 #pragma unroll
     for (int j = 0; j < 6; ++j)
         o[26 + j] = __byte_perm(__byte_perm(F[4 * j], F[4 * j + 1], 0x0040u), __byte_perm(F[4 * j + 2], F[4 * j + 3], 0x0040u),
                                 0x5410u);
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4 *>(arow + ((c ^ (r & 7)) << 4)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 
 // One 2-bit group (32 code bytes at cp): bit plane p of word w is slot block 16w + 4p.
-__device__ __forceinline__ void decode_2b(const unsigned char *cp, unsigned char *arow, int r) {
+__device__ __forceinline__ void decode_2b(const unsigned char *cp, uint32_t (&o)[32]) {
     const uint4 c0 = reinterpret_cast<const uint4 *>(cp)[0], c1 = reinterpret_cast<const uint4 *>(cp)[1];
     const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {  // 16-byte piece c = word c's four planes
+    for (int c = 0; c < 8; ++c) {
         const uint32_t v = cw[c];
-        const uint4 o = make_uint4(v & 0x03030303u, (v >> 2) & 0x03030303u, (v >> 4) & 0x03030303u,
-                                   (v >> 6) & 0x03030303u);
-        *reinterpret_cast<uint4 *>(arow + ((c ^ (r & 7)) << 4)) = o;
+        o[4 * c] = v & 0x03030303u;
+        o[4 * c + 1] = (v >> 2) & 0x03030303u;
+        o[4 * c + 2] = (v >> 4) & 0x03030303u;
+        o[4 * c + 3] = (v >> 6) & 0x03030303u;
+    }
+}
+
+// The order every role follows: the CTA's units [u0, u1) in rounds of NWG (warpgroup w takes the
+// w-th unit of a round), each round's chunks interleaved between its units.
+struct RowsSeq {
+    int u0, u1, ks, cps, nch, nwg;
+    int p, i, w;
+};
+
+__device__ __forceinline__ int unit_chunks(int u, int ks, int cps, int nch, int &c0) {
+    c0 = (u % ks) * cps;
+    return max(0, min(nch, c0 + cps) - c0);
+}
+
+// The next item of the sequence: false at its end.  unit, chunk (global chunk index), the
+// warpgroup, and whether it is the last chunk of its unit.
+__device__ __forceinline__ bool seq_next(RowsSeq &S, int &unit, int &chunk, int &wg, bool &last) {
+    for (;;) {
+        const int ur = S.u0 + S.nwg * S.p;  // the round's first unit
+        if (ur >= S.u1) return false;
+        int mx = 0;
+        for (int w = 0; w < S.nwg && ur + w < S.u1; ++w) {
+            int c0;
+            mx = max(mx, unit_chunks(ur + w, S.ks, S.cps, S.nch, c0));
+        }
+        if (S.i >= mx) {
+            ++S.p;
+            S.i = 0;
+            S.w = 0;
+            continue;
+        }
+        const int w = S.w, i = S.i;
+        if (++S.w == S.nwg) {
+            S.w = 0;
+            ++S.i;
+        }
+        if (ur + w >= S.u1) continue;
+        int c0;
+        const int n = unit_chunks(ur + w, S.ks, S.cps, S.nch, c0);
+        if (i >= n) continue;
+        unit = ur + w;
+        chunk = c0 + i;
+        wg = w;
+        last = i == n - 1;
+        return true;
     }
 }
 
@@ -268,274 +369,392 @@ __device__ __forceinline__ void tmem_ld_bn(uint32_t taddr, int (&v)[BN]) {
     }
 }
 
+constexpr int kRowsMaxWg = 4;
+// Decoder warpgroups: three, with the producer warp 13 warps, so that no SM sub-partition holds more
+// than 4 warps of 128 registers (its 16 K registers; the tensor memory holds per warpgroup two A
+// buffers of 32 columns and two D buffers of BN, after the shared 32 columns of minus ones).
+template <int BN>
+constexpr int rows_nwg() { return 3; }
+
+// Barriers and flags at the start of the dynamic shared memory.
+struct RowsBars {
+    uint64_t full[kRowsMaxD];           // slot loaded (codes, scales, activation tiles)
+    uint64_t freed[kRowsMaxD];          // the MMAs that read the slot are complete
+    uint64_t afull[kRowsMaxWg][2];      // warpgroup w's A buffer s holds a decoded group (4 warp arrivals)
+    uint64_t mdone[kRowsMaxWg][2];      // the MMAs of that group are complete
+    uint64_t fin[4 * kRowsMaxWg];       // per decoder warp: every MMA it issued is complete (the exit)
+    uint32_t slot[kRowsMaxD];           // window addresses of the ring slots
+    uint32_t tmem;                      // tensor-memory base address
+    volatile uint32_t dead;             // a wait ran out somewhere in the CTA
+};
+
+}  // namespace
+
+namespace {
+
+// Registers per thread: 4 warps of 128 fill a sub-partition's 16 K.
 template <int KIND, int BN>
-__global__ void __launch_bounds__(kRowsThreads, 1)
+__global__ void __maxnreg__(128)
     rows_kernel(const __grid_constant__ RowsMaps maps, RowsArgs A, uint32_t *err) {
     extern __shared__ __align__(1024) unsigned char smem[];
+    constexpr int NWG = rows_nwg<BN>();
+    constexpr int NDW = 4 * NWG;  // decoder warps; warp NDW is the producer
+    static_assert(NWG <= kRowsMaxWg, "barrier arrays hold every warpgroup");
+    constexpr bool T5 = KIND == TRX_KIND_TERNARY5;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int r = tid & 127, h = tid >> 7;  // decode: row r, group h of the pair
     pdl_trigger();
-    const int tile = blockIdx.x / A.ks, split = blockIdx.x - tile * A.ks;
-    const int c0 = split * A.cps, c1 = min(A.nch, c0 + A.cps);
     const RowsPlan &P = A.P;
     if (smem_u32(smem) != (uint32_t)A.base) {  // the plan's window layout does not hold
         pdl_wait();
         if (tid == 0) atomicOr(err, TRX_DEV_INTERNAL);
         return;
     }
-    unsigned char *const misc = smem + P.misc_off;
-    const uint32_t bar_code = smem_u32(misc);          // [2] code-ring slots
-    const uint32_t bar_bt = bar_code + 16;             // [3] activation tiles
-    const uint32_t bar_mma = bar_code + 40;            // [2] MMA completion per TMEM/A buffer
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(misc + 64);
-    uint32_t *const flag = tmem_slot + 1;              // a wait ran out somewhere in the CTA
-    uint16_t *const scur = reinterpret_cast<uint16_t *>(misc + 128);  // [2 buf][2 grp][128 rows]
-    int *const xcur = reinterpret_cast<int *>(misc + 128 + 2 * 2 * 128 * 2);  // [2 buf][2 grp][BN]
-    const int G = A.G;
-    const int np = 2 * (c1 - c0);  // pairs (the last ones may hold fewer groups)
-    const uint32_t lane8x = (uint32_t)kRowsLut | ((uint32_t)lane << 3);
+    RowsBars *const bars = reinterpret_cast<RowsBars *>(smem);
+    const uint32_t bfull = smem_u32(bars->full), bfreed = smem_u32(bars->freed);
+    const uint32_t bafull = smem_u32(&bars->afull[0][0]), bmdone = smem_u32(&bars->mdone[0][0]);
+    int *const xs_s = reinterpret_cast<int *>(smem + P.xs_off);  // [G][BN] group sums of the activation
+    const int units = A.tiles * A.ks;
+    RowsSeq S0;
+    S0.u0 = (int)((long long)blockIdx.x * units / gridDim.x);
+    S0.u1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x);
+    S0.ks = A.ks;
+    S0.cps = A.cps;
+    S0.nch = A.nch;
+    S0.nwg = NWG;
+    S0.p = S0.i = S0.w = 0;
+    const int D = P.D, G = A.G;
+    const int tid_prod = 32 * NDW;
+    const int cb = T5 ? kRowsCb5 : kRowsCb2;
+    const uint32_t codes_bytes = (uint32_t)(cb * kRowsM), tile_bytes = (uint32_t)(BN * 128);
 
-    if (KIND == TRX_KIND_TERNARY5) {  // the LUT: entry b at 0x10000 + b*256, one 8-byte replica per lane
+    if (T5 && warp < 8) {  // the LUT: entry b at 0x10000 + b*256 + lane*8; warp w writes entries 32w..32w+31
         uint2 *lw = reinterpret_cast<uint2 *>(smem + P.lut_off);
-        for (int i = tid; i < 256 * 32; i += kRowsThreads) lw[i] = t5_entry8((uint32_t)(i >> 5));
+        const uint2 mine = t5_entry8((uint32_t)(32 * warp + lane));
+        for (int i = 0; i < 32; ++i)
+            lw[(32 * warp + i) * 32 + lane] =
+                make_uint2(__shfl_sync(0xffffffffu, mine.x, i), __shfl_sync(0xffffffffu, mine.y, i));
     }
-    if (tid == 0) {
-        for (int i = 0; i < 7; ++i) mbar_init_s(bar_code + 8u * i, 1);
-        *flag = 0u;
+    if (tid == tid_prod) {
+        for (int d = 0; d < D; ++d) {
+            mbar_init_s(bfull + 8u * d, 1);
+            mbar_init_s(bfreed + 8u * d, 1);
+            bars->slot[d] = smem_u32(smem + P.slot_off[d]);
+        }
+        for (int i = 0; i < 2 * NWG; ++i) {
+            mbar_init_s(bafull + 8u * i, 4);
+            mbar_init_s(bmdone + 8u * i, 1);
+        }
+        for (int i = 0; i < NDW; ++i) mbar_init_s(smem_u32(&bars->fin[i]), 1);
+        bars->dead = 0u;
         mbar_fence_init();
         tma_prefetch_map(&maps.codes);
         tma_prefetch_map(&maps.scales);
         tma_prefetch_map(&maps.xp);
     }
-    if (warp == 0) {  // TMEM: 2 buffers x 2 groups x BN int32 columns
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(4 * BN)
+    if (warp == NDW) {  // tensor memory: per warpgroup A 2 x 32 columns, D 2 x BN
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars->tmem)),
+                     "r"(kRowsTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t slot_bytes = (uint32_t)P.slot;
-    const int cb = KIND == TRX_KIND_TERNARY5 ? kRowsCb5 : kRowsCb2;
-    const int y0 = tile * kRowsM;
+    const uint32_t tmem = bars->tmem;
+    constexpr uint32_t kWgCols = 64 + 2 * BN;
 
-    // Issue (thread 0): chunk k's codes and scales into ring slot k % 2; pair p's activation tiles
-    // into buffer p % 3.  Weights are written by no kernel, so both code slots go before the
-    // dependency wait; the activation is the prep kernel's, after it.
-    auto issue_chunk = [&](int k) {
-        const int c = c0 + k;
-        const uint32_t dst = smem_u32(smem + P.ring_off) + (uint32_t)(k & 1) * slot_bytes;
-        const uint32_t bar = bar_code + 8u * (k & 1);
-        mbar_expect_tx_s(bar, slot_bytes);
-        const int xc = KIND == TRX_KIND_TERNARY5 ? A.sbytes + 104 * c - 8 * (c & 1) : A.sbytes + 128 * c;
-        tma_load_3d(dst, &maps.codes, xc, y0, 0, bar);
-        tma_load_3d(dst + (uint32_t)(cb * kRowsM), &maps.scales, 16 * (c >> 1), y0, 0, bar);
+    // Per-warpgroup rings: warpgroup w's i-th position (chunk of one of its units) lives in slot
+    // w * Dw + i % Dw, so a slow warpgroup never holds up another's refills.
+    const int Dw = D / NWG;
+    // Producer: the codes and scales of each warpgroup's first Dw positions (written by no kernel)
+    // before the dependency wait, their activation tiles after it.
+    auto issue_w = [&](int slot, int unit, int chunk) {
+        const uint32_t dst = bars->slot[slot], bar = bfull + 8u * slot;
+        const int ng = min(4, G - 4 * chunk);
+        mbar_expect_tx_s(bar, codes_bytes + 2048u + (uint32_t)ng * tile_bytes);
+        const int y0 = (unit / A.ks) * kRowsM;
+        const int xc = T5 ? A.sbytes + 104 * chunk - 8 * (chunk & 1) : A.sbytes + 128 * chunk;
+        tma_load_2d(dst + (uint32_t)P.codes_off, &maps.codes, xc, y0, bar);
+        tma_load_2d(dst + (uint32_t)P.scales_off, &maps.scales, 16 * (chunk >> 1), y0, bar);
     };
-    auto issue_bt = [&](int p) {
-        const int g = 4 * c0 + 2 * p;  // first group of the pair
-        const int ng = min(2, G - g);
-        const uint32_t dst = smem_u32(smem + P.bt_off[p % 3]);
-        const uint32_t bar = bar_bt + 8u * (p % 3);
-        mbar_expect_tx_s(bar, (uint32_t)(ng * BN * 128));
-        for (int j = 0; j < ng; ++j) tma_load_2d(dst + (uint32_t)(j * BN * 128), &maps.xp, 128 * (g + j), 0, bar);
+    auto issue_x = [&](int slot, int chunk) {
+        const uint32_t dst = bars->slot[slot], bar = bfull + 8u * slot;
+        const int ng = min(4, G - 4 * chunk);
+        for (int q = 0; q < ng; ++q) tma_load_2d(dst + (uint32_t)q * tile_bytes, &maps.xp, 128 * (4 * chunk + q), 0, bar);
     };
-    // Arms per barrier (thread 0's count; the last armed phase of barrier j is (uses[j] - 1) & 1):
-    // code slots 0, 1; activation tiles 2..4; MMA buffers 5, 6.
-    int uses[7] = {0, 0, 0, 0, 0, 0, 0};
-    if (tid == 0) {
+    // The next position of warpgroup w in the sequence (its unit and chunk): false at its end.
+    auto next_of = [&](RowsSeq &S, int w, int &unit, int &chunk) {
+        int g;
+        bool l;
+        while (seq_next(S, unit, chunk, g, l))
+            if (g == w) return true;
+        return false;
+    };
+    RowsSeq Sp[NWG];
+    int issued_w[NWG], pre_chunk[kRowsMaxD];
+#pragma unroll
+    for (int w = 0; w < NWG; ++w) {
+        Sp[w] = S0;
+        issued_w[w] = 0;
+    }
+    if (tid == tid_prod) {
         fence_proxy_async();
-        for (int k = 0; k < min(2, c1 - c0); ++k) {
-            issue_chunk(k);
-            ++uses[k];
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+            int unit, chunk;
+            while (issued_w[w] < Dw && next_of(Sp[w], w, unit, chunk)) {
+                const int slot = w * Dw + issued_w[w]++;
+                issue_w(slot, unit, chunk);
+                pre_chunk[slot] = chunk;
+            }
         }
     }
     pdl_wait();
-    if (tid == 0 && np > 0) {
-        issue_bt(0);
-        ++uses[2];
-    }
+    // The activation's group sums (the prep kernel's), staged once for every role.
+    for (int i = tid; i < G * BN; i += blockDim.x) xs_s[i] = A.xsum[(i / BN) * 32 + (i % BN)];
+    __syncthreads();
 
-    // Per-row sums of this CTA's groups, per batch row (two threads per row: h = 0, 1).
-    long long acc[BN];
+    if (tid == tid_prod) {
+        // Producer: a warpgroup's positions retire in its order once the MMAs that read their slot
+        // are complete; the freed slot takes the warpgroup's position i + Dw.
 #pragma unroll
-    for (int b = 0; b < BN; ++b) acc[b] = 0;
-    const ScaleFast F = scale_fast(A.B);
-    const uint32_t idesc = umma_idesc_i8<BN>();
-
-    // A warp-uniform bounded wait: lane 0 waits, the lanes learn the outcome, and each lane then
-    // observes the completed phase itself (its own acquire of the data).
-    auto warp_wait = [&](uint32_t bar, uint32_t parity) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait_bounded_s(bar, parity, err);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok) mbar_try_wait_s(bar, parity);
-        return ok;
-    };
-    auto epilogue = [&](int i) {  // pair i: warps w and w + 4 read TMEM lanes 32 (w % 4) .., group w / 4
-        const int eh = warp >> 2, er = 32 * (warp & 3) + lane;
-        const int g = 4 * c0 + 2 * i + eh;
-        if (g >= G) return;
-        tc_fence_after();
-        int v[BN];
-        tmem_ld_bn<BN>(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((i & 1) * 2 * BN + eh * BN), v);
-        tmem_wait_ld();
-        const uint32_t sb = scur[((i & 1) * 2 + eh) * 128 + er];
-        const int *xs = xcur + ((i & 1) * 2 + eh) * BN;
+        for (int w = 0; w < NWG; ++w)
+            for (int i = 0; i < issued_w[w]; ++i) issue_x(w * Dw + i, pre_chunk[w * Dw + i]);
+        int retired_w[NWG];
 #pragma unroll
-        for (int b = 0; b < BN; ++b)
-            if (b < A.nb) acc[b] += contrib(v[b] - xs[b], sb, A.B, F);
-    };
-
-    int done = -1;  // the last pair whose MMAs were committed
-    for (int i = 0; i < np; ++i) {
-        const int k = i >> 1;                  // chunk (local)
-        const int c = c0 + k;
-        const int g0 = 4 * c + 2 * (i & 1);    // the pair's first group
-        if (g0 >= G) break;                    // (uniform)
-        const int ng = min(2, G - g0);
-        // MMA(i - 2) read A[i & 1] and the tiles of pair i - 2; the chunk's codes must be in.
-        bool ok = i < 2 || warp_wait(bar_mma + 8u * (i & 1), ((i - 2) >> 1) & 1u);
-        ok = ok && warp_wait(bar_code + 8u * (k & 1), (k >> 1) & 1u);
-        if (!ok && lane == 0) atomicOr(flag, 1u);
-        __syncthreads();
-        if (*flag) break;                      // (uniform)
-        // Decode: row r, group g0 + h of the pair, into A[i & 1][h].
-        const unsigned char *slot = smem + P.ring_off + (size_t)(k & 1) * slot_bytes;
-        unsigned char *arow = smem + P.a_off + (size_t)((i & 1) * 2 + h) * 16384 + (size_t)r * 128;
-        const int q = 2 * (i & 1) + h;         // group within the chunk
-        if (h < ng) {
-            if (KIND == TRX_KIND_TERNARY5) {
-                const unsigned char *win = slot + (size_t)r * kRowsCb5;
-                switch (q + 4 * (c & 1)) {  // window offset 8 (c & 1) + 26 q
-                    case 0: decode_t5<0>(win, lane8x, arow, r); break;
-                    case 1: decode_t5<26>(win, lane8x, arow, r); break;
-                    case 2: decode_t5<52>(win, lane8x, arow, r); break;
-                    case 3: decode_t5<78>(win, lane8x, arow, r); break;
-                    case 4: decode_t5<8>(win, lane8x, arow, r); break;
-                    case 5: decode_t5<34>(win, lane8x, arow, r); break;
-                    case 6: decode_t5<60>(win, lane8x, arow, r); break;
-                    default: decode_t5<86>(win, lane8x, arow, r); break;
+        for (int w = 0; w < NWG; ++w) retired_w[w] = 0;
+        unsigned long long t_last = global_ns();
+        bool ok = true, more = true;
+        while (more) {
+            if (bars->dead) break;
+            more = false;
+            bool progress = false;
+#pragma unroll
+            for (int w = 0; w < NWG; ++w) {
+                const int rw = retired_w[w];
+                if (rw >= issued_w[w]) continue;
+                more = true;
+                const int slot = w * Dw + rw % Dw;
+                if (!mbar_test_wait_s(bfreed + 8u * slot, (uint32_t)(rw / Dw) & 1u)) continue;
+                int unit, chunk;
+                if (next_of(Sp[w], w, unit, chunk)) {
+                    fence_proxy_async();  // the decoders' reads of the slot (ordered by their arrivals) first
+                    issue_w(slot, unit, chunk);
+                    issue_x(slot, chunk);
+                    ++issued_w[w];
                 }
-            } else {
-                decode_2b(slot + (size_t)r * kRowsCb2 + 32 * q, arow, r);
+                retired_w[w] = rw + 1;
+                progress = true;
             }
-            const uint16_t *sc = reinterpret_cast<const uint16_t *>(slot + cb * kRowsM + (size_t)r * 16 + 8 * (c & 1));
-            scur[((i & 1) * 2 + h) * 128 + r] = sc[q];
+            if (progress) {
+                t_last = global_ns();
+            } else if (more && global_ns() - t_last > kWaitNs) {
+                atomicOr(err, TRX_DEV_TIMEOUT);
+                ok = false;
+                break;
+            }
         }
-        if (tid < 2 * BN) {  // the pair's activation sums
-            const int gh = tid / BN, b = tid - gh * BN;
-            xcur[((i & 1) * 2 + gh) * BN + b] = (gh < ng && b < A.nb) ? A.xsum[(size_t)b * G + g0 + gh] : 0;
-        }
-        fence_proxy_async();  // the A rows (generic stores) before the tensor cores read them
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            // The chunk's slot is free once both its pairs are decoded: chunk k + 2 goes in.
-            if ((i & 1) && k + 2 < c1 - c0) {
-                issue_chunk(k + 2);
-                ++uses[k & 1];
-            }
-            // Pair i + 1's activation tiles: its buffer's last reader, MMA(i - 2), is complete.
-            if (i + 1 < np && 4 * c0 + 2 * (i + 1) < G) {
-                issue_bt(i + 1);
-                ++uses[2 + (i + 1) % 3];
-            }
-            if (mbar_wait_bounded_s(bar_bt + 8u * (i % 3), (uint32_t)(i / 3) & 1u, err)) {
-                tc_fence_after();
-                const uint32_t abase = smem_u32(smem + P.a_off) + (uint32_t)((i & 1) * 2) * 16384u;
-                const uint32_t bbase = smem_u32(smem + P.bt_off[i % 3]);
-                for (int j = 0; j < ng; ++j)
+        if (!ok) bars->dead = 1u;
+        // Every copy issued is complete before the CTA leaves (bounded; an expired wait was recorded).
 #pragma unroll
-                    for (int s2 = 0; s2 < 4; ++s2)
-                        umma_i8(tmem + (uint32_t)((i & 1) * 2 * BN + j * BN),
-                                umma_desc_sw128(abase + (uint32_t)j * 16384u + 32u * s2),
-                                umma_desc_sw128(bbase + (uint32_t)(j * BN * 128) + 32u * s2), idesc, s2);
-                umma_commit(bar_mma + 8u * (i & 1));
-                ++uses[5 + (i & 1)];
+        for (int w = 0; w < NWG; ++w)
+            for (int d = 0; d < Dw && d < issued_w[w]; ++d) {
+                const int plast = d + (issued_w[w] - 1 - d) / Dw * Dw;  // the last position issued into slot d
+                mbar_wait_bounded_s(bfull + 8u * (w * Dw + d), (uint32_t)(plast / Dw) & 1u, nullptr);
+            }
+    } else if (warp < NDW) {
+        // Decoders: warpgroup W, row r of its units' tiles (TMEM lane r).  The warp (position count
+        // mod 4) of the warpgroup issues the MMAs of all groups of that position.
+        const int W = warp >> 2, r = tid & 127;
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const uint32_t lane8x = (uint32_t)kRowsLut | ((uint32_t)lane << 3);
+        const uint32_t tA0 = tmem + (uint32_t)W * kWgCols, tD0 = tA0 + 64u;  // MMA operand addresses (lane 0)
+        const uint32_t tA = tA0 + lane_base, tD = tD0 + lane_base;          // this warp's lanes
+        const uint32_t idesc = umma_idesc_i8<BN>();
+        const ScaleFast F = scale_fast(A.B);
+        long long acc[BN];
+#pragma unroll
+        for (int b = 0; b < BN; ++b) acc[b] = 0;
+        uint32_t sb0 = 0u, sb1 = 0u;  // the scale bits of the items in buffers 0 and 1
+        int g0 = 0, g1 = 0;           // and their groups
+        // Warp-uniform bounded wait: lane 0 waits, the lanes learn the outcome, and each lane then
+        // observes the completed phase itself (its own acquire).
+        auto warp_wait = [&](uint32_t bar, uint32_t parity) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait_bounded_s(bar, parity, err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (ok) mbar_try_wait_s(bar, parity);
+            return ok;
+        };
+        // Item e's group sums: D buffer e & 1 (sum(code * x8)) minus the group's sum(x8), read once
+        // the item's MMAs are complete; its scale contribution in int64.
+        auto epilogue = [&](int e) {
+            const int s = e & 1;
+            if (!warp_wait(bmdone + 8u * (2 * W + s), (uint32_t)(e >> 1) & 1u)) return false;
+            tc_fence_after();
+            int v[BN];
+            tmem_ld_bn<BN>(tD + (uint32_t)(s * BN), v);
+            tmem_wait_ld();
+            const uint32_t sb = s ? sb1 : sb0;
+            const int4 *xs4 = reinterpret_cast<const int4 *>(xs_s + (s ? g1 : g0) * BN);
+#pragma unroll
+            for (int i = 0; i < BN / 4; ++i) {
+                const int4 t = xs4[i];
+                v[4 * i] -= t.x;
+                v[4 * i + 1] -= t.y;
+                v[4 * i + 2] -= t.z;
+                v[4 * i + 3] -= t.w;
+            }
+            const int E = (int)((sb >> 10) & 31u);
+            if ((unsigned)(E - F.lo) <= (unsigned)F.span) {  // one 32 x 32 -> 64 multiply-add per batch row
+                const int f = (int)(((sb & 0x3ffu) | 0x400u) << (E + F.sh));
+                const long long fs = (sb & 0x8000u) ? -(long long)f : (long long)f;
+#pragma unroll
+                for (int b = 0; b < BN; ++b) acc[b] += (long long)v[b] * fs;
             } else {
-                *flag = 1u;
+#pragma unroll
+                for (int b = 0; b < BN; ++b) acc[b] += group_contrib(v[b], sb, A.B);
+            }
+            return true;
+        };
+        auto finish = [&](int b, int n, long long a) {
+            if (acc_bad(a, A.R)) atomicOr(err, TRX_DEV_OVERFLOW);
+            const int res = (int)(a >> A.R);
+            if (A.out_f) {
+                float y = __fmul_rn((float)res, pow2f(A.e8[b] + A.R - A.B));
+                if (A.resid) y = __fadd_rn(A.resid[(size_t)b * A.N + n], y);
+                A.out_f[(size_t)b * A.N + n] = y;
+            } else {
+                A.out_i[(size_t)b * A.N + n] = res;
+            }
+        };
+        // A unit's rows are done: output them (whole K), or add the partial sums and let the row's
+        // last unit (a per-row arrival count, so no barrier between the warps) finish it.
+        auto flush = [&](int unit) {
+            const int n = (unit / A.ks) * kRowsM + r;
+            if (n < A.N) {
+                if (A.ks == 1) {
+#pragma unroll
+                    for (int b = 0; b < BN; ++b)
+                        if (b < A.nb) finish(b, n, acc[b]);
+                } else {
+#pragma unroll
+                    for (int b = 0; b < BN; ++b)
+                        if (b < A.nb) atomicAdd(A.acc + (size_t)b * A.N + n, (unsigned long long)acc[b]);
+                    __threadfence();
+                    if (atomicAdd(A.cnt + n, 1u) == (unsigned)(A.ks - 1)) {
+                        __threadfence();
+                        for (int b = 0; b < A.nb; ++b) {
+                            unsigned long long *p = A.acc + (size_t)b * A.N + n;
+                            finish(b, n, (long long)__ldcg(p));
+                            *p = 0ull;
+                        }
+                        A.cnt[n] = 0u;
+                    }
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < BN; ++b) acc[b] = 0;
+        };
+        RowsSeq Sd = S0;
+        int unit, chunk, wg, j = 0, ep = 0, wpos = 0;
+        bool last, alive = true, issued = false;
+        while (alive && seq_next(Sd, unit, chunk, wg, last)) {
+            if (wg != W) continue;
+            if (bars->dead) {
+                alive = false;
+                break;
+            }
+            const int slot = W * Dw + wpos % Dw;
+            if (!warp_wait(bfull + 8u * slot, (uint32_t)(wpos / Dw) & 1u)) {
+                alive = false;
+                break;
+            }
+            const bool issuer = (warp & 3) == (wpos & 3);
+            ++wpos;
+            const int ng = min(4, G - 4 * chunk);
+            const uint32_t sbase = bars->slot[slot];
+            const unsigned char *sp = smem + (sbase - (uint32_t)A.base);
+            for (int q = 0; q < ng; ++q) {
+                const int s = j & 1;
+                uint32_t o[32];
+                if (T5) {
+                    const unsigned char *win = sp + P.codes_off + r * kRowsCb5;
+                    switch (q + 4 * (chunk & 1)) {  // window offset 8 (chunk & 1) + 26 q
+                        case 0: decode_t5<0>(win, lane8x, o); break;
+                        case 1: decode_t5<26>(win, lane8x, o); break;
+                        case 2: decode_t5<52>(win, lane8x, o); break;
+                        case 3: decode_t5<78>(win, lane8x, o); break;
+                        case 4: decode_t5<8>(win, lane8x, o); break;
+                        case 5: decode_t5<34>(win, lane8x, o); break;
+                        case 6: decode_t5<60>(win, lane8x, o); break;
+                        default: decode_t5<86>(win, lane8x, o); break;
+                    }
+                } else {
+                    decode_2b(sp + P.codes_off + r * kRowsCb2 + 32 * q, o);
+                }
+                const uint32_t sb = *reinterpret_cast<const uint16_t *>(sp + P.scales_off + r * 16 + 8 * (chunk & 1) + 2 * q);
+                if (ep < j - 1) {  // item j - 2 (buffers s) read back before they are reused
+                    if (!epilogue(ep)) {
+                        alive = false;
+                        break;
+                    }
+                    ++ep;
+                }
+                if (s) {
+                    sb1 = sb;
+                    g1 = 4 * chunk + q;
+                } else {
+                    sb0 = sb;
+                    g0 = 4 * chunk + q;
+                }
+                tmem_st32(tA + (uint32_t)(s * 32), o);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_s(bafull + 8u * (2 * W + s));
+                if (issuer) {  // every warp's A rows are in: the group's four MMAs, from one elected lane
+                    if (!warp_wait(bafull + 8u * (2 * W + s), (uint32_t)(j >> 1) & 1u)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ta = tA0 + (uint32_t)(s * 32), td = tD0 + (uint32_t)(s * BN);
+                    const uint32_t sbq = sbase + (uint32_t)q * tile_bytes;
+#pragma unroll
+                    for (int s2 = 0; s2 < 4; ++s2) umma_i8_ta_elect(td, ta + 8u * s2, umma_desc_sw128(sbq + 32u * s2), idesc, s2);
+                    umma_commit_elect(bmdone + 8u * (2 * W + s));
+                    if (q == ng - 1) umma_commit_elect(bfreed + 8u * slot);  // the position's slot: free once done
+                    issued = true;
+                }
+                ++j;
+            }
+            if (!alive) break;
+            if (last) {  // the unit's last chunk: read back its last groups, then output its rows
+                while (ep < j) {
+                    if (!epilogue(ep)) {
+                        alive = false;
+                        break;
+                    }
+                    ++ep;
+                }
+                if (!alive) break;
+                flush(unit);
             }
         }
-        __syncthreads();
-        if (*flag) break;                      // (uniform)
-        done = i;
-        if (i >= 1) {  // epilogue of pair i - 1 (its MMAs were committed an iteration ago)
-            if (warp_wait(bar_mma + 8u * ((i - 1) & 1), ((i - 1) >> 1) & 1u))
-                epilogue(i - 1);
-            else if (lane == 0)
-                atomicOr(flag, 1u);
-            tc_fence_before();
+        if (!alive && lane == 0) bars->dead = 1u;
+        if (issued) {  // this warp's MMAs are complete before the tensor memory is freed (bounded)
+            umma_commit_elect(smem_u32(&bars->fin[warp]));
+            if (lane == 0) mbar_wait_bounded_s(smem_u32(&bars->fin[warp]), 0u, nullptr);
+            __syncwarp();
         }
-    }
-    __syncthreads();
-    if (!*flag && done >= 0) {  // the last pair's epilogue
-        if (warp_wait(bar_mma + 8u * (done & 1), (done >> 1) & 1u))
-            epilogue(done);
-        else if (lane == 0)
-            atomicOr(flag, 1u);
         tc_fence_before();
     }
     __syncthreads();
-    const bool dead = *flag != 0u;
-    if (dead && tid == 0) {  // wait (bounded) for every copy and MMA this CTA armed, then leave
-        for (int j = 0; j < 7; ++j)
-            if (uses[j]) mbar_wait_bounded_s(bar_code + 8u * j, (uint32_t)(uses[j] - 1) & 1u, nullptr);
-    }
-    __syncthreads();
-    if (warp == 0) {
+    if (warp == NDW) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kRowsTmemCols) : "memory");
     }
-    if (dead) return;
-
-    // Two threads per row: h = 1 hands its sums to h = 0 through shared memory (the A tiles are idle).
-    long long *xch = reinterpret_cast<long long *>(smem + P.a_off);
-    if (h == 1)
-#pragma unroll
-        for (int b = 0; b < BN; ++b) xch[b * 128 + r] = acc[b];
-    __syncthreads();
-    const int n = y0 + r;
-    if (h == 0) {
-#pragma unroll
-        for (int b = 0; b < BN; ++b) acc[b] += xch[b * 128 + r];
-    }
-    auto finish = [&](int b, long long a) {
-        if (acc_bad(a, A.R)) atomicOr(err, TRX_DEV_OVERFLOW);
-        const int res = (int)(a >> A.R);
-        if (A.out_f) {
-            float v = __fmul_rn((float)res, pow2f(A.e8[b] + A.R - A.B));
-            if (A.resid) v = __fadd_rn(A.resid[(size_t)b * A.N + n], v);
-            A.out_f[(size_t)b * A.N + n] = v;
-        } else
-            A.out_i[(size_t)b * A.N + n] = res;
-    };
-    if (A.ks == 1) {
-        if (h == 0 && n < A.N)
-#pragma unroll
-            for (int b = 0; b < BN; ++b)
-                if (b < A.nb) finish(b, acc[b]);
-        return;
-    }
-    // K split: exact int64 partial sums, then the tile's last CTA finishes and clears.
-    if (h == 0 && n < A.N)
-#pragma unroll
-        for (int b = 0; b < BN; ++b)
-            if (b < A.nb) atomicAdd(A.acc + (size_t)b * A.N + n, (unsigned long long)acc[b]);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *flag = atomicAdd(A.cnt + tile, 1u) == (unsigned)(A.ks - 1) ? 2u : 0u;
-    __syncthreads();
-    if (*flag != 2u) return;
-    __threadfence();
-    if (h == 0 && n < A.N)
-        for (int b = 0; b < A.nb; ++b) {
-            unsigned long long *p = A.acc + (size_t)b * A.N + n;
-            finish(b, (long long)__ldcg(p));
-            *p = 0ull;
-        }
-    if (tid == 0) A.cnt[tile] = 0u;
 }
 
 }  // namespace
@@ -559,31 +778,46 @@ static EncodeTiledFn2 encode_fn() {
     return f;
 }
 
-static bool encode(CUtensorMap *m, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
+static bool encode(CUtensorMap *m, const void *base, const cuuint64_t *dims, const cuuint64_t *strides,
                    const cuuint32_t *box, CUtensorMapSwizzle sw) {
     const EncodeTiledFn2 f = encode_fn();
     if (!f) return false;
-    const cuuint32_t es[3] = {1, 1, 1};
-    return f(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void *>(base), dims, strides, box, es,
+    const cuuint32_t es[2] = {1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
            CUDA_SUCCESS;
 }
 
-static bool rows_plan(int kind, int BN, int reserved, RowsPlan &P) {
-    const int cb = kind == TRX_KIND_TERNARY5 ? kRowsCb5 : kRowsCb2;
-    P.slot = (cb + 16) * kRowsM;
-    P.ring_off = 0;
-    const int bt = 2 * BN * 128;
-    P.bt_off[0] = (2 * P.slot + 1023) / 1024 * 1024;
-    P.bt_off[1] = P.bt_off[0] + bt;
-    P.misc_off = P.bt_off[1] + bt;
-    const int misc = 128 + 2 * 2 * 128 * 2 + 2 * 2 * BN * 4;
-    P.lut_off = kRowsLut - reserved;
-    if (P.misc_off + misc > P.lut_off) return false;
-    P.a_off = P.lut_off + 65536;                 // window 0x20000: 1024-aligned
-    P.bt_off[2] = P.a_off + 4 * 16384;
-    P.smem = P.bt_off[2] + bt;
-    return (reserved % 1024) == 0 && P.smem <= 227 * 1024;
+// Slots of [activation tiles][codes][scales] (1024-byte multiples, 1024-aligned in the window) after
+// the barriers; trit5: around the LUT at window 0x10000.
+static bool rows_plan(int kind, int BN, int G, int reserved, RowsPlan &P) {
+    if (reserved % 1024) return false;
+    const bool t5 = kind == TRX_KIND_TERNARY5;
+    const int cb = t5 ? kRowsCb5 : kRowsCb2;
+    const int bt = 4 * BN * 128;
+    P.codes_off = bt;
+    P.scales_off = bt + cb * kRowsM;
+    const int slot = (P.scales_off + 16 * kRowsM + 1023) / 1024 * 1024;
+    const int top = 227 * 1024;
+    static_assert(sizeof(RowsBars) <= 1024, "barriers fit the first KiB");
+    P.xs_off = 1024;
+    const int first = 1024 + (G * BN * 4 + 1023) / 1024 * 1024;  // after the group sums
+    P.D = 0;
+    auto region = [&](int lo, int hi) {
+        for (int o = lo; o + slot <= hi && P.D < kRowsMaxD; o += slot) P.slot_off[P.D++] = o;
+    };
+    if (t5) {
+        P.lut_off = kRowsLut - reserved;
+        if (first > P.lut_off) return false;
+        region(first, P.lut_off);
+        region(P.lut_off + 65536, top);
+    } else {
+        P.lut_off = 0;
+        region(first, top);
+    }
+    if (P.D < 2) return false;
+    P.smem = std::max(P.slot_off[P.D - 1] + slot, t5 ? P.lut_off + 65536 : 0);
+    return P.smem <= top;
 }
 
 template <int KIND, int BN>
@@ -593,7 +827,8 @@ static trx_status launch_rows_t(const RowsMaps &maps, const RowsArgs &A, int gri
         return cudaFuncSetAttribute(rows_kernel<KIND, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     });
     if (e != cudaSuccess) return note_cuda(e);
-    return note_cuda(launch_kernel(rows_kernel<KIND, BN>, dim3(grid), dim3(kRowsThreads), A.P.smem, st, maps, A, err));
+    return note_cuda(launch_kernel(rows_kernel<KIND, BN>, dim3(grid), dim3(32 * (4 * rows_nwg<BN>() + 1)), A.P.smem, st,
+                                   maps, A, err));
 }
 
 trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, int R, const float *x, const int8_t *x8,
@@ -612,11 +847,14 @@ trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, i
     A.nb = nb;
     A.B = B;
     A.R = R;
-    const int tiles = (N + kRowsM - 1) / kRowsM;
-    A.ks = tiles >= sms ? 1 : std::min(A.nch, std::max(1, sms / tiles));
+    // Units: (128-row tile, K range).  Split K when the tiles alone give fewer units than the SMs'
+    // decoder warpgroups, within the scratch the partial sums and per-row counts need.
+    const int nwg = BN == 16 ? rows_nwg<16>() : rows_nwg<32>();
+    A.tiles = (N + kRowsM - 1) / kRowsM;
+    A.ks = A.tiles >= nwg * sms ? 1 : std::min(A.nch, (nwg * sms + A.tiles - 1) / A.tiles);
     A.cps = (A.nch + A.ks - 1) / A.ks;
     A.ks = (A.nch + A.cps - 1) / A.cps;  // no empty splits
-    if (A.ks > 1 && ((size_t)nb * N > acc_cap || tiles > cnt_cap)) {
+    if (A.ks > 1 && ((size_t)nb * N > acc_cap || N > cnt_cap)) {
         A.ks = 1;
         A.cps = A.nch;
     }
@@ -628,22 +866,23 @@ trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, i
     A.acc = acc_scratch;
     A.cnt = cnt;
     A.base = reserved;
-    if (!rows_plan(kind, BN, reserved, A.P)) return TRX_ERR_UNSUPPORTED;
+    if (!rows_plan(kind, BN, A.G, reserved, A.P) || A.P.D < nwg) return TRX_ERR_UNSUPPORTED;
     RowsMaps maps;
     memset(&maps, 0, sizeof(maps));
-    const cuuint64_t wd[3] = {(cuuint64_t)A.rb, (cuuint64_t)N, 1}, ws[2] = {(cuuint64_t)A.rb, (cuuint64_t)N * A.rb};
-    const cuuint32_t cbox[3] = {(cuuint32_t)(kind == TRX_KIND_TERNARY5 ? kRowsCb5 : kRowsCb2), (cuuint32_t)kRowsM, 1};
-    const cuuint32_t sbox[3] = {16, (cuuint32_t)kRowsM, 1};
+    const cuuint64_t wd[2] = {(cuuint64_t)A.rb, (cuuint64_t)N}, ws[1] = {(cuuint64_t)A.rb};
+    const cuuint32_t cbox[2] = {(cuuint32_t)(kind == TRX_KIND_TERNARY5 ? kRowsCb5 : kRowsCb2), (cuuint32_t)kRowsM};
+    const cuuint32_t sbox[2] = {16, (cuuint32_t)kRowsM};
     const cuuint64_t xd[2] = {(cuuint64_t)K, (cuuint64_t)nb}, xs[1] = {(cuuint64_t)K};
     const cuuint32_t xbox[2] = {128, (cuuint32_t)BN};
-    if (!encode(&maps.codes, w, 3, wd, ws, cbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&maps.scales, w, 3, wd, ws, sbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&maps.xp, x8p, 2, xd, xs, xbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!encode(&maps.codes, w, wd, ws, cbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&maps.scales, w, wd, ws, sbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&maps.xp, x8p, xd, xs, xbox, CU_TENSOR_MAP_SWIZZLE_128B))
         return TRX_ERR_CUDA;
     // The permuted activation, its group sums and exponents (one CTA per batch row).
     cudaError_t e = launch_kernel(rows_prep_kernel, dim3(nb), dim3(256), (size_t)K, st, x, x8, K, kind, x8p, xsum, e8);
     if (e != cudaSuccess) return note_cuda(e);
-    const int grid = tiles * A.ks;
+    const int units = A.tiles * A.ks;
+    const int grid = std::max(1, std::min(sms, (units + nwg - 1) / nwg));
     if (kind == TRX_KIND_TERNARY5)
         return BN == 16 ? launch_rows_t<TRX_KIND_TERNARY5, 16>(maps, A, grid, err, st)
                         : launch_rows_t<TRX_KIND_TERNARY5, 32>(maps, A, grid, err, st);
