@@ -432,6 +432,8 @@ def main():
                          # 128 tokens at 4096 of context (the down projection K-segmented).
                          "hybrid-2b": decode_leg(ctx, "hybrid-2b", 2048, 256, 8),
                          "hybrid-27b": decode_leg(ctx, "hybrid-27b", 4096, 128, 8)}
+        # Config 2 at batch 16: 16 sequences in lockstep on the tensor-core rows projection.
+        out["decode_batch"] = {"qwen3-8b": batch_decode_leg(ctx, "qwen3-8b", 16, 1024, 16, 3)}
     if world == 1 and not args.no_decode:
         out["q8_matvec"] = q8_leg(ctx, peak)
         out["batched_rows"] = [rows_leg(ctx, peak, k, nb) for k in (5, 0) for nb in (16, 32)]
@@ -567,6 +569,40 @@ def decode_leg(ctx, name, ctx_len, n_tokens, warmup):
            "e2e_tok_s": round(n_tokens / e2e_s, 1), "weight_bytes_per_token": wb,
            "weight_GBps": round(wb / (ms * 1e-3) / 1e9, 1), "launches_per_token": dec.launches_per_step(),
            "distinct_tokens": len(set(toks))}
+    del dec, w
+    torch.cuda.empty_cache()
+    return out
+
+
+def batch_decode_leg(ctx, name, nseq, ctx_len, n_tokens, warmup):
+    """Batched greedy decode (trixium_b200.decoder.BatchDecoder, BASELINE config 2 at batch 16):
+    nseq sequences in lockstep, every projection one tensor-core launch over their rows, one CUDA
+    graph per step.  tok_s counts every sequence's tokens."""
+    import torch
+    from trixium_b200 import decoder as D
+    cfg = D.CONFIGS[name]
+    w = D.SyntheticWeights(cfg, seed=0)
+    dec = D.BatchDecoder(w, nseq, ctx=ctx, max_pos=ctx_len + n_tokens + warmup + 8)
+    dec.fill_context(ctx_len)
+    dec.tok.copy_(torch.arange(7, 7 + nseq, dtype=torch.int32))
+    dec.capture()
+    for _ in range(warmup):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    dec.fill_context(ctx_len)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n_tokens):
+        dec.graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / n_tokens
+    ctx.raise_on_error()
+    wb = cfg.weight_bytes_per_token()
+    out = {"config": name, "kind": "trit5" if cfg.kind == 5 else "2-bit", "context": ctx_len, "batch": nseq,
+           "steps_timed": n_tokens, "ms_per_step": round(ms, 4), "tok_s": round(nseq * 1000.0 / ms, 1),
+           "weight_bytes_per_step": wb, "weight_GBps": round(wb / (ms * 1e-3) / 1e9, 1),
+           "kernel": "trx::rows_kernel (tcgen05.mma kind::i8) for every projection"}
     del dec, w
     torch.cuda.empty_cache()
     return out

@@ -370,6 +370,131 @@ class Decoder:
         return out.cpu().tolist()
 
 
+class BatchDecoder:
+    """Greedy decoding of nseq <= 32 independent sequences in lockstep (BASELINE config 2 at batch
+    16): every projection is one tensor-core launch over the sequences' rows (trx_matvec_f_rows, each
+    row quantised with its own exponent as the batch-1 projection quantises its vector), the norms,
+    SwiGLU, argmax and position advance are row-wise kernels, and attention and the DeltaNet step run
+    over a sequence grid dimension with per-sequence caches, states and positions.  The arithmetic of
+    every sequence is the batch-1 decoder's (mirror.py:1002-1034).  K-segmented tensors (the
+    hybrid-27b down projection) are not taken: one batched launch covers one engine op's K."""
+
+    def __init__(self, weights: SyntheticWeights, nseq, ctx=None, max_pos=4096, kv_dtype=torch.float16):
+        cfg = self.cfg = weights.cfg
+        if not 1 <= nseq <= 32:
+            raise ValueError("BatchDecoder: 1 <= nseq <= 32")
+        if any(isinstance(lw["down"], list) for lw in weights.layers):
+            raise ValueError("BatchDecoder: K-segmented tensors are not supported")
+        self.w, self.nseq = weights, nseq
+        self.ctx = ctx or ops.default_context()
+        dev = weights.emb.device
+        f32 = lambda *shape: torch.zeros(*shape, dtype=torch.float32, device=dev)
+        E, B = cfg.hidden, nseq
+        self.max_pos = max_pos
+        self.x, self.h = f32(B, E), f32(B, E)
+        self.q, self.k, self.v = f32(B, cfg.q_rows), f32(B, cfg.kv_rows), f32(B, cfg.kv_rows)
+        self.attn = f32(B, cfg.n_head * cfg.head_dim)
+        self.g, self.u, self.act = f32(B, cfg.ffn), f32(B, cfg.ffn), f32(B, cfg.ffn)
+        self.logits = f32(B, cfg.vocab)
+        self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.attn_shape = ops.attn_shape(cfg.n_head, cfg.n_kv, cfg.head_dim, max_pos,
+                                         rope_dims=cfg.rope_dims or cfg.head_dim, gated=cfg.attn_gated, eps=cfg.eps)
+        self.kc, self.vc, self.ring, self.state = {}, {}, {}, {}
+        for l in range(cfg.n_layer):
+            if cfg.layer_type(l) == "d":
+                self.ring[l] = f32(B, cfg.dn_conv, cfg.dn_channels)
+                self.state[l] = f32(B, cfg.dn_nv, cfg.dn_hv, cfg.dn_hk)
+            else:
+                self.kc[l] = torch.zeros(B, max_pos, cfg.n_kv, cfg.head_dim, dtype=kv_dtype, device=dev)
+                self.vc[l] = torch.zeros_like(self.kc[l])
+        if self.ring:
+            self.dn_shape = ops.deltanet_shape(cfg.dn_nk, cfg.dn_hk, cfg.dn_nv, cfg.dn_hv, cfg.dn_conv, cfg.eps)
+            self.qkv, self.z = f32(B, cfg.dn_channels), f32(B, cfg.dn_nv * cfg.dn_hv)
+            self.beta, self.alpha = f32(B, cfg.dn_nv), f32(B, cfg.dn_nv)
+            self.og = f32(B, cfg.dn_nv * cfg.dn_hv)
+        # The segments of every layer's input projection as tensors of their own (views of the
+        # packed allocation).
+        self.in_t = [[lw["in"].tensor(i) for i in range(len(lw["in"].entries))] for lw in weights.layers]
+        self.graph = None
+
+    def _mutable(self):
+        return [self.tok, self.pos] + list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + \
+            list(self.state.values())
+
+    def set_states(self, states):
+        """Every sequence's DeltaNet states: states[l] of shape (nv, hv, hk) (the batch-1 decoder's)."""
+        for l, t in self.state.items():
+            t.copy_(states[l].unsqueeze(0).expand_as(t))
+
+    def fill_context(self, n, seed=0):
+        """Synthetic context of n positions in every sequence's attention caches (random fp16 K/V
+        rows) and every position set to n."""
+        g = torch.Generator(device=self.tok.device)
+        g.manual_seed(seed)
+        for l in self.kc:
+            self.kc[l][:, :n] = torch.randn(self.kc[l][:, :n].shape, generator=g, device=self.tok.device).to(self.kc[l].dtype)
+            self.vc[l][:, :n] = torch.randn(self.vc[l][:, :n].shape, generator=g, device=self.tok.device).to(self.vc[l].dtype)
+        self.pos.fill_(n)
+
+    def enqueue_step(self):
+        """One token of every sequence on the current stream: reads self.tok and self.pos, writes the
+        next tokens into self.tok and advances self.pos."""
+        cfg, w, ctx = self.cfg, self.w, self.ctx
+        ops.embed_lookup_rows(ctx, w.emb, self.tok, self.x)
+        for l, lw in enumerate(w.layers):
+            seg = self.in_t[l]
+            ops.rmsnorm_rows(ctx, self.x, lw["attn_norm"], cfg.eps, y=self.h)
+            if cfg.layer_type(l) == "d":
+                for t, y in zip(seg, (self.qkv, self.z, self.beta, self.alpha)):
+                    ops.matvec_f_rows(ctx, t, self.h, out=y)
+                ops.deltanet_step_rows(ctx, self.dn_shape, self.qkv, self.z, self.beta, self.alpha, lw["dt_bias"],
+                                       lw["ssm_a"], lw["conv_w"], lw["ssm_norm"], self.ring[l], self.state[l], self.pos,
+                                       self.og)
+                ops.matvec_f_rows(ctx, lw["out"], self.og, out=self.x, resid=self.x)
+            else:
+                for t, y in zip(seg, (self.q, self.k, self.v)):
+                    ops.matvec_f_rows(ctx, t, self.h, out=y)
+                ops.attn_decode_rows(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"],
+                                     w.rope_freq, self.kc[l], self.vc[l], self.pos, self.attn)
+                ops.matvec_f_rows(ctx, lw["out"], self.attn, out=self.x, resid=self.x)
+            ops.rmsnorm_rows(ctx, self.x, lw["ffn_norm"], cfg.eps, y=self.h)
+            ops.matvec_f_rows(ctx, lw["gate"], self.h, out=self.g)
+            ops.matvec_f_rows(ctx, lw["up"], self.h, out=self.u)
+            ops.silu_mul(ctx, self.g, self.u, self.act)
+            ops.matvec_f_rows(ctx, lw["down"], self.act, out=self.x, resid=self.x)
+        ops.rmsnorm_rows(ctx, self.x, w.out_norm, cfg.eps, y=self.h)
+        ops.matvec_f_rows(ctx, w.lm_head, self.h, out=self.logits)
+        ops.argmax_rows(ctx, self.logits, self.tok)
+        ops.advance_positions(ctx, self.pos)
+
+    def capture(self):
+        """Capture one step as a CUDA graph (positions and tokens live on the device)."""
+        return Decoder.capture(self)
+
+    def step(self, tokens=None):
+        if tokens is not None:
+            self.tok.copy_(torch.as_tensor(tokens, dtype=torch.int32))
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.enqueue_step()
+
+    def generate(self, prompts, n_new):
+        """Greedy decode of every sequence: prompts [nseq][P] (equal lengths), then n_new tokens each.
+        Returns [nseq][n_new] ids."""
+        P = len(prompts[0])
+        for t in range(P):
+            self.step([p[t] for p in prompts])
+        out = torch.empty(n_new, self.nseq, dtype=torch.int32, device=self.tok.device)
+        for i in range(n_new):
+            out[i].copy_(self.tok)
+            if i + 1 < n_new:
+                self.step()
+        self.ctx.raise_on_error()
+        return out.t().cpu().tolist()
+
+
 def main(argv=None):
     """Decode timing on synthetic weights: python -m trixium_b200.decoder --config qwen3-8b
     --context 1024 --tokens 64 [--eager].  Prints one JSON line (ms and tok/s per token)."""
