@@ -359,6 +359,20 @@ trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *shape, cons
                              cudaStream_t stream);
 
 /*
+ * The integer gated-DeltaNet head step (model/deltanet.py:99-147, head_step; the vector unit's
+ * bit-exact fast path): nheads independent heads, each an int16 state hv x hk (d_state
+ * [nheads][hv][hk], value = m * 2^exp) at exponent d_exp[h] with d_maxabs[h] its max |m| as the
+ * previous step left it (negative: computed from the state, the reference's maxM=None); fp32 key
+ * and query d_k, d_q [nheads][hk], value d_v [nheads][hv], decay and beta d_decay, d_beta [nheads].
+ * The state, exponent and max are updated in place; d_out [nheads][hv] receives o (fp32).  hv <= 256,
+ * hk <= 128.  A value outside the reference's asserted ranges sets TRX_DEV_OVERFLOW.
+ */
+trx_status trx_deltanet_int_step(trx_ctx *ctx, uint32_t nheads, uint32_t hv, uint32_t hk, int16_t *d_state,
+                                 int32_t *d_exp, int32_t *d_maxabs, const float *d_k, const float *d_q,
+                                 const float *d_v, const float *d_decay, const float *d_beta, float *d_out,
+                                 cudaStream_t stream);
+
+/*
  * trx_deltanet_step for a batch of nseq independent sequences in one launch: every per-sequence
  * argument (qkv, z, beta, alpha, conv ring, state, position, output) is nseq consecutive copies of
  * the single-sequence layout; the weights (dt_bias, ssm_a, conv_w, norm_w) are shared.

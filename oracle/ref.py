@@ -397,3 +397,92 @@ def deltanet_step(qkv, z, beta_raw, alpha, dt_bias, ssm_a, conv_w, win, S, norm_
         gpos = kh * rep + h // nk
         og[gpos * hv:(gpos + 1) * hv] = (rmsnorm(oh, norm_w, eps) * silu(z[h * hv:(h + 1) * hv])).astype(f32)
     return og
+
+
+# Integer DeltaNet head step (model/deltanet.py) ----------------------------------------------------
+
+DN_DELTA_FRAC = 19            # model/deltanet.py:49 (delta, -v and the decayed dot in units of 2^-19)
+DN_O_SHIFT = 8                # model/deltanet.py:50
+DN_STATE_LIM = (1 << 15) - 4  # model/deltanet.py:51
+
+
+def lroundf64(x):
+    """Round half away from zero on float64 values (model/deltanet.py:55-58)."""
+    x = np.asarray(x, dtype=np.float64)
+    return np.where(x >= 0, np.floor(x + 0.5), np.ceil(x - 0.5)).astype(np.int64)
+
+
+def q16_head(x):
+    """model/deltanet.py:60-68: int16 mantissas, one exponent (|m| in [2^14, 2^15) at the max)."""
+    x = np.asarray(x, dtype=f32)
+    amax = np.abs(x).max()
+    if amax == 0:
+        return np.zeros(len(x), dtype=np.int64), 0
+    e = int(np.frexp(f32(amax))[1]) - 15
+    return np.clip(lroundf64(x * f32(np.exp2(-e))), -32767, 32767), e
+
+
+def q15(x):
+    """model/deltanet.py:70-72."""
+    return int(np.clip(lroundf64(f32(x) * f32(32768.0)), 0, 32767))
+
+
+def rne_shift(v, k):
+    """model/bitexact.py:35-45: round-to-nearest-even right shift."""
+    v = np.asarray(v, dtype=np.int64)
+    if k == 0:
+        return v.copy()
+    q = v >> k
+    rnd = (v >> (k - 1)) & 1
+    sticky = (v & ((1 << (k - 1)) - 1)) != 0 if k > 1 else np.zeros_like(v, dtype=bool)
+    return q + (rnd & (sticky | ((q & 1) == 1)).astype(np.int64))
+
+
+def arith_shift(v, k):
+    """model/bitexact.py:47-50: left if k >= 0, floor right otherwise."""
+    v = np.asarray(v, dtype=np.int64)
+    return v << k if k >= 0 else v >> (-k)
+
+
+def dn_ratchet(maxM, maxD, eM, ek, k16max, decay):
+    """model/deltanet.py:82-89."""
+    kmax = float(k16max) * float(np.exp2(ek))
+    t = (maxM * float(decay) + maxD * float(np.exp2(-DN_DELTA_FRAC)) * kmax * float(np.exp2(-eM))) / float(DN_STATE_LIM)
+    return 0 if t <= 1.0 else int(np.ceil(np.log2(t)))
+
+
+def dn_head_step(M, eM, kk, qh, vh, decay, beta, maxM=None):
+    """model/deltanet.py:99-147 (head_step): one head, one token.  M int64 (hv, hk) updated in
+    place; returns (o float32 (hv,), eM2, maxM2, bad) with bad set where the reference asserts."""
+    bad = False
+    k16, ek = q16_head(kk)
+    q16, eq = q16_head(qh)
+    if maxM is None:
+        maxM = int(np.abs(M).max())
+    shift_a = DN_DELTA_FRAC + eM + ek                                  # :77-79
+    d15, nbq = q15(decay), -q15(beta)
+    dot = M.astype(np.int64) @ k16.astype(np.int64)                   # pass A
+    dot_r = arith_shift(dot, shift_a)
+    bad |= bool(np.abs(dot_r).max() >= (1 << 31))
+    ddr = (dot_r * d15) >> 15
+    nv = -lroundf64(np.asarray(vh, dtype=f32).astype(np.float64) * float(1 << DN_DELTA_FRAC))   # :75-80
+    bad |= bool(np.abs(nv).max() >= (1 << 31))
+    delta = ((ddr + nv) * nbq) >> 15
+    maxD = int(np.abs(delta).max())
+    n = dn_ratchet(maxM, maxD, eM, ek, int(np.abs(k16).max()), decay)  # the CPU's algebra
+    eM2 = eM + n
+    sh = eM2 + 7 - ek                                                  # :91-97
+    d15n = int(np.clip(lroundf64(f32(decay) * f32(np.exp2(15 - n))), 0, 32767))
+    rnd = (1 << (sh - 1)) if sh > 0 else 0
+    d8 = 8 * delta                                                     # pass B
+    bad |= bool(np.abs(d8 + rnd).max() >= (1 << 31))
+    delta_s = arith_shift(d8 + rnd, -sh)
+    bad |= bool(np.abs(delta_s).max() >= (1 << 16))
+    newM = rne_shift(M.astype(np.int64) * d15n + np.outer(delta_s, k16.astype(np.int64)), 15)
+    bad |= bool(np.abs(newM).max() > 32767)
+    M[:] = newM
+    maxM2 = int(np.abs(newM).max())
+    o_r = (newM @ q16.astype(np.int64)) >> DN_O_SHIFT
+    bad |= bool(np.abs(o_r).max() >= (1 << 31))
+    of = (o_r.astype(np.float64) * float(np.exp2(eM2 + eq + DN_O_SHIFT))).astype(f32)
+    return of, eM2, maxM2, bad

@@ -7,8 +7,8 @@ root directory:
 
 It imports the reference's `model.bons` (TensorSpec + encode_rows: the converter's row-packet
 bytes, with its per-tensor B/R), `model.bitexact` (matvec_ternary and matvec_q8, the engine's integer specs),
-`model.mirror` (_quantize_f_pow2 and _sumsq64), and writes small .npz files next to this
-script.  The GPU box never reads the reference: the tests read only these fixtures.
+`model.mirror` (_quantize_f_pow2 and _sumsq64), `model.deltanet` (head_step, the integer DeltaNet
+head), and writes small .npz files next to this script.  The GPU box never reads the reference: the tests read only these fixtures.
 
 Cases follow the reference's own tests where they exist:
 * test/model/test_bitexact.py:36-56 (seed 42, 64x512, uniform scales, uniform x8),
@@ -371,8 +371,37 @@ def kseg_case(name, rows, cols, kind, seed):
                         B=spec.bias, R=spec.rshift, x=x, y=y, **out)
 
 
+def dn_int_case():
+    """The integer DeltaNet head step (model/deltanet.py head_step) over a few tokens per shape, as
+    test/model/test_asm.py:554-590 drives it (the state starts at exponent -20 and empty, so the
+    first tokens ratchet and the small last one does not).  Token t starts from token t-1's state
+    (zero at token 0)."""
+    from model import deltanet as dn
+    out = {}
+    for (hv, hk, seed) in [(64, 64, 1), (128, 128, 2), (128, 128, 3), (32, 64, 4)]:
+        rng = np.random.default_rng(seed)
+        M = np.zeros((hv, hk), dtype=np.int64)
+        eM, maxM = -20, 0
+        tag = f"h{hv}x{hk}s{seed}"
+        for tok in range(4):
+            kk = rng.standard_normal(hk).astype(f32); kk /= np.linalg.norm(kk)
+            qh = rng.standard_normal(hk).astype(f32); qh /= np.linalg.norm(qh)
+            vh = (rng.standard_normal(hv) * (3.0 if tok < 2 else 0.05)).astype(f32)
+            decay, beta = f32(rng.uniform(0.3, 1.0)), f32(rng.uniform(0.2, 1.0))
+            o, eM2, maxM2 = dn.head_step(M, eM, kk, qh, vh, decay, beta, maxM=maxM)
+            out.update({f"{tag}_t{tok}_eM": np.int32(eM),
+                        f"{tag}_t{tok}_maxM": np.int32(maxM), f"{tag}_t{tok}_k": kk, f"{tag}_t{tok}_q": qh,
+                        f"{tag}_t{tok}_v": vh, f"{tag}_t{tok}_decay": decay, f"{tag}_t{tok}_beta": beta,
+                        f"{tag}_t{tok}_o": o, f"{tag}_t{tok}_M": M.astype(np.int16),
+                        f"{tag}_t{tok}_eM2": np.int32(eM2), f"{tag}_t{tok}_maxM2": np.int32(maxM2)})
+            eM, maxM = eM2, maxM2
+    out["shapes"] = np.array([(64, 64, 1), (128, 128, 2), (128, 128, 3), (32, 64, 4)], dtype=np.int32)
+    np.savez_compressed(os.path.join(HERE, "dn_int_steps.npz"), **out)
+
+
 def main():
     from model import tinygen
+    dn_int_case()
     # Decode attention and the DeltaNet step, pinned to the mirror (identity output projections).
     hybrid_kernel_case("hd64", _hybrid_cfg(tinygen.BONSAI_TINY_HYBRID, hadamard_block=0, dn_num_v_heads=4,
                                            name="kernels-hd64"))

@@ -256,3 +256,24 @@ def test_kseg_oracle_bit_exact(name):
         c = np.concatenate([a[2] for a in segs], axis=1)
         whole = ref.matvec_f(s, c, d["x"], int(d["B"]), int(d["R"]))
         assert not np.array_equal(whole.view(np.uint32), d["y"].view(np.uint32))
+
+
+def test_int_deltanet_oracle_pinned():
+    """oracle/ref.py dn_head_step against the reference's own head_step (model/deltanet.py:99-147)
+    over the token schedule of test/model/test_asm.py:554-590: state, exponent, max and output
+    bit-exact, the ratchet firing on the first tokens and not on the last."""
+    d = load(os.path.join(GOLDEN, "dn_int_steps.npz"))
+    for hv, hk, seed in d["shapes"]:
+        tag = f"h{hv}x{hk}s{seed}"
+        M = np.zeros((hv, hk), dtype=np.int64)
+        for t in range(4):
+            g = lambda n: d[f"{tag}_t{t}_{n}"]
+            o, eM2, maxM2, bad = ref.dn_head_step(M, int(g("eM")), g("k"), g("q"), g("v"), g("decay"), g("beta"),
+                                                  maxM=int(g("maxM")))
+            assert not bad
+            assert np.array_equal(M, g("M").astype(np.int64)), (tag, t)
+            assert (eM2, maxM2) == (int(g("eM2")), int(g("maxM2")))
+            assert np.array_equal(o.view(np.uint32), g("o").view(np.uint32))
+            if t == 0:
+                assert eM2 > -20  # the empty -20 state ratchets on the first update
+        assert eM2 == int(d[f"{tag}_t2_eM2"])  # the small last update does not ratchet

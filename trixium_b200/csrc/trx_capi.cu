@@ -682,6 +682,28 @@ trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, const f
                                   d_conv_ring, d_state, d_pos, d_out, stream);
 }
 
+trx_status trx_deltanet_int_step(trx_ctx *ctx, uint32_t nheads, uint32_t hv, uint32_t hk, int16_t *d_state,
+                                 int32_t *d_exp, int32_t *d_maxabs, const float *d_k, const float *d_q, const float *d_v,
+                                 const float *d_decay, const float *d_beta, float *d_out, cudaStream_t stream) {
+    if (!ctx || nheads == 0 || nheads > (1u << 20) || hv == 0 || hk == 0) return TRX_ERR_ARG;
+    if (!d_state || !d_exp || !d_maxabs || !d_k || !d_q || !d_v || !d_decay || !d_beta || !d_out) return TRX_ERR_ARG;
+    if (hv > 256 || hk > 128) return TRX_ERR_UNSUPPORTED;
+    trx::DnIntArgs A{};
+    A.nh = (int)nheads;
+    A.hv = (int)hv;
+    A.hk = (int)hk;
+    A.M = d_state;
+    A.eM = d_exp;
+    A.maxM = d_maxabs;
+    A.k = d_k;
+    A.q = d_q;
+    A.v = d_v;
+    A.decay = d_decay;
+    A.beta = d_beta;
+    A.out = d_out;
+    return trx::launch_dn_int(A, ctx->err, stream);
+}
+
 trx_status trx_deltanet_step_rows(trx_ctx *ctx, const trx_deltanet_shape *sh, int32_t nseq, const float *d_qkv,
                                   const float *d_z, const float *d_beta, const float *d_alpha, const float *d_dt_bias,
                                   const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,

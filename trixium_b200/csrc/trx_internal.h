@@ -153,6 +153,18 @@ struct DnArgs {
 };
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
+
+// The integer DeltaNet head step (trx_dn_int.cu, model/deltanet.py:99-147): nh heads, each an int16
+// state hv x hk at exponent eM[h] with maxM[h] (< 0: computed from the state), fp32 k, q [nh][hk],
+// v [nh][hv], decay and beta [nh]; M, eM, maxM updated in place, out [nh][hv].
+struct DnIntArgs {
+    int nh, hv, hk;
+    int16_t *M;
+    int *eM, *maxM;
+    const float *k, *q, *v, *decay, *beta;
+    float *out;
+};
+trx_status launch_dn_int(const DnIntArgs &A, uint32_t *err, cudaStream_t st);
 size_t attn_smem_bytes(int hd, int rep, int chunk, int esize);
 int attn_chunk(int max_pos, int hd, int esize);
 

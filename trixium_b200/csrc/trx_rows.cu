@@ -81,21 +81,9 @@ __device__ __forceinline__ uint32_t umma_idesc_i8() {
     return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kRowsM >> 4) << 24);
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]^T: A in tensor memory (lane = row, 4 int8 K elements per column).
-__device__ __forceinline__ void umma_i8_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, int acc) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// The same issued by one elected lane of a converged warp (all lanes execute it; warp-uniform
-// operands): measured on B200 about 2.5x the issue rate of a thread in a divergent branch.
+// D[tmem] (+)= A[tmem] * B[smem]^T, A in tensor memory (lane = row, 4 int8 K elements per column),
+// issued by one elected lane of a converged warp (all lanes execute it; warp-uniform operands):
+// measured on B200 about 2.5x the issue rate of a thread in a divergent branch.
 __device__ __forceinline__ void umma_i8_ta_elect(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                                  int acc) {
     asm volatile(
@@ -105,6 +93,7 @@ __device__ __forceinline__ void umma_i8_ta_elect(uint32_t tmem_d, uint32_t tmem_
         : "memory");
 }
 
+// Commit this warp's MMAs issued so far to an mbarrier (one arrival once they are complete).
 __device__ __forceinline__ void umma_commit_elect(uint32_t bar) {
     asm volatile(
         "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"

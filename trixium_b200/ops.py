@@ -508,6 +508,25 @@ def deltanet_step_rows(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, 
     return out
 
 
+def deltanet_int_step(ctx, state, exp, maxabs, k, q, v, decay, beta, out=None):
+    """The integer DeltaNet head step of nheads heads (trx_deltanet_int_step, model/deltanet.py:99-147):
+    state int16 [nheads, hv, hk], exp and maxabs int32 [nheads] (maxabs < 0: computed), k, q float32
+    [nheads, hk], v [nheads, hv], decay, beta [nheads].  Updates state, exp and maxabs in place and
+    returns o [nheads, hv] float32."""
+    nh, hv, hk = state.shape
+    _need(state, torch.int16, "state")
+    _need(exp, torch.int32, "exp")
+    _need(maxabs, torch.int32, "maxabs")
+    for t, n in ((k, "k"), (q, "q"), (v, "v"), (decay, "decay"), (beta, "beta")):
+        _need(t, torch.float32, n)
+    if out is None:
+        out = torch.empty(nh, hv, dtype=torch.float32, device=state.device)
+    _lib.check(_lib.lib().trx_deltanet_int_step(ctx.h, nh, hv, hk, _ptr(state), _ptr(exp), _ptr(maxabs), _ptr(k),
+                                                _ptr(q), _ptr(v), _ptr(decay), _ptr(beta), _ptr(out), _stream()),
+               "trx_deltanet_int_step")
+    return out
+
+
 def row_bytes(cols, kind):
     return int(_lib.lib().trx_row_bytes(cols, kind))
 
