@@ -167,6 +167,14 @@ trx_status trx_matvec_fp(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
                          const float *d_x, float *d_y, cudaStream_t stream);
 
 /*
+ * fp-mode projection of nrows rows (model/fastref.py:119-125, HybridRef.matmul(entry, X)):
+ * d_y [nrows][rows] = d_x [nrows][cols] . W^T in fp32, W = (code - 1) * scale; d_resid (or NULL),
+ * [nrows][rows], is added (the K-segments of one entry accumulate this way).
+ */
+trx_status trx_matvec_fp_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
+                              int32_t nrows, const float *d_resid, float *d_y, cudaStream_t stream);
+
+/*
  * Gate/up projection with the SwiGLU epilogue (model/mirror.py:1016-1020;
  * model/fastref.py:253-255): act[i] = silu(gate(x)[i]) * up(x)[i], both projections in the
  * engine's arithmetic on the same quantised (optionally RMS-normalised) x.

@@ -332,6 +332,35 @@ def hybrid_tokens_case(name, cfg, trit5, kseg_max, n_prompt=6, n_new=128, seed=1
                         logits=np.stack([logits[p] for p in steps]), **ckpt)
 
 
+def fastref_case(name):
+    """The fp-mode projections of the reference's fast engine (model/fastref.py HybridRef: matmul of
+    an entry, proj of (role, layer) with the Hadamard rotation and K-segments) on the reference-made
+    image tokens_<name>.img.gz, for seeded X of 5 rows."""
+    import gzip
+    import shutil
+    import tempfile
+    from model import fastref
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "img")
+        with gzip.open(os.path.join(HERE, f"tokens_{name}.img.gz"), "rb") as src, open(path, "wb") as dst:
+            shutil.copyfileobj(src, dst)
+        img = bons.BONSReader(path)
+        ref = fastref.HybridRef(img)
+        rng = np.random.default_rng(77)
+        out = {}
+        roles = [(layout.ROLE_FFN_GATE, 0), (layout.ROLE_FFN_DOWN, 0), (layout.ROLE_FFN_UP, 1), (layout.ROLE_LM_HEAD, 0)]
+        for i, (role, l) in enumerate(roles):
+            e = ref._entry(role, l)
+            cols = sum(t["cols"] for t in ref._ksegs(e))
+            X = (rng.standard_normal((5, cols)) * 0.7).astype(f32)
+            out[f"proj{i}_role"] = np.int32(role)
+            out[f"proj{i}_layer"] = np.int32(l)
+            out[f"proj{i}_X"] = X
+            out[f"proj{i}_Y"] = ref.proj(role, l, X)
+            out[f"proj{i}_M"] = ref.matmul(e, X)   # the same entry without the rotation
+        np.savez_compressed(os.path.join(HERE, f"fastref_{name}.npz"), n=np.int32(len(roles)), **out)
+
+
 def kseg_case(name, rows, cols, kind, seed):
     """A K-segmented projection (model/bons.py:83-113 split_wide: equal column ranges, the whole
     tensor's B/R in each segment) through the converter's row packets and the mirror's float
@@ -413,6 +442,7 @@ def main():
     hybrid_tokens_case("hybrid_t5_kseg", tinygen.BONSAI_TINY_HYBRID, trit5=True, kseg_max=256)
     hybrid_tokens_case("hybrid_2b", tinygen.BONSAI_TINY_HYBRID, trit5=False, kseg_max=None)
     # K-segmented projections at the hybrid-27b down projection's width and a wide Q8 tensor.
+    fastref_case("hybrid_t5_kseg")
     kseg_case("t5_24x17408", 24, 17408, layout.KIND_TERNARY5, 50)
     kseg_case("2b_40x17408", 40, 17408, layout.KIND_TERNARY, 51)
     kseg_case("q8_20x9216", 20, 9216, layout.KIND_Q8, 52)

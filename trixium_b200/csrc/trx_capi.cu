@@ -352,6 +352,23 @@ trx_status trx_matvec_fp(trx_ctx *ctx, const trx_entry *e, const void *d_packed,
     return trx::launch_matvec_fp(J, ctx->err, stream);
 }
 
+trx_status trx_matvec_fp_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, int32_t nrows,
+                              const float *d_resid, float *d_y, cudaStream_t stream) {
+    if (!ctx) return TRX_ERR_ARG;
+    trx_status s = check_entry(e);
+    if (s) return s;
+    if (!d_packed || !d_x || !d_y || nrows < 1 || nrows > (1 << 20)) return TRX_ERR_ARG;
+    trx::MvJobs J = base_jobs(ctx, e, d_packed);
+    J.x = d_x;
+    J.njobs = nrows;
+    J.x_stride = e->cols;
+    J.y_stride = e->rows;
+    J.seg[0].y = d_y;
+    J.seg[0].resid = d_resid;
+    J.out = trx::OUT_F32;
+    return trx::launch_matvec_fp(J, ctx->err, stream);
+}
+
 trx_status trx_matvec_swiglu(trx_ctx *ctx, const trx_entry *gate, const void *d_gate, const trx_entry *up,
                              const void *d_up, const float *d_x, const float *d_norm_w, float eps, float *d_act,
                              cudaStream_t stream) {

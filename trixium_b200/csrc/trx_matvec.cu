@@ -1050,57 +1050,70 @@ __global__ void __launch_bounds__(kMvThreads, 1)
     }
 }
 
-// fp-mode kernel (model/fastref.py:103-125): thread per (row, group); x fp32 in shared memory;
-// per-group fp32 sums of (code-1)*x, times the fp32 scale, reduced over groups in group order.
+// fp-mode kernel (model/fastref.py:103-125, HybridRef.matmul): Y[t] = X[t] . W^T in fp32 for the
+// launch's J.njobs rows of X (x_stride / y_stride apart), W = (code - 1) * scale (exact in the fp16
+// weight cache the reference builds).  Thread per (row, group): the group's 128 codes are decoded
+// once per chunk of TT rows of X staged in shared memory, each row's group sum (code - 1) * x in
+// fp32 times the fp32 scale, then the groups added in group order (+ the optional residual).
 template <int KIND>
-__global__ void __launch_bounds__(256) tmv_fp_kernel(MvJobs J, int TR, uint32_t *err) {
+__global__ void __launch_bounds__(256) tmv_fp_kernel(MvJobs J, int TR, int TT, uint32_t *err) {
     extern __shared__ __align__(128) unsigned char smem[];
     pdl_trigger();
     pdl_wait();
-    float *xs = reinterpret_cast<float *>(smem);
-    float *part = xs + J.cols;  // [TR][G+1]
     const int G = J.cols / 128, K = J.cols;
+    float *xs = reinterpret_cast<float *>(smem);  // [TT][K]
+    float *part = xs + (size_t)TT * K;            // [TT][TR][G + 1]
     const int sbytes = (G + 15) / 16 * 32;
     const int rb = sbytes + ((KIND == TRX_KIND_TERNARY5 ? 26 : 32) * G + 31) / 32 * 32;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) xs[k] = J.x[k];
-    __syncthreads();
     const int units = TR * G;
-    for (int r0 = blockIdx.x * TR; r0 < J.rows; r0 += gridDim.x * TR) {
-        const int nr = min(TR, J.rows - r0);
-        for (int u = threadIdx.x; u < units; u += blockDim.x) {
-            const int rr = u / G, g = u % G;
-            if (rr >= nr) continue;
-            const uint8_t *row = J.w + (uint64_t)(r0 + rr) * rb;
-            const float *xg = xs + g * 128;
-            float s = 0.f;
-            if (KIND == TRX_KIND_TERNARY5) {
-                const uint8_t *cb = row + sbytes + 26 * g;
-                for (int i = 0; i < 26; ++i) {
-                    uint32_t b = cb[i];
-                    for (int k = 0; k < 5; ++k) {
-                        const int l = 5 * i + k;
-                        const int d = (int)(b % 3u);
-                        b /= 3u;
-                        if (l < 128) s = __fadd_rn(s, __fmul_rn((float)(d - 1), xg[l]));
+    float *const y = reinterpret_cast<float *>(J.seg[0].y);
+    for (int t0 = 0; t0 < J.njobs; t0 += TT) {
+        const int nt = min(TT, J.njobs - t0);
+        __syncthreads();  // the previous chunk is done with xs and part
+        for (int i = threadIdx.x; i < nt * K; i += blockDim.x)
+            xs[i] = J.x[(uint64_t)(t0 + i / K) * J.x_stride + i % K];
+        __syncthreads();
+        for (int r0 = blockIdx.x * TR; r0 < J.rows; r0 += gridDim.x * TR) {
+            const int nr = min(TR, J.rows - r0);
+            for (int u = threadIdx.x; u < units; u += blockDim.x) {
+                const int rr = u / G, g = u % G;
+                if (rr >= nr) continue;
+                const uint8_t *row = J.w + (uint64_t)(r0 + rr) * rb;
+                float s[4] = {0.f, 0.f, 0.f, 0.f};
+                auto add = [&](int l, int d) {  // weight l of the group is d - 1
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        if (t < nt) s[t] = __fadd_rn(s[t], __fmul_rn((float)(d - 1), xs[t * K + g * 128 + l]));
+                };
+                if (KIND == TRX_KIND_TERNARY5) {
+                    const uint8_t *cb = row + sbytes + 26 * g;
+                    for (int i = 0; i < 26; ++i) {
+                        uint32_t b = cb[i];
+                        for (int k = 0; k < 5; ++k) {
+                            const int l = 5 * i + k;
+                            const int d = (int)(b % 3u);
+                            b /= 3u;
+                            if (l < 128) add(l, d);
+                        }
                     }
+                } else {
+                    const uint8_t *cb = row + sbytes + 32 * g;
+                    for (int l = 0; l < 128; ++l) add(l, (cb[l >> 2] >> (2 * (l & 3))) & 3);
                 }
-            } else {
-                const uint8_t *cb = row + sbytes + 32 * g;
-                for (int l = 0; l < 128; ++l) {
-                    const int c = (cb[l >> 2] >> (2 * (l & 3))) & 3;
-                    s = __fadd_rn(s, __fmul_rn((float)(c - 1), xg[l]));
-                }
+                const float sc = __half2float(reinterpret_cast<const __half *>(row)[g]);
+                for (int t = 0; t < nt; ++t) part[(t * TR + rr) * (G + 1) + g] = __fmul_rn(s[t], sc);
             }
-            const float sc = __half2float(reinterpret_cast<const __half *>(row)[g]);
-            part[rr * (G + 1) + g] = __fmul_rn(s, sc);
+            __syncthreads();
+            for (int i = threadIdx.x; i < nt * nr; i += blockDim.x) {
+                const int t = i / nr, rr = i - t * nr;
+                float a = 0.f;
+                for (int g = 0; g < G; ++g) a = __fadd_rn(a, part[(t * TR + rr) * (G + 1) + g]);
+                const uint64_t o = (uint64_t)(t0 + t) * J.y_stride + r0 + rr;
+                if (J.seg[0].resid) a = __fadd_rn(J.seg[0].resid[o], a);
+                y[o] = a;
+            }
+            __syncthreads();
         }
-        __syncthreads();
-        for (int rr = threadIdx.x; rr < nr; rr += blockDim.x) {
-            float a = 0.f;
-            for (int g = 0; g < G; ++g) a = __fadd_rn(a, part[rr * (G + 1) + g]);
-            reinterpret_cast<float *>(J.seg[0].y)[r0 + rr] = a;
-        }
-        __syncthreads();
     }
 }
 
@@ -1380,19 +1393,23 @@ trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cu
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st) {
     const int G = J.cols / 128;
     const int TR = 16;
-    const int smem = J.cols * 4 + TR * (G + 1) * 4;
-    if (smem > kSmemMax) return TRX_ERR_UNSUPPORTED;
+    // Rows of X per chunk: up to 4 while the chunk and the group partials fit shared memory.
+    int TT = 4;
+    auto bytes = [&](int tt) { return (size_t)tt * J.cols * 4 + (size_t)tt * TR * (G + 1) * 4; };
+    while (TT > 1 && bytes(TT) > (size_t)kSmemMax) --TT;
+    const size_t smem = bytes(TT);
+    if (smem > (size_t)kSmemMax || J.njobs < 1) return TRX_ERR_UNSUPPORTED;
     int grid = (J.rows + TR - 1) / TR;
     if (grid > num_sms() * 4) grid = num_sms() * 4;
     cudaError_t e;
     if (J.kind == TRX_KIND_TERNARY5) {
-        e = cudaFuncSetAttribute(tmv_fp_kernel<TRX_KIND_TERNARY5>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(tmv_fp_kernel<TRX_KIND_TERNARY5>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return note_cuda(e);
-        e = launch_kernel(tmv_fp_kernel<TRX_KIND_TERNARY5>, dim3(grid), dim3(256), smem, st, J, TR, err);
+        e = launch_kernel(tmv_fp_kernel<TRX_KIND_TERNARY5>, dim3(grid), dim3(256), smem, st, J, TR, TT, err);
     } else {
-        e = cudaFuncSetAttribute(tmv_fp_kernel<TRX_KIND_TERNARY>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(tmv_fp_kernel<TRX_KIND_TERNARY>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
         if (e != cudaSuccess) return note_cuda(e);
-        e = launch_kernel(tmv_fp_kernel<TRX_KIND_TERNARY>, dim3(grid), dim3(256), smem, st, J, TR, err);
+        e = launch_kernel(tmv_fp_kernel<TRX_KIND_TERNARY>, dim3(grid), dim3(256), smem, st, J, TR, TT, err);
     }
     return note_cuda(e);
 }

@@ -508,6 +508,20 @@ def deltanet_step_rows(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, 
     return out
 
 
+def matvec_fp_rows(ctx, w: DeviceTensor, X, out=None, resid=None):
+    """fp-mode projection of the rows of X [T, cols] float32 (trx_matvec_fp_rows,
+    model/fastref.py:119-125): returns [T, rows] float32 (plus resid)."""
+    _need(X, torch.float32, "X")
+    T = X.shape[0]
+    if out is None:
+        out = torch.empty(T, w.rows, dtype=torch.float32, device=X.device)
+    if resid is not None:
+        _need(resid, torch.float32, "resid")
+    _lib.check(_lib.lib().trx_matvec_fp_rows(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(X), T, _ptr(resid),
+                                             _ptr(out), _stream()), "trx_matvec_fp_rows")
+    return out
+
+
 def deltanet_int_step(ctx, state, exp, maxabs, k, q, v, decay, beta, out=None):
     """The integer DeltaNet head step of nheads heads (trx_deltanet_int_step, model/deltanet.py:99-147):
     state int16 [nheads, hv, hk], exp and maxabs int32 [nheads] (maxabs < 0: computed), k, q float32
