@@ -13,11 +13,13 @@
 //    of their own rows never conflict).
 //  * Row blocks are dealt to CTAs (up to 16 warps, one CTA per SM) in contiguous ranges of
 //    (job, row block) space.  A warp streams its blocks global -> shared through a private ring of
-//    D slots with 16-byte cp.async copies (each copy instruction reads 4 rows x 128 contiguous
-//    bytes), tracked with cp.async.wait_group: no producer warp.  Measured on B200, 1-D bulk (TMA)
-//    copies complete one after another per SM (~0.8 us exposed each) and a 227 KB ring cannot keep
-//    enough of them in flight while blocks are decoded; per-warp cp.async rings keep 70-150 KB in
-//    flight.
+//    D slots: one elected lane issues a block's TMA boxes (per tensor, the codes box {cb bytes, 32
+//    rows} and the scales box {16 bytes, 32 rows} of the packed tensor viewed as [jobs][rows][row
+//    bytes]) on the slot's mbarrier; the lanes wait on it (bounded) and the slot is refilled with
+//    the block D ahead.  No producer warp and no CTA barrier inside a job.  (Measured on B200: the
+//    2-D boxes keep the rings' bytes in flight without the per-copy issue cost of 16-byte cp.async;
+//    the 96-copy config-0 batch went from 2.4 to 3.2 TB/s for trit5 and from 3.9 to 4.7 TB/s for
+//    2-bit.)
 //  * When a CTA holds fewer row blocks than warps (a single decode matvec), S warps share a row
 //    block, each taking a range of its chunks; after every round the S partial int64 sums per row
 //    are added in a fixed order through shared memory behind a named barrier (exact, no atomics).
