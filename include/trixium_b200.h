@@ -121,6 +121,19 @@ trx_status trx_matvec_i8_rows(trx_ctx *ctx, const trx_entry *e, const void *d_pa
 trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x,
                              int nb, const float *d_resid, float *d_y, cudaStream_t stream);
 
+/*
+ * The batched form of trx_matvec_f_multi: nseg <= 4 tensors of the same cols and kind, their row
+ * packets back to back in d_packed, on the same nb <= 32 activation rows d_x [nb][cols] (each row
+ * optionally RMS-normalised with d_norm_w first, the canonical sum of squares of
+ * model/mirror.py:576-591,697-700, then quantised with its own exponent); segment i's rows go to
+ * d_y[i] [nb][rows_i] (device pointers in a host array), plus d_resid[i] when d_resid (a host array
+ * of device pointers or NULLs) is given.  One tensor-core launch (model/bitexact.py:121-125 per
+ * tensor, model/mirror.py:648-678 per row).
+ */
+trx_status trx_matvec_f_rows_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
+                                   const float *d_x, int nb, const float *d_norm_w, float eps, float *const *d_y,
+                                   const float *const *d_resid, cudaStream_t stream);
+
 /* The per-row steps around the batched projections of a decode batch (nrows independent sequences;
  * model/mirror.py:1002-1034 per sequence):
  *   trx_embed_lookup_rows: x[r] = table[tokens[r]] (as trx_embed_lookup, fp16 or fp32 table);

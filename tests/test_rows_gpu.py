@@ -89,3 +89,25 @@ def test_rows_large_tile_count_and_k_split(ops, ctx, kind):
         y2 = ops.matvec_i8_rows(ctx, w, torch.from_numpy(x8).cuda()).cpu().numpy()
         assert np.array_equal(y, y2)
     assert ctx.errors() == 0
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_rows_multi_segments_with_norm(ops, ctx, kind):
+    """trx_matvec_f_rows_multi (three tensors back to back, 128-row-aligned and not, the RMSNorm in
+    front, a residual on one) equals the row-wise norm followed by one batched launch per tensor,
+    bit for bit."""
+    from trixium_b200 import decoder as D, layout as L
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    K = 1024
+    p = D.Packed(gen, [("a", 384), ("b", 200), ("c", 130)], K, kind, "cuda")
+    nb = 12
+    x = torch.randn(nb, K, generator=gen, device="cuda")
+    nw = (1 + 0.1 * torch.randn(K, generator=gen, device="cuda")).contiguous()
+    ys = [torch.empty(nb, e.rows, device="cuda") for e in p.entries]
+    rs = [None, torch.randn(nb, 200, generator=gen, device="cuda"), None]
+    ops.matvec_f_rows_multi(ctx, p.entries, p.data, x, ys, norm_w=nw, eps=1e-6, resids=rs)
+    h = ops.rmsnorm_rows(ctx, x, nw, 1e-6)
+    for i in range(3):
+        want = ops.matvec_f_rows(ctx, p.tensor(i), h, resid=rs[i])
+        assert torch.equal(ys[i].view(torch.int32), want.view(torch.int32)), i
+    assert ctx.errors() == 0

@@ -28,7 +28,7 @@ SYMBOLS = (
     "trx_attn_decode_tp", "trx_embed_lookup_bfp16", "trx_rmsnorm", "trx_matvec_f_kseg",
     "trx_attn_decode_f32cache", "trx_matvec_f_rows", "trx_embed_lookup_rows", "trx_rmsnorm_rows", "trx_silu_mul",
     "trx_argmax_rows", "trx_advance_positions", "trx_attn_decode_rows", "trx_deltanet_step_rows",
-    "trx_deltanet_int_step", "trx_matvec_fp_rows",
+    "trx_deltanet_int_step", "trx_matvec_fp_rows", "trx_matvec_f_rows_multi",
 )
 
 TP_MAX = 8
@@ -146,6 +146,8 @@ def lib():
             "trx_deltanet_int_step": ([_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32] + [_vp] * 10,
                                       ctypes.c_int),
             "trx_matvec_fp_rows": ([_vp, E, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp], ctypes.c_int),
+            "trx_matvec_f_rows_multi": ([_vp, E, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp, ctypes.c_float, _vp, _vp,
+                                         _vp], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -219,10 +219,11 @@ trx_status trx_matvec_q8_f(trx_ctx *ctx, const trx_entry *e, const void *d_packe
 
 static trx_status rows_tc(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, const int8_t *d_x8,
                           int nb, int32_t *d_out_i, float *d_out_f, const float *d_resid, cudaStream_t stream) {
-    return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed), (int)e->rows, (int)e->cols, e->kind,
-                                   e->bias, e->rshift, d_x, d_x8, nb, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8,
-                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsCnt, d_out_i, d_out_f, d_resid,
-                                   ctx->err, trx::device_sms(), trx::device_reserved_smem(), stream);
+    trx::RowsSeg sg{(int)e->rows, e->bias, e->rshift, d_out_i, d_out_f, d_resid};
+    return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed), (int)e->cols, e->kind, &sg, 1, d_x, d_x8, nb,
+                                   nullptr, 0.f, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8, ctx->rows_acc, kRowsAcc,
+                                   ctx->rows_cnt, kRowsCnt, ctx->err, trx::device_sms(), trx::device_reserved_smem(),
+                                   stream);
 }
 
 trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, int nb,
@@ -232,6 +233,24 @@ trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_pac
     if (s) return s;
     if (!d_packed || !d_x || !d_y || nb < 1 || nb > kRowsMax || !aligned16(d_packed)) return TRX_ERR_ARG;
     return rows_tc(ctx, e, d_packed, d_x, nullptr, nb, nullptr, d_y, d_resid, stream);
+}
+
+trx_status trx_matvec_f_rows_multi(trx_ctx *ctx, const trx_entry *entries, int nseg, const void *d_packed,
+                                   const float *d_x, int nb, const float *d_norm_w, float eps, float *const *d_y,
+                                   const float *const *d_resid, cudaStream_t stream) {
+    if (!ctx || !entries || !d_y || nseg < 1 || nseg > trx::kRowsMaxSegs) return TRX_ERR_ARG;
+    if (!d_packed || !d_x || nb < 1 || nb > kRowsMax || !aligned16(d_packed) || !(eps >= 0.f)) return TRX_ERR_ARG;
+    trx::RowsSeg sg[trx::kRowsMaxSegs];
+    for (int i = 0; i < nseg; ++i) {
+        if (trx_status s = check_entry(entries + i)) return s;
+        if (entries[i].cols != entries[0].cols || entries[i].kind != entries[0].kind || !d_y[i]) return TRX_ERR_ARG;
+        sg[i] = trx::RowsSeg{(int)entries[i].rows, entries[i].bias, entries[i].rshift, nullptr, d_y[i],
+                             d_resid ? d_resid[i] : nullptr};
+    }
+    return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed), (int)entries[0].cols, entries[0].kind, sg,
+                                   nseg, d_x, nullptr, nb, d_norm_w, eps, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8,
+                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsCnt, ctx->err, trx::device_sms(),
+                                   trx::device_reserved_smem(), stream);
 }
 
 trx_status trx_embed_lookup_rows(trx_ctx *ctx, const void *d_table, uint32_t vocab, uint32_t dim, int32_t f16,

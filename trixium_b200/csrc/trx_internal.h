@@ -187,13 +187,22 @@ trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token,
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st);
 // Batched rows on the tensor cores (trx_rows.cu): nb <= 32 rows of x (fp32, each quantised with its
-// own exponent) or x8 (int8), int32 or fp32 outputs [nb][N].  x8p/xsum/e8: scratch of nb*K bytes,
-// K/128*32 ints and nb ints; acc_scratch (acc_cap int64) and cnt (cnt_cap per-row counts) zero
-// between launches.
-trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, int R, const float *x, const int8_t *x8,
-                              int nb, int8_t *x8p, int *xsum, int *e8, unsigned long long *acc_scratch,
-                              size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f,
-                              const float *resid, uint32_t *err, int sms, int reserved, cudaStream_t st);
+// own exponent, optionally RMS-normalised first with norm_w) or x8 (int8), against nseg <= 4 tensors
+// of the same cols and kind packed back to back (segment s: rows, its B and R, int32 or fp32 output
+// [nb][rows], an optional fp32 residual [nb][rows]).  x8p/xsum/e8: scratch of nb*K bytes, K/128*32
+// ints and nb ints; acc_scratch (acc_cap int64) and cnt (cnt_cap per-row counts) zero between
+// launches.
+struct RowsSeg {
+    int rows, B, R;
+    int32_t *out_i;
+    float *out_f;
+    const float *resid;
+};
+constexpr int kRowsMaxSegs = 4;
+trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *segs, int nseg, const float *x,
+                              const int8_t *x8, int nb, const float *norm_w, float eps, int8_t *x8p, int *xsum,
+                              int *e8, unsigned long long *acc_scratch, size_t acc_cap, unsigned *cnt, int cnt_cap,
+                              uint32_t *err, int sms, int reserved, cudaStream_t st);
 int device_sms();
 int device_reserved_smem();
 // The Q8 row dot (trx_q8.cu): int32 results, or with e8 the float projection (fp32 out).

@@ -173,20 +173,39 @@ __host__ __device__ __forceinline__ int slot_lane(int kind, int s) {
     return 16 * (s >> 4) + 4 * (s & 3) + ((s >> 2) & 3);
 }
 
-// Per batch row: the quantised activation (fp32 rows: the power-of-two quantiser with its own
-// exponent, model/mirror.py:45-51; int8 rows: as given), permuted per group to the decoders' K
-// order (x8p [nb][K]), and each group's activation sum (xsum [G][32], batch row minor).  One CTA per
-// batch row.
-__global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const int8_t *x8, int K, int kind,
-                                                        int8_t *x8p, int *xsum, int *e8_out) {
-    extern __shared__ int8_t q[];  // K bytes
+// Per batch row: the quantised activation (fp32 rows: optionally RMS-normalised first, y = (x * r) * w
+// with the canonical 64-partial sum of squares, model/mirror.py:576-591,697-700; then the
+// power-of-two quantiser with its own exponent, model/mirror.py:45-51; int8 rows: as given), permuted
+// per group to the decoders' K order (x8p [nb][K]), and each group's activation sum (xsum [G][32],
+// batch row minor).  One CTA of 256 threads per batch row; K floats (norm) + K bytes of shared memory.
+__global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const int8_t *x8, const float *nw, float eps,
+                                                        int K, int kind, int8_t *x8p, int *xsum, int *e8_out) {
+    extern __shared__ __align__(16) unsigned char prep_smem[];
+    int8_t *const q = reinterpret_cast<int8_t *>(prep_smem);  // K bytes
+    float *const v = reinterpret_cast<float *>(prep_smem + (K + 15) / 16 * 16);  // K floats (norm only)
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.x, t = threadIdx.x;
     __shared__ uint32_t amax_s;
+    __shared__ float part[64];
     if (x) {
         const float *xr = x + (size_t)b * K;
         if (t == 0) amax_s = 0;
+        if (nw) {
+            if (t < 64) {
+                float p = 0.f;
+                for (int i = t; i < K; i += 64) p = __fadd_rn(p, __fmul_rn(xr[i], xr[i]));
+                part[t] = p;
+            }
+            __syncthreads();
+            for (int h = 32; h >= 1; h >>= 1) {
+                if (t < h) part[t] = __fadd_rn(part[t], part[t + h]);
+                __syncthreads();
+            }
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(part[0], (float)K), eps)));
+            for (int i = t; i < K; i += blockDim.x) v[i] = __fmul_rn(__fmul_rn(xr[i], r), nw[i]);
+            xr = v;
+        }
         __syncthreads();
         uint32_t m = 0;
         for (int k = t; k < K; k += blockDim.x) {
@@ -201,10 +220,10 @@ __global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const in
         const float inv = amax ? pow2f(-e8) : 0.f;
         for (int k = t; k < K; k += blockDim.x) {
             // The mirror's rounding: floor(|x| 2^-e8 + 0.5) in fp32, clamped to 127, signed.
-            const float v = __fmul_rn(xr[k], inv);
-            const float a = __fadd_rn(fabsf(v), 0.5f);
+            const float vv = __fmul_rn(xr[k], inv);
+            const float a = __fadd_rn(fabsf(vv), 0.5f);
             const int mm = a < 128.0f ? (int)floorf(a) : 127;
-            q[k] = (int8_t)(v < 0.f ? -mm : mm);
+            q[k] = (int8_t)(vv < 0.f ? -mm : mm);
         }
         if (t == 0) e8_out[b] = e8;
     } else {
@@ -230,13 +249,12 @@ __global__ void __launch_bounds__(256) rows_prep_kernel(const float *x, const in
 // One batched launch (host-built, by value).
 struct RowsArgs {
     int N, K, G, nch, sbytes, rb, kind, nb;
-    int B, R;
     int tiles, ks, cps;       // row tiles, K splits per tile, chunks per split (unit u: tile u / ks, split u % ks)
     const int *xsum;          // [G][32]
     const int *e8;            // [nb] (float outputs)
-    int32_t *out_i;           // [nb][N] int32, or
-    float *out_f;             // [nb][N] fp32
-    const float *resid;       // [nb][N] added to the fp32 results, or nullptr
+    int nseg;                 // segments (tensors packed back to back): rows [start, end) of the launch
+    int seg_end[kRowsMaxSegs];
+    RowsSeg seg[kRowsMaxSegs];  // B, R, output [nb][rows] (int32 or fp32), residual of each
     unsigned long long *acc;  // [nb][N] int64 partial sums (ks > 1), zero between launches
     unsigned *cnt;            // [tiles] arrival counts (ks > 1), zero between launches
     RowsPlan P;
@@ -560,7 +578,10 @@ __global__ void __maxnreg__(128)
         const uint32_t tA0 = tmem + (uint32_t)W * kWgCols, tD0 = tA0 + 64u;  // MMA operand addresses (lane 0)
         const uint32_t tA = tA0 + lane_base, tD = tD0 + lane_base;          // this warp's lanes
         const uint32_t idesc = umma_idesc_i8<BN>();
-        const ScaleFast F = scale_fast(A.B);
+        // This thread's row of the current unit: its segment (tensor) gives B and the fast range.
+        int Brow = A.seg[0].B;
+        ScaleFast F = scale_fast(Brow);
+        int cur_unit = -1;
         long long acc[BN];
 #pragma unroll
         for (int b = 0; b < BN; ++b) acc[b] = 0;
@@ -602,19 +623,25 @@ __global__ void __maxnreg__(128)
                 for (int b = 0; b < BN; ++b) acc[b] += (long long)v[b] * fs;
             } else {
 #pragma unroll
-                for (int b = 0; b < BN; ++b) acc[b] += group_contrib(v[b], sb, A.B);
+                for (int b = 0; b < BN; ++b) acc[b] += group_contrib(v[b], sb, Brow);
             }
             return true;
         };
         auto finish = [&](int b, int n, long long a) {
-            if (acc_bad(a, A.R)) atomicOr(err, TRX_DEV_OVERFLOW);
-            const int res = (int)(a >> A.R);
-            if (A.out_f) {
-                float y = __fmul_rn((float)res, pow2f(A.e8[b] + A.R - A.B));
-                if (A.resid) y = __fadd_rn(A.resid[(size_t)b * A.N + n], y);
-                A.out_f[(size_t)b * A.N + n] = y;
+            int sg = 0;
+#pragma unroll
+            for (int i = 0; i < kRowsMaxSegs - 1; ++i) sg += (i < A.nseg - 1 && n >= A.seg_end[i]) ? 1 : 0;
+            const RowsSeg &S = A.seg[sg];
+            const int sn = n - (sg ? A.seg_end[sg - 1] : 0);  // the row within its tensor
+            if (acc_bad(a, S.R)) atomicOr(err, TRX_DEV_OVERFLOW);
+            const int res = (int)(a >> S.R);
+            const size_t o = (size_t)b * S.rows + sn;
+            if (S.out_f) {
+                float y = __fmul_rn((float)res, pow2f(A.e8[b] + S.R - S.B));
+                if (S.resid) y = __fadd_rn(S.resid[o], y);
+                S.out_f[o] = y;
             } else {
-                A.out_i[(size_t)b * A.N + n] = res;
+                S.out_i[o] = res;
             }
         };
         // A unit's rows are done: output them (whole K), or add the partial sums and let the row's
@@ -653,6 +680,15 @@ __global__ void __maxnreg__(128)
             if (bars->dead) {
                 alive = false;
                 break;
+            }
+            if (unit != cur_unit) {  // a new unit: this thread's row, its tensor's B
+                cur_unit = unit;
+                const int n = (unit / A.ks) * kRowsM + r;
+                int sg = 0;
+#pragma unroll
+                for (int i = 0; i < kRowsMaxSegs - 1; ++i) sg += (i < A.nseg - 1 && n >= A.seg_end[i]) ? 1 : 0;
+                Brow = A.seg[sg].B;
+                F = scale_fast(Brow);
             }
             const int slot = W * Dw + wpos % Dw;
             if (!warp_wait(bfull + 8u * slot, (uint32_t)(wpos / Dw) & 1u)) {
@@ -820,12 +856,20 @@ static trx_status launch_rows_t(const RowsMaps &maps, const RowsArgs &A, int gri
                                    maps, A, err));
 }
 
-trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, int R, const float *x, const int8_t *x8,
-                              int nb, int8_t *x8p, int *xsum, int *e8, unsigned long long *acc_scratch,
-                              size_t acc_cap, unsigned *cnt, int cnt_cap, int32_t *out_i, float *out_f,
-                              const float *resid, uint32_t *err, int sms, int reserved, cudaStream_t st) {
+trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *segs, int nseg, const float *x,
+                              const int8_t *x8, int nb, const float *norm_w, float eps, int8_t *x8p, int *xsum,
+                              int *e8, unsigned long long *acc_scratch, size_t acc_cap, unsigned *cnt, int cnt_cap,
+                              uint32_t *err, int sms, int reserved, cudaStream_t st) {
+    if (nseg < 1 || nseg > kRowsMaxSegs) return TRX_ERR_ARG;
+    int N = 0;
     const int BN = nb <= 16 ? 16 : 32;
     RowsArgs A{};
+    A.nseg = nseg;
+    for (int i = 0; i < nseg; ++i) {
+        A.seg[i] = segs[i];
+        N += segs[i].rows;
+        A.seg_end[i] = N;
+    }
     A.N = N;
     A.K = K;
     A.G = K / 128;
@@ -834,8 +878,6 @@ trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, i
     A.rb = A.sbytes + ((kind == TRX_KIND_TERNARY5 ? 26 : 32) * A.G + 31) / 32 * 32;
     A.kind = kind;
     A.nb = nb;
-    A.B = B;
-    A.R = R;
     // Units: (128-row tile, K range).  Split K when the tiles alone give fewer units than the SMs'
     // decoder warpgroups, within the scratch the partial sums and per-row counts need.
     const int nwg = BN == 16 ? rows_nwg<16>() : rows_nwg<32>();
@@ -849,9 +891,6 @@ trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, i
     }
     A.xsum = xsum;
     A.e8 = e8;
-    A.out_i = out_i;
-    A.out_f = out_f;
-    A.resid = resid;
     A.acc = acc_scratch;
     A.cnt = cnt;
     A.base = reserved;
@@ -868,7 +907,15 @@ trx_status launch_matvec_rows(const uint8_t *w, int N, int K, int kind, int B, i
         !encode(&maps.xp, x8p, xd, xs, xbox, CU_TENSOR_MAP_SWIZZLE_128B))
         return TRX_ERR_CUDA;
     // The permuted activation, its group sums and exponents (one CTA per batch row).
-    cudaError_t e = launch_kernel(rows_prep_kernel, dim3(nb), dim3(256), (size_t)K, st, x, x8, K, kind, x8p, xsum, e8);
+    const size_t prep_smem = (size_t)(K + 15) / 16 * 16 + (norm_w ? (size_t)K * 4 : 0);
+    constexpr int kPrepSmemMax = 192 * 1024;  // K <= 32768: 32 KiB of q8 and 128 KiB of normalised x
+    if (prep_smem > (size_t)kPrepSmemMax) return TRX_ERR_UNSUPPORTED;
+    static DevBits prep_configured{0};
+    cudaError_t e = once_per_device(prep_configured, [] {
+        return cudaFuncSetAttribute(rows_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmemMax);
+    });
+    if (e != cudaSuccess) return note_cuda(e);
+    e = launch_kernel(rows_prep_kernel, dim3(nb), dim3(256), prep_smem, st, x, x8, norm_w, eps, K, kind, x8p, xsum, e8);
     if (e != cudaSuccess) return note_cuda(e);
     const int units = A.tiles * A.ks;
     const int grid = std::max(1, std::min(sms, (units + nwg - 1) / nwg));

@@ -372,12 +372,14 @@ class Decoder:
 
 class BatchDecoder:
     """Greedy decoding of nseq <= 32 independent sequences in lockstep (BASELINE config 2 at batch
-    16): every projection is one tensor-core launch over the sequences' rows (trx_matvec_f_rows, each
-    row quantised with its own exponent as the batch-1 projection quantises its vector), the norms,
-    SwiGLU, argmax and position advance are row-wise kernels, and attention and the DeltaNet step run
-    over a sequence grid dimension with per-sequence caches, states and positions.  The arithmetic of
-    every sequence is the batch-1 decoder's (mirror.py:1002-1034).  K-segmented tensors (the
-    hybrid-27b down projection) are not taken: one batched launch covers one engine op's K."""
+    16): the tensors sharing an input run as one tensor-core launch over the sequences' rows
+    (trx_matvec_f_rows_multi: q/k/v or qkv/z/beta/alpha, gate/up; the RMSNorm in front, each row
+    quantised with its own exponent as the batch-1 projection quantises its vector), the output and
+    down projections add the residual, SwiGLU, the final norm, argmax and position advance are
+    row-wise kernels, and attention and the DeltaNet step run over a sequence grid dimension with
+    per-sequence caches, states and positions.  The arithmetic of every sequence is the batch-1
+    decoder's (mirror.py:1002-1034).  K-segmented tensors (the hybrid-27b down projection) are not
+    taken: one batched launch covers one engine op's K."""
 
     def __init__(self, weights: SyntheticWeights, nseq, ctx=None, max_pos=4096, kv_dtype=torch.float16):
         cfg = self.cfg = weights.cfg
@@ -413,9 +415,6 @@ class BatchDecoder:
             self.qkv, self.z = f32(B, cfg.dn_channels), f32(B, cfg.dn_nv * cfg.dn_hv)
             self.beta, self.alpha = f32(B, cfg.dn_nv), f32(B, cfg.dn_nv)
             self.og = f32(B, cfg.dn_nv * cfg.dn_hv)
-        # The segments of every layer's input projection as tensors of their own (views of the
-        # packed allocation).
-        self.in_t = [[lw["in"].tensor(i) for i in range(len(lw["in"].entries))] for lw in weights.layers]
         self.graph = None
 
     def _mutable(self):
@@ -443,24 +442,23 @@ class BatchDecoder:
         cfg, w, ctx = self.cfg, self.w, self.ctx
         ops.embed_lookup_rows(ctx, w.emb, self.tok, self.x)
         for l, lw in enumerate(w.layers):
-            seg = self.in_t[l]
-            ops.rmsnorm_rows(ctx, self.x, lw["attn_norm"], cfg.eps, y=self.h)
+            p = lw["in"]
             if cfg.layer_type(l) == "d":
-                for t, y in zip(seg, (self.qkv, self.z, self.beta, self.alpha)):
-                    ops.matvec_f_rows(ctx, t, self.h, out=y)
+                ops.matvec_f_rows_multi(ctx, p.entries, p.data, self.x, [self.qkv, self.z, self.beta, self.alpha],
+                                        norm_w=lw["attn_norm"], eps=cfg.eps)
                 ops.deltanet_step_rows(ctx, self.dn_shape, self.qkv, self.z, self.beta, self.alpha, lw["dt_bias"],
                                        lw["ssm_a"], lw["conv_w"], lw["ssm_norm"], self.ring[l], self.state[l], self.pos,
                                        self.og)
                 ops.matvec_f_rows(ctx, lw["out"], self.og, out=self.x, resid=self.x)
             else:
-                for t, y in zip(seg, (self.q, self.k, self.v)):
-                    ops.matvec_f_rows(ctx, t, self.h, out=y)
+                ops.matvec_f_rows_multi(ctx, p.entries, p.data, self.x, [self.q, self.k, self.v],
+                                        norm_w=lw["attn_norm"], eps=cfg.eps)
                 ops.attn_decode_rows(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"],
                                      w.rope_freq, self.kc[l], self.vc[l], self.pos, self.attn)
                 ops.matvec_f_rows(ctx, lw["out"], self.attn, out=self.x, resid=self.x)
-            ops.rmsnorm_rows(ctx, self.x, lw["ffn_norm"], cfg.eps, y=self.h)
-            ops.matvec_f_rows(ctx, lw["gate"], self.h, out=self.g)
-            ops.matvec_f_rows(ctx, lw["up"], self.h, out=self.u)
+            ffn = lw["ffn_packed"]
+            ops.matvec_f_rows_multi(ctx, ffn.entries, ffn.data, self.x, [self.g, self.u], norm_w=lw["ffn_norm"],
+                                    eps=cfg.eps)
             ops.silu_mul(ctx, self.g, self.u, self.act)
             ops.matvec_f_rows(ctx, lw["down"], self.act, out=self.x, resid=self.x)
         ops.rmsnorm_rows(ctx, self.x, w.out_norm, cfg.eps, y=self.h)

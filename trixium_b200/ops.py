@@ -375,6 +375,23 @@ def matvec_f_multi(ctx, entries, packed, x, ys, norm_w=None, eps=1e-6, resids=No
     return ys
 
 
+def matvec_f_rows_multi(ctx, entries, packed, xrows, ys, norm_w=None, eps=1e-6, resids=None):
+    """The batched form of matvec_f_multi (trx_matvec_f_rows_multi): up to 4 tensors packed back to
+    back on the same activation rows xrows [nb, cols] (optionally RMS-normalised per row first); ys:
+    one [nb, rows_i] float32 output per tensor, resids the same or None."""
+    n = len(entries)
+    _need(xrows, torch.float32, "xrows")
+    arr = (_lib.Entry * n)(*entries)
+    yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    rp = None
+    if resids is not None:
+        rp = (ctypes.c_void_p * n)(*[(r.data_ptr() if r is not None else None) for r in resids])
+    _lib.check(_lib.lib().trx_matvec_f_rows_multi(ctx.h, arr, n, _ptr(packed), _ptr(xrows), xrows.shape[0],
+                                                  _ptr(norm_w), ctypes.c_float(eps), yp, rp, _stream()),
+               "trx_matvec_f_rows_multi")
+    return ys
+
+
 def embed_lookup(ctx, table, token, x):
     """x = table[token] (float16 or float32 table [vocab, dim]; token: int32 device tensor)."""
     _need(token, torch.int32, "token")
