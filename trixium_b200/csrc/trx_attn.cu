@@ -887,27 +887,38 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
     __syncthreads();
     // Combine the warps in order: M = max m_w, o = sum e^(m_w - M) o_w, l = sum e^(m_w - M) l_w.
     const int nwu = min(NWARP, max(nb16, 1));  // warps that held a block (warp 0 at least, possibly empty)
-    for (int i = tid; i < rep * HD; i += kClThreads) {
-        const int r = i / HD, d = i - r * HD;
-        float M = -INFINITY;
-        for (int w = 0; w < nwu; ++w) M = fmaxf(M, wp[(w * rep + r) * (HD + 2)]);
-        float o = 0.f;
-        if (M != -INFINITY)
-            for (int w = 0; w < nwu; ++w) {
-                const float *pw = wp + (w * rep + r) * (HD + 2);
-                o = fmaf(expf(pw[0] - M), pw[2 + d], o);
-            }
-        om[i] = o;
-        if (d == 0) {
-            float L = 0.f;
-            if (M != -INFINITY)
-                for (int w = 0; w < nwu; ++w) {
-                    const float *pw = wp + (w * rep + r) * (HD + 2);
-                    L = fmaf(expf(pw[0] - M), pw[1], L);
-                }
+    // Warps 0-1, one lane per (row r, warp w): M_r by a shuffle over the row's 8 lanes, then the
+    // warp's scale e^(m_w - M_r) into wt[8 r + w] (free until the rank-0 merge), and l_r summed in
+    // warp order by the row's first lane.  rep <= 8, so 64 lanes cover every (r, w).
+    if (tid < 64) {
+        const int r = tid >> 3, w = tid & 7;
+        const bool live = r < rep && w < nwu;
+        const float mw = live ? wp[(w * rep + r) * (HD + 2)] : -INFINITY;
+        float M = mw;
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
+        const float e = (live && M != -INFINITY) ? expf(mw - M) : 0.f;
+        const float lw = live ? wp[(w * rep + r) * (HD + 2) + 1] : 0.f;
+        if (r < rep) wt[r * 8 + w] = e;
+        float L = 0.f;
+        for (int j = 0; j < NWARP; ++j) {
+            const float ej = __shfl_sync(0xffffffffu, e, (lane & ~7) + j), lj = __shfl_sync(0xffffffffu, lw, (lane & ~7) + j);
+            if (j < nwu && M != -INFINITY) L = fmaf(ej, lj, L);
+        }
+        if (w == 0 && r < rep) {
             mrow[r] = M;
             lrow[r] = L;
         }
+    }
+    __syncthreads();
+    // o = sum e^(m_w - M) o_w in warp order.
+    for (int i = tid; i < rep * HD; i += kClThreads) {
+        const int r = i / HD, d = i - r * HD;
+        float o = 0.f;
+        if (mrow[r] != -INFINITY)
+            for (int w = 0; w < nwu; ++w) o = fmaf(wt[r * 8 + w], wp[(w * rep + r) * (HD + 2) + 2 + d], o);
+        om[i] = o;
     }
     // Merge at rank 0, as in attn_cluster_kernel.
     const int slot = rep * (HD + 2);
