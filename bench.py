@@ -53,10 +53,13 @@ def measured_peaks():
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one 96-copy batch launch of the
-# matvec kernel, per kind, from the ncu capture summarised in profiles/matvec_k{kind}_config0_ncu.md,
+# matvec kernel, per kind, from the ncu capture summarised in profiles/matvec_config0_traffic.md,
 # with the sha256 of the kernel sources it was captured from.  When the sources have changed since,
 # the figure no longer describes the kernel and the line reports null.
-KERNEL_TRAFFIC = {}
+KERNEL_TRAFFIC = {
+    5: (267212288, "fb19ef16cb50051c38524e1ed8d7971293c36053c1c31b17066472a07663675e"),
+    0: (324044288, "fb19ef16cb50051c38524e1ed8d7971293c36053c1c31b17066472a07663675e"),
+}
 KERNEL_SOURCES = ("trixium_b200/csrc/trx_matvec.cu", "trixium_b200/csrc/trx_common.cuh")
 
 
