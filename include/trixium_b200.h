@@ -427,6 +427,15 @@ typedef struct trx_tp_xfer {
     const uint32_t *wait;            /* this rank's counter to wait on, or NULL           */
     const int32_t *step;             /* this rank's step counter                          */
     uint32_t *arrive;                /* arrival count of the signalling launch            */
+    /* Tagged words (tag_points > 0).  Each element of an exchanged vector is one 64-bit word, the
+     * value's bits | tag << 32, written by one single-copy-atomic store; the tag of gather point p
+     * at step s is s * tag_points + p + 1.  tag_out >= 0: the output goes to dst[r] of EVERY rank
+     * (this rank's included) as tagged words, and signal/arrive are not used.  tag_in >= 0: d_x
+     * points to tagged words, and the kernel reads each one once it carries point tag_in's tag
+     * of this step (bounded wait, TRX_DEV_TIMEOUT); wait is not used.  All zero: counters only. */
+    uint32_t tag_points;
+    int32_t tag_out;                 /* gather point of the output, or -1                */
+    int32_t tag_in;                  /* gather point of the tagged input, or -1          */
 } trx_tp_xfer;
 
 /* trx_matvec_f with an exchange: float results copied to dst (offset + row), input waited on. */

@@ -69,7 +69,15 @@ class TpXfer(ctypes.Structure):
     """trx_tp_xfer: a launch's tensor-parallel exchange over peer memory."""
     _fields_ = [("world", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("dst", ctypes.c_void_p * TP_MAX),
                 ("offset", ctypes.c_uint32), ("signal", ctypes.c_void_p * TP_MAX), ("wait", ctypes.c_void_p),
-                ("step", ctypes.c_void_p), ("arrive", ctypes.c_void_p)]
+                ("step", ctypes.c_void_p), ("arrive", ctypes.c_void_p), ("tag_points", ctypes.c_uint32),
+                ("tag_out", ctypes.c_int32), ("tag_in", ctypes.c_int32)]
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        if "tag_out" not in k:
+            self.tag_out = -1
+        if "tag_in" not in k:
+            self.tag_in = -1
 
 
 class Entry(ctypes.Structure):

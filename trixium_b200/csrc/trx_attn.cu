@@ -960,9 +960,7 @@ __global__ void __launch_bounds__(kClThreads, 2) attn_mma_kernel(AttnArgs A, uin
             o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg))));
         }
         A.out[(size_t)h * HD + d] = o;
-        for (int rr = 0; rr < A.tp.world; ++rr)  // the other ranks' copies (tensor-parallel gather)
-            if (rr != A.tp.rank && A.tp.dst[rr])
-                reinterpret_cast<float *>(A.tp.dst[rr])[A.tp.offset + (size_t)h * HD + d] = o;
+        if (A.tp.world) tp_push_all(A.tp, (size_t)h * HD + d, o);  // the ranks' copies (tensor-parallel gather)
     }
     tp_signal(A.tp, gridDim.y);  // the rank-0 CTAs of the clusters arrive
 }

@@ -332,6 +332,24 @@ static trx_status tp_resolve(const trx_tp_xfer *t, int what, trx::TpXfer &X) {
         X.wait = t->wait;
         X.step = t->step;
     }
+    if (t->tag_points) {  // tagged words: every rank's dst for the output, the input polled
+        if (!t->step || t->tag_out >= (int32_t)t->tag_points || t->tag_in >= (int32_t)t->tag_points) return TRX_ERR_ARG;
+        X.tag_points = t->tag_points;
+        X.step = t->step;
+        X.tag_out = (what & TP_PUSH) ? t->tag_out : -1;
+        X.tag_in = (what & TP_WAIT) ? t->tag_in : -1;
+        if (X.tag_out >= 0) {
+            for (uint32_t r = 0; r < t->world; ++r) {
+                if (!t->dst[r] || (reinterpret_cast<uintptr_t>(t->dst[r]) & 7)) return TRX_ERR_ARG;
+                X.dst[r] = t->dst[r];
+            }
+            for (int r = 0; r < trx::kTpMax; ++r) X.signal[r] = nullptr;  // no counters for a tagged output
+            X.arrive = nullptr;
+        }
+        if (X.tag_in >= 0) X.wait = nullptr;
+    } else {
+        X.tag_out = X.tag_in = -1;
+    }
     return TRX_OK;
 }
 

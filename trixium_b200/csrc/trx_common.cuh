@@ -168,6 +168,38 @@ __device__ __forceinline__ void tp_signal(const T &X, unsigned arrivals) {
     }
 }
 
+// Tagged words (TpXfer::tag_points > 0): value bits | tag << 32 in one 64-bit store.
+template <typename T>
+__device__ __forceinline__ unsigned tp_tag(const T &X, int point) {
+    return (unsigned)(*X.step) * X.tag_points + (unsigned)point + 1u;
+}
+
+__device__ __forceinline__ void st_tagged(void *base, size_t i, float v, unsigned tag) {
+    const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(reinterpret_cast<unsigned long long *>(base) + i), "l"(w)
+                 : "memory");
+}
+
+__device__ __forceinline__ ulonglong2 ld_tagged2(const ulonglong2 *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// Result i of a producing launch into the exchange: tagged words into every rank's copy, or plain
+// floats into the other ranks' copies (the counter protocol; this rank's own copy is the launch's
+// output).
+template <typename T>
+__device__ __forceinline__ void tp_push_all(const T &X, size_t i, float v) {
+    if (X.tag_out >= 0 && X.tag_points) {
+        const unsigned tag = tp_tag(X, X.tag_out);
+        for (int r = 0; r < X.world; ++r) st_tagged(X.dst[r], X.offset + i, v, tag);
+    } else {
+        for (int r = 0; r < X.world; ++r)
+            if (r != X.rank && X.dst[r]) reinterpret_cast<float *>(X.dst[r])[X.offset + i] = v;
+    }
+}
+
 // Integer dot products ---------------------------------------------------------------------------
 // acc + sum_k a.byte[k] * b.byte[k], a's bytes unsigned, b's signed (PTX dp4a.u32.s32).
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int acc) {

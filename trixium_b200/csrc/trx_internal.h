@@ -64,6 +64,12 @@ struct TpXfer {
     const unsigned *wait;       // this rank's counter to wait on before reading the input (nullptr: none)
     const int *step;            // this rank's step counter
     unsigned *arrive;           // this launch's arrival count, zero between launches
+    // Tagged words (tag_points > 0): an element is one 64-bit word, value bits | tag << 32, stored
+    // in one single-copy-atomic access, so a reader that sees the tag sees the value (no fence, no
+    // counter).  The tag of gather point p at step s is s * tag_points + p + 1.
+    unsigned tag_points;        // gather points per step (0: no tagged words)
+    int tag_out;                // the point this launch's output fills in every rank's dst, or -1
+    int tag_in;                 // the point of the tagged input this launch reads, or -1
 };
 
 constexpr int kMaxSegs = 4;

@@ -376,32 +376,69 @@ __device__ __forceinline__ uint32_t absmax4(float4 v) {
                max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
 }
 
+// x as tagged words (tensor-parallel exchange): every thread polls its words, eight loads in flight,
+// until each carries `tag`, and writes the values to xs.  False when a wait ran out (recorded).
+__device__ __forceinline__ bool gather_tagged(const unsigned long long *xt, unsigned tag, int K, float *xs,
+                                              uint32_t *err) {
+    constexpr int U = 8;
+    const ulonglong2 *const p = reinterpret_cast<const ulonglong2 *>(xt);
+    float2 *const xs2 = reinterpret_cast<float2 *>(xs);
+    const int n2 = K / 2, nt = blockDim.x;
+    unsigned long long t0 = 0ull;
+    for (int base = threadIdx.x; base < n2; base += U * nt) {
+        ulonglong2 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (base + u * nt < n2) v[u] = ld_tagged2(p + base + u * nt);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * nt;
+            if (i < n2) {
+                while ((unsigned)(v[u].x >> 32) != tag || (unsigned)(v[u].y >> 32) != tag) {
+                    if (!t0) {
+                        t0 = global_ns();
+                    } else if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(err, TRX_DEV_TIMEOUT);
+                        return false;
+                    }
+                    v[u] = ld_tagged2(p + i);
+                }
+                xs2[i] = make_float2(__uint_as_float((uint32_t)v[u].x), __uint_as_float((uint32_t)v[u].y));
+            }
+        }
+    }
+    return true;
+}
+
 template <int KIND>
 __device__ int build_activation_cp(const float *x, const float *nw, bool nw_ready, float eps, int K, float *xs,
                                    float *nws, uint32_t *xp, float *red64, uint64_t *mb, uint32_t parity,
-                                   uint32_t *err, bool &ok) {
+                                   uint32_t *err, bool &ok, unsigned xtag) {
     const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5, nwarps = blockDim.x >> 5;
     const int G = K / 128, n4 = K / 4;
     float4 *const xs4 = reinterpret_cast<float4 *>(xs);
     // One bulk copy each (tracked by its own barrier, not by the weight rings' barriers); thread 0
     // waits, bounded, and the block learns the outcome at the barrier.  (Measured on B200 in decode
     // launches: the bulk copy of x reaches the built activation sooner than coalesced loads by
-    // every thread.)
+    // every thread.)  xtag != 0: x is tagged words, polled by every thread instead.
     uint32_t *const flag = reinterpret_cast<uint32_t *>(red64) + 48;
     if (ct == 0) {
         fence_proxy_async();  // earlier generic accesses to these bytes come first
-        mbar_arrive_expect_tx(mb, 4u * K);
-        bulk_g2s(xs, x, 4u * K, mb);
+        if (!xtag) {
+            mbar_arrive_expect_tx(mb, 4u * K);
+            bulk_g2s(xs, x, 4u * K, mb);
+        }
         if (nw && !nw_ready) {
             mbar_arrive_expect_tx(mb + 1, 4u * K);
             bulk_g2s(nws, nw, 4u * K, mb + 1);
         }
-        bool w = mbar_wait_bounded(mb, parity, err);
+        bool w = xtag ? true : mbar_wait_bounded(mb, parity, err);
         if (nw) w = mbar_wait_bounded(mb + 1, parity, err) && w;
         *flag = w ? 1u : 0u;
     }
-    __syncthreads();
-    ok = *flag != 0u;
+    const bool tbad = xtag ? !gather_tagged(reinterpret_cast<const unsigned long long *>(x), xtag, K, xs, err) : false;
+    const int anybad = __syncthreads_or(tbad ? 1 : 0);
+    ok = *flag != 0u && !anybad;
     if (!ok) return 0;
     uint32_t m = 0;
     if (nw) {
@@ -651,11 +688,10 @@ __device__ __forceinline__ RowOut row_out(const MvJobs &J, const MvSeg *segs, in
     return o;
 }
 
-// A result's copies into the other ranks' destinations (tensor-parallel all-gather by stores over
-// peer memory).
+// A result's copies into the ranks' destinations (tensor-parallel all-gather by stores over peer
+// memory).
 __device__ __forceinline__ void tp_push(const TpXfer &T, int i, float v) {
-    for (int r = 0; r < T.world; ++r)
-        if (r != T.rank && T.dst[r]) reinterpret_cast<float *>(T.dst[r])[T.offset + i] = v;
+    if (T.world) tp_push_all(T, (size_t)i, v);
 }
 
 // Finish one row (srow: index within its segment) from its int64 sum(s): >> R, the overflow
@@ -896,6 +932,8 @@ __global__ void __launch_bounds__(kMvThreads, 1)
         if (tid == 0) tp_wait(J.tp, err);
         __syncthreads();
     }
+    // A tagged input: the tag its words carry once this step's producers (every rank's) stored them.
+    const unsigned xtag = (J.tp.tag_points && J.tp.tag_in >= 0) ? tp_tag(J.tp, J.tp.tag_in) : 0u;
     if (J.skip && *J.skip) {
         drain();
         return;
@@ -912,7 +950,7 @@ __global__ void __launch_bounds__(kMvThreads, 1)
         const int8_t *x8j = J.x8 ? J.x8 + (uint64_t)job * J.x_stride : nullptr;
         bool ok = true;
         const int e8 = fast ? build_activation_cp<KIND>(xj, J.norm_w, first, J.eps, J.cols, xs, nws, xp, red64, mb,
-                                                        (uint32_t)(npiece & 1), err, ok)
+                                                        (uint32_t)(npiece & 1), err, ok, xtag)
                             : build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
         ++npiece;
         if (!ok) {  // a staging copy timed out (recorded)
@@ -1375,6 +1413,8 @@ trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cu
     const DevInfo di = dev_info();
     const int nw = J.w2 ? 2 : 1;
     if (!plan_matvec(J, nw, di.sms, di.reserved, M)) return TRX_ERR_UNSUPPORTED;
+    // A tagged input is read only by the staged prologue, one job at a time.
+    if (J.tp.tag_points && J.tp.tag_in >= 0 && (!M.xfast || !J.x || J.njobs != 1)) return TRX_ERR_UNSUPPORTED;
     MvMaps maps;
     const trx_status s = encode_maps(J, M, maps);
     if (s != TRX_OK) return s;

@@ -31,6 +31,11 @@ def _need(t, dtype, name):
                          f"on {t.device} (contiguous={t.is_contiguous()})")
 
 
+def _need_x(x, tp):
+    """A matvec input: float32, or tagged 64-bit words (int64) when the exchange reads a tagged input."""
+    _need(x, torch.int64 if (tp is not None and tp.tag_points and tp.tag_in >= 0) else torch.float32, "x")
+
+
 class Context:
     """One per device: the library context (device error word, the trit5 LUT)."""
 
@@ -224,7 +229,7 @@ def quantize_pow2(ctx, x, x8=None, e8=None):
 
 
 def matvec_f(ctx, w: DeviceTensor, x, y=None, norm_w=None, eps=1e-6, resid=None, tp=None):
-    _need(x, torch.float32, "x")
+    _need_x(x, tp)
     if norm_w is not None:
         _need(norm_w, torch.float32, "norm_w")
     if resid is not None:
@@ -251,7 +256,7 @@ def matvec_fp(ctx, w: DeviceTensor, x, y=None):
 
 
 def matvec_swiglu(ctx, gate: DeviceTensor, up: DeviceTensor, x, act=None, norm_w=None, eps=1e-6, tp=None):
-    _need(x, torch.float32, "x")
+    _need_x(x, tp)
     if act is None:
         act = torch.empty(gate.rows, dtype=torch.float32, device=x.device)
     if tp is not None:
@@ -359,7 +364,7 @@ def matvec_f_multi(ctx, entries, packed, x, ys, norm_w=None, eps=1e-6, resids=No
     """Segments sharing one input (trx_matvec_f_multi): entries (list of _lib.Entry), packed (their row
     packets back to back, uint8 CUDA tensor), ys (one float32 output per segment)."""
     n = len(entries)
-    _need(x, torch.float32, "x")
+    _need_x(x, tp)
     arr = (_lib.Entry * n)(*entries)
     yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
     rp = None
@@ -465,7 +470,7 @@ def lmhead_argmax(ctx, w: DeviceTensor, x, token=None, logits=None, norm_w=None,
 def lmhead_argmax_key(ctx, w: DeviceTensor, x, key, row_offset=0, logits=None, norm_w=None, eps=1e-6, tp=None):
     """One shard of a row-sharded LM head: key (int64 device tensor of one element) = the shard's
     argmax key with global row = local row + row_offset (trx_lmhead_argmax_key)."""
-    _need(x, torch.float32, "x")
+    _need_x(x, tp)
     _need(key, torch.int64, "key")
     if tp is not None:
         _lib.check(_lib.lib().trx_lmhead_argmax_key_tp(ctx.h, ctypes.byref(w.entry), _ptr(w.data), _ptr(x),

@@ -208,11 +208,13 @@ class TPDecoder:
             self._setup_p2p(a_sh)
 
     # Exchange over peer memory ------------------------------------------------------------------
-    # Instead of an NCCL all-gather after each sharded projection, the producing kernel stores its
-    # rows into every rank's copy of the vector (peer-mapped symmetric buffers) and signals each
-    # rank's counter of that gather point; the consuming kernel waits on its own counter.  Gather
-    # points per step: per layer attention output, x after o, act, x after down; then the LM-head
-    # keys.
+    # Instead of an NCCL all-gather after each sharded projection, the producing kernel stores each
+    # result into every rank's copy of the vector (peer-mapped symmetric buffers) as one tagged
+    # 64-bit word (value bits | tag << 32, tag = step * points + point + 1); the consuming kernel
+    # polls its own copy until every word carries the tag it expects.  No fence, no counter, no
+    # collective on the path.  Gather points per step: per layer attention output (4l), x after o
+    # (4l+1), act (4l+2), x after down (4l+3); then the LM-head keys (4L), exchanged as plain words
+    # with a completion counter (one per step).
     def _p2p_supported(self, a_sh):
         cfg = self.cfg
         if any(cfg.layer_type(l) != "a" for l in range(cfg.n_layer)) or a_sh is None:
@@ -240,9 +242,9 @@ class TPDecoder:
 
         E, F, N = cfg.hidden, cfg.ffn, self.world
         self.n_points = 4 * cfg.n_layer + 1
-        self.x, px = shared(E, torch.float32)
-        self.attn, pa = shared(cfg.n_head * cfg.head_dim, torch.float32)
-        self.act, pf = shared(F, torch.float32)
+        self.x_tag, px = shared(E, torch.int64)
+        self.attn_tag, pa = shared(cfg.n_head * cfg.head_dim, torch.int64)
+        self.act_tag, pf = shared(F, torch.int64)
         self.keys, pk = shared(N, torch.int64)
         self.cnt, pc = shared(self.n_points, torch.int32)
         self.step_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -251,27 +253,33 @@ class TPDecoder:
         dist.barrier(group=self.group)
         w, r = self.w, self.rank
         a0 = a_sh.kv0 * (a_sh.n_head // a_sh.n_kv) * cfg.head_dim
+        lm_point = 4 * cfg.n_layer
 
-        def xfer(dst_ptrs=None, offset=0, signal=None, wait=None):
+        def xfer(op, sig, wt):
             t = _lib.TpXfer()
-            t.world, t.rank, t.offset = N, r, offset
-            if dst_ptrs is not None:
-                for q in range(N):
-                    t.dst[q] = dst_ptrs[q] if q != r else None
-            if signal is not None:
-                for q in range(N):
-                    t.signal[q] = pc[q] + 4 * signal
-                t.arrive = self.arrive.data_ptr() + 4 * signal
-            if wait is not None:
-                t.wait = self.cnt.data_ptr() + 4 * wait
+            t.world, t.rank = N, r
             t.step = self.step_ctr.data_ptr()
+            t.tag_points = self.n_points
+            if op == "lm":  # the key: a plain word into the other ranks' slots, then their counters
+                t.offset = r
+                for q in range(N):
+                    t.dst[q] = pk[q] if q != r else None
+                    t.signal[q] = pc[q] + 4 * lm_point
+                t.arrive = self.arrive.data_ptr() + 4 * lm_point
+            elif op == "token":
+                t.wait = self.cnt.data_ptr() + 4 * lm_point
+            elif sig is not None:  # a tagged output into every rank's copy, this rank's included
+                ptrs, t.offset = {"attn": (pa, a0), "o": (px, w.e0), "swiglu": (pf, w.f0), "down": (px, w.e0)}[op]
+                for q in range(N):
+                    t.dst[q] = ptrs[q]
+                t.tag_out = sig
+            if wt is not None and op != "token":
+                t.tag_in = wt
             return t
 
-        dst = {"attn": (pa, a0), "o": (px, w.e0), "swiglu": (pf, w.f0), "down": (px, w.e0), "lm": (pk, r)}
         self._tp = [dict() for _ in range(cfg.n_layer)]
         for op, l, sig, wt in exchange_plan(cfg.n_layer):
-            ptrs, off = dst.get(op, (None, 0))
-            t = xfer(ptrs, off, signal=sig, wait=wt) if (sig is not None or wt is not None) else None
+            t = xfer(op, sig, wt) if (sig is not None or wt is not None) else None
             if op == "lm":
                 self._tp_lm = t
             elif op == "token":
@@ -347,26 +355,22 @@ class TPDecoder:
     def _enqueue_step_p2p(self):
         from . import ops
         cfg, w, ctx = self.cfg, self.w, self.ctx
-        xr = self.x[w.e0:w.e1]
-        hd = cfg.head_dim
-        a_loc = None
+        x_loc = self.x_loc  # this rank's rows of the residual stream (local floats)
         ops.embed_lookup(ctx, w.emb, self.tok, self.x)
         for l, lw in enumerate(w.layers):
             t = self._tp[l]
             p = lw["in"]
-            sh = lw["shard"]
-            if a_loc is None:
-                a0 = sh.kv0 * (sh.n_head // sh.n_kv) * hd
-                a_loc = self.attn[a0:a0 + sh.n_head * hd]
-            ops.matvec_f_multi(ctx, p.entries, p.data, self.x, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
+            xin = self.x if l == 0 else self.x_tag  # the embedding (local floats), then the tagged x
+            ops.matvec_f_multi(ctx, p.entries, p.data, xin, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
                                eps=cfg.eps, tp=t["qkv"])
             ops.attn_decode(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"], w.rope_freq,
-                            self.kc[l], self.vc[l], self.pos, a_loc, tp=t["attn"])
-            ops.matvec_f(ctx, lw["out"], self.attn, y=xr, resid=xr, tp=t["o"])
-            ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x, act=self.act[w.f0:w.f1], norm_w=lw["ffn_norm"],
+                            self.kc[l], self.vc[l], self.pos, self.attn_loc, tp=t["attn"])
+            ops.matvec_f(ctx, lw["out"], self.attn_tag, y=x_loc, resid=self.x[w.e0:w.e1] if l == 0 else x_loc,
+                         tp=t["o"])
+            ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x_tag, act=self.act_loc, norm_w=lw["ffn_norm"],
                               eps=cfg.eps, tp=t["swiglu"])
-            ops.matvec_f(ctx, lw["down"], self.act, y=xr, resid=xr, tp=t["down"])
-        ops.lmhead_argmax_key(ctx, w.lm_head, self.x, self.keys[self.rank:self.rank + 1], row_offset=w.v0,
+            ops.matvec_f(ctx, lw["down"], self.act_tag, y=x_loc, resid=x_loc, tp=t["down"])
+        ops.lmhead_argmax_key(ctx, w.lm_head, self.x_tag, self.keys[self.rank:self.rank + 1], row_offset=w.v0,
                               norm_w=w.out_norm, eps=cfg.eps, tp=self._tp_lm)
         ops.argmax_token(ctx, self.keys, self.tok, tp=self._tp_tok)
         ops.advance_position(ctx, self.pos)
@@ -379,7 +383,7 @@ class TPDecoder:
         return 4 * self.cfg.n_layer + 1
 
     def _mutable(self):
-        extra = [self.cnt, self.step_ctr, self.arrive] if self.p2p else []
+        extra = [self.cnt, self.step_ctr, self.arrive, self.x_tag, self.attn_tag, self.act_tag] if self.p2p else []
         return [self.tok, self.pos] + list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + \
             list(self.state.values()) + extra
 
