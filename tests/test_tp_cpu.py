@@ -1,6 +1,7 @@
-"""Tensor-parallel shard plan on the CPU: the plan covers every row once, the DeltaNet head
-renumbering keeps the kernel's tiled head map, and the oracle model run sharded over gloo ranks
-(world size 2) generates the same tokens as the unsharded oracle model on the same image.
+"""Tensor-parallel shard plan on the CPU: the plan covers every row (kv heads replicated when the
+ranks outnumber them), the DeltaNet head renumbering keeps the kernel's tiled head map, and the
+oracle model run sharded over gloo ranks (world size 2, and 4 with replicated kv heads) generates
+the same tokens as the unsharded oracle model on the same image.
 """
 import os
 import socket
@@ -16,8 +17,8 @@ from trixium_b200 import tp
 PROMPT = [5, 17, 300, 42]
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny-hybrid"])
-@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("name,world", [("tiny", 1), ("tiny", 2), ("tiny", 4), ("tiny-hybrid", 1),
+                                        ("tiny-hybrid", 2), ("tiny-kv1", 2)])
 def test_shard_plan_covers_rows(name, world):
     cfg = D.CONFIGS[name]
     for l in range(cfg.n_layer):
@@ -32,7 +33,12 @@ def test_shard_plan_covers_rows(name, world):
         else:
             shards = [tp.AttnShard(cfg, r, world) for r in range(world)]
             assert sorted(np.concatenate([s.q_rows for s in shards])) == list(range(cfg.q_rows))
-            assert sorted(np.concatenate([s.k_rows for s in shards])) == list(range(cfg.kv_rows))
+            g = max(1, world // cfg.n_kv)  # ranks per kv head (replicated when world > kv heads)
+            assert sorted(np.concatenate([s.k_rows for s in shards])) == sorted(list(range(cfg.kv_rows)) * g)
+            assert [s.head0 for s in shards] == [r * cfg.n_head // world for r in range(world)]
+            rep = cfg.n_head // cfg.n_kv
+            for s in shards:  # every query head sits with its own kv head
+                assert s.head0 // rep == s.kv0 and (s.head0 + s.n_head - 1) // rep == s.kv1 - 1
 
 
 def _free_port():
@@ -57,8 +63,9 @@ def _rank(rank, world, port, name, out):
         torch.distributed.destroy_process_group()
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny-hybrid"])
-def test_sharded_oracle_matches_unsharded(name):
+@pytest.mark.parametrize("name,world", [("tiny", 2), ("tiny-hybrid", 2), ("tiny", 4), ("tiny-kv1", 2)])
+def test_sharded_oracle_matches_unsharded(name, world):
+    """World 4 on "tiny" (2 kv heads): each kv head replicated on two ranks."""
     from oracle.model import OracleModel
     full = D.SyntheticWeights(D.CONFIGS[name], seed=3, device="cpu")
     cfg = full.cfg
@@ -71,13 +78,13 @@ def test_sharded_oracle_matches_unsharded(name):
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, name, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, name, out)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    assert out[0] == want and out[1] == want
+    assert all(out[r] == want for r in range(world))
 
 
 @pytest.mark.parametrize("n_layer", [1, 2, 36])

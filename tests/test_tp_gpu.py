@@ -63,8 +63,9 @@ def _rank(rank, world, port, name, out, p2p=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("name", ["tiny", "tiny-hybrid"])
+@pytest.mark.parametrize("name", ["tiny", "tiny-hybrid", "tiny-kv1"])
 def test_tp_world2_matches_decoder(name):
+    """tiny-kv1 has one kv head: both ranks hold it (replicated) and split its query heads."""
     want = single_gpu_tokens(name)
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
@@ -82,15 +83,17 @@ def test_tp_world2_matches_decoder(name):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp_world2_peer_exchange_matches_decoder():
-    """The all-gathers done by the kernels themselves over peer memory (no NCCL on the data path)."""
-    want = single_gpu_tokens("tiny")
+@pytest.mark.parametrize("name", ["tiny", "tiny-kv1"])
+def test_tp_world2_peer_exchange_matches_decoder(name):
+    """The all-gathers done by the kernels themselves over peer memory (tagged words, no NCCL on the
+    data path)."""
+    want = single_gpu_tokens(name)
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, "tiny", out, True)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, name, out, True)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

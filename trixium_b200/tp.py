@@ -32,18 +32,36 @@ def span(total, rank, world):
 
 
 class AttnShard:
-    """Rows of one rank's attention-layer shard (query rows per head: hd, or 2*hd when gated)."""
+    """Rows of one rank's attention-layer shard (query rows per head: hd, or 2*hd when gated).
+
+    With at least as many kv heads as ranks, rank r owns kv heads [kv0, kv1) and all their query
+    heads.  With fewer (world a multiple of the kv heads, e.g. 4 kv heads on 8 GPUs), each kv head is
+    replicated on g = world / n_kv ranks: the g ranks each compute that head's k/v rows and keep
+    their own copy of its cache, and split its query heads evenly.  Either way rank r's query heads
+    are [head0, head0 + n_head) with head0 = r * n_head, so the head outputs all-gather in rank
+    order."""
 
     def __init__(self, cfg, rank, world):
         H, Hkv, hd = cfg.n_head, cfg.n_kv, cfg.head_dim
-        if Hkv % world:
-            raise ValueError(f"{Hkv} kv heads do not split over {world} ranks")
         rep = H // Hkv
-        self.kv0, self.kv1 = span(Hkv, rank, world)
-        self.n_kv = self.kv1 - self.kv0
-        self.n_head = self.n_kv * rep
         qh = hd * (2 if cfg.attn_gated else 1)
-        self.q_rows = np.arange(self.kv0 * rep * qh, self.kv1 * rep * qh)
+        if Hkv % world == 0:
+            self.kv0, self.kv1 = span(Hkv, rank, world)
+            self.n_kv = self.kv1 - self.kv0
+            self.n_head = self.n_kv * rep
+            self.head0 = self.kv0 * rep
+            self.replicas = 1
+        elif world % Hkv == 0 and rep % (world // Hkv) == 0:
+            g = world // Hkv
+            self.kv0 = rank // g
+            self.kv1 = self.kv0 + 1
+            self.n_kv = 1
+            self.n_head = rep // g
+            self.head0 = self.kv0 * rep + (rank % g) * self.n_head
+            self.replicas = g
+        else:
+            raise ValueError(f"{Hkv} kv heads ({H} query heads) do not split over {world} ranks")
+        self.q_rows = np.arange(self.head0 * qh, (self.head0 + self.n_head) * qh)
         self.k_rows = np.arange(self.kv0 * hd, self.kv1 * hd)
         self.v_rows = self.k_rows.copy()
 
@@ -122,11 +140,13 @@ class TPWeights:
         self.lm_head = _slice_rows(full.lm_head, np.arange(self.v0, self.v1))
         self.layers = []
         for l, lw in enumerate(full.layers):
-            if isinstance(lw["down"], list):
-                raise ValueError("tensor-parallel decoding takes no K-segmented tensors (ffn wider than 16384)")
+            # A K-segmented down projection (ffn wider than one tensor) keeps its segments, each cut
+            # to the rank's output rows.
+            down = ([_slice_rows(sg, er) for sg in lw["down"]] if isinstance(lw["down"], list)
+                    else _slice_rows(lw["down"], er))
             w = {"attn_norm": lw["attn_norm"], "ffn_norm": lw["ffn_norm"],
                  "gate": _slice_rows(lw["gate"], fr), "up": _slice_rows(lw["up"], fr),
-                 "down": _slice_rows(lw["down"], er), "out": _slice_rows(lw["out"], er)}
+                 "down": down, "out": _slice_rows(lw["out"], er)}
             if cfg.layer_type(l) == "d":
                 sh = w["shard"] = DeltaNetShard(cfg, rank, world)
                 w["in"] = ShardPacked(lw["in"], [sh.channels, sh.z_rows, sh.head_rows, sh.head_rows])
@@ -219,6 +239,8 @@ class TPDecoder:
         cfg = self.cfg
         if any(cfg.layer_type(l) != "a" for l in range(cfg.n_layer)) or a_sh is None:
             return False  # DeltaNet outputs are gathered with NCCL
+        if any(isinstance(lw["down"], list) for lw in self.w.layers):
+            return False  # the K-segmented projection has no exchanging launch
         rep = a_sh.n_head // a_sh.n_kv
         return cfg.head_dim in (64, 128) and 1 <= rep <= 8  # the tensor-core attention exchanges
 
@@ -252,7 +274,7 @@ class TPDecoder:
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         w, r = self.w, self.rank
-        a0 = a_sh.kv0 * (a_sh.n_head // a_sh.n_kv) * cfg.head_dim
+        a0 = a_sh.head0 * cfg.head_dim
         lm_point = 4 * cfg.n_layer
 
         def xfer(op, sig, wt):
@@ -307,10 +329,12 @@ class TPDecoder:
             t.copy_(full.index_select(0, heads))
 
     def fill_context(self, n, seed=0):
-        """Synthetic context of n positions (random fp16 K/V rows of this rank's heads), position n."""
+        """Synthetic context of n positions (random fp16 K/V rows of this rank's heads), position n.
+        Seeded by the rank's first kv head, so ranks that replicate a kv head hold the same cache."""
         import torch
         g = torch.Generator(device=self.tok.device)
-        g.manual_seed(seed + self.rank)
+        a_sh = next((lw["shard"] for lw in self.w.layers if isinstance(lw["shard"], AttnShard)), None)
+        g.manual_seed(seed + (a_sh.kv0 if a_sh is not None else self.rank))
         for l in self.kc:
             self.kc[l][:n] = torch.randn(self.kc[l][:n].shape, generator=g, device=self.tok.device).half()
             self.vc[l][:n] = torch.randn(self.vc[l][:n].shape, generator=g, device=self.tok.device).half()
@@ -345,7 +369,10 @@ class TPDecoder:
             self._gather(self.x, self.x_loc)
             ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x, act=self.act_loc, norm_w=lw["ffn_norm"], eps=cfg.eps)
             self._gather(self.act, self.act_loc)
-            ops.matvec_f(ctx, lw["down"], self.act, y=self.x_loc, resid=xr)
+            if isinstance(lw["down"], list):
+                ops.matvec_f_kseg(ctx, lw["down"], self.act, y=self.x_loc, resid=xr)
+            else:
+                ops.matvec_f(ctx, lw["down"], self.act, y=self.x_loc, resid=xr)
             self._gather(self.x, self.x_loc)
         ops.lmhead_argmax_key(ctx, w.lm_head, self.x, self.key, row_offset=w.v0, norm_w=w.out_norm, eps=cfg.eps)
         self._gather(self.keys, self.key)
