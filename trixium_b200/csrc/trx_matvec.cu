@@ -759,22 +759,21 @@ __device__ __forceinline__ void lane_row(const MvJobs &J, const MvSeg *segs, int
 }
 
 // The matvec kernel ---------------------------------------------------------------------------------
-// Ring depth: trit5 shares shared memory with its 64 KiB LUT, a SwiGLU pair streams two tensors.
+// Default ring depth (plan_matvec): trit5 shares shared memory with its 64 KiB LUT, a SwiGLU pair
+// streams two tensors.
 #ifndef TRX_MV_D_T5
 #define TRX_MV_D_T5 2
 #endif
-template <int KIND, int NW>
-constexpr int ring_depth() { return KIND == TRX_KIND_TERNARY5 ? (NW == 2 ? 2 : TRX_MV_D_T5) : (NW == 2 ? 2 : 3); }
 
 // Work decomposition: a row block is 32 R rows (lane l owns rows l, l + 32, ...); a block is one
 // chunk (4 groups) of a row block.  Each warp streams its blocks through a private ring of D slots:
 // one elected lane issues the block's TMA boxes (codes and scales of each tensor) on the slot's
 // mbarrier; the lanes wait on it (bounded), decode, and the slot is refilled with the block D
 // ahead.  No producer warp, no CTA barrier inside a job.
-template <int KIND, int NW, int R>
+template <int KIND, int NW, int R, int D>
 __global__ void __launch_bounds__(kMvThreads, 1)
     tmv_kernel(const __grid_constant__ MvMaps maps, MvJobs J, MvGeom M, uint32_t *err) {
-    constexpr int D = ring_depth<KIND, NW>();
+    // D: ring depth, chosen per launch by plan_matvec (M.D), a compile-time constant of the kernel.
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -1246,32 +1245,11 @@ int device_reserved_smem() { return dev_info().reserved; }
 // Plan a launch: chunks, rows per lane, tasks (rows split over tasks only when the launch has too
 // few row blocks to give every warp slot of the GPU one), warps and ring depth that fit shared
 // memory.
-bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
-    const int kind = J.kind;
-    const bool t5 = kind == TRX_KIND_TERNARY5;
-    M.G = J.cols / 128;
-    M.nch = (M.G + kCG - 1) / kCG;
-    M.sbytes = (M.G + 15) / 16 * 32;
-    M.rb = M.sbytes + ((t5 ? 26 : 32) * M.G + 31) / 32 * 32;
-    M.nw = nw;
-    M.xw = t5 ? kXwT5 : kXw2b;
-    M.cb = t5 ? kCbT5 : kCb2b;
-    M.D = t5 ? (nw == 2 ? 2 : TRX_MV_D_T5) : (nw == 2 ? 2 : 3);
-    M.wjob = (J.njobs > 1 && J.w_stride != 0) ? 1 : 0;
-    // Row blocks are dealt to CTAs; when a CTA gets fewer row blocks than it has warps, the warps
-    // share row blocks (S per row block, chunks split between them, sums combined in shared memory)
-    // and a lane owns one row; otherwise R rows.
-    bool split = false;
-    long long rbc = 0;
-    for (int R = nw == 2 ? 1 : (t5 ? TRX_MV_R_T5 : TRX_MV_R_2B);; R = 1) {
-        M.R = R;
-        M.nrb = (J.rows + 32 * R - 1) / (32 * R);
-        const long long rbt = (long long)J.njobs * M.nrb;
-        M.grid = (int)std::min<long long>(sms, rbt);
-        rbc = (rbt + M.grid - 1) / M.grid;
-        split = rbc < kMaxWarps && M.nch > 1;
-        if (!split || R == 1) break;
-    }
+// The rings and shared-memory carve-up of a launch whose row-block split is decided (M.R, M.nrb,
+// M.grid, M.D set): the warps, the regions and the prologue's staging area.
+static bool plan_rings(const MvJobs &J, int reserved, bool split, long long rbc, MvGeom &M) {
+    const bool t5 = J.kind == TRX_KIND_TERNARY5;
+    const int nw = M.nw;
     M.cbytes = 32 * M.R * M.cb;
     M.slot = nw * 32 * M.R * (M.cb + kScBox);
     int fixed = M.G * M.xw * 4 + 64 * 4 + 16 + 16 + kMaxSegs * (int)sizeof(MvSeg);
@@ -1348,6 +1326,57 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     return M.smem <= kSmemMax;
 }
 
+bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
+    const int kind = J.kind;
+    const bool t5 = kind == TRX_KIND_TERNARY5;
+    M.G = J.cols / 128;
+    M.nch = (M.G + kCG - 1) / kCG;
+    M.sbytes = (M.G + 15) / 16 * 32;
+    M.rb = M.sbytes + ((t5 ? 26 : 32) * M.G + 31) / 32 * 32;
+    M.nw = nw;
+    M.xw = t5 ? kXwT5 : kXw2b;
+    M.cb = t5 ? kCbT5 : kCb2b;
+    M.D = t5 ? (nw == 2 ? 2 : TRX_MV_D_T5) : (nw == 2 ? 2 : 3);
+    M.wjob = (J.njobs > 1 && J.w_stride != 0) ? 1 : 0;
+    // Row blocks are dealt to CTAs; when a CTA gets fewer row blocks than it has warps, the warps
+    // share row blocks (S per row block, chunks split between them, sums combined in shared memory)
+    // and a lane owns one row; otherwise R rows.
+    bool split = false;
+    long long rbc = 0;
+    for (int R = nw == 2 ? 1 : (t5 ? TRX_MV_R_T5 : TRX_MV_R_2B);; R = 1) {
+        M.R = R;
+        M.nrb = (J.rows + 32 * R - 1) / (32 * R);
+        const long long rbt = (long long)J.njobs * M.nrb;
+        M.grid = (int)std::min<long long>(sms, rbt);
+        rbc = (rbt + M.grid - 1) / M.grid;
+        split = rbc < kMaxWarps && M.nch > 1;
+        if (!split || R == 1) break;
+    }
+    // A decode-size launch (warps share row blocks) whose CTA share of the weights is more than the
+    // rings hold at the default depth (with the warps that depth leaves, a power of two): shallower
+    // rings when that gives the full warp count with the prologue's staging in a region of its own,
+    // so the weights still go in flight before the dependency wait and twice the warps decode them.
+    // (Measured on B200, 8B decode: 1.854 -> 1.810 ms per token, from the gate/up pair; making the
+    // rings shallower where the default rings hold the whole share made the step slower.)
+    bool default_holds = false;
+    {
+        MvGeom T = M;
+        if (plan_rings(J, reserved, split, rbc, T))
+            default_holds = (long long)T.warps * T.D * T.slot >= (rbc * 32 * T.R) * (long long)T.rb * T.nw;
+    }
+    if (split && !default_holds) {
+        for (int D = M.D - 1; D >= 1; --D) {
+            MvGeom T = M;
+            T.D = D;
+            if (plan_rings(J, reserved, split, rbc, T) && T.warps == kMaxWarps && T.ebl == T.D) {
+                M = T;
+                return true;
+            }
+        }
+    }
+    return plan_rings(J, reserved, split, rbc, M);
+}
+
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime (the library links
 // only the CUDA runtime).
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -1396,15 +1425,27 @@ static trx_status encode_maps(const MvJobs &J, const MvGeom &M, MvMaps &maps) {
     return TRX_OK;
 }
 
-template <int KIND, int NW, int R>
-static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, const MvMaps &maps, uint32_t *err, cudaStream_t st) {
+template <int KIND, int NW, int R, int D>
+static trx_status launch_tmv_d(const MvJobs &J, const MvGeom &M, const MvMaps &maps, uint32_t *err, cudaStream_t st) {
     static DevBits configured{0};  // devices whose attribute is set
     const cudaError_t e = once_per_device(configured, [] {
-        return cudaFuncSetAttribute(tmv_kernel<KIND, NW, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        return cudaFuncSetAttribute(tmv_kernel<KIND, NW, R, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
     });
     if (e != cudaSuccess) return note_cuda(e);
     return note_cuda(
-        launch_kernel(tmv_kernel<KIND, NW, R>, dim3(M.grid), dim3(M.warps * 32), M.smem, st, maps, J, M, err));
+        launch_kernel(tmv_kernel<KIND, NW, R, D>, dim3(M.grid), dim3(M.warps * 32), M.smem, st, maps, J, M, err));
+}
+
+// The depths plan_matvec gives: the default (3 for a single 2-bit tensor, else 2), or shallower
+// for a decode-size launch.
+template <int KIND, int NW, int R>
+static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, const MvMaps &maps, uint32_t *err, cudaStream_t st) {
+    if (M.D == 1) return launch_tmv_d<KIND, NW, R, 1>(J, M, maps, err, st);
+    if (M.D == 2) return launch_tmv_d<KIND, NW, R, 2>(J, M, maps, err, st);
+    if constexpr (KIND == TRX_KIND_TERNARY && NW == 1) {
+        if (M.D == 3) return launch_tmv_d<KIND, NW, R, 3>(J, M, maps, err, st);
+    }
+    return TRX_ERR_UNSUPPORTED;
 }
 
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st) {
