@@ -458,12 +458,27 @@ trx_status trx_lmhead_argmax_key_tp(trx_ctx *ctx, const trx_entry *e, const void
                                     const float *d_norm_w, float eps, uint32_t row_offset, float *d_logits,
                                     uint64_t *d_key, const trx_tp_xfer *tp, cudaStream_t stream);
 
+/* trx_deltanet_step with an exchange: the grouped output copied to dst (offset + index) of every rank
+ * as tagged words (tag_points > 0 and tag_out >= 0 required). */
+trx_status trx_deltanet_step_tp(trx_ctx *ctx, const trx_deltanet_shape *shape, const float *d_qkv, const float *d_z,
+                                const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                                const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                                float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                                const trx_tp_xfer *tp, cudaStream_t stream);
+
+/* trx_matvec_f_kseg with an exchange (tagged words only): the input read as tagged words when
+ * tag_in >= 0, the float results copied to dst (offset + row) of every rank when tag_out >= 0. */
+trx_status trx_matvec_f_kseg_tp(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
+                                const float *d_x, const float *d_resid, float *d_y, const trx_tp_xfer *tp,
+                                cudaStream_t stream);
+
 /* trx_argmax_token after waiting for the exchange of the keys. */
 trx_status trx_argmax_token_tp(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token,
                                const trx_tp_xfer *tp, cudaStream_t stream);
 
-/* trx_attn_decode with an exchange: out[h][d] copied to dst (offset + h*hd + d).  Head dims 64 and
- * 128 with at most 8 query heads per kv head only (TRX_ERR_UNSUPPORTED otherwise). */
+/* trx_attn_decode with an exchange: out[h][d] copied to dst (offset + h*hd + d).  Tagged words: any
+ * shape.  Plain words with completion counters: head dims 64 and 128 with at most 8 query heads per
+ * kv head only (TRX_ERR_UNSUPPORTED otherwise). */
 trx_status trx_attn_decode_tp(trx_ctx *ctx, const trx_attn_shape *shape, const float *d_q, const float *d_k,
                               const float *d_v, const float *d_qnorm_w, const float *d_knorm_w,
                               const float *d_rope_freq, void *d_kcache, void *d_vcache, const int32_t *d_pos,

@@ -301,6 +301,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs A, u
             o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
         }
         A.out[(size_t)h * hd + d] = o;
+        if (A.tp.world) tp_push_all(A.tp, (size_t)h * hd + d, o);  // tensor-parallel gather (tagged words)
     }
     if (tid == 0) A.cnt[kh] = 0u;
 }
@@ -628,6 +629,7 @@ __global__ void __launch_bounds__(kClThreads) attn_cluster_kernel(AttnArgs A, ui
             o = __fmul_rn(o, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
         }
         A.out[(size_t)h * hd + d] = o;
+        if (A.tp.world) tp_push_all(A.tp, (size_t)h * hd + d, o);  // tensor-parallel gather (tagged words)
     }
 }
 
@@ -1089,7 +1091,8 @@ trx_status launch_attn_decode(const AttnArgs &A0, uint32_t *err, cudaStream_t st
             const cudaError_t e = A0.hd == 64 ? launch_mma<64>(C, err, csmem, st) : launch_mma<128>(C, err, csmem, st);
             if (e != cudaErrorNotSupported) return note_cuda(e);
         }
-        if (A0.tp.world) return TRX_ERR_UNSUPPORTED;  // only the tensor-core kernel exchanges its output
+        // The other kernels exchange their output as tagged words only (no completion counters).
+        if (A0.tp.world && !(A0.tp.tag_points && A0.tp.tag_out >= 0)) return TRX_ERR_UNSUPPORTED;
         if (cl_plan(A0, C.chunk, C.nsplit, csmem, C.merge_own)) {
             // 16 dims per lane up to 4 heads, 8 beyond: rep * DPL query values in registers <= 64.
             cudaError_t e;

@@ -524,7 +524,17 @@ trx_status trx_rmsnorm(trx_ctx *ctx, const float *d_x, const float *d_w, uint32_
 
 trx_status trx_matvec_f_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
                              const float *d_x, const float *d_resid, float *d_y, cudaStream_t stream) {
+    return trx_matvec_f_kseg_tp(ctx, segs, nseg, d_packed, d_x, d_resid, d_y, nullptr, stream);
+}
+
+trx_status trx_matvec_f_kseg_tp(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
+                                const float *d_x, const float *d_resid, float *d_y, const trx_tp_xfer *tp,
+                                cudaStream_t stream) {
     if (!ctx || !segs || !d_packed || !d_x || !d_y || nseg < 1 || nseg > 64) return TRX_ERR_ARG;
+    trx::TpXfer X;
+    if (trx_status s = tp_resolve(tp, TP_PUSH | TP_WAIT, X)) return s;
+    if (X.world && (X.signal[0] || X.wait)) return TRX_ERR_UNSUPPORTED;  // tagged words only
+    const bool tagged_in = X.tag_points && X.tag_in >= 0;
     const uint32_t rows = segs[0].rows;
     uint64_t K = 0;
     for (int i = 0; i < nseg; ++i) {
@@ -538,7 +548,8 @@ trx_status trx_matvec_f_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, cons
     if (K > kQ8MaxCols) return TRX_ERR_UNSUPPORTED;
     if ((uint64_t)nseg * rows > kKsegPartInts) return TRX_ERR_UNSUPPORTED;
     int *e8 = reinterpret_cast<int *>(ctx->q8x + kQ8MaxCols);
-    trx_status s = trx::launch_quantize(d_x, (int)K, ctx->q8x, e8, stream);
+    trx_status s = tagged_in ? trx::launch_quantize_tagged(d_x, (int)K, ctx->q8x, e8, X, ctx->err, stream)
+                             : trx::launch_quantize(d_x, (int)K, ctx->q8x, e8, stream);
     if (s) return s;
     uint64_t c0 = 0;
     for (int i = 0; i < nseg; ++i) {
@@ -558,7 +569,7 @@ trx_status trx_matvec_f_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, cons
         c0 += e->cols;
     }
     return trx::launch_kseg_combine(ctx->kseg_part, nseg, (int)rows, e8, segs[0].rshift, segs[0].bias, d_resid, d_y,
-                                    stream);
+                                    stream, X.world ? &X : nullptr);
 }
 
 trx_status trx_advance_position(trx_ctx *ctx, int32_t *d_pos, int32_t n, cudaStream_t stream) {
@@ -727,13 +738,28 @@ trx_status trx_attn_decode_f32cache(trx_ctx *ctx, const trx_attn_shape *sh, cons
     return trx::launch_attn_decode(A, ctx->err, stream);
 }
 
+static trx_status deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, int32_t nseq, const float *d_qkv,
+                                const float *d_z, const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                                const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                                float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                                const trx_tp_xfer *tp, cudaStream_t stream);
+
 trx_status trx_deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, const float *d_qkv, const float *d_z,
                              const float *d_beta, const float *d_alpha, const float *d_dt_bias,
                              const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
                              float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
                              cudaStream_t stream) {
-    return trx_deltanet_step_rows(ctx, sh, 1, d_qkv, d_z, d_beta, d_alpha, d_dt_bias, d_ssm_a, d_conv_w, d_norm_w,
-                                  d_conv_ring, d_state, d_pos, d_out, stream);
+    return deltanet_step(ctx, sh, 1, d_qkv, d_z, d_beta, d_alpha, d_dt_bias, d_ssm_a, d_conv_w, d_norm_w, d_conv_ring,
+                         d_state, d_pos, d_out, nullptr, stream);
+}
+
+trx_status trx_deltanet_step_tp(trx_ctx *ctx, const trx_deltanet_shape *sh, const float *d_qkv, const float *d_z,
+                                const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                                const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                                float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                                const trx_tp_xfer *tp, cudaStream_t stream) {
+    return deltanet_step(ctx, sh, 1, d_qkv, d_z, d_beta, d_alpha, d_dt_bias, d_ssm_a, d_conv_w, d_norm_w, d_conv_ring,
+                         d_state, d_pos, d_out, tp, stream);
 }
 
 trx_status trx_deltanet_int_step(trx_ctx *ctx, uint32_t nheads, uint32_t hv, uint32_t hk, int16_t *d_state,
@@ -763,6 +789,15 @@ trx_status trx_deltanet_step_rows(trx_ctx *ctx, const trx_deltanet_shape *sh, in
                                   const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
                                   float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
                                   cudaStream_t stream) {
+    return deltanet_step(ctx, sh, nseq, d_qkv, d_z, d_beta, d_alpha, d_dt_bias, d_ssm_a, d_conv_w, d_norm_w,
+                         d_conv_ring, d_state, d_pos, d_out, nullptr, stream);
+}
+
+static trx_status deltanet_step(trx_ctx *ctx, const trx_deltanet_shape *sh, int32_t nseq, const float *d_qkv,
+                                const float *d_z, const float *d_beta, const float *d_alpha, const float *d_dt_bias,
+                                const float *d_ssm_a, const float *d_conv_w, const float *d_norm_w,
+                                float *d_conv_ring, float *d_state, const int32_t *d_pos, float *d_out,
+                                const trx_tp_xfer *tp, cudaStream_t stream) {
     if (!ctx || !sh || nseq < 1 || nseq > 65535) return TRX_ERR_ARG;
     const uint32_t nk = sh->n_k_heads, hk = sh->k_head_dim, nv = sh->n_v_heads, hv = sh->v_head_dim;
     const uint32_t K = sh->conv_kernel;
@@ -803,6 +838,8 @@ trx_status trx_deltanet_step_rows(trx_ctx *ctx, const trx_deltanet_shape *sh, in
     A.out = d_out;
     A.part = ctx->attn_part;
     A.cnt = ctx->attn_cnt;
+    if (trx_status st = tp_resolve(tp, TP_PUSH, A.tp)) return st;
+    if (A.tp.world && (nseq != 1 || A.tp.tag_out < 0)) return TRX_ERR_UNSUPPORTED;  // tagged words, one sequence
     return trx::launch_deltanet(A, ctx->err, stream);
 }
 

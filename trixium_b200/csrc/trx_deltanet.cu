@@ -174,7 +174,9 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_kernel(DnArgs A, uint32_t
     const int gpos = kh * (A.nv / nk) + h / nk;
     for (int j = tid; j < hv; j += kDnThreads) {
         const float nv_ = __fmul_rn(__fmul_rn(o[j], r), __ldg(A.norm_w + j));
-        A.out[(size_t)gpos * hv + j] = __fmul_rn(nv_, silu_dn(__ldg(A.z + (size_t)h * hv + j)));
+        const float v = __fmul_rn(nv_, silu_dn(__ldg(A.z + (size_t)h * hv + j)));
+        A.out[(size_t)gpos * hv + j] = v;
+        if (A.tp.world) tp_push_all(A.tp, (size_t)gpos * hv + j, v);  // tensor-parallel gather
     }
     if (tid == 0) A.cnt[h] = 0u;
 }

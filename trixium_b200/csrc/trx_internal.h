@@ -156,6 +156,7 @@ struct DnArgs {
     float eps, scale;
     int nseq;           // independent sequences (blockIdx.z; 0 or 1: one), each with its own
                         // inputs, ring, state, position, output, partials and counts
+    TpXfer tp;          // tensor-parallel exchange of the output (tp.world == 0: none; one sequence)
 };
 
 trx_status launch_deltanet(const DnArgs &A, uint32_t *err, cudaStream_t st);
@@ -187,7 +188,7 @@ trx_status launch_embed_bfp16(const int16_t *mant, const int *exps, int vocab, i
                               uint32_t *err, cudaStream_t st);
 trx_status launch_rmsnorm(const float *x, const float *w, int n, float eps, float *y, cudaStream_t st);
 trx_status launch_kseg_combine(const int *parts, int nseg, int rows, const int *e8, int R, int B, const float *resid,
-                               float *y, cudaStream_t st);
+                               float *y, cudaStream_t st, const TpXfer *tp = nullptr);
 trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, const TpXfer &tp, uint32_t *err,
                               cudaStream_t st);
 
@@ -216,6 +217,9 @@ trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, 
                             void *out, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);
 trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStream_t st);
+// The same over a tagged input (x: tagged words of tp.tag_in, polled, bounded).
+trx_status launch_quantize_tagged(const void *x, int n, int8_t *x8, int *e8, const TpXfer &tp, uint32_t *err,
+                                  cudaStream_t st);
 trx_status launch_validate_t5(const uint8_t *w, int rows, int cols, uint32_t *err, cudaStream_t st);
 trx_status launch_build_lut(uint32_t *lut, cudaStream_t st);
 size_t lut_bytes();

@@ -1501,6 +1501,66 @@ trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStrea
     return note_cuda(launch_kernel(quantize_kernel, dim3(1), dim3(1024), 0, st, x, n, x8, e8));
 }
 
+// The quantiser over tagged words (a tensor-parallel gather point): every thread first polls its
+// words until they carry the point's tag of this step (bounded; TRX_DEV_TIMEOUT and zeros when a
+// wait runs out), then the max and the quantiser read the values (the low halves).  The words do
+// not change until this launch's successors have run, so they are read again without a poll.
+__global__ void __launch_bounds__(1024) quantize_tagged_kernel(const unsigned long long *xt, int n, int8_t *x8,
+                                                               int *e8_out, TpXfer tp, uint32_t *err) {
+    __shared__ uint32_t amax_s;
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) amax_s = 0;
+    const unsigned tag = tp_tag(tp, tp.tag_in);
+    bool bad = false;
+    unsigned long long t0 = 0ull;
+    for (int k = threadIdx.x; k < n && !bad; k += blockDim.x) {
+        unsigned long long w;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(xt + k) : "memory");
+        while ((unsigned)(w >> 32) != tag) {
+            if (!t0) {
+                t0 = global_ns();
+            } else if (global_ns() - t0 > kWaitNs) {
+                atomicOr(err, TRX_DEV_TIMEOUT);
+                bad = true;
+                break;
+            }
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(xt + k) : "memory");
+        }
+    }
+    if (__syncthreads_or(bad ? 1 : 0)) {
+        for (int k = threadIdx.x; k < n; k += blockDim.x) x8[k] = 0;
+        if (threadIdx.x == 0) *e8_out = 0;
+        return;
+    }
+    uint32_t m = 0;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        unsigned long long w;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(xt + k) : "memory");
+        const uint32_t a = (uint32_t)w & 0x7fffffffu;  // |value| bits
+        m = a > m ? a : m;
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    if ((threadIdx.x & 31) == 0) atomicMax(&amax_s, m);
+    __syncthreads();
+    const uint32_t amax = amax_s;
+    const int e8 = amax ? frexp_exp(__uint_as_float(amax)) - 7 : 0;
+    const float inv = pow2f(-e8);
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        unsigned long long w;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(xt + k) : "memory");
+        x8[k] = amax ? quant_one(__uint_as_float((uint32_t)w), inv) : (int8_t)0;
+    }
+    if (threadIdx.x == 0) *e8_out = e8;
+}
+
+trx_status launch_quantize_tagged(const void *x, int n, int8_t *x8, int *e8, const TpXfer &tp, uint32_t *err,
+                                  cudaStream_t st) {
+    if (!tp.tag_points || tp.tag_in < 0 || !tp.step) return TRX_ERR_ARG;
+    return note_cuda(launch_kernel(quantize_tagged_kernel, dim3(1), dim3(1024), 0, st,
+                                   static_cast<const unsigned long long *>(x), n, x8, e8, tp, err));
+}
+
 trx_status launch_validate_t5(const uint8_t *w, int rows, int cols, uint32_t *err, cudaStream_t st) {
     const int G = cols / 128;
     const int sb = (G + 15) / 16 * 32;

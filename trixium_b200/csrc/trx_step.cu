@@ -113,7 +113,7 @@ __global__ void advance_rows_kernel(int *pos, int count, int n) {
 // The float result of a K-segmented projection (model/mirror.py:664-678): the segments' int32
 // engine results added in int64, wrapped to int32, times 2^(e8 + R - B), plus the residual.
 __global__ void kseg_combine_kernel(const int *parts, int nseg, int rows, const int *e8, int R, int B,
-                                    const float *resid, float *y) {
+                                    const float *resid, float *y, TpXfer tp) {
     pdl_trigger();
     pdl_wait();
     const float sc = pow2f(*e8 + R - B);
@@ -123,6 +123,7 @@ __global__ void kseg_combine_kernel(const int *parts, int nseg, int rows, const 
         float v = __fmul_rn((float)(int)(uint32_t)(unsigned long long)a, sc);
         if (resid) v = __fadd_rn(resid[r], v);
         y[r] = v;
+        if (tp.world) tp_push_all(tp, (size_t)r, v);  // tensor-parallel gather of the rows
     }
 }
 
@@ -188,11 +189,12 @@ trx_status launch_rmsnorm(const float *x, const float *w, int n, float eps, floa
 }
 
 trx_status launch_kseg_combine(const int *parts, int nseg, int rows, const int *e8, int R, int B, const float *resid,
-                               float *y, cudaStream_t st) {
+                               float *y, cudaStream_t st, const TpXfer *tp) {
     int blocks = (rows + 255) / 256;
     if (blocks > 148) blocks = 148;
+    const TpXfer X = tp ? *tp : TpXfer{};
     return note_cuda(
-        launch_kernel(kseg_combine_kernel, dim3(blocks), dim3(256), 0, st, parts, nseg, rows, e8, R, B, resid, y));
+        launch_kernel(kseg_combine_kernel, dim3(blocks), dim3(256), 0, st, parts, nseg, rows, e8, R, B, resid, y, X));
 }
 
 trx_status launch_argmax_keys(const unsigned long long *keys, int n, int *token, const TpXfer &tp, uint32_t *err,

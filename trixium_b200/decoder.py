@@ -105,6 +105,8 @@ CONFIGS = {
     "tiny": DecoderConfig("tiny", 2, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY5),
     # One kv head: tensor parallelism replicates it on every rank.
     "tiny-kv1": DecoderConfig("tiny-kv1", 2, 256, 4, 1, 64, 512, 1000, L.KIND_TERNARY),
+    # An ffn wider than one tensor: the down projection is K-segmented (16384 + 128 columns).
+    "tiny-kseg": DecoderConfig("tiny-kseg", 2, 256, 4, 2, 64, 16512, 1000, L.KIND_TERNARY),
     "tiny-hybrid": DecoderConfig("tiny-hybrid", 4, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY, rope_dims=32,
                                  attn_gated=True, pattern="dda" + "a", dn_nk=2, dn_hk=64, dn_nv=4, dn_hv=64,
                                  dn_conv=4),

@@ -431,15 +431,20 @@ def rmsnorm(ctx, x, w, eps=1e-6, y=None):
     return y
 
 
-def matvec_f_kseg(ctx, segs, x, y=None, resid=None):
+def matvec_f_kseg(ctx, segs, x, y=None, resid=None, tp=None):
     """Float projection of a K-segmented tensor (trx_matvec_f_kseg): segs, the segments' DeviceTensors
-    in column order (ternary or KIND_Q8, the tensor's B/R in each); x: the full input."""
-    _need(x, torch.float32, "x")
+    in column order (ternary or KIND_Q8, the tensor's B/R in each); x: the full input.  tp: a
+    _lib.TpXfer of tagged words (trx_matvec_f_kseg_tp)."""
+    _need_x(x, tp)
     n = len(segs)
     arr = (_lib.Entry * n)(*[t.entry for t in segs])
     ptrs = (ctypes.c_void_p * n)(*[t.data.data_ptr() for t in segs])
     if y is None:
         y = torch.empty(segs[0].rows, dtype=torch.float32, device=x.device)
+    if tp is not None:
+        _lib.check(_lib.lib().trx_matvec_f_kseg_tp(ctx.h, arr, n, ptrs, _ptr(x), _ptr(resid), _ptr(y),
+                                                   ctypes.byref(tp), _stream()), "trx_matvec_f_kseg_tp")
+        return y
     _lib.check(_lib.lib().trx_matvec_f_kseg(ctx.h, arr, n, ptrs, _ptr(x), _ptr(resid), _ptr(y), _stream()),
                "trx_matvec_f_kseg")
     return y
@@ -501,15 +506,23 @@ def deltanet_shape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel=4, 
     return _lib.DeltaNetShape(n_k_heads, k_head_dim, n_v_heads, v_head_dim, conv_kernel, eps)
 
 
-def deltanet_step(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, norm_w, conv_ring, state, pos, out=None):
+def deltanet_step(ctx, shape, qkv, z, beta, alpha, dt_bias, ssm_a, conv_w, norm_w, conv_ring, state, pos, out=None,
+                  tp=None):
     """One gated-DeltaNet decode step (trx_deltanet_step); conv_ring [K, C] and state [nv, hv, hk]
-    float32 are updated in place; pos: int32 device tensor of one element."""
+    float32 are updated in place; pos: int32 device tensor of one element.  tp: a _lib.TpXfer whose
+    tagged output receives the grouped output too (trx_deltanet_step_tp)."""
     for t, n in ((qkv, "qkv"), (z, "z"), (beta, "beta"), (alpha, "alpha"), (dt_bias, "dt_bias"), (ssm_a, "ssm_a"),
                  (conv_w, "conv_w"), (norm_w, "norm_w"), (conv_ring, "conv_ring"), (state, "state")):
         _need(t, torch.float32, n)
     _need(pos, torch.int32, "pos")
     if out is None:
         out = torch.empty(shape.n_v_heads * shape.v_head_dim, dtype=torch.float32, device=qkv.device)
+    if tp is not None:
+        _lib.check(_lib.lib().trx_deltanet_step_tp(ctx.h, ctypes.byref(shape), _ptr(qkv), _ptr(z), _ptr(beta),
+                                                   _ptr(alpha), _ptr(dt_bias), _ptr(ssm_a), _ptr(conv_w),
+                                                   _ptr(norm_w), _ptr(conv_ring), _ptr(state), _ptr(pos), _ptr(out),
+                                                   ctypes.byref(tp), _stream()), "trx_deltanet_step_tp")
+        return out
     _lib.check(_lib.lib().trx_deltanet_step(ctx.h, ctypes.byref(shape), _ptr(qkv), _ptr(z), _ptr(beta), _ptr(alpha),
                                             _ptr(dt_bias), _ptr(ssm_a), _ptr(conv_w), _ptr(norm_w), _ptr(conv_ring),
                                             _ptr(state), _ptr(pos), _ptr(out), _stream()), "trx_deltanet_step")

@@ -1,4 +1,4 @@
-"""Tensor-parallel batch-1 decoding over N GPUs of one node (one process per GPU, NCCL).
+"""Tensor-parallel batch-1 decoding over N GPUs of one node (one process per GPU).
 
 Every weight matrix is sharded by output rows (the reference's channel sharding,
 model/layout.py:219-223). After each projection the ranks all-gather the output vector, so
@@ -177,8 +177,9 @@ def exchange_plan(n_layer):
 
 
 class TPDecoder:
-    """Greedy batch-1 decoding of a TPWeights shard; every rank runs the same steps in the same order
-    (the all-gathers are NCCL collectives on `group`, captured with the kernels in one CUDA graph)."""
+    """Greedy batch-1 decoding of a TPWeights shard; every rank runs the same steps in the same order.
+    The exchanges are NCCL all-gathers on `group` captured with the kernels in one CUDA graph, or
+    (p2p=True) tagged words that the kernels store into every rank's copy and poll themselves."""
 
     def __init__(self, weights: TPWeights, group=None, ctx=None, max_pos=4096, p2p=False):
         import torch
@@ -236,13 +237,9 @@ class TPDecoder:
     # (4l+1), act (4l+2), x after down (4l+3); then the LM-head keys (4L), exchanged as plain words
     # with a completion counter (one per step).
     def _p2p_supported(self, a_sh):
-        cfg = self.cfg
-        if any(cfg.layer_type(l) != "a" for l in range(cfg.n_layer)) or a_sh is None:
-            return False  # DeltaNet outputs are gathered with NCCL
-        if any(isinstance(lw["down"], list) for lw in self.w.layers):
-            return False  # the K-segmented projection has no exchanging launch
-        rep = a_sh.n_head // a_sh.n_kv
-        return cfg.head_dim in (64, 128) and 1 <= rep <= 8  # the tensor-core attention exchanges
+        """Every layer type and tensor exchanges tagged words (attention of any head dim, DeltaNet,
+        K-segmented projections)."""
+        return True
 
     def _setup_p2p(self, a_sh):
         import torch
@@ -263,9 +260,11 @@ class TPDecoder:
             return t, [b + off for b in base]
 
         E, F, N = cfg.hidden, cfg.ffn, self.world
+        types = {cfg.layer_type(l) for l in range(cfg.n_layer)}
         self.n_points = 4 * cfg.n_layer + 1
         self.x_tag, px = shared(E, torch.int64)
-        self.attn_tag, pa = shared(cfg.n_head * cfg.head_dim, torch.int64)
+        self.attn_tag, pa = shared(cfg.n_head * cfg.head_dim, torch.int64) if "a" in types else (None, None)
+        self.og_tag, pg = shared(cfg.dn_nv * cfg.dn_hv, torch.int64) if "d" in types else (None, None)
         self.act_tag, pf = shared(F, torch.int64)
         self.keys, pk = shared(N, torch.int64)
         self.cnt, pc = shared(self.n_points, torch.int32)
@@ -274,10 +273,9 @@ class TPDecoder:
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         w, r = self.w, self.rank
-        a0 = a_sh.head0 * cfg.head_dim
         lm_point = 4 * cfg.n_layer
 
-        def xfer(op, sig, wt):
+        def xfer(op, l, sig, wt):
             t = _lib.TpXfer()
             t.world, t.rank = N, r
             t.step = self.step_ctr.data_ptr()
@@ -291,7 +289,11 @@ class TPDecoder:
             elif op == "token":
                 t.wait = self.cnt.data_ptr() + 4 * lm_point
             elif sig is not None:  # a tagged output into every rank's copy, this rank's included
-                ptrs, t.offset = {"attn": (pa, a0), "o": (px, w.e0), "swiglu": (pf, w.f0), "down": (px, w.e0)}[op]
+                sh = w.layers[l]["shard"]
+                if op == "attn":  # the mixer's output: attention heads or the DeltaNet grouped block
+                    ptrs, t.offset = (pg, sh.out0) if cfg.layer_type(l) == "d" else (pa, sh.head0 * cfg.head_dim)
+                else:
+                    ptrs, t.offset = {"o": (px, w.e0), "swiglu": (pf, w.f0), "down": (px, w.e0)}[op]
                 for q in range(N):
                     t.dst[q] = ptrs[q]
                 t.tag_out = sig
@@ -301,7 +303,7 @@ class TPDecoder:
 
         self._tp = [dict() for _ in range(cfg.n_layer)]
         for op, l, sig, wt in exchange_plan(cfg.n_layer):
-            t = xfer(op, sig, wt) if (sig is not None or wt is not None) else None
+            t = xfer(op, l, sig, wt) if (sig is not None or wt is not None) else None
             if op == "lm":
                 self._tp_lm = t
             elif op == "token":
@@ -388,15 +390,26 @@ class TPDecoder:
             t = self._tp[l]
             p = lw["in"]
             xin = self.x if l == 0 else self.x_tag  # the embedding (local floats), then the tagged x
-            ops.matvec_f_multi(ctx, p.entries, p.data, xin, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
-                               eps=cfg.eps, tp=t["qkv"])
-            ops.attn_decode(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"], w.rope_freq,
-                            self.kc[l], self.vc[l], self.pos, self.attn_loc, tp=t["attn"])
-            ops.matvec_f(ctx, lw["out"], self.attn_tag, y=x_loc, resid=self.x[w.e0:w.e1] if l == 0 else x_loc,
-                         tp=t["o"])
+            if cfg.layer_type(l) == "d":
+                ops.matvec_f_multi(ctx, p.entries, p.data, xin, [self.qkv, self.z, self.beta, self.alpha],
+                                   norm_w=lw["attn_norm"], eps=cfg.eps, tp=t["qkv"])
+                ops.deltanet_step(ctx, self.dn_shape, self.qkv, self.z, self.beta, self.alpha, lw["dt_bias"],
+                                  lw["ssm_a"], lw["conv_w"], lw["ssm_norm"], self.ring[l], self.state[l], self.pos,
+                                  self.og_loc, tp=t["attn"])
+                mix = self.og_tag
+            else:
+                ops.matvec_f_multi(ctx, p.entries, p.data, xin, [self.q, self.k, self.v], norm_w=lw["attn_norm"],
+                                   eps=cfg.eps, tp=t["qkv"])
+                ops.attn_decode(ctx, self.attn_shape, self.q, self.k, self.v, lw["q_norm"], lw["k_norm"],
+                                w.rope_freq, self.kc[l], self.vc[l], self.pos, self.attn_loc, tp=t["attn"])
+                mix = self.attn_tag
+            ops.matvec_f(ctx, lw["out"], mix, y=x_loc, resid=self.x[w.e0:w.e1] if l == 0 else x_loc, tp=t["o"])
             ops.matvec_swiglu(ctx, lw["gate"], lw["up"], self.x_tag, act=self.act_loc, norm_w=lw["ffn_norm"],
                               eps=cfg.eps, tp=t["swiglu"])
-            ops.matvec_f(ctx, lw["down"], self.act_tag, y=x_loc, resid=x_loc, tp=t["down"])
+            if isinstance(lw["down"], list):
+                ops.matvec_f_kseg(ctx, lw["down"], self.act_tag, y=x_loc, resid=x_loc, tp=t["down"])
+            else:
+                ops.matvec_f(ctx, lw["down"], self.act_tag, y=x_loc, resid=x_loc, tp=t["down"])
         ops.lmhead_argmax_key(ctx, w.lm_head, self.x_tag, self.keys[self.rank:self.rank + 1], row_offset=w.v0,
                               norm_w=w.out_norm, eps=cfg.eps, tp=self._tp_lm)
         ops.argmax_token(ctx, self.keys, self.tok, tp=self._tp_tok)
@@ -410,7 +423,8 @@ class TPDecoder:
         return 4 * self.cfg.n_layer + 1
 
     def _mutable(self):
-        extra = [self.cnt, self.step_ctr, self.arrive, self.x_tag, self.attn_tag, self.act_tag] if self.p2p else []
+        extra = ([self.cnt, self.step_ctr, self.arrive, self.x_tag, self.act_tag] +
+                 [t for t in (self.attn_tag, self.og_tag) if t is not None]) if self.p2p else []
         return [self.tok, self.pos] + list(self.kc.values()) + list(self.vc.values()) + list(self.ring.values()) + \
             list(self.state.values()) + extra
 
