@@ -57,8 +57,8 @@ def measured_peaks():
 # with the sha256 of the kernel sources it was captured from.  When the sources have changed since,
 # the figure no longer describes the kernel and the line reports null.
 KERNEL_TRAFFIC = {
-    5: (267212288, "fb19ef16cb50051c38524e1ed8d7971293c36053c1c31b17066472a07663675e"),
-    0: (324044288, "fb19ef16cb50051c38524e1ed8d7971293c36053c1c31b17066472a07663675e"),
+    5: (267322112, "e211e6972875dca6d9879a4a3a731355ab43d1ed81bf66035d53d892f880292a"),
+    0: (323825408, "e211e6972875dca6d9879a4a3a731355ab43d1ed81bf66035d53d892f880292a"),
 }
 KERNEL_SOURCES = ("trixium_b200/csrc/trx_matvec.cu", "trixium_b200/csrc/trx_common.cuh")
 
@@ -426,7 +426,10 @@ def main():
     if world == 1 and not args.no_extra:
         out["other_kind"] = other_kind_leg(ctx, 0 if kind == 5 else 5, C, args.steps, args.warmup, dev, rank, peak)
     if world > 1 and not args.no_decode:
-        out["decode"] = {"qwen3-8b": tp_decode_leg(ctx, "qwen3-8b", 1024, 64, 5, rank, world, dev)}
+        # Tensor-parallel batch-1 decode: config 2, and config 4 (4 kv heads: replicated above 4 GPUs;
+        # the down projection K-segmented) at 4096 of context.
+        out["decode"] = {"qwen3-8b": tp_decode_leg(ctx, "qwen3-8b", 1024, 64, 5, rank, world, dev),
+                         "hybrid-27b": tp_decode_leg(ctx, "hybrid-27b", 4096, 32, 3, rank, world, dev)}
     if world == 1 and not args.no_decode:
         # The metric's second half: 8B-shape batch-1 decode tok/s (config 2), and config 1.
         out["decode"] = {"qwen3-8b": decode_leg(ctx, "qwen3-8b", 1024, 128, 8),
@@ -614,8 +617,8 @@ def batch_decode_leg(ctx, name, nseq, ctx_len, n_tokens, warmup):
 def tp_decode_leg(ctx, name, ctx_len, n_tokens, warmup, rank, world, dev):
     """Tensor-parallel batch-1 decode tok/s over `world` GPUs (trixium_b200.tp): every rank draws the
     same synthetic image and keeps its row shard; one CUDA graph per token holds the kernels, which
-    exchange the sharded vectors themselves over peer memory (NCCL all-gathers where a layer type
-    has no exchanging kernel); the time is the max over ranks."""
+    exchange the sharded vectors themselves over peer memory as tagged words (TRX_TP_EXCHANGE=nccl:
+    NCCL all-gathers instead); the time is the max over ranks."""
     import torch
     import torch.distributed as dist
     from trixium_b200 import decoder as D, tp

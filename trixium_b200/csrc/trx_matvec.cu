@@ -1336,7 +1336,9 @@ bool plan_matvec(const MvJobs &J, int nw, int sms, int reserved, MvGeom &M) {
     M.nw = nw;
     M.xw = t5 ? kXwT5 : kXw2b;
     M.cb = t5 ? kCbT5 : kCb2b;
-    M.D = t5 ? (nw == 2 ? 2 : TRX_MV_D_T5) : (nw == 2 ? 2 : 3);
+    // Two slots per warp: 16 warps fit (measured on B200, a single 2-bit tensor: depth 2 with 16 warps
+    // against depth 3 with 14 streamed the config-0 batch at 4.80 against 4.40 TB/s).
+    M.D = t5 ? (nw == 2 ? 2 : TRX_MV_D_T5) : 2;
     M.wjob = (J.njobs > 1 && J.w_stride != 0) ? 1 : 0;
     // Row blocks are dealt to CTAs; when a CTA gets fewer row blocks than it has warps, the warps
     // share row blocks (S per row block, chunks split between them, sums combined in shared memory)
@@ -1436,15 +1438,11 @@ static trx_status launch_tmv_d(const MvJobs &J, const MvGeom &M, const MvMaps &m
         launch_kernel(tmv_kernel<KIND, NW, R, D>, dim3(M.grid), dim3(M.warps * 32), M.smem, st, maps, J, M, err));
 }
 
-// The depths plan_matvec gives: the default (3 for a single 2-bit tensor, else 2), or shallower
-// for a decode-size launch.
+// The depths plan_matvec gives: the default 2, or 1 for a decode-size launch.
 template <int KIND, int NW, int R>
 static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, const MvMaps &maps, uint32_t *err, cudaStream_t st) {
     if (M.D == 1) return launch_tmv_d<KIND, NW, R, 1>(J, M, maps, err, st);
     if (M.D == 2) return launch_tmv_d<KIND, NW, R, 2>(J, M, maps, err, st);
-    if constexpr (KIND == TRX_KIND_TERNARY && NW == 1) {
-        if (M.D == 3) return launch_tmv_d<KIND, NW, R, 3>(J, M, maps, err, st);
-    }
     return TRX_ERR_UNSUPPORTED;
 }
 
