@@ -547,6 +547,31 @@ trx_status trx_matvec_f_kseg_tp(trx_ctx *ctx, const trx_entry *segs, int nseg, c
     }
     if (K > kQ8MaxCols) return TRX_ERR_UNSUPPORTED;
     if ((uint64_t)nseg * rows > kKsegPartInts) return TRX_ERR_UNSUPPORTED;
+    // Two ternary segments (every ternary split of K <= 32768): two launches.  Each takes the
+    // exponent of the whole input in its prologue and builds the activation words of its own
+    // columns; the first writes its int32 results, the second adds them to its own before the
+    // float scaling (the mirror's sum of the segments' results), then the residual and the
+    // exchange.  Otherwise: the quantiser, one launch per segment and the combine.
+    if (nseg == 2 && segs[0].kind != TRX_KIND_Q8 && segs[1].kind != TRX_KIND_Q8 && aligned16(d_x)) {
+        trx::MvJobs J0 = base_jobs(ctx, segs, d_packed[0]), J1 = base_jobs(ctx, segs + 1, d_packed[1]);
+        J0.x = J1.x = d_x;
+        J0.x_cols = J1.x_cols = (int)K;
+        J0.x_off = 0;
+        J1.x_off = (int)segs[0].cols;
+        J0.seg[0].y = ctx->kseg_part;
+        J0.out = trx::OUT_I32;
+        J1.part_in = ctx->kseg_part;
+        J1.seg[0].y = d_y;
+        J1.seg[0].resid = d_resid;
+        J1.out = trx::OUT_F32;
+        J1.tp = X;
+        J0.tp = X;  // the tagged input only: its results stay on this rank
+        J0.tp.tag_out = -1;
+        if (trx::matvec_launchable(J0) && trx::matvec_launchable(J1)) {
+            if (trx_status s = trx::launch_matvec(J0, ctx->lut, ctx->err, stream)) return s;
+            return trx::launch_matvec(J1, ctx->lut, ctx->err, stream);
+        }
+    }
     int *e8 = reinterpret_cast<int *>(ctx->q8x + kQ8MaxCols);
     trx_status s = tagged_in ? trx::launch_quantize_tagged(d_x, (int)K, ctx->q8x, e8, X, ctx->err, stream)
                              : trx::launch_quantize(d_x, (int)K, ctx->q8x, e8, stream);

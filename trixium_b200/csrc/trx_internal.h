@@ -109,6 +109,12 @@ struct MvJobs {
     int row_offset;              // added to the row in the argmax key (a shard's first global row)
     const int *skip;             // if set and *skip != 0, the launch does nothing
     TpXfer tp;                   // tensor-parallel exchange (tp.world == 0: none)
+    // A K-segment of a wider input (one job, the staged prologue only): x holds x_cols elements,
+    // the quantiser's exponent covers all of them, and this tensor's columns are x[x_off, x_off +
+    // cols).  x_cols == 0: x is the tensor's own input.
+    int x_cols, x_off;
+    const int *part_in;          // OUT_F32: per row, the int32 sum of the earlier K-segments, added
+                                 // before the float scaling (nullptr: none)
 };
 
 // Argmax key of (value, row): orderable float bits in the high word, ~row in the low word, so
@@ -217,6 +223,8 @@ trx_status launch_matvec_q8(const uint8_t *w, int rows, int cols, int B, int R, 
                             void *out, uint32_t *err, cudaStream_t st);
 trx_status launch_matvec_fp(const MvJobs &J, uint32_t *err, cudaStream_t st);
 trx_status launch_quantize(const float *x, int n, int8_t *x8, int *e8, cudaStream_t st);
+// launch_matvec would accept J (its plan exists and its input path applies); launches nothing.
+bool matvec_launchable(const MvJobs &J);
 // The same over a tagged input (x: tagged words of tp.tag_in, polled, bounded).
 trx_status launch_quantize_tagged(const void *x, int n, int8_t *x8, int *e8, const TpXfer &tp, uint32_t *err,
                                   cudaStream_t st);

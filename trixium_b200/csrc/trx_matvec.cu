@@ -413,9 +413,11 @@ __device__ __forceinline__ bool gather_tagged(const unsigned long long *xt, unsi
 template <int KIND>
 __device__ int build_activation_cp(const float *x, const float *nw, bool nw_ready, float eps, int K, float *xs,
                                    float *nws, uint32_t *xp, float *red64, uint64_t *mb, uint32_t parity,
-                                   uint32_t *err, bool &ok, unsigned xtag) {
+                                   uint32_t *err, bool &ok, unsigned xtag, int Kw, int x_off) {
+    // K: the elements of x (the exponent and any norm cover them all); the activation words are built
+    // for the Kw columns from x_off on.
     const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5, nwarps = blockDim.x >> 5;
-    const int G = K / 128, n4 = K / 4;
+    const int G = Kw / 128, n4 = K / 4;
     float4 *const xs4 = reinterpret_cast<float4 *>(xs);
     // One bulk copy each (tracked by its own barrier, not by the weight rings' barriers); thread 0
     // waits, bounded, and the block learns the outcome at the barrier.  (Measured on B200 in decode
@@ -475,7 +477,7 @@ __device__ int build_activation_cp(const float *x, const float *nw, bool nw_read
     const float inv = amax ? pow2f(-e8) : 0.f;  // all-zero x: every q is 0
 #pragma unroll 2
     for (int g = warp; g < G; g += nwarps) {
-        const float4 v = xs4[g * 32 + lane];
+        const float4 v = xs4[(x_off >> 2) + g * 32 + lane];
         const int q0 = quant_one(v.x, inv), q1 = quant_one(v.y, inv), q2 = quant_one(v.z, inv),
                   q3 = quant_one(v.w, inv);
         // This lane's bytes x8[4l .. 4l+3] of the group.
@@ -704,7 +706,11 @@ __device__ __forceinline__ unsigned long long finish_row(const MvJobs &J, const 
     if (J.out == OUT_I32) {
         reinterpret_cast<int *>(o.y)[srow] = (int)(a >> o.R);
     } else if (J.out == OUT_F32) {
-        float v = __fmul_rn((float)(int)(a >> o.R), o.sc);
+        // The earlier K-segments' int32 sum, added as the mirror sums the segments' results (int64,
+        // then the int32 wrap).
+        const int res = J.part_in ? (int)(uint32_t)(unsigned long long)((long long)J.part_in[srow] + (a >> o.R))
+                                  : (int)(a >> o.R);
+        float v = __fmul_rn((float)res, o.sc);
         if (o.resid) v = __fadd_rn(o.resid[srow], v);
         if (o.y) reinterpret_cast<float *>(o.y)[srow] = v;
         if (J.argmax) key = argmax_key(v, (uint32_t)(row + J.row_offset));
@@ -836,7 +842,8 @@ __global__ void __launch_bounds__(kMvThreads, 1)
     const int gi = warp / M.S, sub = warp - gi * M.S;
     const int cA = sub * M.cpt, cB = min(M.nch, cA + M.cpt);
     const int nc = cB > cA ? cB - cA : 0;
-    float *const xs = M.stage >= ((J.cols + 15) / 16) * 16 + 4 * J.cols
+    const int Kx = J.x_cols ? J.x_cols : J.cols;  // elements of x
+    float *const xs = M.stage >= ((J.cols + 15) / 16) * 16 + 4 * Kx
                           ? reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(q8) + ((J.cols + 15) / 16) * 16)
                           : nullptr;
 
@@ -901,7 +908,7 @@ __global__ void __launch_bounds__(kMvThreads, 1)
     // share while the previous kernel still runs.
     const bool fast = M.xfast && J.x;
     const int xs_off = M.stage_off + ((J.cols + 15) / 16) * 16;
-    float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * J.cols);
+    float *const nws = reinterpret_cast<float *>(smem + xs_off + 4 * Kx);
     const int ne = (warp < M.na) == (M.sreg == 0) ? min(D, M.ebl) : D;
     if (lane == 0) {
 #pragma unroll
@@ -919,8 +926,8 @@ __global__ void __launch_bounds__(kMvThreads, 1)
     if (lane == 0) mbar_fence_init();
     __syncwarp();
     if (tid == 0 && fast && J.norm_w) {  // the norm weight is written by no kernel: requested before the wait
-        mbar_arrive_expect_tx(mb + 1, 4u * J.cols);
-        bulk_g2s(nws, J.norm_w, 4u * J.cols, mb + 1);
+        mbar_arrive_expect_tx(mb + 1, 4u * Kx);
+        bulk_g2s(nws, J.norm_w, 4u * Kx, mb + 1);
     }
     piece_begin(t0);
 #pragma unroll
@@ -948,8 +955,8 @@ __global__ void __launch_bounds__(kMvThreads, 1)
         const float *xj = J.x ? J.x + (uint64_t)job * J.x_stride : nullptr;
         const int8_t *x8j = J.x8 ? J.x8 + (uint64_t)job * J.x_stride : nullptr;
         bool ok = true;
-        const int e8 = fast ? build_activation_cp<KIND>(xj, J.norm_w, first, J.eps, J.cols, xs, nws, xp, red64, mb,
-                                                        (uint32_t)(npiece & 1), err, ok, xtag)
+        const int e8 = fast ? build_activation_cp<KIND>(xj, J.norm_w, first, J.eps, Kx, xs, nws, xp, red64, mb,
+                                                        (uint32_t)(npiece & 1), err, ok, xtag, J.cols, J.x_off)
                             : build_activation<KIND>(xj, x8j, J.norm_w, J.eps, J.cols, q8, xs, xp, amax_s, red64);
         ++npiece;
         if (!ok) {  // a staging copy timed out (recorded)
@@ -1306,7 +1313,8 @@ static bool plan_rings(const MvJobs &J, int reserved, bool split, long long rbc,
     const int band = (M.sreg ? nc : M.na) * M.slot;
     const bool aligned = !(reinterpret_cast<uintptr_t>(J.x) & 15) && !(reinterpret_cast<uintptr_t>(J.norm_w) & 15) &&
                          !(J.x_stride & 3);
-    const int need = aligned ? (J.cols + 15) / 16 * 16 + 4 * J.cols * (J.norm_w ? 2 : 1) : J.cols;
+    const int Kx = J.x_cols ? J.x_cols : J.cols;  // elements of x
+    const int need = aligned ? (J.cols + 15) / 16 * 16 + 4 * Kx * (J.norm_w ? 2 : 1) : J.cols;
     const int own = (M.smem + 127) / 128 * 128;
     if (own + need <= kSmemMax) {  // a region of its own after the rings: no slot waits for the prologue
         M.stage_off = own;
@@ -1446,14 +1454,23 @@ static trx_status launch_tmv(const MvJobs &J, const MvGeom &M, const MvMaps &map
     return TRX_ERR_UNSUPPORTED;
 }
 
+bool matvec_launchable(const MvJobs &J) {
+    MvGeom M;
+    const DevInfo di = dev_info();
+    if (!plan_matvec(J, J.w2 ? 2 : 1, di.sms, di.reserved, M)) return false;
+    return !(((J.tp.tag_points && J.tp.tag_in >= 0) || J.x_cols) && (!M.xfast || !J.x || J.njobs != 1));
+}
+
 trx_status launch_matvec(const MvJobs &J, const uint32_t *lut, uint32_t *err, cudaStream_t st) {
     (void)lut;  // the trit5 LUT is built in each CTA's shared memory
     MvGeom M;
     const DevInfo di = dev_info();
     const int nw = J.w2 ? 2 : 1;
     if (!plan_matvec(J, nw, di.sms, di.reserved, M)) return TRX_ERR_UNSUPPORTED;
-    // A tagged input is read only by the staged prologue, one job at a time.
-    if (J.tp.tag_points && J.tp.tag_in >= 0 && (!M.xfast || !J.x || J.njobs != 1)) return TRX_ERR_UNSUPPORTED;
+    // A tagged input, or a K-segment of a wider input, is read only by the staged prologue, one job at
+    // a time.
+    if (((J.tp.tag_points && J.tp.tag_in >= 0) || J.x_cols) && (!M.xfast || !J.x || J.njobs != 1))
+        return TRX_ERR_UNSUPPORTED;
     MvMaps maps;
     const trx_status s = encode_maps(J, M, maps);
     if (s != TRX_OK) return s;

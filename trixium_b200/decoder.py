@@ -326,11 +326,16 @@ class Decoder:
 
     def launches_per_step(self):
         # embedding; per layer 5 (input projections, attention or DeltaNet, output projection,
-        # gate/up, down), a K-segmented down projection nseg + 2 (quantise, segments, combine);
-        # LM head and position advance.
+        # gate/up, down), a K-segmented down projection one launch per segment, plus the quantiser
+        # and the combine unless it has two ternary segments (trx_matvec_f_kseg); LM head and
+        # position advance.
+        def kseg_launches(segs):
+            two = len(segs) == 2 and all(t.kind != L.KIND_Q8 for t in segs)
+            return len(segs) + (0 if two else 2)
+
         n = 1 + 2
         for lw in self.w.layers:
-            n += 4 + (len(lw["down"]) + 2 if isinstance(lw["down"], list) else 1)
+            n += 4 + (kseg_launches(lw["down"]) if isinstance(lw["down"], list) else 1)
         return n
 
     def capture(self):
