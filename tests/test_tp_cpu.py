@@ -63,7 +63,8 @@ def _rank(rank, world, port, name, out):
         torch.distributed.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,world", [("tiny", 2), ("tiny-hybrid", 2), ("tiny", 4), ("tiny-kv1", 2)])
+@pytest.mark.parametrize("name,world", [("tiny", 2), ("tiny-hybrid", 2), ("tiny", 4), ("tiny-kv1", 2),
+                                        ("tiny-hd256", 2)])
 def test_sharded_oracle_matches_unsharded(name, world):
     """World 4 on "tiny" (2 kv heads): each kv head replicated on two ranks."""
     from oracle.model import OracleModel

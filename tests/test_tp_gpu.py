@@ -63,7 +63,7 @@ def _rank(rank, world, port, name, out, p2p=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("name", ["tiny", "tiny-hybrid", "tiny-kv1", "tiny-kseg"])
+@pytest.mark.parametrize("name", ["tiny", "tiny-hybrid", "tiny-kv1", "tiny-kseg", "tiny-hd256"])
 def test_tp_world2_matches_decoder(name):
     """tiny-kv1 has one kv head: both ranks hold it (replicated) and split its query heads."""
     want = single_gpu_tokens(name)
@@ -83,7 +83,7 @@ def test_tp_world2_matches_decoder(name):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("name", ["tiny", "tiny-kv1", "tiny-hybrid", "tiny-kseg"])
+@pytest.mark.parametrize("name", ["tiny", "tiny-kv1", "tiny-hybrid", "tiny-kseg", "tiny-hd256"])
 def test_tp_world2_peer_exchange_matches_decoder(name):
     """The all-gathers done by the kernels themselves over peer memory (tagged words, no NCCL on the
     data path)."""

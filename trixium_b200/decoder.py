@@ -105,6 +105,10 @@ CONFIGS = {
     "tiny": DecoderConfig("tiny", 2, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY5),
     # One kv head: tensor parallelism replicates it on every rank.
     "tiny-kv1": DecoderConfig("tiny-kv1", 2, 256, 4, 1, 64, 512, 1000, L.KIND_TERNARY),
+    # Head dim 256 with one kv head and 6 query heads: over two ranks each holds the kv head and
+    # 3 query heads, the shape config 4 has on 8 GPUs (the scratch-merge attention kernel).
+    "tiny-hd256": DecoderConfig("tiny-hd256", 2, 256, 6, 1, 256, 512, 1000, L.KIND_TERNARY, rope_dims=64,
+                                attn_gated=True),
     # An ffn wider than one tensor: the down projection is K-segmented (16384 + 128 columns).
     "tiny-kseg": DecoderConfig("tiny-kseg", 2, 256, 4, 2, 64, 16512, 1000, L.KIND_TERNARY),
     "tiny-hybrid": DecoderConfig("tiny-hybrid", 4, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY, rope_dims=32,
