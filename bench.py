@@ -57,8 +57,8 @@ def measured_peaks():
 # with the sha256 of the kernel sources it was captured from.  When the sources have changed since,
 # the figure no longer describes the kernel and the line reports null.
 KERNEL_TRAFFIC = {
-    5: (267322112, "e211e6972875dca6d9879a4a3a731355ab43d1ed81bf66035d53d892f880292a"),
-    0: (323825408, "e211e6972875dca6d9879a4a3a731355ab43d1ed81bf66035d53d892f880292a"),
+    5: (267236608, "eae26433eef9aaa685f48c62a261732b400e1a9b09d00a734678f71f3be39b8c"),
+    0: (323869696, "eae26433eef9aaa685f48c62a261732b400e1a9b09d00a734678f71f3be39b8c"),
 }
 KERNEL_SOURCES = ("trixium_b200/csrc/trx_matvec.cu", "trixium_b200/csrc/trx_common.cuh")
 
