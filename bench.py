@@ -439,7 +439,10 @@ def main():
                          "hybrid-2b": decode_leg(ctx, "hybrid-2b", 2048, 256, 8),
                          "hybrid-27b": decode_leg(ctx, "hybrid-27b", 4096, 128, 8)}
         # Config 2 at batch 16: 16 sequences in lockstep on the tensor-core rows projection.
-        out["decode_batch"] = {"qwen3-8b": batch_decode_leg(ctx, "qwen3-8b", 16, 1024, 16, 3)}
+        # Config 4 at batch 32: 32 sequences at 4096 of context, the K-segmented down projection on
+        # the tensor cores (trx_matvec_f_rows_kseg).
+        out["decode_batch"] = {"qwen3-8b": batch_decode_leg(ctx, "qwen3-8b", 16, 1024, 16, 3),
+                               "hybrid-27b": batch_decode_leg(ctx, "hybrid-27b", 32, 4096, 8, 3)}
     if world == 1 and not args.no_decode:
         out["q8_matvec"] = q8_leg(ctx, peak)
         out["batched_rows"] = [rows_leg(ctx, peak, k, nb) for k in (5, 0) for nb in (16, 32)]
@@ -581,7 +584,8 @@ def decode_leg(ctx, name, ctx_len, n_tokens, warmup):
 
 
 def batch_decode_leg(ctx, name, nseq, ctx_len, n_tokens, warmup):
-    """Batched greedy decode (trixium_b200.decoder.BatchDecoder, BASELINE config 2 at batch 16):
+    """Batched greedy decode (trixium_b200.decoder.BatchDecoder; BASELINE config 2 at batch 16, config 4
+    at batch 32):
     nseq sequences in lockstep, every projection one tensor-core launch over their rows, one CUDA
     graph per step.  tok_s counts every sequence's tokens."""
     import torch

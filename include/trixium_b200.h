@@ -472,6 +472,13 @@ trx_status trx_matvec_f_kseg_tp(trx_ctx *ctx, const trx_entry *segs, int nseg, c
                                 const float *d_x, const float *d_resid, float *d_y, const trx_tp_xfer *tp,
                                 cudaStream_t stream);
 
+/* trx_matvec_f_kseg for a batch of nb <= 32 rows on the tensor cores (model/mirror.py:648-678 per row):
+ * d_x [nb][K] with K the segments' total width, each row quantised with one exponent over all K,
+ * d_y [nb][rows] (plus d_resid [nb][rows] when given).  Two ternary segments of one kind only
+ * (TRX_ERR_UNSUPPORTED otherwise). */
+trx_status trx_matvec_f_rows_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
+                                  const float *d_x, int nb, const float *d_resid, float *d_y, cudaStream_t stream);
+
 /* trx_argmax_token after waiting for the exchange of the keys. */
 trx_status trx_argmax_token_tp(trx_ctx *ctx, const uint64_t *d_keys, int32_t n, int32_t *d_token,
                                const trx_tp_xfer *tp, cudaStream_t stream);

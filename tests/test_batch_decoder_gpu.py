@@ -34,11 +34,27 @@ def test_batch_decoder_tokens_match_oracle(name, graph):
         assert got[i] == orc.generate(prompt, 24), i
 
 
+def test_batch_decoder_k_segments_match_decoder():
+    """A K-segmented down projection (two ternary segments, trx_matvec_f_rows_kseg): every sequence's
+    tokens equal the batch-1 decoder's (whose K-segment projection is pinned bit-exact to the
+    reference's own segments), eagerly and replayed from a CUDA graph."""
+    from trixium_b200 import decoder as D
+    w = D.SyntheticWeights(D.CONFIGS["tiny-kseg"], seed=5)
+    assert isinstance(w.layers[0]["down"], list) and len(w.layers[0]["down"]) == 2
+    want = [D.Decoder(w, max_pos=64).generate(p, 24) for p in PROMPTS]
+    for graph in (False, True):
+        bd = D.BatchDecoder(w, len(PROMPTS), max_pos=64)
+        if graph:
+            bd.capture()
+        assert bd.generate(PROMPTS, 24) == want, graph
+
+
 def test_batch_decoder_rejects_k_segments():
+    """More than two K-segments: refused."""
     from trixium_b200 import decoder as D
     cfg = D.CONFIGS["tiny"]
     w = D.SyntheticWeights(cfg, seed=1)
-    w.layers[0]["down"] = [w.layers[0]["down"], w.layers[0]["down"]]
+    w.layers[0]["down"] = [w.layers[0]["down"]] * 3
     with pytest.raises(ValueError):
         D.BatchDecoder(w, 2, max_pos=32)
     with pytest.raises(ValueError):

@@ -111,3 +111,21 @@ def test_rows_multi_segments_with_norm(ops, ctx, kind):
         want = ops.matvec_f_rows(ctx, p.tensor(i), h, resid=rs[i])
         assert torch.equal(ys[i].view(torch.int32), want.view(torch.int32)), i
     assert ctx.errors() == 0
+
+
+@pytest.mark.parametrize("nb", [3, 16, 32])
+@pytest.mark.parametrize("kind", KINDS)
+def test_rows_k_segments_bit_exact(ops, ctx, kind, nb):
+    """trx_matvec_f_rows_kseg (two K-segments of 8704 columns, one exponent per row over both,
+    a residual) equals trx_matvec_f_kseg on each row, bit for bit."""
+    from trixium_b200 import decoder as D
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    segs = D.ksegmented(gen, 300, 17408, kind, "cuda")
+    assert len(segs) == 2
+    x = torch.randn(nb, 17408, generator=gen, device="cuda")
+    r = torch.randn(nb, 300, generator=gen, device="cuda")
+    y = ops.matvec_f_rows_kseg(ctx, segs, x, resid=r)
+    for b in range(nb):
+        want = ops.matvec_f_kseg(ctx, segs, x[b].contiguous(), resid=r[b].contiguous())
+        assert torch.equal(y[b].view(torch.int32), want.view(torch.int32)), b
+    assert ctx.errors() == 0

@@ -29,7 +29,7 @@ SYMBOLS = (
     "trx_attn_decode_f32cache", "trx_matvec_f_rows", "trx_embed_lookup_rows", "trx_rmsnorm_rows", "trx_silu_mul",
     "trx_argmax_rows", "trx_advance_positions", "trx_attn_decode_rows", "trx_deltanet_step_rows",
     "trx_deltanet_int_step", "trx_matvec_fp_rows", "trx_matvec_f_rows_multi", "trx_deltanet_step_tp",
-    "trx_matvec_f_kseg_tp",
+    "trx_matvec_f_kseg_tp", "trx_matvec_f_rows_kseg",
 )
 
 TP_MAX = 8
@@ -141,6 +141,7 @@ def lib():
             "trx_rmsnorm": ([_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_float, _vp, _vp], ctypes.c_int),
             "trx_matvec_f_kseg": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
             "trx_matvec_f_kseg_tp": ([_vp, E, ctypes.c_int, _vp, _vp, _vp, _vp, T, _vp], ctypes.c_int),
+            "trx_matvec_f_rows_kseg": ([_vp, E, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
             "trx_deltanet_step_tp": ([_vp, ctypes.POINTER(DeltaNetShape)] + [_vp] * 12 + [T, _vp], ctypes.c_int),
             "trx_attn_decode_f32cache": ([_vp, ctypes.POINTER(AttnShape)] + [_vp] * 11, ctypes.c_int),
             "trx_matvec_f_rows": ([_vp, E, _vp, _vp, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),

@@ -226,6 +226,38 @@ static trx_status rows_tc(trx_ctx *ctx, const trx_entry *e, const void *d_packed
                                    stream);
 }
 
+trx_status trx_matvec_f_rows_kseg(trx_ctx *ctx, const trx_entry *segs, int nseg, const void *const *d_packed,
+                                  const float *d_x, int nb, const float *d_resid, float *d_y, cudaStream_t stream) {
+    if (!ctx || !segs || !d_packed || !d_x || !d_y || nb < 1 || nb > kRowsMax) return TRX_ERR_ARG;
+    if (nseg != 2) return TRX_ERR_UNSUPPORTED;  // two ternary segments (every split of K <= 32768)
+    const uint32_t rows = segs[0].rows;
+    uint32_t K = 0;
+    for (int i = 0; i < nseg; ++i) {
+        if (trx_status s = check_entry(segs + i)) return s;
+        if (!d_packed[i] || !aligned16(d_packed[i])) return TRX_ERR_ARG;
+        if (segs[i].rows != rows || segs[i].bias != segs[0].bias || segs[i].rshift != segs[0].rshift ||
+            segs[i].kind != segs[0].kind)
+            return TRX_ERR_ARG;
+        K += segs[i].cols;
+    }
+    if (K > kQ8MaxCols) return TRX_ERR_UNSUPPORTED;
+    if ((uint64_t)nb * rows > kKsegPartInts) return TRX_ERR_UNSUPPORTED;
+    // Segment 0: the prep over all K columns (one exponent per row), its int32 results; segment 1:
+    // the same prepped activation from column cols0 on, plus segment 0's results, then the scaling.
+    trx::RowsSeg s0{(int)rows, segs[0].bias, segs[0].rshift, ctx->kseg_part, nullptr, nullptr, nullptr};
+    trx::RowsSeg s1{(int)rows, segs[1].bias, segs[1].rshift, nullptr, d_y, d_resid, ctx->kseg_part};
+    const int sms = trx::device_sms(), res = trx::device_reserved_smem();
+    trx_status s = trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed[0]), (int)segs[0].cols, segs[0].kind,
+                                           &s0, 1, d_x, nullptr, nb, nullptr, 0.f, ctx->rows_x8p, ctx->rows_xsum,
+                                           ctx->rows_e8, ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsCnt, ctx->err, sms,
+                                           res, stream, (int)K, 0, true);
+    if (s) return s;
+    return trx::launch_matvec_rows(static_cast<const uint8_t *>(d_packed[1]), (int)segs[1].cols, segs[1].kind, &s1, 1,
+                                   d_x, nullptr, nb, nullptr, 0.f, ctx->rows_x8p, ctx->rows_xsum, ctx->rows_e8,
+                                   ctx->rows_acc, kRowsAcc, ctx->rows_cnt, kRowsCnt, ctx->err, sms, res, stream, (int)K,
+                                   (int)segs[0].cols, false);
+}
+
 trx_status trx_matvec_f_rows(trx_ctx *ctx, const trx_entry *e, const void *d_packed, const float *d_x, int nb,
                              const float *d_resid, float *d_y, cudaStream_t stream) {
     if (!ctx) return TRX_ERR_ARG;

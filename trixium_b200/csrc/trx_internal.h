@@ -210,12 +210,17 @@ struct RowsSeg {
     int32_t *out_i;
     float *out_f;
     const float *resid;
+    const int32_t *part_in;  // [nb][rows] int32 sum of the earlier K-segments, added before the scaling
 };
 constexpr int kRowsMaxSegs = 4;
 trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *segs, int nseg, const float *x,
                               const int8_t *x8, int nb, const float *norm_w, float eps, int8_t *x8p, int *xsum,
                               int *e8, unsigned long long *acc_scratch, size_t acc_cap, unsigned *cnt, int cnt_cap,
-                              uint32_t *err, int sms, int reserved, cudaStream_t st);
+                              uint32_t *err, int sms, int reserved, cudaStream_t st, int K_full = 0, int k_off = 0,
+                              bool prep = true);
+// K_full (0: K): the width of x (and of x8p, xsum); the tensor's columns are [k_off, k_off + K) of
+// it.  prep: quantise x into x8p/xsum/e8 first (false: they already hold it, from a launch over
+// another K-segment of the same x).
 int device_sms();
 int device_reserved_smem();
 // The Q8 row dot (trx_q8.cu): int32 results, or with e8 the float projection (fp32 out).

@@ -634,8 +634,11 @@ __global__ void __maxnreg__(128)
             const RowsSeg &S = A.seg[sg];
             const int sn = n - (sg ? A.seg_end[sg - 1] : 0);  // the row within its tensor
             if (acc_bad(a, S.R)) atomicOr(err, TRX_DEV_OVERFLOW);
-            const int res = (int)(a >> S.R);
             const size_t o = (size_t)b * S.rows + sn;
+            // With earlier K-segments: their int32 sum plus this one's, wrapped to int32 (the mirror's
+            // int64 sum of the segments' results).
+            const int res = S.part_in ? (int)(uint32_t)(unsigned long long)((long long)S.part_in[o] + (a >> S.R))
+                                      : (int)(a >> S.R);
             if (S.out_f) {
                 float y = __fmul_rn((float)res, pow2f(A.e8[b] + S.R - S.B));
                 if (S.resid) y = __fadd_rn(S.resid[o], y);
@@ -859,8 +862,11 @@ static trx_status launch_rows_t(const RowsMaps &maps, const RowsArgs &A, int gri
 trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *segs, int nseg, const float *x,
                               const int8_t *x8, int nb, const float *norm_w, float eps, int8_t *x8p, int *xsum,
                               int *e8, unsigned long long *acc_scratch, size_t acc_cap, unsigned *cnt, int cnt_cap,
-                              uint32_t *err, int sms, int reserved, cudaStream_t st) {
+                              uint32_t *err, int sms, int reserved, cudaStream_t st, int K_full, int k_off,
+                              bool prep) {
     if (nseg < 1 || nseg > kRowsMaxSegs) return TRX_ERR_ARG;
+    if (!K_full) K_full = K;
+    if (k_off < 0 || k_off % 128 || k_off + K > K_full || (!prep && !x8p)) return TRX_ERR_ARG;
     int N = 0;
     const int BN = nb <= 16 ? 16 : 32;
     RowsArgs A{};
@@ -889,7 +895,7 @@ trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *
         A.ks = 1;
         A.cps = A.nch;
     }
-    A.xsum = xsum;
+    A.xsum = xsum + (size_t)(k_off / 128) * 32;  // this segment's groups
     A.e8 = e8;
     A.acc = acc_scratch;
     A.cnt = cnt;
@@ -900,14 +906,14 @@ trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *
     const cuuint64_t wd[2] = {(cuuint64_t)A.rb, (cuuint64_t)N}, ws[1] = {(cuuint64_t)A.rb};
     const cuuint32_t cbox[2] = {(cuuint32_t)(kind == TRX_KIND_TERNARY5 ? kRowsCb5 : kRowsCb2), (cuuint32_t)kRowsM};
     const cuuint32_t sbox[2] = {16, (cuuint32_t)kRowsM};
-    const cuuint64_t xd[2] = {(cuuint64_t)K, (cuuint64_t)nb}, xs[1] = {(cuuint64_t)K};
+    const cuuint64_t xd[2] = {(cuuint64_t)K, (cuuint64_t)nb}, xs[1] = {(cuuint64_t)K_full};
     const cuuint32_t xbox[2] = {128, (cuuint32_t)BN};
     if (!encode(&maps.codes, w, wd, ws, cbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !encode(&maps.scales, w, wd, ws, sbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&maps.xp, x8p, xd, xs, xbox, CU_TENSOR_MAP_SWIZZLE_128B))
+        !encode(&maps.xp, x8p + k_off, xd, xs, xbox, CU_TENSOR_MAP_SWIZZLE_128B))
         return TRX_ERR_CUDA;
     // The permuted activation, its group sums and exponents (one CTA per batch row).
-    const size_t prep_smem = (size_t)(K + 15) / 16 * 16 + (norm_w ? (size_t)K * 4 : 0);
+    const size_t prep_smem = (size_t)(K_full + 15) / 16 * 16 + (norm_w ? (size_t)K_full * 4 : 0);
     constexpr int kPrepSmemMax = 192 * 1024;  // K <= 32768: 32 KiB of q8 and 128 KiB of normalised x
     if (prep_smem > (size_t)kPrepSmemMax) return TRX_ERR_UNSUPPORTED;
     static DevBits prep_configured{0};
@@ -915,8 +921,11 @@ trx_status launch_matvec_rows(const uint8_t *w, int K, int kind, const RowsSeg *
         return cudaFuncSetAttribute(rows_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmemMax);
     });
     if (e != cudaSuccess) return note_cuda(e);
-    e = launch_kernel(rows_prep_kernel, dim3(nb), dim3(256), prep_smem, st, x, x8, norm_w, eps, K, kind, x8p, xsum, e8);
-    if (e != cudaSuccess) return note_cuda(e);
+    if (prep) {
+        e = launch_kernel(rows_prep_kernel, dim3(nb), dim3(256), prep_smem, st, x, x8, norm_w, eps, K_full, kind, x8p,
+                          xsum, e8);
+        if (e != cudaSuccess) return note_cuda(e);
+    }
     const int units = A.tiles * A.ks;
     const int grid = std::max(1, std::min(sms, (units + nwg - 1) / nwg));
     if (kind == TRX_KIND_TERNARY5)

@@ -109,7 +109,7 @@ CONFIGS = {
     # 3 query heads, the shape config 4 has on 8 GPUs (the scratch-merge attention kernel).
     "tiny-hd256": DecoderConfig("tiny-hd256", 2, 256, 6, 1, 256, 512, 1000, L.KIND_TERNARY, rope_dims=64,
                                 attn_gated=True),
-    # An ffn wider than one tensor: the down projection is K-segmented (16384 + 128 columns).
+    # An ffn wider than one tensor: the down projection is K-segmented (two segments, 8192 + 8320 columns).
     "tiny-kseg": DecoderConfig("tiny-kseg", 2, 256, 4, 2, 64, 16512, 1000, L.KIND_TERNARY),
     "tiny-hybrid": DecoderConfig("tiny-hybrid", 4, 256, 4, 2, 64, 512, 1000, L.KIND_TERNARY, rope_dims=32,
                                  attn_gated=True, pattern="dda" + "a", dn_nk=2, dn_hk=64, dn_nv=4, dn_hv=64,
@@ -391,15 +391,17 @@ class BatchDecoder:
     down projections add the residual, SwiGLU, the final norm, argmax and position advance are
     row-wise kernels, and attention and the DeltaNet step run over a sequence grid dimension with
     per-sequence caches, states and positions.  The arithmetic of every sequence is the batch-1
-    decoder's (mirror.py:1002-1034).  K-segmented tensors (the hybrid-27b down projection) are not
-    taken: one batched launch covers one engine op's K."""
+    decoder's (mirror.py:1002-1034).  A K-segmented down projection (hybrid-27b) of two ternary
+    segments takes trx_matvec_f_rows_kseg: one exponent per sequence over the whole act."""
 
     def __init__(self, weights: SyntheticWeights, nseq, ctx=None, max_pos=4096, kv_dtype=torch.float16):
         cfg = self.cfg = weights.cfg
         if not 1 <= nseq <= 32:
             raise ValueError("BatchDecoder: 1 <= nseq <= 32")
-        if any(isinstance(lw["down"], list) for lw in weights.layers):
-            raise ValueError("BatchDecoder: K-segmented tensors are not supported")
+        for lw in weights.layers:
+            d = lw["down"]
+            if isinstance(d, list) and (len(d) != 2 or any(t.kind == L.KIND_Q8 for t in d)):
+                raise ValueError("BatchDecoder: a K-segmented tensor needs two ternary segments")
         self.w, self.nseq = weights, nseq
         self.ctx = ctx or ops.default_context()
         dev = weights.emb.device
@@ -473,7 +475,10 @@ class BatchDecoder:
             ops.matvec_f_rows_multi(ctx, ffn.entries, ffn.data, self.x, [self.g, self.u], norm_w=lw["ffn_norm"],
                                     eps=cfg.eps)
             ops.silu_mul(ctx, self.g, self.u, self.act)
-            ops.matvec_f_rows(ctx, lw["down"], self.act, out=self.x, resid=self.x)
+            if isinstance(lw["down"], list):
+                ops.matvec_f_rows_kseg(ctx, lw["down"], self.act, out=self.x, resid=self.x)
+            else:
+                ops.matvec_f_rows(ctx, lw["down"], self.act, out=self.x, resid=self.x)
         ops.rmsnorm_rows(ctx, self.x, w.out_norm, cfg.eps, y=self.h)
         ops.matvec_f_rows(ctx, w.lm_head, self.h, out=self.logits)
         ops.argmax_rows(ctx, self.logits, self.tok)

@@ -164,6 +164,23 @@ def matvec_f_rows(ctx, w: DeviceTensor, xrows, out=None, resid=None):
     return out
 
 
+def matvec_f_rows_kseg(ctx, segs, xrows, out=None, resid=None):
+    """Batched float projection of a K-segmented tensor (trx_matvec_f_rows_kseg): segs, the two
+    segments' DeviceTensors in column order; xrows [nb, K] float32 (nb <= 32), each row quantised
+    with one exponent over all K; returns [nb, rows] float32 (plus resid)."""
+    _need(xrows, torch.float32, "xrows")
+    nb, n = xrows.shape[0], len(segs)
+    if out is None:
+        out = torch.empty(nb, segs[0].rows, dtype=torch.float32, device=xrows.device)
+    if resid is not None:
+        _need(resid, torch.float32, "resid")
+    arr = (_lib.Entry * n)(*[t.entry for t in segs])
+    ptrs = (ctypes.c_void_p * n)(*[t.data.data_ptr() for t in segs])
+    _lib.check(_lib.lib().trx_matvec_f_rows_kseg(ctx.h, arr, n, ptrs, _ptr(xrows), nb, _ptr(resid), _ptr(out),
+                                                 _stream()), "trx_matvec_f_rows_kseg")
+    return out
+
+
 def embed_lookup_rows(ctx, table, tokens, x):
     """x[r] = table[tokens[r]] for every row r (fp16 or fp32 table [vocab, dim])."""
     _need(tokens, torch.int32, "tokens")
