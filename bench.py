@@ -72,9 +72,10 @@ def kernel_sources_sha():
     return h.hexdigest()
 
 
-def measured_traffic(kind):
+def measured_traffic(kind, copies=96):
+    """The captured figure, for the 96-copy launch it was captured on and the sources it describes."""
     t = KERNEL_TRAFFIC.get(kind)
-    return float(t[0]) if t and t[1] == kernel_sources_sha() else None
+    return float(t[0]) if t and copies == 96 and t[1] == kernel_sources_sha() else None
 
 
 class ClockSampler:
@@ -255,7 +256,7 @@ def other_kind_leg(ctx, kind, C, steps, warmup, dev, rank, peak):
     return {"metric": metric_name(kind), "value": round(achieved, 1), "unit": "GB/s", "ms_per_launch": launch_ms,
             "parity_copy0_bitexact": parity,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": measured_traffic(kind),
+                         "frac": round(achieved / peak, 4), "traffic": measured_traffic(kind, C),
                          "algorithmic_bytes_per_launch": alg}}
 
 
@@ -412,7 +413,7 @@ def main():
         "frac_of_8tbs_nominal": round(value / world / NOMINAL_HBM_GBS, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                     "traffic": measured_traffic(kind), "kernel_sources_sha256": kernel_sources_sha(),
+                     "traffic": measured_traffic(kind, C), "kernel_sources_sha256": kernel_sources_sha(),
                      "algorithmic_bytes_per_launch": alg_per_step,
                      "kernel": "trx::tmv_kernel (trx_matvec_f_batch)"},
         "per_launch_single_matvec": None if single_ms is None else {
